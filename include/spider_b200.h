@@ -1,0 +1,260 @@
+/*
+ * spider_b200.h -- C ABI of the B200-native recurrent Spider-MoE block.
+ *
+ * The library (libspider_b200.so, built for sm_100a) exports plain extern "C"
+ * functions: raw device pointers, sizes and a cudaStream_t passed as void*.
+ * No torch types cross this boundary.  Every function returns an int status
+ * (0 = ok), the convention of the reference C ABI
+ * (kernels/include/spider_kernels.h:26-150: 0 ok, 1 bad argument, 2 index out
+ * of range) extended with the codes below.  Work is only enqueued on the given
+ * stream; nothing synchronises.  The library never allocates device memory on
+ * a hot path: scratch space is a caller-owned workspace whose size the
+ * *_workspace_bytes queries return (the pattern of the reference's
+ * spider_cuda_expert_workspace_bytes, kernels/cuda/spider_expert_v2.cu:61-64).
+ *
+ * The arithmetic follows the reference PyTorch block (spider_moe/model.py:
+ * 240-317), not the reference's own native kernels (which use tanh-GELU and a
+ * static CSR graph, kernels/scalar/scalar.cpp:55-73).
+ */
+#ifndef SPIDER_B200_H
+#define SPIDER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define SB_API __declspec(dllexport)
+#else
+#define SB_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ codes */
+enum {
+  SB_OK = 0,
+  SB_ERR_ARG = 1,           /* bad argument (reference code 1) */
+  SB_ERR_INDEX = 2,         /* index out of range (reference code 2) */
+  SB_ERR_UNSUPPORTED = 3,   /* shape / format this build does not handle */
+  SB_ERR_NO_DEVICE = 4,     /* no sm_100 device current */
+  SB_ERR_WORKSPACE = 5,     /* workspace missing or too small */
+  SB_ERR_DEVICE_STATUS = 6, /* a kernel recorded a device-side status word */
+  SB_ERR_CUDA_BASE = 1000   /* 1000 + cudaError_t of a failed runtime call */
+};
+
+/* activation storage / compute types of the token rows */
+enum { SB_F32 = 0, SB_BF16 = 1 };
+/* expert weight formats (spider_moe/quant.py) */
+enum {
+  SB_W_F32 = 0,  /* fp32 weights (CUDA-core engine only) */
+  SB_W_BF16 = 1,
+  SB_W_FP8 = 2,  /* e4m3 bytes + fp32 scale per output row (quant.py:146-169) */
+  SB_W_INT4 = 3  /* packed nibbles, even index low, + bf16 scale per row group (quant.py:89-143) */
+};
+/* expert activation */
+enum { SB_ACT_GELU = 0, SB_ACT_SWIGLU = 1 };
+/* grouped-GEMM epilogues */
+enum {
+  SB_EPI_LINEAR = 0, /* out_f32[row, m] = (acc + bias[m]) * row_scale[row]  (bias, scale optional) */
+  SB_EPI_GELU = 1,   /* out_act[row, m] = gelu_erf(acc + bias[m])                             */
+  SB_EPI_SWIGLU = 2  /* out_act[row, m] = silu(acc_gate + bias_gate[m]) * (acc + bias[m])      */
+};
+/* GEMM engines */
+enum { SB_ENGINE_AUTO = 0, SB_ENGINE_SIMT = 1, SB_ENGINE_TCGEN05 = 2 };
+/* grouping flags */
+enum { SB_GROUP_POSITIVE_ONLY = 1 };
+
+/* ------------------------------------------------------------------ info */
+/* Bit 0: library built for sm_100a; bit 1: current device is compute capability 10.x. */
+SB_API int sb_capabilities(void);
+SB_API const char* sb_version(void);
+SB_API const char* sb_error_string(int code);
+
+/* ------------------------------------------------------------------ router
+ * Replaces spider_router_f32 (kernels/include/spider_kernels.h:26-28) and the
+ * router lines of SpiderMoELayer.forward (spider_moe/model.py:254-258):
+ * logits = h . router_w^T + loop_bias_l; fp32 softmax over E; top-k of the
+ * probabilities (descending; equal values -> smaller expert id first);
+ * weights renormalised by max(sum, 1e-9).  probs may be NULL.
+ * h: [n_tokens, hidden] (act_dtype); router_w: [E, hidden] (act_dtype). */
+SB_API int sb_router(const void* h, int act_dtype, int n_tokens, int hidden, const void* router_w,
+                     const float* loop_bias_l, int num_experts, int top_k, int32_t* top_idx,
+                     float* top_w, float* probs, void* stream);
+
+/* ------------------------------------------------------------------ grouping
+ * Replaces build_dispatch_plan (spider_infer/forge/ep/dispatch.py:56-115) as a
+ * device permutation.  Entries are idx[row, slot] (row-major, `slots` per row).
+ * Within a row, repeats of a group id are merged into the first occurrence and
+ * their weights summed (sparse_experts.py:52-55).  With SB_GROUP_POSITIVE_ONLY
+ * an entry whose summed weight is <= 0 is dropped (dispatch.py:94).  Groups
+ * are laid out in ascending id, each with its rows in ascending order, so the
+ * permutation is identical to the reference plan.
+ * Outputs: offsets[G+1]; for permuted position p < offsets[G]: perm_row[p]
+ * (token row), perm_slot[p] (row*slots+slot of the first occurrence),
+ * perm_w[p] (summed weight; w may be NULL -> 1); inv[row*slots+slot] = p or -1.
+ * Group ids outside [0, G) are skipped (expert-parallel ranks pass ids already
+ * mapped to local experts, -1 for remote ones). */
+SB_API size_t sb_group_workspace_bytes(int n_rows, int slots, int num_groups);
+SB_API int sb_group(const int32_t* idx, const float* w, int n_rows, int slots, int num_groups,
+                    int flags, int32_t* offsets, int32_t* perm_row, int32_t* perm_slot,
+                    float* perm_w, int32_t* inv, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/* dst[p, :] = src[perm_row[p], :] for p < offsets[num_groups] (rows of `cols` elements). */
+SB_API int sb_gather_rows(const void* src, int act_dtype, int cols, const int32_t* perm_row,
+                          const int32_t* offsets, int num_groups, int max_rows, void* dst,
+                          void* stream);
+
+/* ------------------------------------------------------------------ grouped GEMM
+ * Replaces spider_expert_grouped_gemm_f32/_f16 (spider_kernels.h:89-97) and
+ * spider_cuda_expert_grouped_gemm_v2_f32 (spider_cuda.h:22-26).  For every
+ * group g and permuted row r in [offsets[g], offsets[g+1]):
+ *   acc[r, m] = sum_k A_g[m, k] * x[r, k],  A_g = rows g*a_group_rows + [0, m_rows) of a
+ * followed by the epilogue.  Weights (a) are K-major [rows, lda] in wfmt; x is
+ * [x_rows, ldx] in act_dtype.  With splits > 1 (SB_EPI_LINEAR only) split s
+ * covers k in [s*k/splits, (s+1)*k/splits) and writes out + s*split_stride;
+ * only split 0 adds the bias. */
+typedef struct sb_grouped_gemm_args {
+  int engine;             /* SB_ENGINE_* */
+  int wfmt;               /* SB_W_* */
+  int act_dtype;          /* SB_F32 / SB_BF16 (x and GELU/SwiGLU outputs) */
+  int epilogue;           /* SB_EPI_* */
+  int num_groups;
+  int m_rows;             /* output features per group */
+  int k;                  /* reduction length */
+  int group_size;         /* int4 group size along k */
+  int64_t a_group_rows;   /* row offset between groups in a */
+  int64_t lda;            /* elements per row of a (bytes per row = lda/2 for int4) */
+  int64_t a_rows_total;   /* rows of a (bounds of the weight tensor) */
+  const void* a;
+  const void* a_scale;    /* fp8: float[a_rows_total]; int4: bf16[a_rows_total, lda/group_size] */
+  const void* a_gate;     /* SwiGLU gate weights, same layout as a */
+  const void* a_gate_scale;
+  const float* bias;      /* bias[g*bias_group_stride + m], may be NULL */
+  const float* bias_gate;
+  int64_t bias_group_stride;
+  const void* x;
+  int64_t ldx;
+  int max_rows;           /* rows allocated in x / out (upper bound of offsets[G]) */
+  int rows_hint;          /* host estimate of offsets[G] (tile shape choice only) */
+  const int32_t* offsets; /* [G+1] device */
+  const float* row_scale; /* [max_rows] per permuted row, SB_EPI_LINEAR only, may be NULL */
+  void* out;
+  int64_t ldo;
+  int splits;
+  int64_t split_stride;
+  int* status;            /* device status word (may be NULL) */
+} sb_grouped_gemm_args;
+
+SB_API int sb_grouped_gemm(const sb_grouped_gemm_args* args, void* stream);
+
+/* ------------------------------------------------------------------ edge top-M
+ * Replaces spider_edge_topk_f32 (spider_kernels.h:58-60; scalar_phase1_2.cpp:
+ * 11-47) and model.py:264-266 for the rows the router selected: for permuted
+ * row p (a (token, source) pair) take logits[p, 0:E], top-M (descending,
+ * equal values -> smaller destination first), softmax over the M values;
+ * write edge_idx[perm_slot[p]*M + m], edge_w[...]. */
+SB_API int sb_edge_topm(const float* logits, int64_t ld, int num_experts, int edges,
+                        const int32_t* perm_slot, const int32_t* offsets, int num_groups,
+                        int max_rows, int32_t* edge_idx, float* edge_w, void* stream);
+
+/* ------------------------------------------------------------------ combines
+ * Row combine: out[t, :] = sum_{j<slots, inv[t*slots+j]>=0} sum_s y[s][inv[t*slots+j], :]
+ * (fixed ascending order, no atomics).  out_f32 and/or out_act may be NULL;
+ * scatter_inv (may be NULL) additionally writes the combined row, in act_dtype,
+ * to rows scatter_inv[t*scatter_slots+k] >= 0 of scatter_out. */
+SB_API int sb_combine_rows(const float* y, int64_t ldy, int splits, int64_t split_stride,
+                           const int32_t* inv, int slots, int n_tokens, int cols, float* out_f32,
+                           const int32_t* scatter_inv, int scatter_slots, void* scatter_out,
+                           int act_dtype, void* stream);
+
+/* Loop epilogue, replaces spider_loop_epilogue_f32 (spider_kernels.h:99-101)
+ * with the block's LayerNorm (model.py:317):
+ *   u = (h + alpha * delta) + beta * x0,  out = LayerNorm(u) * ln_w + ln_b,
+ * where delta[t] = sum over the token's expert rows of y (inv / splits as in
+ * sb_combine_rows) or, if y is NULL, the dense delta_in [n_tokens, cols].
+ * delta_out (may be NULL) receives the fp32 delta. */
+SB_API int sb_combine_ln(const float* y, int64_t ldy, int splits, int64_t split_stride,
+                         const int32_t* inv, int slots, const float* delta_in, const void* h,
+                         const void* x0, int act_dtype, int n_tokens, int cols, const float* ln_w,
+                         const float* ln_b, float alpha, float beta, float eps, void* out,
+                         float* delta_out, void* stream);
+
+/* ------------------------------------------------------------------ whole block
+ * Replaces spider_moe_loop_step_f32 / spider_cuda_moe_loop_step_f32
+ * (spider_kernels.h:113-121, spider_cuda.h:36-45) with the semantics of
+ * SpiderMoELayer.forward (model.py:240-317) applied for loops
+ * [loop_begin, loop_end) (SpiderWebLM._run_recurrent_full, model.py:445-448). */
+typedef struct sb_block_dims {
+  int hidden, num_experts, top_k, edges_per_expert, ffn, num_loops;
+  int act_dtype;   /* SB_F32 or SB_BF16 (token rows and dense weights) */
+  int wfmt;        /* expert weight format */
+  int activation;  /* SB_ACT_* */
+  int group_size;  /* int4 */
+  int engine;      /* SB_ENGINE_* for the grouped GEMMs */
+  int max_tokens;
+  float residual_scale, reinject, ln_eps;
+} sb_block_dims;
+
+typedef struct sb_block_weights {
+  const void* router_w;   /* [E, H] act dtype              router.weight           */
+  const float* loop_bias; /* [L, E]                         loop_bias               */
+  const void* gen_w;      /* [E*E, H] act dtype             edge_generator.weight[:, :H] */
+  const float* gen_bias;  /* [L, E*E] edge_generator.bias + weight[:, H:] . loop_embedding[l] */
+  const void* edge_w;     /* [E, H, H] act dtype            edge_value.{d}.weight   */
+  const void* w_up;   const void* s_up;   const float* b_up;   /* [E, U, H] */
+  const void* w_gate; const void* s_gate; const float* b_gate; /* SwiGLU only */
+  const void* w_down; const void* s_down; const float* b_down; /* [E, H, U] */
+  const float* ln_w;  const float* ln_b;                       /* norm.{weight,bias} */
+} sb_block_weights;
+
+/* Optional copies of the last executed loop's intermediates (any may be NULL). */
+typedef struct sb_block_taps {
+  int32_t* top_idx;     /* [n, K]     */
+  float* top_w;         /* [n, K]     */
+  int32_t* edge_idx;    /* [n, K, M]  (for each selected source, in router slot order) */
+  float* edge_w;        /* [n, K, M]  */
+  float* messages;      /* [n, H] fp32 */
+  float* delta;         /* [n, H] fp32 */
+  int32_t* ffn_offsets; /* [E+1]      */
+  int32_t* ffn_rows;    /* [n*K]      */
+  float* ffn_weights;   /* [n*K]      */
+} sb_block_taps;
+
+SB_API size_t sb_block_workspace_bytes(const sb_block_dims* dims);
+SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block_weights* w, const void* h_in,
+                            const void* x0, void* h_out, int n_tokens, int loop_begin,
+                            int loop_end, void* workspace, size_t workspace_bytes,
+                            const sb_block_taps* taps, void* stream);
+
+/* ------------------------------------------------------------------ sparse expert delta
+ * Replaces sparse_expert_delta (spider_moe/sparse_experts.py:11-68) for one
+ * rank: delta[t] = sum over the token's experts e in [0, E) with e % world ==
+ * rank of tw * ffn_e(messages[t]) (no cross-rank reduction; the caller
+ * all-reduces as expert_parallel.all_reduce_sum_ does). */
+SB_API size_t sb_expert_delta_workspace_bytes(const sb_block_dims* dims, int n_tokens);
+SB_API int sb_expert_delta(const sb_block_dims* dims, const sb_block_weights* w,
+                           const void* messages, const int32_t* top_idx, const float* top_w,
+                           int n_tokens, int rank, int world, float* delta, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* Byte offset of the device status word inside every workspace above. */
+SB_API size_t sb_status_offset(void);
+
+/* ------------------------------------------------------------------ profiling aid
+ * Per-stage CUDA-event timing of sb_block_forward (no reference counterpart;
+ * off by default and not for use during stream capture).  sb_stage_timing(1)
+ * clears and starts collecting; sb_stage_timing_read synchronises the
+ * recorded events and returns, per stage, the summed milliseconds and the
+ * number of launches (arrays of at least sb_num_stages() entries). */
+SB_API int sb_num_stages(void);
+SB_API const char* sb_stage_name(int stage);
+SB_API int sb_stage_timing(int enable);
+SB_API int sb_stage_timing_read(double* ms, int* launches, int n_stages);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPIDER_B200_H */

@@ -1,0 +1,527 @@
+// Whole-block driver and the small exported entry points.
+//
+// sb_block_forward runs SpiderMoELayer.forward (spider_moe/model.py:240-317)
+// for a range of loops as a fixed sequence of kernels on one stream, with all
+// scratch carved from the caller's workspace.  No step needs the host to read
+// device data, so the whole sequence can be captured in a CUDA graph.
+//
+// Per loop:
+//   1  sb_router            top-k over experts                       (model.py:254-258)
+//   2  sb_group (sources)   rows grouped by selected source expert
+//   3  sb_gather_rows       h rows in source order
+//   4  grouped GEMM         edge logits of the selected sources      (model.py:261-263)
+//   5  sb_edge_topm         top-M destinations + softmax             (model.py:264-266)
+//   6  sb_group (dest.)     (token, destination) pairs, coefficients summed
+//   7  sb_gather_rows       h rows in destination order
+//   8  grouped GEMM         c * W_edge[d] h                          (model.py:271-288)
+//   9  sb_group (experts)   dispatch plan                            (dispatch.py:56-115)
+//  10  sb_combine_rows      messages, scattered into expert order
+//  11  grouped GEMM         up projection + GELU / SwiGLU            (sparse_experts.py:60-61)
+//  12  grouped GEMM         down projection * routing weight         (sparse_experts.py:62-63)
+//  13  sb_combine_ln        delta + LayerNorm epilogue               (model.py:317)
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "sb_common.cuh"
+#include "sb_internal.h"
+
+namespace sb {
+
+int current_sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = v > 0 ? v : 148;
+  }
+  return cached[dev];
+}
+
+int current_cc_major() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (!cached[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrComputeCapabilityMajor, dev);
+    cached[dev] = v;
+  }
+  return cached[dev];
+}
+
+static int act_size(int dt) { return dt == SB_F32 ? 4 : 2; }
+
+__global__ void remap_local_kernel(const int32_t* __restrict__ idx, int n, int E, int rank, int world,
+                                   int32_t* __restrict__ out) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int e = idx[i];
+    out[i] = (e >= 0 && e < E && e % world == rank) ? e / world : -1;
+  }
+}
+
+// ------------------------------------------------------------------ stage timing
+// Optional per-stage CUDA-event timing of sb_block_forward (a profiling aid;
+// off by default, never used during graph capture).
+constexpr int kNumStages = 13;
+static const char* kStageNames[kNumStages] = {
+    "router", "group_sources", "gather_sources", "gemm_edge_logits", "edge_topm", "group_destinations",
+    "gather_destinations", "gemm_edge_values", "group_experts", "combine_messages", "gemm_expert_up",
+    "gemm_expert_down", "combine_layernorm"};
+struct StageTiming {
+  bool on = false;
+  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> marks;
+  std::mutex mu;
+};
+static StageTiming g_timing;
+
+struct StageScope {
+  int stage;
+  cudaStream_t st;
+  cudaEvent_t a = nullptr, b = nullptr;
+  StageScope(int s, cudaStream_t stream) : stage(s), st(stream) {
+    if (!g_timing.on) return;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    cudaEventRecord(a, st);
+  }
+  ~StageScope() {
+    if (!a) return;
+    cudaEventRecord(b, st);
+    std::lock_guard<std::mutex> lk(g_timing.mu);
+    g_timing.marks.push_back({stage, {a, b}});
+  }
+};
+
+// ------------------------------------------------------------------ workspace layout
+
+struct BlockBuffers {
+  int* status;
+  int32_t *top_idx; float* top_w;
+  int32_t *src_off, *src_row, *src_slot, *src_inv; float* src_w;
+  void* x_src; float* elog;
+  int32_t* edge_idx; float* edge_w;
+  int32_t *dst_off, *dst_row, *dst_slot, *dst_inv; float* dst_w;
+  void* x_dst; float* y_msg;
+  float* msg_f32;
+  int32_t *ffn_off, *ffn_row, *ffn_slot, *ffn_inv; float* ffn_w;
+  void* x_ffn; void* act; float* y_ffn;
+  void* hbuf[2];
+  void* group_ws; size_t group_ws_bytes;
+  int64_t cap_dst, y_msg_stride, y_ffn_stride;
+};
+
+static int max_splits_for(int n_tokens) { return n_tokens <= 512 ? 4 : 1; }
+
+static size_t carve_block(const sb_block_dims& d, int n_cap, void* base, size_t size, BlockBuffers* b) {
+  Carver c(base, size);
+  const int64_t N = n_cap, H = d.hidden, E = d.num_experts, K = d.top_k, M = d.edges_per_expert, U = d.ffn;
+  const int as = act_size(d.act_dtype);
+  const int64_t cap_dst = N * (E < K * M ? E : K * M);
+  const int64_t small = N < 512 ? N : 512;
+  const int64_t small_dst = small * (E < K * M ? E : K * M);
+  const int64_t msg_rows = cap_dst > 4 * small_dst ? cap_dst : 4 * small_dst;
+  const int64_t ffn_rows = N * K > 4 * small * K ? N * K : 4 * small * K;
+  b->status = c.take<int>(kStatusBytes / sizeof(int));
+  b->top_idx = c.take<int32_t>(N * K);
+  b->top_w = c.take<float>(N * K);
+  b->src_off = c.take<int32_t>(E + 1);
+  b->src_row = c.take<int32_t>(N * K);
+  b->src_slot = c.take<int32_t>(N * K);
+  b->src_w = c.take<float>(N * K);
+  b->src_inv = c.take<int32_t>(N * K);
+  b->x_src = c.take<char>(N * K * H * as);
+  b->elog = c.take<float>(N * K * E);
+  b->edge_idx = c.take<int32_t>(N * K * M);
+  b->edge_w = c.take<float>(N * K * M);
+  b->dst_off = c.take<int32_t>(E + 1);
+  b->dst_row = c.take<int32_t>(cap_dst);
+  b->dst_slot = c.take<int32_t>(cap_dst);
+  b->dst_w = c.take<float>(cap_dst);
+  b->dst_inv = c.take<int32_t>(N * K * M);
+  b->x_dst = c.take<char>(cap_dst * H * as);
+  b->y_msg = c.take<float>(msg_rows * H);
+  b->msg_f32 = c.take<float>(N * H);
+  b->ffn_off = c.take<int32_t>(E + 1);
+  b->ffn_row = c.take<int32_t>(N * K);
+  b->ffn_slot = c.take<int32_t>(N * K);
+  b->ffn_w = c.take<float>(N * K);
+  b->ffn_inv = c.take<int32_t>(N * K);
+  b->x_ffn = c.take<char>(N * K * H * as);
+  b->act = c.take<char>(N * K * U * as);
+  b->y_ffn = c.take<float>(ffn_rows * H);
+  b->hbuf[0] = c.take<char>(N * H * as);
+  b->hbuf[1] = c.take<char>(N * H * as);
+  b->group_ws_bytes = sb_group_workspace_bytes(static_cast<int>(N), static_cast<int>(K * M), static_cast<int>(E));
+  b->group_ws = c.take<char>(b->group_ws_bytes);
+  b->cap_dst = cap_dst;
+  return c.overflow ? static_cast<size_t>(-1) : align_up(c.used, 256);
+}
+
+static int check_dims(const sb_block_dims* d) {
+  if (!d || d->hidden <= 0 || d->hidden % 8 || d->num_experts <= 0 || d->num_experts > 256 || d->top_k <= 0 ||
+      d->top_k > d->num_experts || d->edges_per_expert <= 0 || d->edges_per_expert > d->num_experts ||
+      d->top_k * d->edges_per_expert > 64 || d->ffn <= 0 || d->ffn % 8 || d->num_loops <= 0 ||
+      d->max_tokens < 0 || (d->act_dtype != SB_F32 && d->act_dtype != SB_BF16) ||
+      d->wfmt < SB_W_F32 || d->wfmt > SB_W_INT4 || (d->activation != SB_ACT_GELU && d->activation != SB_ACT_SWIGLU))
+    return SB_ERR_ARG;
+  if (d->top_k > 32 || d->edges_per_expert > 32) return SB_ERR_UNSUPPORTED;
+  if (d->wfmt == SB_W_INT4 && (d->group_size <= 0 || d->hidden % d->group_size || d->ffn % d->group_size))
+    return SB_ERR_ARG;
+  if (d->wfmt == SB_W_F32 && d->act_dtype != SB_F32) return SB_ERR_ARG;
+  return SB_OK;
+}
+
+static int run_gemm(sb_grouped_gemm_args& a, int engine_pref, cudaStream_t st) {
+  if (engine_pref == SB_ENGINE_SIMT) return gemm_simt(a, st);
+  const bool tc_ok = tcgen05_supported(a);
+  if (engine_pref == SB_ENGINE_TCGEN05) return tc_ok ? gemm_tcgen05(a, st) : SB_ERR_UNSUPPORTED;
+  return tc_ok ? gemm_tcgen05(a, st) : gemm_simt(a, st);
+}
+
+// K-split factor for a LINEAR GEMM: spread small grids over the SMs.
+static int pick_splits(int m_rows, int k, int rows_hint, int groups, int max_splits, bool tc) {
+  const int m_tiles = (m_rows + 127) / 128;
+  const int per_group = (rows_hint + groups - 1) / (groups > 0 ? groups : 1);
+  const int bn = per_group <= 16 ? 16 : per_group <= 32 ? 32 : per_group <= 64 ? 64 : per_group <= 128 ? 128 : 256;
+  int tiles = m_tiles * (rows_hint / bn + (groups < rows_hint ? groups : rows_hint));
+  if (tiles < 1) tiles = 1;
+  const int sms = current_sm_count();
+  int s = 1;
+  while (s * 2 <= max_splits && tiles * s * 2 <= sms && (k % ((tc ? 64 : 32) * s * 2)) == 0) s *= 2;
+  return s;
+}
+
+static void fill_expert_gemm(sb_grouped_gemm_args& a, const sb_block_dims& d, bool up, const void* w,
+                             const void* sc, const float* bias, const void* wg, const void* sg, const float* bg) {
+  std::memset(&a, 0, sizeof(a));
+  a.engine = d.engine;
+  a.wfmt = d.wfmt;
+  a.act_dtype = d.act_dtype;
+  a.m_rows = up ? d.ffn : d.hidden;
+  a.k = up ? d.hidden : d.ffn;
+  a.group_size = d.group_size;
+  a.lda = a.k;
+  a.a_group_rows = a.m_rows;
+  a.a_rows_total = static_cast<int64_t>(d.num_experts) * a.m_rows;
+  a.a = w;
+  a.a_scale = sc;
+  a.a_gate = wg;
+  a.a_gate_scale = sg;
+  a.bias = bias;
+  a.bias_gate = bg;
+  a.bias_group_stride = a.m_rows;
+}
+
+// Restrict an expert GEMM to the experts e = rank + world * g of one rank.
+static void shard_expert_gemm(sb_grouped_gemm_args& a, const sb_block_dims& d, int rank, int world) {
+  if (world <= 1) return;
+  const int64_t shift_rows = static_cast<int64_t>(rank) * a.m_rows;
+  auto shift = [&](const void* p, int64_t elems_per_row_bytes) -> const void* {
+    return p ? static_cast<const char*>(p) + shift_rows * elems_per_row_bytes : nullptr;
+  };
+  int64_t row_bytes = d.wfmt == SB_W_F32 ? a.lda * 4 : d.wfmt == SB_W_BF16 ? a.lda * 2 : d.wfmt == SB_W_FP8 ? a.lda : a.lda / 2;
+  a.a = shift(a.a, row_bytes);
+  a.a_gate = shift(a.a_gate, row_bytes);
+  if (d.wfmt == SB_W_FP8) {
+    a.a_scale = shift(a.a_scale, 4);
+    a.a_gate_scale = shift(a.a_gate_scale, 4);
+  } else if (d.wfmt == SB_W_INT4) {
+    a.a_scale = shift(a.a_scale, (a.lda / d.group_size) * 2);
+    a.a_gate_scale = shift(a.a_gate_scale, (a.lda / d.group_size) * 2);
+  }
+  a.bias = a.bias ? a.bias + shift_rows : nullptr;
+  a.bias_gate = a.bias_gate ? a.bias_gate + shift_rows : nullptr;
+  a.a_group_rows = static_cast<int64_t>(world) * a.m_rows;
+  a.bias_group_stride = a.a_group_rows;
+  a.a_rows_total -= shift_rows;
+}
+
+}  // namespace sb
+
+using namespace sb;
+
+extern "C" SB_API int sb_capabilities(void) {
+  int caps = 1;  // compiled for sm_100a
+  if (current_cc_major() == 10) caps |= 2;
+  return caps;
+}
+
+extern "C" SB_API const char* sb_version(void) { return "spider_b200 0.1 (sm_100a)"; }
+
+extern "C" SB_API const char* sb_error_string(int code) {
+  switch (code) {
+    case SB_OK: return "ok";
+    case SB_ERR_ARG: return "bad argument";
+    case SB_ERR_INDEX: return "index out of range";
+    case SB_ERR_UNSUPPORTED: return "unsupported shape or format";
+    case SB_ERR_NO_DEVICE: return "no sm_100 device";
+    case SB_ERR_WORKSPACE: return "workspace missing or too small";
+    case SB_ERR_DEVICE_STATUS: return "a kernel recorded a device-side status";
+    default:
+      if (code >= SB_ERR_CUDA_BASE) return cudaGetErrorString(static_cast<cudaError_t>(code - SB_ERR_CUDA_BASE));
+      return "unknown error";
+  }
+}
+
+extern "C" SB_API size_t sb_status_offset(void) { return 0; }
+
+extern "C" SB_API int sb_grouped_gemm(const sb_grouped_gemm_args* args, void* stream) {
+  if (!args) return SB_ERR_ARG;
+  const sb_grouped_gemm_args& a = *args;
+  if (!a.a || !a.x || !a.out || !a.offsets || a.num_groups <= 0 || a.m_rows <= 0 || a.k <= 0 || a.lda < a.k ||
+      a.ldx < a.k || a.max_rows < 0 || a.splits <= 0 || a.a_rows_total <= 0 ||
+      (a.epilogue != SB_EPI_LINEAR && a.splits != 1) || (a.epilogue == SB_EPI_SWIGLU && !a.a_gate) ||
+      (a.wfmt != SB_W_BF16 && a.wfmt != SB_W_F32 && !a.a_scale) || a.epilogue < 0 || a.epilogue > 2)
+    return SB_ERR_ARG;
+  if (a.max_rows == 0) return SB_OK;
+  sb_grouped_gemm_args c = a;
+  return run_gemm(c, a.engine, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" SB_API size_t sb_block_workspace_bytes(const sb_block_dims* dims) {
+  if (check_dims(dims) != SB_OK) return 0;
+  BlockBuffers b;
+  return carve_block(*dims, dims->max_tokens > 0 ? dims->max_tokens : 1, nullptr, ~size_t(0) >> 1, &b);
+}
+
+extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block_weights* w, const void* h_in,
+                                       const void* x0, void* h_out, int n_tokens, int loop_begin, int loop_end,
+                                       void* workspace, size_t workspace_bytes, const sb_block_taps* taps,
+                                       void* stream) {
+  int rc = check_dims(dims);
+  if (rc) return rc;
+  const sb_block_dims& d = *dims;
+  if (!w || !w->router_w || !w->loop_bias || !w->gen_w || !w->gen_bias || !w->edge_w || !w->w_up || !w->b_up ||
+      !w->w_down || !w->b_down || !w->ln_w || !w->ln_b || n_tokens < 0 || n_tokens > d.max_tokens ||
+      loop_begin < 0 || loop_end > d.num_loops || loop_begin > loop_end ||
+      (d.activation == SB_ACT_SWIGLU && (!w->w_gate || !w->b_gate)) ||
+      ((d.wfmt == SB_W_FP8 || d.wfmt == SB_W_INT4) && (!w->s_up || !w->s_down)))
+    return SB_ERR_ARG;
+  if (n_tokens == 0 || loop_begin == loop_end) return SB_OK;
+  if (!h_in || !x0 || !h_out) return SB_ERR_ARG;
+  BlockBuffers b;
+  const size_t need = carve_block(d, d.max_tokens, workspace, workspace_bytes, &b);
+  if (!workspace || need == static_cast<size_t>(-1) || workspace_bytes < need) return SB_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int N = n_tokens, H = d.hidden, E = d.num_experts, K = d.top_k, M = d.edges_per_expert, U = d.ffn;
+  const int KM = K * M;
+  const int dense_fmt = d.act_dtype == SB_F32 ? SB_W_F32 : SB_W_BF16;
+  const int64_t cap_dst = static_cast<int64_t>(N) * (E < KM ? E : KM);
+  const bool tc_pref = d.engine != SB_ENGINE_SIMT;
+  const void* cur = h_in;
+#define SB_TRY(x) do { rc = (x); if (rc) return rc; } while (0)
+  for (int l = loop_begin; l < loop_end; ++l) {
+    void* next = (l == loop_end - 1) ? h_out : b.hbuf[(l - loop_begin) & 1];
+    // 1. router
+    { StageScope sc_(0, st); SB_TRY(sb_router(cur, d.act_dtype, N, H, w->router_w, w->loop_bias + static_cast<int64_t>(l) * E, E, K,
+                     b.top_idx, b.top_w, nullptr, st)); }
+    // 2-3. rows grouped by selected source; gather h
+    { StageScope sc_(1, st); SB_TRY(sb_group(b.top_idx, nullptr, N, K, E, 0, b.src_off, b.src_row, b.src_slot, b.src_w, b.src_inv,
+                    b.group_ws, b.group_ws_bytes, st)); }
+    { StageScope sc_(2, st); SB_TRY(sb_gather_rows(cur, d.act_dtype, H, b.src_row, b.src_off, E, N * K, b.x_src, st)); }
+    // 4. edge logits of the selected sources: rows [s*E, s*E+E) of the generator
+    {
+      sb_grouped_gemm_args a;
+      std::memset(&a, 0, sizeof(a));
+      a.engine = d.engine; a.wfmt = dense_fmt; a.act_dtype = d.act_dtype; a.epilogue = SB_EPI_LINEAR;
+      a.num_groups = E; a.m_rows = E; a.k = H; a.a_group_rows = E; a.lda = H;
+      a.a_rows_total = static_cast<int64_t>(E) * E; a.a = w->gen_w;
+      a.bias = w->gen_bias + static_cast<int64_t>(l) * E * E; a.bias_group_stride = E;
+      a.x = b.x_src; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K; a.offsets = b.src_off;
+      a.out = b.elog; a.ldo = E; a.splits = 1; a.status = b.status;
+      { StageScope sc_(3, st); SB_TRY(run_gemm(a, d.engine, st)); }
+    }
+    // 5. top-M destinations per (token, source)
+    { StageScope sc_(4, st); SB_TRY(sb_edge_topm(b.elog, E, E, M, b.src_slot, b.src_off, E, N * K, b.edge_idx, b.edge_w, st)); }
+    // 6-7. (token, destination) pairs with summed coefficients; gather h
+    { StageScope sc_(5, st); SB_TRY(sb_group(b.edge_idx, b.edge_w, N, KM, E, 0, b.dst_off, b.dst_row, b.dst_slot, b.dst_w, b.dst_inv,
+                    b.group_ws, b.group_ws_bytes, st)); }
+    { StageScope sc_(6, st); SB_TRY(sb_gather_rows(cur, d.act_dtype, H, b.dst_row, b.dst_off, E, static_cast<int>(cap_dst), b.x_dst, st)); }
+    // 8. c[t,d] * W_edge[d] h[t]
+    int msg_splits = 1;
+    {
+      sb_grouped_gemm_args a;
+      std::memset(&a, 0, sizeof(a));
+      a.engine = d.engine; a.wfmt = dense_fmt; a.act_dtype = d.act_dtype; a.epilogue = SB_EPI_LINEAR;
+      a.num_groups = E; a.m_rows = H; a.k = H; a.a_group_rows = H; a.lda = H;
+      a.a_rows_total = static_cast<int64_t>(E) * H; a.a = w->edge_w;
+      a.x = b.x_dst; a.ldx = H; a.max_rows = static_cast<int>(cap_dst);
+      a.rows_hint = static_cast<int>(cap_dst * 7 / 8); a.offsets = b.dst_off; a.row_scale = b.dst_w;
+      msg_splits = pick_splits(H, H, a.rows_hint, E, max_splits_for(N), tc_pref);
+      a.splits = msg_splits; a.split_stride = cap_dst * H;
+      a.out = b.y_msg; a.ldo = H; a.status = b.status;
+      { StageScope sc_(7, st); SB_TRY(run_gemm(a, d.engine, st)); }
+    }
+    // 9. dispatch plan of the expert FFN
+    { StageScope sc_(8, st); SB_TRY(sb_group(b.top_idx, b.top_w, N, K, E, SB_GROUP_POSITIVE_ONLY, b.ffn_off, b.ffn_row, b.ffn_slot,
+                    b.ffn_w, b.ffn_inv, b.group_ws, b.group_ws_bytes, st)); }
+    // 10. messages (sum over the token's destinations), scattered into expert order
+    { StageScope sc_(9, st); SB_TRY(sb_combine_rows(b.y_msg, H, msg_splits, cap_dst * H, b.dst_inv, KM, N, H,
+                           (taps && taps->messages) ? b.msg_f32 : nullptr, b.ffn_inv, K, b.x_ffn, d.act_dtype,
+                           st)); }
+    // 11. up projection + activation
+    {
+      sb_grouped_gemm_args a;
+      fill_expert_gemm(a, d, true, w->w_up, w->s_up, w->b_up, w->w_gate, w->s_gate, w->b_gate);
+      a.epilogue = d.activation == SB_ACT_SWIGLU ? SB_EPI_SWIGLU : SB_EPI_GELU;
+      a.num_groups = E; a.x = b.x_ffn; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K;
+      a.offsets = b.ffn_off; a.out = b.act; a.ldo = U; a.splits = 1; a.status = b.status;
+      { StageScope sc_(10, st); SB_TRY(run_gemm(a, d.engine, st)); }
+    }
+    // 12. down projection, scaled by the routing weight
+    int ffn_splits = 1;
+    {
+      sb_grouped_gemm_args a;
+      fill_expert_gemm(a, d, false, w->w_down, w->s_down, w->b_down, nullptr, nullptr, nullptr);
+      a.epilogue = SB_EPI_LINEAR;
+      a.num_groups = E; a.x = b.act; a.ldx = U; a.max_rows = N * K; a.rows_hint = N * K;
+      a.offsets = b.ffn_off; a.row_scale = b.ffn_w;
+      ffn_splits = pick_splits(H, U, N * K, E, max_splits_for(N), tc_pref);
+      a.splits = ffn_splits; a.split_stride = static_cast<int64_t>(N) * K * H;
+      a.out = b.y_ffn; a.ldo = H; a.status = b.status;
+      { StageScope sc_(11, st); SB_TRY(run_gemm(a, d.engine, st)); }
+    }
+    // 13. delta + LayerNorm epilogue
+    { StageScope sc_(12, st); SB_TRY(sb_combine_ln(b.y_ffn, H, ffn_splits, static_cast<int64_t>(N) * K * H, b.ffn_inv, K, nullptr, cur, x0,
+                         d.act_dtype, N, H, w->ln_w, w->ln_b, d.residual_scale, d.reinject, d.ln_eps, next,
+                         (taps && taps->delta && l == loop_end - 1) ? taps->delta : nullptr, st)); }
+    if (taps && l == loop_end - 1) {
+      auto cp = [&](void* dst, const void* src, size_t bytes) -> int {
+        return dst ? cuda_status(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, st)) : SB_OK;
+      };
+      SB_TRY(cp(taps->top_idx, b.top_idx, sizeof(int32_t) * N * K));
+      SB_TRY(cp(taps->top_w, b.top_w, sizeof(float) * N * K));
+      SB_TRY(cp(taps->edge_idx, b.edge_idx, sizeof(int32_t) * N * KM));
+      SB_TRY(cp(taps->edge_w, b.edge_w, sizeof(float) * N * KM));
+      SB_TRY(cp(taps->messages, b.msg_f32, sizeof(float) * static_cast<size_t>(N) * H));
+      SB_TRY(cp(taps->ffn_offsets, b.ffn_off, sizeof(int32_t) * (E + 1)));
+      SB_TRY(cp(taps->ffn_rows, b.ffn_row, sizeof(int32_t) * N * K));
+      SB_TRY(cp(taps->ffn_weights, b.ffn_w, sizeof(float) * N * K));
+    }
+    cur = next;
+  }
+#undef SB_TRY
+  return SB_OK;
+}
+
+// ------------------------------------------------------------------ sparse expert delta
+
+static size_t carve_delta(const sb_block_dims& d, int n, void* base, size_t size, BlockBuffers* b) {
+  Carver c(base, size);
+  const int64_t N = n, H = d.hidden, E = d.num_experts, K = d.top_k, U = d.ffn;
+  const int as = act_size(d.act_dtype);
+  b->status = c.take<int>(kStatusBytes / sizeof(int));
+  b->top_idx = c.take<int32_t>(N * K);  // local expert ids
+  b->ffn_off = c.take<int32_t>(E + 1);
+  b->ffn_row = c.take<int32_t>(N * K);
+  b->ffn_slot = c.take<int32_t>(N * K);
+  b->ffn_w = c.take<float>(N * K);
+  b->ffn_inv = c.take<int32_t>(N * K);
+  b->x_ffn = c.take<char>(N * K * H * as);
+  b->act = c.take<char>(N * K * U * as);
+  b->y_ffn = c.take<float>(4 * N * K * H);
+  b->group_ws_bytes = sb_group_workspace_bytes(static_cast<int>(N), static_cast<int>(K), static_cast<int>(E));
+  b->group_ws = c.take<char>(b->group_ws_bytes);
+  return c.overflow ? static_cast<size_t>(-1) : align_up(c.used, 256);
+}
+
+extern "C" SB_API size_t sb_expert_delta_workspace_bytes(const sb_block_dims* dims, int n_tokens) {
+  if (check_dims(dims) != SB_OK || n_tokens < 0) return 0;
+  BlockBuffers b;
+  return carve_delta(*dims, n_tokens > 0 ? n_tokens : 1, nullptr, ~size_t(0) >> 1, &b);
+}
+
+extern "C" SB_API int sb_expert_delta(const sb_block_dims* dims, const sb_block_weights* w, const void* messages,
+                                      const int32_t* top_idx, const float* top_w, int n_tokens, int rank,
+                                      int world, float* delta, void* workspace, size_t workspace_bytes,
+                                      void* stream) {
+  int rc = check_dims(dims);
+  if (rc) return rc;
+  const sb_block_dims& d = *dims;
+  if (!w || !w->w_up || !w->b_up || !w->w_down || !w->b_down || n_tokens < 0 || world <= 0 || rank < 0 ||
+      rank >= world || (d.activation == SB_ACT_SWIGLU && (!w->w_gate || !w->b_gate)) ||
+      ((d.wfmt == SB_W_FP8 || d.wfmt == SB_W_INT4) && (!w->s_up || !w->s_down)))
+    return SB_ERR_ARG;
+  if (n_tokens == 0) return SB_OK;
+  if (!messages || !top_idx || !top_w || !delta) return SB_ERR_ARG;
+  BlockBuffers b;
+  const size_t need = carve_delta(d, n_tokens, workspace, workspace_bytes, &b);
+  if (!workspace || need == static_cast<size_t>(-1) || workspace_bytes < need) return SB_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int N = n_tokens, H = d.hidden, E = d.num_experts, K = d.top_k, U = d.ffn;
+  const int G = (E - rank + world - 1) / world;
+  if (G <= 0) return cuda_status(cudaMemsetAsync(delta, 0, sizeof(float) * static_cast<size_t>(N) * H, st));
+  remap_local_kernel<<<(N * K + 255) / 256, 256, 0, st>>>(top_idx, N * K, E, rank, world, b.top_idx);
+  if ((rc = sb_last_launch_status())) return rc;
+#define SB_TRY(x) do { rc = (x); if (rc) return rc; } while (0)
+  SB_TRY(sb_group(b.top_idx, top_w, N, K, G, SB_GROUP_POSITIVE_ONLY, b.ffn_off, b.ffn_row, b.ffn_slot, b.ffn_w,
+                  b.ffn_inv, b.group_ws, b.group_ws_bytes, st));
+  SB_TRY(sb_gather_rows(messages, d.act_dtype, H, b.ffn_row, b.ffn_off, G, N * K, b.x_ffn, st));
+  {
+    sb_grouped_gemm_args a;
+    fill_expert_gemm(a, d, true, w->w_up, w->s_up, w->b_up, w->w_gate, w->s_gate, w->b_gate);
+    shard_expert_gemm(a, d, rank, world);
+    a.epilogue = d.activation == SB_ACT_SWIGLU ? SB_EPI_SWIGLU : SB_EPI_GELU;
+    a.num_groups = G; a.x = b.x_ffn; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K;
+    a.offsets = b.ffn_off; a.out = b.act; a.ldo = U; a.splits = 1; a.status = b.status;
+    SB_TRY(run_gemm(a, d.engine, st));
+  }
+  int splits = 1;
+  {
+    sb_grouped_gemm_args a;
+    fill_expert_gemm(a, d, false, w->w_down, w->s_down, w->b_down, nullptr, nullptr, nullptr);
+    shard_expert_gemm(a, d, rank, world);
+    a.epilogue = SB_EPI_LINEAR;
+    a.num_groups = G; a.x = b.act; a.ldx = U; a.max_rows = N * K; a.rows_hint = N * K;
+    a.offsets = b.ffn_off; a.row_scale = b.ffn_w;
+    splits = pick_splits(H, U, N * K, G, 4, d.engine != SB_ENGINE_SIMT);
+    a.splits = splits; a.split_stride = static_cast<int64_t>(N) * K * H;
+    a.out = b.y_ffn; a.ldo = H; a.status = b.status;
+    SB_TRY(run_gemm(a, d.engine, st));
+  }
+  SB_TRY(sb_combine_rows(b.y_ffn, H, splits, static_cast<int64_t>(N) * K * H, b.ffn_inv, K, N, H, delta, nullptr, 0,
+                         nullptr, d.act_dtype, st));
+#undef SB_TRY
+  return SB_OK;
+}
+
+extern "C" SB_API int sb_stage_timing(int enable) {
+  std::lock_guard<std::mutex> lk(g_timing.mu);
+  g_timing.on = enable != 0;
+  if (enable) {
+    for (auto& m : g_timing.marks) {
+      cudaEventDestroy(m.second.first);
+      cudaEventDestroy(m.second.second);
+    }
+    g_timing.marks.clear();
+  }
+  return SB_OK;
+}
+
+extern "C" SB_API int sb_stage_timing_read(double* ms, int* launches, int n_stages) {
+  if (!ms || !launches || n_stages < kNumStages) return SB_ERR_ARG;
+  std::lock_guard<std::mutex> lk(g_timing.mu);
+  for (int i = 0; i < kNumStages; ++i) { ms[i] = 0.0; launches[i] = 0; }
+  int rc = SB_OK;
+  for (auto& m : g_timing.marks) {
+    float t = 0.f;
+    cudaError_t e = cudaEventSynchronize(m.second.second);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&t, m.second.first, m.second.second);
+    if (e != cudaSuccess) rc = cuda_status(e);
+    ms[m.first] += t;
+    launches[m.first] += 1;
+    cudaEventDestroy(m.second.first);
+    cudaEventDestroy(m.second.second);
+  }
+  g_timing.marks.clear();
+  return rc;
+}
+
+extern "C" SB_API const char* sb_stage_name(int stage) {
+  return (stage >= 0 && stage < kNumStages) ? kStageNames[stage] : "";
+}
+
+extern "C" SB_API int sb_num_stages(void) { return kNumStages; }

@@ -1,0 +1,406 @@
+// tcgen05 / TMEM grouped GEMM for sm_100a, fed by TMA.
+//
+// Orientation: the weight rows are the MMA M side (128 output features per
+// CTA tile) and the permuted token rows are the N side (BN = 16..256).  Decode
+// batches put only a handful of tokens on each expert, and the M=128 x N=16
+// instruction keeps the tensor core busy on weights streamed from HBM, while
+// prefill batches use N = 256.  Accumulators live in TMEM; the epilogue reads
+// them with tcgen05.ld (one TMEM lane quarter per epilogue warp).
+//
+// Warp roles (192 threads):
+//   warps 0-3  dequantise fp8 / int4 weight tiles to bf16 in shared memory
+//              during the main loop, then run the epilogue;
+//   warp 4     TMA producer (one elected lane);
+//   warp 5     TMEM allocator and MMA issuer (one elected lane).
+// Every mbarrier wait is bounded (sb_common.cuh): a wait that runs out records
+// a bit in the caller's status word and the CTA winds down instead of hanging.
+//
+// No load in this file uses cluster multicast: every CTA fetches its own tiles,
+// so the kernel is safe on expert-parallel runs where operands may live in
+// buffers filled by other GPUs.
+#include <unordered_map>
+#include <mutex>
+#include <tuple>
+
+#include "sb_gemm_common.cuh"
+#include "sb_internal.h"
+
+namespace sb {
+
+constexpr int kTcBM = 128;
+constexpr int kTcBK = 64;
+constexpr int kTcThreads = 192;
+constexpr int kTcSmemBudget = 200 * 1024;
+
+template <int BN, int WFMT, int EPI>
+struct TcCfg {
+  static constexpr bool kGate = EPI == SB_EPI_SWIGLU;
+  static constexpr bool kConvert = WFMT != SB_W_BF16;
+  static constexpr int kABytes = kTcBM * kTcBK * 2;                       // bf16 tile
+  static constexpr int kBBytes = BN * kTcBK * 2;
+  static constexpr int kRawBytes = WFMT == SB_W_FP8 ? kTcBM * kTcBK : (WFMT == SB_W_INT4 ? kTcBM * kTcBK / 2 : 0);
+  static constexpr int kStageBytes = kABytes * (kGate ? 2 : 1) + kBBytes + kRawBytes * (kGate ? 2 : 1);
+  static constexpr int kStagesRaw = kTcSmemBudget / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
+  static constexpr int kTmemCols = (BN * (kGate ? 2 : 1)) <= 32 ? 32 : BN * (kGate ? 2 : 1);
+  // shared memory layout (offsets from a 1024-aligned base)
+  static constexpr int kOffA = 0;
+  static constexpr int kOffG = kOffA + kStages * kABytes;
+  static constexpr int kOffB = kOffG + (kGate ? kStages * kABytes : 0);
+  static constexpr int kOffRaw = kOffB + kStages * kBBytes;
+  static constexpr int kOffRawG = kOffRaw + kStages * kRawBytes;
+  static constexpr int kOffBar = kOffRawG + (kGate ? kStages * kRawBytes : 0);
+  static constexpr int kOffMisc = kOffBar + (3 * kStages + 1) * 8;
+  static constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
+  static_assert(kTmemCols <= 512, "TMEM holds 512 columns");
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "M=128 MMA needs N in [16, 256], N % 16 == 0");
+};
+
+// Convert the raw fp8 / int4 tile of this stage into the swizzled bf16 tile.
+template <int WFMT>
+SB_DEVINL void convert_tile(const uint8_t* raw, uint8_t* dst, const sb_grouped_gemm_args& p,
+                            const void* scales, int64_t arow0, int k0, int tid) {
+  if (WFMT == SB_W_FP8) {
+    // 128 rows x 64 bytes; item = (row, 16-byte chunk): 512 items over 128 threads.
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int item = tid + 128 * q;
+      const int row = item >> 2, c16 = item & 3;
+      const uint4 v = *reinterpret_cast<const uint4*>(raw + row * 64 + c16 * 16);
+      const uint8_t* b = reinterpret_cast<const uint8_t*>(&v);
+      uint32_t out[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(
+            static_cast<__nv_fp8x2_storage_t>(b[2 * j] | (b[2 * j + 1] << 8)), __NV_E4M3);
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+        const __nv_bfloat162 bb = __floats2bfloat162_rn(f.x, f.y);
+        out[j] = *reinterpret_cast<const uint32_t*>(&bb);
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int kc = c16 * 2 + h;  // 16-byte chunk (8 bf16) index along k
+        *reinterpret_cast<uint4*>(dst + row * 128 + ((kc ^ (row & 7)) << 4)) =
+            make_uint4(out[4 * h], out[4 * h + 1], out[4 * h + 2], out[4 * h + 3]);
+      }
+    }
+  } else {
+    // 128 rows x 32 bytes; item = (row, 16-byte chunk): 256 items over 128 threads.
+    const int groups = static_cast<int>(p.lda / p.group_size);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int item = tid + 128 * q;
+      const int row = item >> 1, c16 = item & 1;
+      const int64_t arow = arow0 + row;
+      const float s = arow < p.a_rows_total
+                          ? __bfloat162float(static_cast<const __nv_bfloat16*>(scales)[arow * groups + k0 / p.group_size])
+                          : 0.f;
+      const uint4 v = *reinterpret_cast<const uint4*>(raw + row * 32 + c16 * 16);
+      const uint8_t* b = reinterpret_cast<const uint8_t*>(&v);
+      uint32_t out[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const __nv_bfloat162 bb = __floats2bfloat162_rn(static_cast<float>(int4_nibble(b[j], 0)) * s,
+                                                        static_cast<float>(int4_nibble(b[j], 1)) * s);
+        out[j] = *reinterpret_cast<const uint32_t*>(&bb);
+      }
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const int kc = c16 * 4 + h;
+        *reinterpret_cast<uint4*>(dst + row * 128 + ((kc ^ (row & 7)) << 4)) =
+            make_uint4(out[4 * h], out[4 * h + 1], out[4 * h + 2], out[4 * h + 3]);
+      }
+    }
+  }
+}
+
+template <int BN, int WFMT, int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmG,
+               const __grid_constant__ CUtensorMap tmB, const sb_grouped_gemm_args p) {
+  using C = TcCfg<BN, WFMT, EPI>;
+  constexpr int S = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* empty = full + S;
+  uint64_t* conv = empty + S;
+  uint64_t* done = conv + S;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
+  int* s_sched = reinterpret_cast<int*>(smem + C::kOffMisc + 16);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (warp == 0) {
+    int g, n0, n_end;
+    const bool ok = schedule_tile(p.offsets, p.num_groups, BN, blockIdx.y, g, n0, n_end);
+    if (lane == 0) {
+      s_sched[0] = ok ? g : -1;
+      s_sched[1] = n0;
+      s_sched[2] = min(n_end, p.max_rows);
+    }
+  }
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 128);
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int g = s_sched[0];
+  if (g < 0) return;  // surplus CTA of the upper-bound grid
+  const int n0 = s_sched[1], n_end = s_sched[2];
+  const int m0 = blockIdx.x * kTcBM;
+  const int ks = p.k / p.splits;
+  const int kb = blockIdx.z * ks;
+  const int nk = ks / kTcBK;
+  const int64_t arow0 = static_cast<int64_t>(g) * p.a_group_rows + m0;
+
+  if (warp == 5) {
+    tmem_alloc(s_tmem, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      if (C::kGate) tma_prefetch_desc(&tmG);
+      constexpr uint32_t kTx = (C::kConvert ? C::kRawBytes : C::kABytes) * (C::kGate ? 2 : 1) + C::kBBytes;
+      int issued = 0;
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % S;
+        const uint32_t ph = (it / S) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, p.status, SB_DEVERR_MMA_WAIT)) break;
+        mbar_expect_tx(&full[s], kTx);
+        const int k0 = kb + it * kTcBK;
+        const int acol = WFMT == SB_W_INT4 ? k0 / 2 : k0;
+        uint8_t* adst = C::kConvert ? smem + C::kOffRaw + s * C::kRawBytes : smem + C::kOffA + s * C::kABytes;
+        tma_load_2d(adst, &tmA, &full[s], acol, static_cast<int>(arow0));
+        if (C::kGate) {
+          uint8_t* gdst = C::kConvert ? smem + C::kOffRawG + s * C::kRawBytes : smem + C::kOffG + s * C::kABytes;
+          tma_load_2d(gdst, &tmG, &full[s], acol, static_cast<int>(arow0));
+        }
+        tma_load_2d(smem + C::kOffB + s * C::kBBytes, &tmB, &full[s], k0, n0);
+        ++issued;
+      }
+      // Drain: every issued copy must have landed before the CTA may exit.
+      for (int it = issued - S > 0 ? issued - S : 0; it < issued; ++it)
+        if (!mbar_wait(&full[it % S], (it / S) & 1, p.status, SB_DEVERR_DRAIN)) break;
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kTcBM, BN);
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % S;
+        const uint32_t ph = (it / S) & 1;
+        const bool ok = C::kConvert ? mbar_wait(&conv[s], ph, p.status, SB_DEVERR_CONV_WAIT)
+                                    : mbar_wait(&full[s], ph, p.status, SB_DEVERR_TMA_WAIT);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(smem + C::kOffA + s * C::kABytes);
+        const uint32_t g_base = smem_u32(smem + C::kOffG + s * C::kABytes);
+        const uint32_t b_base = smem_u32(smem + C::kOffB + s * C::kBBytes);
+#pragma unroll
+        for (int kk = 0; kk < kTcBK / 16; ++kk) {
+          const uint64_t bdesc = smem_desc_k_sw128(b_base + kk * 32);
+          const uint32_t accum = (it > 0 || kk > 0) ? 1u : 0u;
+          tc_mma_bf16(tmem, smem_desc_k_sw128(a_base + kk * 32), bdesc, idesc, accum);
+          if (C::kGate) tc_mma_bf16(tmem + BN, smem_desc_k_sw128(g_base + kk * 32), bdesc, idesc, accum);
+        }
+        tc_commit(&empty[s]);
+      }
+      tc_commit(done);
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- dequant + epilogue
+    if (C::kConvert) {
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % S;
+        const uint32_t ph = (it / S) & 1;
+        if (!mbar_wait(&full[s], ph, p.status, SB_DEVERR_TMA_WAIT)) break;
+        const int k0 = kb + it * kTcBK;
+        convert_tile<WFMT>(smem + C::kOffRaw + s * C::kRawBytes, smem + C::kOffA + s * C::kABytes, p,
+                           p.a_scale, arow0, k0, tid);
+        if (C::kGate)
+          convert_tile<WFMT>(smem + C::kOffRawG + s * C::kRawBytes, smem + C::kOffG + s * C::kABytes, p,
+                             p.a_gate_scale, arow0, k0, tid);
+        fence_proxy_async_smem();
+        mbar_arrive(&conv[s]);
+      }
+    }
+    // tcgen05.ld is warp-collective: every lane must take the same branch.
+    const bool acc_ready = __all_sync(0xffffffffu, mbar_wait(done, 0, p.status, SB_DEVERR_EPI_WAIT));
+    tc_fence_after();
+    if (acc_ready) {
+      const int mloc = warp * 32 + lane;
+      const int m = m0 + mloc;
+      const int64_t arow = arow0 + mloc;
+      const bool mvalid = m < p.m_rows && arow < p.a_rows_total;
+      const float sa = (WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_scale)[arow] : 1.f;
+      const float sg = (C::kGate && WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_gate_scale)[arow] : 1.f;
+      const float bias = (p.bias && mvalid && blockIdx.z == 0) ? p.bias[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
+      const float bgate = (C::kGate && p.bias_gate && mvalid) ? p.bias_gate[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
+      const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        if (n0 + c0 >= n_end) break;
+        float v[16], vg[16];
+        tmem_ld16(lane_addr + c0, v);
+        if (C::kGate) tmem_ld16(lane_addr + BN + c0, vg);
+        if (!mvalid) continue;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int r = n0 + c0 + j;
+          if (r >= n_end) break;
+          const float x = v[j] * sa + bias;
+          if (EPI == SB_EPI_LINEAR) {
+            const float rs = p.row_scale ? p.row_scale[r] : 1.f;
+            static_cast<float*>(p.out)[blockIdx.z * p.split_stride + static_cast<int64_t>(r) * p.ldo + m] = x * rs;
+          } else if (EPI == SB_EPI_GELU) {
+            static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(r) * p.ldo + m] = __float2bfloat16_rn(gelu_erf(x));
+          } else {
+            const float gx = vg[j] * sg + bgate;
+            static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(r) * p.ldo + m] = __float2bfloat16_rn(silu(gx) * x);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D tensor map: inner extent `cols` elements, `rows` rows, row pitch in bytes.
+static bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t cols, uint64_t rows,
+                     uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static bool weight_map(CUtensorMap* m, const sb_grouped_gemm_args& a, const void* base) {
+  if (a.wfmt == SB_W_BF16)
+    return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.lda, a.a_rows_total, a.lda * 2, kTcBK, kTcBM,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  if (a.wfmt == SB_W_FP8)
+    return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.lda, a.a_rows_total, a.lda, kTcBK, kTcBM,
+                    CU_TENSOR_MAP_SWIZZLE_NONE);
+  return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.lda / 2, a.a_rows_total, a.lda / 2, kTcBK / 2, kTcBM,
+                  CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+bool tcgen05_supported(const sb_grouped_gemm_args& a) {
+  if (a.act_dtype != SB_BF16) return false;
+  if (a.wfmt != SB_W_BF16 && a.wfmt != SB_W_FP8 && a.wfmt != SB_W_INT4) return false;
+  if (a.splits <= 0 || a.k % (kTcBK * a.splits)) return false;
+  if (a.wfmt == SB_W_INT4 && (a.group_size <= 0 || a.group_size % kTcBK || a.lda % a.group_size)) return false;
+  if (a.ldx % 8 || (a.wfmt == SB_W_BF16 && a.lda % 8) || (a.wfmt != SB_W_BF16 && a.lda % 32)) return false;
+  if (reinterpret_cast<uintptr_t>(a.a) % 16 || reinterpret_cast<uintptr_t>(a.x) % 16) return false;
+  if (a.epilogue == SB_EPI_SWIGLU && (!a.a_gate || reinterpret_cast<uintptr_t>(a.a_gate) % 16)) return false;
+  if (a.a_rows_total > 0x7fffffffLL || a.max_rows <= 0) return false;
+  return current_cc_major() == 10;
+}
+
+template <int BN, int WFMT, int EPI>
+static int launch_tc(const sb_grouped_gemm_args& a, cudaStream_t st) {
+  using C = TcCfg<BN, WFMT, EPI>;
+  auto kern = tc_gemm_kernel<BN, WFMT, EPI>;
+  static int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e);
+    configured_device = dev;
+  }
+  CUtensorMap ma, mg, mb;
+  if (!weight_map(&ma, a, a.a)) return SB_ERR_UNSUPPORTED;
+  mg = ma;
+  if (C::kGate && !weight_map(&mg, a, a.a_gate)) return SB_ERR_UNSUPPORTED;
+  if (!make_map(&mb, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.k, a.max_rows, a.ldx * 2, kTcBK, BN,
+                CU_TENSOR_MAP_SWIZZLE_128B))
+    return SB_ERR_UNSUPPORTED;
+  const dim3 grid((a.m_rows + kTcBM - 1) / kTcBM, (a.max_rows + BN - 1) / BN + a.num_groups, a.splits);
+  kern<<<grid, kTcThreads, C::kSmemBytes, st>>>(ma, mg, mb, a);
+  return sb_last_launch_status();
+}
+
+template <int WFMT, int EPI>
+static int launch_bn(const sb_grouped_gemm_args& a, cudaStream_t st, int bn) {
+  switch (bn) {
+    case 16: return launch_tc<16, WFMT, EPI>(a, st);
+    case 32: return launch_tc<32, WFMT, EPI>(a, st);
+    case 64: return launch_tc<64, WFMT, EPI>(a, st);
+    case 128: return launch_tc<128, WFMT, EPI>(a, st);
+    default: return launch_tc<256, WFMT, EPI>(a, st);
+  }
+}
+
+template <int WFMT>
+static int launch_epi(const sb_grouped_gemm_args& a, cudaStream_t st, int bn) {
+  switch (a.epilogue) {
+    case SB_EPI_LINEAR: return launch_bn<WFMT, SB_EPI_LINEAR>(a, st, bn);
+    case SB_EPI_GELU: return launch_bn<WFMT, SB_EPI_GELU>(a, st, bn);
+    default: return launch_bn<WFMT, SB_EPI_SWIGLU>(a, st, bn);
+  }
+}
+
+// Column tile: the smallest of 16..256 that covers the expected rows per group.
+static int choose_bn(const sb_grouped_gemm_args& a) {
+  const int hint = a.rows_hint > 0 ? a.rows_hint : a.max_rows;
+  const int per_group = (hint + a.num_groups - 1) / a.num_groups;
+  if (per_group <= 16) return 16;
+  if (per_group <= 32) return 32;
+  if (per_group <= 64) return 64;
+  if (per_group <= 128) return 128;
+  return 256;
+}
+
+int gemm_tcgen05(const sb_grouped_gemm_args& a, cudaStream_t st) {
+  const int bn = choose_bn(a);
+  switch (a.wfmt) {
+    case SB_W_BF16: return launch_epi<SB_W_BF16>(a, st, bn);
+    case SB_W_FP8: return launch_epi<SB_W_FP8>(a, st, bn);
+    case SB_W_INT4: return launch_epi<SB_W_INT4>(a, st, bn);
+    default: return SB_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace sb

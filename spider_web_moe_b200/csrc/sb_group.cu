@@ -1,0 +1,162 @@
+// Device dispatch plan: stable grouping of (row, slot) entries by group id.
+//
+// This is build_dispatch_plan (spider_infer/forge/ep/dispatch.py:56-115) and
+// the per-expert token selection of sparse_expert_delta (spider_moe/
+// sparse_experts.py:51-57) as one permutation: groups in ascending id, rows
+// ascending inside a group, repeated ids of one row merged into their first
+// slot with the weights summed, and (optionally) entries with summed weight
+// <= 0 dropped.  The result is deterministic: ranks come from warp match masks
+// and a fixed-order scan, never from atomics.
+#include "sb_common.cuh"
+#include "sb_internal.h"
+
+namespace sb {
+
+constexpr int kGroupThreads = 1024;
+constexpr int kGroupMaxG = 256;
+
+// Evaluate entry e = row*slots + s: returns its group (or -1) and summed weight.
+SB_DEVINL int entry_group(const int32_t* __restrict__ idx, const float* __restrict__ w, int slots,
+                          int G, int flags, int64_t e, float& wsum) {
+  const int64_t row0 = (e / slots) * slots;
+  const int s = static_cast<int>(e - row0);
+  const int g = idx[e];
+  wsum = 0.f;
+  if (g < 0 || g >= G) return -1;
+  for (int j = 0; j < s; ++j)
+    if (idx[row0 + j] == g) return -1;  // merged into an earlier slot of the same row
+  float acc = 0.f;
+  for (int j = 0; j < slots; ++j)
+    if (idx[row0 + j] == g) acc += w ? w[row0 + j] : 1.f;
+  wsum = acc;
+  if ((flags & SB_GROUP_POSITIVE_ONLY) && !(acc > 0.f)) return -1;
+  return g;
+}
+
+__global__ void __launch_bounds__(kGroupThreads, 1)
+group_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w, int n_rows, int slots,
+             int G, int flags, int32_t* __restrict__ offsets, int32_t* __restrict__ perm_row,
+             int32_t* __restrict__ perm_slot, float* __restrict__ perm_w, int32_t* __restrict__ inv,
+             int32_t* __restrict__ rank_scratch, float* __restrict__ w_scratch) {
+  __shared__ int wcnt[32][kGroupMaxG];
+  __shared__ int run_total[kGroupMaxG];
+  __shared__ int s_off[kGroupMaxG + 1];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t total = static_cast<int64_t>(n_rows) * slots;
+  for (int g = tid; g < G; g += kGroupThreads) run_total[g] = 0;
+  const unsigned lt_mask = (1u << lane) - 1u;
+
+  for (int64_t base = 0; base < total; base += kGroupThreads) {
+    for (int i = tid; i < 32 * kGroupMaxG; i += kGroupThreads) (&wcnt[0][0])[i] = 0;
+    __syncthreads();
+    const int64_t e = base + tid;
+    float wsum = 0.f;
+    const int g = e < total ? entry_group(idx, w, slots, G, flags, e, wsum) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, g);
+    const int rank_w = __popc(peers & lt_mask);
+    if (g >= 0 && rank_w == 0) wcnt[warp][g] = __popc(peers);
+    __syncthreads();
+    for (int gg = tid; gg < G; gg += kGroupThreads) {
+      int acc = run_total[gg];
+      for (int ww = 0; ww < 32; ++ww) {
+        const int c = wcnt[ww][gg];
+        wcnt[ww][gg] = acc;
+        acc += c;
+      }
+      run_total[gg] = acc;
+    }
+    __syncthreads();
+    if (e < total) {
+      rank_scratch[e] = g >= 0 ? wcnt[warp][g] + rank_w : -1;
+      w_scratch[e] = wsum;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    int acc = 0;
+    for (int g = 0; g < G; ++g) {
+      s_off[g] = acc;
+      acc += run_total[g];
+    }
+    s_off[G] = acc;
+  }
+  __syncthreads();
+  for (int g = tid; g <= G; g += kGroupThreads) offsets[g] = s_off[g];
+  for (int64_t e = tid; e < total; e += kGroupThreads) {
+    const int r = rank_scratch[e];
+    if (r < 0) {
+      inv[e] = -1;
+      continue;
+    }
+    const int g = idx[e];
+    const int pos = s_off[g] + r;
+    perm_row[pos] = static_cast<int32_t>(e / slots);
+    perm_slot[pos] = static_cast<int32_t>(e);
+    perm_w[pos] = w_scratch[e];
+    inv[e] = pos;
+  }
+}
+
+template <typename V>
+__global__ void gather_rows_kernel(const V* __restrict__ src, int vec_per_row,
+                                   const int32_t* __restrict__ perm_row,
+                                   const int32_t* __restrict__ offsets, int G, int max_rows,
+                                   V* __restrict__ dst) {
+  const int rows = min(offsets[G], max_rows);
+  const int64_t n = static_cast<int64_t>(rows) * vec_per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / vec_per_row;
+    const int c = static_cast<int>(i - r * vec_per_row);
+    dst[i] = src[static_cast<int64_t>(perm_row[r]) * vec_per_row + c];
+  }
+}
+
+}  // namespace sb
+
+using namespace sb;
+
+extern "C" SB_API size_t sb_group_workspace_bytes(int n_rows, int slots, int num_groups) {
+  (void)num_groups;
+  const size_t total = static_cast<size_t>(n_rows > 0 ? n_rows : 0) * (slots > 0 ? slots : 0);
+  return kStatusBytes + align_up(total * sizeof(int32_t), 256) + align_up(total * sizeof(float), 256);
+}
+
+extern "C" SB_API int sb_group(const int32_t* idx, const float* w, int n_rows, int slots,
+                               int num_groups, int flags, int32_t* offsets, int32_t* perm_row,
+                               int32_t* perm_slot, float* perm_w, int32_t* inv, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (n_rows < 0 || slots <= 0 || num_groups <= 0 || num_groups > kGroupMaxG || !offsets ||
+      (n_rows > 0 && (!idx || !perm_row || !perm_slot || !perm_w || !inv)))
+    return SB_ERR_ARG;
+  const size_t need = sb_group_workspace_bytes(n_rows, slots, num_groups);
+  if (!workspace || workspace_bytes < need) return SB_ERR_WORKSPACE;
+  Carver c(workspace, workspace_bytes);
+  c.take<char>(kStatusBytes);
+  const size_t total = static_cast<size_t>(n_rows) * slots;
+  int32_t* rank_scratch = c.take<int32_t>(total);
+  float* w_scratch = c.take<float>(total);
+  group_kernel<<<1, kGroupThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      idx, w, n_rows, slots, num_groups, flags, offsets, perm_row, perm_slot, perm_w, inv,
+      rank_scratch, w_scratch);
+  return sb_last_launch_status();
+}
+
+extern "C" SB_API int sb_gather_rows(const void* src, int act_dtype, int cols,
+                                     const int32_t* perm_row, const int32_t* offsets, int num_groups,
+                                     int max_rows, void* dst, void* stream) {
+  if (!src || !perm_row || !offsets || !dst || cols <= 0 || num_groups <= 0 || max_rows < 0)
+    return SB_ERR_ARG;
+  const int esize = act_dtype == SB_F32 ? 4 : (act_dtype == SB_BF16 ? 2 : 0);
+  if (!esize || (static_cast<int64_t>(cols) * esize) % 16) return SB_ERR_ARG;
+  if (max_rows == 0) return SB_OK;
+  const int vpr = cols * esize / 16;
+  int64_t n = static_cast<int64_t>(max_rows) * vpr;
+  int blocks = static_cast<int>((n + 255) / 256);
+  const int cap = 8 * current_sm_count();
+  blocks = blocks > cap ? cap : blocks;
+  gather_rows_kernel<uint4><<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), vpr, perm_row, offsets, num_groups, max_rows,
+      static_cast<uint4*>(dst));
+  return sb_last_launch_status();
+}

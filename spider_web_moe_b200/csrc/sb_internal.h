@@ -1,0 +1,47 @@
+// Internal host-side helpers shared by the translation units of libspider_b200.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "spider_b200.h"
+
+namespace sb {
+
+inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? SB_OK : SB_ERR_CUDA_BASE + static_cast<int>(e); }
+
+inline int sb_last_launch_status() { return cuda_status(cudaGetLastError()); }
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Bump allocator over a caller-owned workspace; every carve is 256-byte aligned.
+struct Carver {
+  char* base;
+  size_t size;
+  size_t used = 0;
+  bool overflow = false;
+  Carver(void* b, size_t s) : base(static_cast<char*>(b)), size(s) {}
+  template <typename T>
+  T* take(size_t count) {
+    used = align_up(used, 256);
+    T* p = base ? reinterpret_cast<T*>(base + used) : nullptr;
+    used += count * sizeof(T);
+    if (used > size) overflow = true;
+    return p;
+  }
+};
+
+// Bytes reserved at the start of every workspace for the device status word.
+constexpr size_t kStatusBytes = 256;
+
+// Grouped GEMM engines (sb_gemm_simt.cu, sb_gemm_tc.cu).
+int gemm_simt(const sb_grouped_gemm_args& a, cudaStream_t st);
+int gemm_tcgen05(const sb_grouped_gemm_args& a, cudaStream_t st);
+bool tcgen05_supported(const sb_grouped_gemm_args& a);
+
+// Device properties cached per device.
+int current_sm_count();
+int current_cc_major();
+
+}  // namespace sb

@@ -1,0 +1,250 @@
+"""Device-side state of one recurrent Spider-MoE block and the calls into the C ABI.
+
+``BlockEngine`` packs a block's parameters (reference state-dict names,
+spider_moe/model.py:165-216) into the layouts the kernels read, owns the
+workspace, and runs loops of the block through ``sb_block_forward``.  Packed
+layouts in HBM:
+
+* router ``[E, H]``, edge-generator hidden part ``[E*E, H]``, edge values
+  ``[E, H, H]`` -- all in the activation dtype, row-major, i.e. each weight
+  row is one K-major MMA operand row;
+* per-loop edge-generator bias ``[L, E*E]`` fp32: the generator bias plus the
+  loop-embedding columns applied to ``loop_embedding[l]``, folded once at
+  packing time (the loop embedding is constant per loop, model.py:260-263);
+* experts ``w_up [E, U, H]`` / ``w_down [E, H, U]`` in bf16, fp8 (+ fp32
+  scale per output row) or packed int4 (+ bf16 scale per row and group of
+  the reduction dim), biases fp32.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import torch
+
+from . import _lib as L
+from .config import ModelConfig, from_any
+from .quant import Int4Tensor, quantize_fp8_per_channel, quantize_int4
+
+
+def _act_code(dtype: torch.dtype) -> int:
+    if dtype == torch.float32:
+        return L.SB_F32
+    if dtype == torch.bfloat16:
+        return L.SB_BF16
+    raise TypeError(f"activation dtype {dtype} not supported (float32 or bfloat16)")
+
+
+def _stream_ptr(stream=None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def stacked(sd: dict, fmt: str, e: int) -> torch.Tensor:
+    return torch.stack([sd[fmt.format(i)] for i in range(e)])
+
+
+class BlockEngine:
+    """Packed weights + workspace for one block on one device."""
+
+    def __init__(self, cfg, state: dict, device, act_dtype=torch.bfloat16, max_tokens: int = 64,
+                 weight_format: str | None = None, engine: str = "auto",
+                 int4: dict | None = None, fp8: dict | None = None):
+        self.cfg = from_any(cfg)
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise RuntimeError("BlockEngine runs on CUDA devices only (no CPU path)")
+        self.lib = L.load()
+        self.act_dtype = act_dtype
+        cfg = self.cfg
+        H, E, U, Lp = cfg.hidden_size, cfg.num_experts, cfg.expert_ffn_size, cfg.num_loops
+        fmt = weight_format or cfg.expert_weight_format
+        if int4 is not None:
+            fmt = "int4"
+        elif fp8 is not None:
+            fmt = "fp8"
+        if fmt == "native":
+            fmt = "f32" if act_dtype == torch.float32 else "bf16"
+        if fmt == "f32" and act_dtype != torch.float32:
+            raise ValueError("fp32 expert weights need fp32 activations")
+        self.weight_format = fmt
+        dev, dt = self.device, act_dtype
+        f32 = torch.float32
+        g = lambda k: state[k].detach().to(dev)  # noqa: E731
+        self.t = {}
+        t = self.t
+        if "router.weight" in state:  # experts-only engines (sparse_expert_delta) skip the dense parts
+            t["router_w"] = g("router.weight").to(dt).contiguous()
+            t["loop_bias"] = g("loop_bias").to(f32).contiguous()
+            gen_full = g("edge_generator.weight").to(f32)
+            t["gen_w"] = gen_full[:, :H].to(dt).contiguous()
+            emb = g("loop_embedding.weight").to(f32)                  # [L, Le]
+            t["gen_bias"] = (g("edge_generator.bias").to(f32).unsqueeze(0)
+                             + emb @ gen_full[:, H:].t()).contiguous()  # [L, E*E]
+            del gen_full
+            t["edge_w"] = stacked(state, "edge_value.{}.weight", E).to(dev, dt).contiguous()
+            t["ln_w"] = g("norm.weight").to(f32).contiguous()
+            t["ln_b"] = g("norm.bias").to(f32).contiguous()
+        t["b_up"] = stacked(state, "experts.{}.0.bias", E).to(dev, f32).contiguous()
+        t["b_down"] = stacked(state, "experts.{}.2.bias", E).to(dev, f32).contiguous()
+        swiglu = cfg.expert_activation == "swiglu"
+        if swiglu:
+            t["b_gate"] = stacked(state, "expert_gates.{}.bias", E).to(dev, f32).contiguous()
+        self.group_size = 0
+        names = [("up", "experts.{}.0.weight")] + ([("gate", "expert_gates.{}.weight")] if swiglu else []) \
+            + [("down", "experts.{}.2.weight")]
+        for short, key in names:
+            if fmt in ("f32", "bf16"):
+                t["w_" + short] = stacked(state, key, E).to(dev, f32 if fmt == "f32" else torch.bfloat16).contiguous()
+            elif fmt == "fp8":
+                if fp8 is not None and short in fp8:
+                    q, s = fp8[short]
+                else:
+                    q8 = quantize_fp8_per_channel(stacked(state, key, E).to(dev, f32))
+                    q, s = q8.q, q8.scale
+                t["w_" + short] = q.to(dev).view(torch.uint8).contiguous()
+                t["s_" + short] = s.to(dev, f32).contiguous()
+            elif fmt == "int4":
+                if int4 is not None and short in int4:
+                    qt: Int4Tensor = int4[short]
+                else:
+                    gs = cfg.moe_int4_group_size
+                    qt = quantize_int4(stacked(state, key, E).to(dev, f32), gs)
+                self.group_size = qt.group_size
+                t["w_" + short] = qt.packed.to(dev).contiguous()
+                t["s_" + short] = qt.device_scales().to(dev).contiguous()
+            else:
+                raise ValueError(f"unknown weight format {fmt}")
+        wcode = {"f32": L.SB_W_F32, "bf16": L.SB_W_BF16, "fp8": L.SB_W_FP8, "int4": L.SB_W_INT4}[fmt]
+        self.dims = L.BlockDims(
+            hidden=H, num_experts=E, top_k=cfg.top_k, edges_per_expert=cfg.edges_per_expert, ffn=U,
+            num_loops=Lp, act_dtype=_act_code(dt), wfmt=wcode,
+            activation=L.SB_ACT_SWIGLU if swiglu else L.SB_ACT_GELU, group_size=self.group_size,
+            engine=L.ENGINES[engine], max_tokens=int(max_tokens),
+            residual_scale=float(cfg.residual_scale), reinject=float(cfg.re_inject_weight), ln_eps=1e-5)
+        p = lambda k: t[k].data_ptr() if k in t else None  # noqa: E731
+        self.weights = L.BlockWeights(
+            router_w=p("router_w"), loop_bias=p("loop_bias"), gen_w=p("gen_w"), gen_bias=p("gen_bias"),
+            edge_w=p("edge_w"), w_up=p("w_up"), s_up=p("s_up"), b_up=p("b_up"), w_gate=p("w_gate"),
+            s_gate=p("s_gate"), b_gate=p("b_gate"), w_down=p("w_down"), s_down=p("s_down"),
+            b_down=p("b_down"), ln_w=p("ln_w"), ln_b=p("ln_b"))
+        self.workspace = None
+        self._ensure_workspace(int(max_tokens))
+
+    # ------------------------------------------------------------------ workspace
+    def _ensure_workspace(self, n_tokens: int):
+        if self.workspace is not None and n_tokens <= self.dims.max_tokens:
+            return
+        self.dims.max_tokens = max(int(n_tokens), int(self.dims.max_tokens))
+        nbytes = self.lib.sb_block_workspace_bytes(C.byref(self.dims))
+        if nbytes == 0:
+            raise L.SpiderB200Error(L.SB_ERR_ARG, "sb_block_workspace_bytes")
+        self.workspace = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+
+    def weight_bytes(self) -> int:
+        return sum(v.numel() * v.element_size() for v in self.t.values())
+
+    def status(self) -> int:
+        """Device status word (non-zero: a bounded wait ran out); synchronises."""
+        off = self.lib.sb_status_offset()
+        return int(self.workspace[off:off + 4].view(torch.int32).item())
+
+    def check_status(self):
+        s = self.status()
+        if s:
+            raise L.SpiderB200Error(L.SB_ERR_DEVICE_STATUS, f"device status 0x{s:x}")
+
+    # ------------------------------------------------------------------ calls
+    def forward(self, h: torch.Tensor, x0: torch.Tensor, loop_begin: int = 0, loop_end: int | None = None,
+                out: torch.Tensor | None = None, taps: dict | None = None, stream=None) -> torch.Tensor:
+        """Run loops [loop_begin, loop_end) on h (shape [..., H]); x0 is the block input."""
+        H = self.cfg.hidden_size
+        loop_end = self.cfg.num_loops if loop_end is None else loop_end
+        if h.device != self.device or x0.device != self.device:
+            raise RuntimeError("inputs must live on the engine's CUDA device")
+        n = h.numel() // H
+        self._ensure_workspace(n)
+        h2 = h.reshape(n, H)
+        if h2.dtype != self.act_dtype or not h2.is_contiguous():
+            h2 = h2.to(self.act_dtype).contiguous()
+        x2 = x0.reshape(n, H)
+        if x2.dtype != self.act_dtype or not x2.is_contiguous():
+            x2 = x2.to(self.act_dtype).contiguous()
+        if out is None:
+            out = torch.empty((n, H), dtype=self.act_dtype, device=self.device)
+        ctaps = None
+        if taps is not None:
+            ctaps = L.BlockTaps(**{k: (v.data_ptr() if v is not None else None) for k, v in taps.items()})
+        rc = self.lib.sb_block_forward(C.byref(self.dims), C.byref(self.weights), h2.data_ptr(), x2.data_ptr(),
+                                       out.data_ptr(), n, int(loop_begin), int(loop_end),
+                                       self.workspace.data_ptr(), self.workspace.numel(),
+                                       C.byref(ctaps) if ctaps is not None else None, _stream_ptr(stream))
+        L.check(rc, "sb_block_forward")
+        if os.environ.get("SPIDER_B200_CHECK"):
+            self.check_status()
+        return out.view(h.shape)
+
+    def make_taps(self, n: int) -> dict:
+        cfg = self.cfg
+        K, M, E, H = cfg.top_k, cfg.edges_per_expert, cfg.num_experts, cfg.hidden_size
+        z = lambda *s, dt=torch.float32: torch.zeros(*s, dtype=dt, device=self.device)  # noqa: E731
+        return dict(top_idx=z(n, K, dt=torch.int32), top_w=z(n, K), edge_idx=z(n, K, M, dt=torch.int32),
+                    edge_w=z(n, K, M), messages=z(n, H), delta=z(n, H),
+                    ffn_offsets=z(E + 1, dt=torch.int32), ffn_rows=z(n * K, dt=torch.int32),
+                    ffn_weights=z(n * K))
+
+    def expert_delta(self, messages: torch.Tensor, top_idx: torch.Tensor, top_w: torch.Tensor,
+                     rank: int = 0, world: int = 1, stream=None) -> torch.Tensor:
+        """sparse_expert_delta for this rank's experts (e % world == rank), fp32 [n, H]."""
+        H, K = self.cfg.hidden_size, self.cfg.top_k
+        n = messages.numel() // H
+        m2 = messages.reshape(n, H)
+        if m2.dtype != self.act_dtype or not m2.is_contiguous():
+            m2 = m2.to(self.act_dtype).contiguous()
+        idx = top_idx.reshape(n, K).to(torch.int32).contiguous()
+        w = top_w.reshape(n, K).to(torch.float32).contiguous()
+        delta = torch.empty((n, H), dtype=torch.float32, device=self.device)
+        nbytes = self.lib.sb_expert_delta_workspace_bytes(C.byref(self.dims), n)
+        ws = self._delta_ws(nbytes)
+        rc = self.lib.sb_expert_delta(C.byref(self.dims), C.byref(self.weights), m2.data_ptr(), idx.data_ptr(),
+                                      w.data_ptr(), n, int(rank), int(world), delta.data_ptr(), ws.data_ptr(),
+                                      ws.numel(), _stream_ptr(stream))
+        L.check(rc, "sb_expert_delta")
+        return delta
+
+    def _delta_ws(self, nbytes: int) -> torch.Tensor:
+        ws = getattr(self, "_dws", None)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+            self._dws = ws
+        return ws
+
+
+class CapturedBlock:
+    """All loops of a block for a fixed token count, captured in one CUDA graph."""
+
+    def __init__(self, engine: BlockEngine, n_tokens: int, loop_begin: int = 0, loop_end: int | None = None):
+        self.engine = engine
+        H = engine.cfg.hidden_size
+        dev, dt = engine.device, engine.act_dtype
+        engine._ensure_workspace(n_tokens)
+        self.h = torch.zeros(n_tokens, H, dtype=dt, device=dev)
+        self.x0 = torch.zeros(n_tokens, H, dtype=dt, device=dev)
+        self.out = torch.zeros(n_tokens, H, dtype=dt, device=dev)
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            engine.forward(self.h, self.x0, loop_begin, loop_end, out=self.out)  # warm-up (lazy init)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            engine.forward(self.h, self.x0, loop_begin, loop_end, out=self.out)
+
+    def __call__(self, h=None, x0=None):
+        if h is not None:
+            self.h.copy_(h.reshape(self.h.shape))
+        if x0 is not None:
+            self.x0.copy_(x0.reshape(self.x0.shape))
+        self.graph.replay()
+        return self.out

@@ -1,0 +1,166 @@
+"""Drop-in ``SpiderMoELayer`` running on the B200 kernels.
+
+Same constructor, parameter names (so ``load_state_dict`` of a reference
+checkpoint works unchanged), ``forward(h, x0, loop_idx, return_stats=False)``
+signature and ``quantize_experts(group_size)`` / ``dequantize_experts()`` as
+the reference module (spider_moe/model.py:163-349).  The forward pass runs in
+libspider_b200 on CUDA tensors; CPU tensors raise (there is no CPU path).
+
+Expert parallel (reference semantics, spider_moe/expert_parallel.py:1-37):
+when ``torch.distributed`` is initialised with more than one rank and
+``cfg.expert_parallel`` is true, every rank holds all tokens, computes its own
+experts (``e % world == rank``) and the delta is summed across ranks before
+the LayerNorm epilogue, so every rank returns the same output.  The
+token-sharded all-to-all variant lives in ``spider_web_moe_b200.ep``.
+"""
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from . import expert_parallel as ep_helpers
+from .config import from_any
+from .engine import BlockEngine
+from .quant import Int4Tensor, quantize_fp8_per_channel, quantize_int4
+
+
+class SpiderMoELayer(nn.Module):
+    """Shared recurrent layer: token router + per-loop sparse graph + expert FFNs."""
+
+    def __init__(self, cfg):
+        super().__init__()
+        cfg = from_any(cfg)
+        self.cfg = cfg
+        h, e = cfg.hidden_size, cfg.num_experts
+        self.num_experts, self.top_k = e, cfg.top_k
+        self.top_dobu = int(getattr(cfg, "offload_max_gpu_experts", 4))
+        self.edges_per_expert = cfg.edges_per_expert
+        self.router = nn.Linear(h, e, bias=False)
+        self.loop_bias = nn.Parameter(torch.zeros(cfg.num_loops, e))
+        self.loop_embedding = nn.Embedding(cfg.num_loops, cfg.loop_embed_size)
+        self.edge_generator = nn.Linear(h + cfg.loop_embed_size, e * e)
+        self.edge_value = nn.ModuleList([nn.Linear(h, h, bias=False) for _ in range(e)])
+        self.experts = nn.ModuleList([
+            nn.Sequential(nn.Linear(h, cfg.expert_ffn_size), nn.GELU(), nn.Linear(cfg.expert_ffn_size, h))
+            for _ in range(e)
+        ])
+        self.norm = nn.LayerNorm(h)
+        self.exit_head = nn.Linear(h, 1)
+        if cfg.expert_activation == "swiglu":
+            self.expert_gates = nn.ModuleList([nn.Linear(h, cfg.expert_ffn_size) for _ in range(e)])
+        self.residual_scale = cfg.residual_scale
+        self.reinject_weight = cfg.re_inject_weight
+        self.expert_parallel = bool(getattr(cfg, "expert_parallel", True))
+        self.engine_name = "auto"
+        self._int4_w_up: Int4Tensor | None = None
+        self._int4_w_down: Int4Tensor | None = None
+        self._int4_w_gate: Int4Tensor | None = None
+        self._fp8 = None
+        self._engine: BlockEngine | None = None
+        self._engine_key = None
+
+    # ------------------------------------------------------------------ weight formats
+    @torch.no_grad()
+    def quantize_experts(self, group_size: int = 64) -> None:
+        """Pack expert up/down weights to group-wise INT4 (reference: model.py:218-231)."""
+        stack = lambda j: torch.stack([ex[j].weight.detach() for ex in self.experts], dim=0)  # noqa: E731
+        self._int4_w_up = quantize_int4(stack(0), group_size=group_size)
+        self._int4_w_down = quantize_int4(stack(2), group_size=group_size)
+        if hasattr(self, "expert_gates"):
+            self._int4_w_gate = quantize_int4(torch.stack([g.weight.detach() for g in self.expert_gates]),
+                                              group_size=group_size)
+        self._fp8 = None
+        self.invalidate()
+
+    @torch.no_grad()
+    def quantize_experts_fp8(self) -> None:
+        """e4m3 expert weights with one fp32 scale per output channel (absmax/448)."""
+        stack = lambda j: torch.stack([ex[j].weight.detach() for ex in self.experts], dim=0)  # noqa: E731
+        up = quantize_fp8_per_channel(stack(0))
+        down = quantize_fp8_per_channel(stack(2))
+        self._fp8 = {"up": (up.q, up.scale), "down": (down.q, down.scale)}
+        if hasattr(self, "expert_gates"):
+            gt = quantize_fp8_per_channel(torch.stack([g.weight.detach() for g in self.expert_gates]))
+            self._fp8["gate"] = (gt.q, gt.scale)
+        self._int4_w_up = self._int4_w_down = self._int4_w_gate = None
+        self.invalidate()
+
+    def dequantize_experts(self) -> None:
+        """Clear quantised expert buffers and use the nn.Linear weights again."""
+        self._int4_w_up = self._int4_w_down = self._int4_w_gate = None
+        self._fp8 = None
+        self.invalidate()
+
+    def invalidate(self) -> None:
+        """Drop packed device weights (call after changing parameters in place)."""
+        self._engine = None
+        self._engine_key = None
+
+    def _load_from_state_dict(self, *args, **kwargs):
+        self.invalidate()
+        return super()._load_from_state_dict(*args, **kwargs)
+
+    def engine(self, device, act_dtype, n_tokens: int) -> BlockEngine:
+        key = (str(device), act_dtype, self.engine_name)
+        if self._engine is None or self._engine_key != key:
+            int4 = None
+            if self._int4_w_up is not None:
+                int4 = {"up": self._int4_w_up, "down": self._int4_w_down}
+                if self._int4_w_gate is not None:
+                    int4["gate"] = self._int4_w_gate
+            self._engine = BlockEngine(self.cfg, self.state_dict(), device, act_dtype=act_dtype,
+                                       max_tokens=max(n_tokens, 1), engine=self.engine_name,
+                                       int4=int4, fp8=self._fp8)
+            self._engine_key = key
+        return self._engine
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, h, x0, loop_idx, return_stats=False):
+        """One loop of the block (model.py:240-317) on CUDA tensors [B, T, H]."""
+        if not h.is_cuda:
+            raise RuntimeError("spider_b200 SpiderMoELayer runs on CUDA tensors only")
+        n = h.numel() // h.shape[-1]
+        eng = self.engine(h.device, h.dtype if h.dtype in (torch.float32, torch.bfloat16) else torch.float32, n)
+        use_ep = self.expert_parallel and ep_helpers.ep_enabled()
+        if not use_ep and not return_stats:
+            return eng.forward(h, x0, loop_idx, loop_idx + 1).to(h.dtype)
+        taps = eng.make_taps(n)
+        if not use_ep:
+            out = eng.forward(h, x0, loop_idx, loop_idx + 1, taps=taps).to(h.dtype)
+        else:
+            out = self._forward_ep(eng, h, x0, loop_idx, taps)
+        if not return_stats:
+            return out
+        return out, self._stats(taps, out)
+
+    def _forward_ep(self, eng, h, x0, loop_idx, taps):
+        """Reference expert-parallel semantics: local experts, SUM all-reduce of delta."""
+        rank, world = ep_helpers.get_rank_world()
+        eng.forward(h, x0, loop_idx, loop_idx + 1, taps=taps)  # routing + messages for all tokens
+        delta = eng.expert_delta(taps["messages"], taps["top_idx"], taps["top_w"], rank, world)
+        ep_helpers.all_reduce_sum_(delta)
+        n, H = delta.shape
+        hh = h.reshape(n, H).float()
+        u = hh + self.residual_scale * delta + self.reinject_weight * x0.reshape(n, H).float()
+        out = torch.nn.functional.layer_norm(u, (H,), eng.t["ln_w"], eng.t["ln_b"], 1e-5)
+        return out.to(h.dtype).view(h.shape)
+
+    def run_loops(self, h, x0, loop_begin: int = 0, loop_end: int | None = None):
+        """All loops [loop_begin, loop_end) in one library call (model.py:445-448)."""
+        n = h.numel() // h.shape[-1]
+        eng = self.engine(h.device, h.dtype, n)
+        return eng.forward(h, x0, loop_begin, loop_end)
+
+    def _stats(self, taps, out):
+        """Router / edge load statistics of model.py:327-349 from the loop's taps."""
+        e = self.num_experts
+        ti = taps["top_idx"].long().reshape(-1)
+        load = torch.bincount(ti, minlength=e).float()
+        load = load / load.sum().clamp_min(1.0)
+        ei = taps["edge_idx"].long().reshape(-1)
+        edge_load = torch.bincount(ei, minlength=e).float()
+        edge_load = edge_load / edge_load.sum().clamp_min(1.0)
+        confidence = torch.sigmoid(self.exit_head(out.float() if out.dtype != self.exit_head.weight.dtype
+                                                  else out).float()).squeeze(-1)
+        return {"expert_load": load, "edge_load": edge_load, "confidence": confidence,
+                "top_indices": taps["top_idx"], "top_weights": taps["top_w"]}
