@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--activation", default="gelu", choices=["gelu", "swiglu"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-only", action="store_true",
+                    help="capture the graph, replay warmup+steps times, print nothing else (for ncu)")
     return ap.parse_args()
 
 
@@ -211,6 +213,9 @@ def stage_timing(eng, h, steps):
     ns = lib.sb_num_stages()
     lib.sb_stage_timing(1)
     for _ in range(steps):
+        # Keep the GPU busy while the host enqueues the step, so every event
+        # pair brackets device execution, not host launch latency.
+        torch.cuda._sleep(4_000_000)
         eng.forward(h, h)
     torch.cuda.synchronize()
     ms = (C.c_double * ns)()
@@ -333,6 +338,14 @@ def run_b200(args):
         g.graph.replay()
     torch.cuda.synchronize(device)
     eng.check_status()
+    if args.profile_only:
+        for _ in range(args.steps):
+            g.graph.replay()
+        torch.cuda.synchronize(device)
+        eng.check_status()
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
