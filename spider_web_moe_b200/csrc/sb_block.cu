@@ -52,10 +52,21 @@ int current_cc_major() {
   return cached[dev];
 }
 
+bool pdl_enabled() {
+  static int cached = -1;
+  if (cached < 0) {
+    const char* v = getenv("SPIDER_B200_PDL");
+    cached = (v && v[0] == '0') ? 0 : 1;
+  }
+  return cached == 1;
+}
+
 static int act_size(int dt) { return dt == SB_F32 ? 4 : 2; }
 
 __global__ void remap_local_kernel(const int32_t* __restrict__ idx, int n, int E, int rank, int world,
                                    int32_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const int e = idx[i];
     out[i] = (e >= 0 && e < E && e % world == rank) ? e / world : -1;
@@ -188,9 +199,10 @@ static int pick_splits(int m_rows, int k, int rows_hint, int groups, int max_spl
   const int bn = per_group <= 16 ? 16 : per_group <= 32 ? 32 : per_group <= 64 ? 64 : per_group <= 128 ? 128 : 256;
   int tiles = m_tiles * (rows_hint / bn + (groups < rows_hint ? groups : rows_hint));
   if (tiles < 1) tiles = 1;
-  const int sms = current_sm_count();
+  // Small column tiles run two CTAs per SM: aim for about two CTAs per SM.
+  const int target = (bn <= 64 ? 2 : 1) * current_sm_count();
   int s = 1;
-  while (s * 2 <= max_splits && tiles * s * 2 <= sms && (k % ((tc ? 64 : 32) * s * 2)) == 0) s *= 2;
+  while (s * 2 <= max_splits && tiles * s * 2 <= target && (k % ((tc ? 64 : 32) * s * 2)) == 0) s *= 2;
   return s;
 }
 
@@ -454,8 +466,9 @@ extern "C" SB_API int sb_expert_delta(const sb_block_dims* dims, const sb_block_
   const int N = n_tokens, H = d.hidden, E = d.num_experts, K = d.top_k, U = d.ffn;
   const int G = (E - rank + world - 1) / world;
   if (G <= 0) return cuda_status(cudaMemsetAsync(delta, 0, sizeof(float) * static_cast<size_t>(N) * H, st));
-  remap_local_kernel<<<(N * K + 255) / 256, 256, 0, st>>>(top_idx, N * K, E, rank, world, b.top_idx);
-  if ((rc = sb_last_launch_status())) return rc;
+  rc = launch(remap_local_kernel, dim3((N * K + 255) / 256), dim3(256), 0, st, top_idx, N * K, E, rank, world,
+              b.top_idx);
+  if (rc) return rc;
 #define SB_TRY(x) do { rc = (x); if (rc) return rc; } while (0)
   SB_TRY(sb_group(b.top_idx, top_w, N, K, G, SB_GROUP_POSITIVE_ONLY, b.ffn_off, b.ffn_row, b.ffn_slot, b.ffn_w,
                   b.ffn_inv, b.group_ws, b.group_ws_bytes, st));

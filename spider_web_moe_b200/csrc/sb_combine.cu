@@ -11,6 +11,28 @@
 namespace sb {
 
 constexpr int kCombineThreads = 128;
+
+template <typename T> struct Vec4;
+template <> struct Vec4<float> {
+  static SB_DEVINL float4 load(const float* p) { return *reinterpret_cast<const float4*>(p); }
+  static SB_DEVINL void store(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+};
+template <> struct Vec4<__nv_bfloat16> {
+  static SB_DEVINL float4 load(const __nv_bfloat16* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  static SB_DEVINL void store(__nv_bfloat16* p, float4 v) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&a);
+    u.y = *reinterpret_cast<const uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(p) = u;
+  }
+};
+
 constexpr int kMaxSlots = 64;
 
 template <typename T>
@@ -21,6 +43,8 @@ combine_rows_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_
                     int scatter_slots, T* __restrict__ scatter_out) {
   __shared__ int s_rows[kMaxSlots];
   __shared__ int s_dst[kMaxSlots];
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   if (threadIdx.x < slots) s_rows[threadIdx.x] = inv[static_cast<int64_t>(t) * slots + threadIdx.x];
   if (scatter_inv && threadIdx.x < scatter_slots)
@@ -42,16 +66,14 @@ combine_rows_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_
       for (int k = 0; k < scatter_slots; ++k) {
         const int q = s_dst[k];
         if (q < 0) continue;
-        T* o = scatter_out + static_cast<int64_t>(q) * cols + c;
-        o[0] = from_f32<T>(acc.x); o[1] = from_f32<T>(acc.y);
-        o[2] = from_f32<T>(acc.z); o[3] = from_f32<T>(acc.w);
+        Vec4<T>::store(scatter_out + static_cast<int64_t>(q) * cols + c, acc);
       }
     }
   }
 }
 
 constexpr int kLnThreads = 256;
-constexpr int kLnMaxPerThread = 16;  // hidden <= 4096
+constexpr int kLnMaxVec = 4;  // float4 chunks per thread: hidden <= 256*4*4 = 4096
 
 SB_DEVINL float block_sum(float v, float* red) {
   v = warp_sum(v);
@@ -69,6 +91,7 @@ SB_DEVINL float block_sum(float v, float* red) {
   return red[0];
 }
 
+// One CTA per token; thread t owns float4 chunks t, t+256, ... of the row.
 template <typename T>
 __global__ void __launch_bounds__(kLnThreads)
 combine_ln_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t split_stride,
@@ -76,53 +99,76 @@ combine_ln_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t 
                   const T* __restrict__ h, const T* __restrict__ x0, int cols,
                   const float* __restrict__ ln_w, const float* __restrict__ ln_b, float alpha,
                   float beta, float eps, T* __restrict__ out, float* __restrict__ delta_out) {
-  __shared__ int s_rows[kMaxSlots];
   __shared__ float red[32];
-  const int t = blockIdx.x;
-  if (y && threadIdx.x < slots) s_rows[threadIdx.x] = inv[static_cast<int64_t>(t) * slots + threadIdx.x];
-  __syncthreads();
-  float u[kLnMaxPerThread];
+  pdl_wait();
+  pdl_trigger();
+  const int64_t t = blockIdx.x;
+  const int nvec = cols >> 2;
+  float4 u[kLnMaxVec], hv[kLnMaxVec], xv[kLnMaxVec];
+#pragma unroll
+  for (int i = 0; i < kLnMaxVec; ++i) {
+    const int v = threadIdx.x + i * kLnThreads;
+    if (v < nvec) {
+      hv[i] = Vec4<T>::load(h + t * cols + 4 * v);
+      xv[i] = Vec4<T>::load(x0 + t * cols + 4 * v);
+    }
+  }
+  int rows[kMaxSlots];
+  int nrows = 0;
+  if (y) {
+    for (int j = 0; j < slots; ++j) {
+      const int r = inv[t * slots + j];
+      if (r >= 0) rows[nrows++] = r;
+    }
+  }
   float local = 0.f;
 #pragma unroll
-  for (int i = 0; i < kLnMaxPerThread; ++i) {
-    const int c = threadIdx.x + i * kLnThreads;
-    u[i] = 0.f;
-    if (c < cols) {
-      float d = 0.f;
+  for (int i = 0; i < kLnMaxVec; ++i) {
+    const int v = threadIdx.x + i * kLnThreads;
+    u[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (v < nvec) {
+      float4 d = make_float4(0.f, 0.f, 0.f, 0.f);
       if (y) {
-        for (int j = 0; j < slots; ++j) {
-          const int r = s_rows[j];
-          if (r < 0) continue;
-          for (int s = 0; s < splits; ++s) d += y[s * split_stride + static_cast<int64_t>(r) * ldy + c];
-        }
+        for (int j = 0; j < nrows; ++j)
+          for (int s = 0; s < splits; ++s) {
+            const float4 a = *reinterpret_cast<const float4*>(y + s * split_stride + static_cast<int64_t>(rows[j]) * ldy + 4 * v);
+            d.x += a.x; d.y += a.y; d.z += a.z; d.w += a.w;
+          }
       } else {
-        d = delta_in[static_cast<int64_t>(t) * cols + c];
+        d = *reinterpret_cast<const float4*>(delta_in + t * cols + 4 * v);
       }
-      if (delta_out) delta_out[static_cast<int64_t>(t) * cols + c] = d;
-      const float hv = to_f32(h[static_cast<int64_t>(t) * cols + c]);
-      const float xv = to_f32(x0[static_cast<int64_t>(t) * cols + c]);
-      const float a = hv + alpha * d;
-      u[i] = a + beta * xv;
-      local += u[i];
+      if (delta_out) *reinterpret_cast<float4*>(delta_out + t * cols + 4 * v) = d;
+      u[i].x = (hv[i].x + alpha * d.x) + beta * xv[i].x;
+      u[i].y = (hv[i].y + alpha * d.y) + beta * xv[i].y;
+      u[i].z = (hv[i].z + alpha * d.z) + beta * xv[i].z;
+      u[i].w = (hv[i].w + alpha * d.w) + beta * xv[i].w;
+      local += (u[i].x + u[i].y) + (u[i].z + u[i].w);
     }
   }
   const float mean = block_sum(local, red) / static_cast<float>(cols);
   float sq = 0.f;
 #pragma unroll
-  for (int i = 0; i < kLnMaxPerThread; ++i) {
-    const int c = threadIdx.x + i * kLnThreads;
-    if (c < cols) {
-      const float dv = u[i] - mean;
-      sq += dv * dv;
+  for (int i = 0; i < kLnMaxVec; ++i) {
+    const int v = threadIdx.x + i * kLnThreads;
+    if (v < nvec) {
+      const float a = u[i].x - mean, b = u[i].y - mean, c = u[i].z - mean, e = u[i].w - mean;
+      sq += (a * a + b * b) + (c * c + e * e);
     }
   }
-  const float var = block_sum(sq, red) / static_cast<float>(cols);
-  const float rstd = rsqrtf(var + eps);
+  const float rstd = rsqrtf(block_sum(sq, red) / static_cast<float>(cols) + eps);
 #pragma unroll
-  for (int i = 0; i < kLnMaxPerThread; ++i) {
-    const int c = threadIdx.x + i * kLnThreads;
-    if (c < cols)
-      out[static_cast<int64_t>(t) * cols + c] = from_f32<T>((u[i] - mean) * rstd * ln_w[c] + ln_b[c]);
+  for (int i = 0; i < kLnMaxVec; ++i) {
+    const int v = threadIdx.x + i * kLnThreads;
+    if (v < nvec) {
+      const float4 g = *reinterpret_cast<const float4*>(ln_w + 4 * v);
+      const float4 b = *reinterpret_cast<const float4*>(ln_b + 4 * v);
+      float4 o;
+      o.x = (u[i].x - mean) * rstd * g.x + b.x;
+      o.y = (u[i].y - mean) * rstd * g.y + b.y;
+      o.z = (u[i].z - mean) * rstd * g.z + b.z;
+      o.w = (u[i].w - mean) * rstd * g.w + b.w;
+      Vec4<T>::store(out + t * cols + 4 * v, o);
+    }
   }
 }
 
@@ -141,16 +187,13 @@ extern "C" SB_API int sb_combine_rows(const float* y, int64_t ldy, int splits, i
   if (n_tokens == 0) return SB_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (act_dtype == SB_F32)
-    combine_rows_kernel<float><<<n_tokens, kCombineThreads, 0, st>>>(
-        y, ldy, splits, split_stride, inv, slots, cols, out_f32, scatter_inv, scatter_slots,
-        static_cast<float*>(scatter_out));
-  else if (act_dtype == SB_BF16)
-    combine_rows_kernel<__nv_bfloat16><<<n_tokens, kCombineThreads, 0, st>>>(
-        y, ldy, splits, split_stride, inv, slots, cols, out_f32, scatter_inv, scatter_slots,
-        static_cast<__nv_bfloat16*>(scatter_out));
-  else
-    return SB_ERR_ARG;
-  return sb_last_launch_status();
+    return launch(combine_rows_kernel<float>, dim3(n_tokens), dim3(kCombineThreads), 0, st, y, ldy, splits,
+                  split_stride, inv, slots, cols, out_f32, scatter_inv, scatter_slots, static_cast<float*>(scatter_out));
+  if (act_dtype == SB_BF16)
+    return launch(combine_rows_kernel<__nv_bfloat16>, dim3(n_tokens), dim3(kCombineThreads), 0, st, y, ldy, splits,
+                  split_stride, inv, slots, cols, out_f32, scatter_inv, scatter_slots,
+                  static_cast<__nv_bfloat16*>(scatter_out));
+  return SB_ERR_ARG;
 }
 
 extern "C" SB_API int sb_combine_ln(const float* y, int64_t ldy, int splits, int64_t split_stride,
@@ -159,23 +202,20 @@ extern "C" SB_API int sb_combine_ln(const float* y, int64_t ldy, int splits, int
                                     int cols, const float* ln_w, const float* ln_b, float alpha,
                                     float beta, float eps, void* out, float* delta_out,
                                     void* stream) {
-  if (n_tokens < 0 || cols <= 0 || cols > kLnThreads * kLnMaxPerThread || !ln_w || !ln_b ||
+  if (n_tokens < 0 || cols <= 0 || cols > kLnThreads * kLnMaxVec * 4 || cols % 4 || !ln_w || !ln_b ||
       (y && (!inv || slots <= 0 || slots > kMaxSlots || splits <= 0 || ldy < cols)) ||
       (!y && !delta_in) || (n_tokens > 0 && (!h || !x0 || !out)))
     return SB_ERR_ARG;
   if (n_tokens == 0) return SB_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (act_dtype == SB_F32)
-    combine_ln_kernel<float><<<n_tokens, kLnThreads, 0, st>>>(
-        y, ldy, splits, split_stride, inv, slots, delta_in, static_cast<const float*>(h),
-        static_cast<const float*>(x0), cols, ln_w, ln_b, alpha, beta, eps, static_cast<float*>(out),
-        delta_out);
-  else if (act_dtype == SB_BF16)
-    combine_ln_kernel<__nv_bfloat16><<<n_tokens, kLnThreads, 0, st>>>(
-        y, ldy, splits, split_stride, inv, slots, delta_in, static_cast<const __nv_bfloat16*>(h),
-        static_cast<const __nv_bfloat16*>(x0), cols, ln_w, ln_b, alpha, beta, eps,
-        static_cast<__nv_bfloat16*>(out), delta_out);
-  else
-    return SB_ERR_ARG;
-  return sb_last_launch_status();
+    return launch(combine_ln_kernel<float>, dim3(n_tokens), dim3(kLnThreads), 0, st, y, ldy, splits, split_stride,
+                  inv, slots, delta_in, static_cast<const float*>(h), static_cast<const float*>(x0), cols, ln_w,
+                  ln_b, alpha, beta, eps, static_cast<float*>(out), delta_out);
+  if (act_dtype == SB_BF16)
+    return launch(combine_ln_kernel<__nv_bfloat16>, dim3(n_tokens), dim3(kLnThreads), 0, st, y, ldy, splits,
+                  split_stride, inv, slots, delta_in, static_cast<const __nv_bfloat16*>(h),
+                  static_cast<const __nv_bfloat16*>(x0), cols, ln_w, ln_b, alpha, beta, eps,
+                  static_cast<__nv_bfloat16*>(out), delta_out);
+  return SB_ERR_ARG;
 }

@@ -67,6 +67,13 @@ SB_DEVINL void warp_argmax(float& v, int& i) {
   }
 }
 
+// Programmatic dependent launch: wait until the preceding kernel in the stream
+// has completed and its writes are visible (a no-op for a normal launch), and
+// allow the next kernel to be scheduled.  Every kernel launched with the PDL
+// attribute calls pdl_wait() before its first read of a predecessor's output.
+SB_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+SB_DEVINL void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 SB_DEVINL void record_error(int* status, int bits) {
   if (status) atomicOr(status, bits);
 }

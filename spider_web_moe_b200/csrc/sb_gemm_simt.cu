@@ -44,6 +44,8 @@ simt_gemm_kernel(const sb_grouped_gemm_args p) {
   __shared__ float Gs[kGate ? kSimtBK : 1][kSimtBM + 4];
   __shared__ float Bs[kSimtBK][kSimtBN + 4];
   __shared__ int s_sched[4];
+  pdl_wait();
+  pdl_trigger();
   const int tid = threadIdx.x;
   if (tid < 32) {
     int g, n0, n_end;
@@ -140,11 +142,8 @@ int gemm_simt(const sb_grouped_gemm_args& a, cudaStream_t st) {
   const int m_tiles = (a.m_rows + kSimtBM - 1) / kSimtBM;
   const int n_slots = (a.max_rows + kSimtBN - 1) / kSimtBN + a.num_groups;
   const dim3 grid(m_tiles, n_slots, a.splits);
-  if (a.epilogue == SB_EPI_SWIGLU)
-    simt_gemm_kernel<true><<<grid, kSimtThreads, 0, st>>>(a);
-  else
-    simt_gemm_kernel<false><<<grid, kSimtThreads, 0, st>>>(a);
-  return sb_last_launch_status();
+  if (a.epilogue == SB_EPI_SWIGLU) return launch(simt_gemm_kernel<true>, grid, dim3(kSimtThreads), 0, st, a);
+  return launch(simt_gemm_kernel<false>, grid, dim3(kSimtThreads), 0, st, a);
 }
 
 }  // namespace sb

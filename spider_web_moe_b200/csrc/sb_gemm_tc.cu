@@ -30,7 +30,10 @@ namespace sb {
 constexpr int kTcBM = 128;
 constexpr int kTcBK = 64;
 constexpr int kTcThreads = 192;
-constexpr int kTcSmemBudget = 200 * 1024;
+// Shared memory for the pipeline stages: small column tiles (decode) keep two
+// CTAs per SM (two independent TMA/MMA latency chains), large ones take one.
+constexpr int kTcSmemBudgetSmallN = 110 * 1024;
+constexpr int kTcSmemBudgetLargeN = 200 * 1024;
 
 template <int BN, int WFMT, int EPI>
 struct TcCfg {
@@ -40,7 +43,8 @@ struct TcCfg {
   static constexpr int kBBytes = BN * kTcBK * 2;
   static constexpr int kRawBytes = WFMT == SB_W_FP8 ? kTcBM * kTcBK : (WFMT == SB_W_INT4 ? kTcBM * kTcBK / 2 : 0);
   static constexpr int kStageBytes = kABytes * (kGate ? 2 : 1) + kBBytes + kRawBytes * (kGate ? 2 : 1);
-  static constexpr int kStagesRaw = kTcSmemBudget / kStageBytes;
+  static constexpr int kBudget = BN <= 64 ? kTcSmemBudgetSmallN : kTcSmemBudgetLargeN;
+  static constexpr int kStagesRaw = kBudget / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
   static constexpr int kTmemCols = (BN * (kGate ? 2 : 1)) <= 32 ? 32 : BN * (kGate ? 2 : 1);
   // shared memory layout (offsets from a 1024-aligned base)
@@ -130,15 +134,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   int* s_sched = reinterpret_cast<int*>(smem + C::kOffMisc + 16);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (warp == 0) {
-    int g, n0, n_end;
-    const bool ok = schedule_tile(p.offsets, p.num_groups, BN, blockIdx.y, g, n0, n_end);
-    if (lane == 0) {
-      s_sched[0] = ok ? g : -1;
-      s_sched[1] = n0;
-      s_sched[2] = min(n_end, p.max_rows);
-    }
-  }
+  // Set-up that reads no predecessor output runs before the dependency wait.
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
@@ -147,6 +143,22 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     mbar_init(done, 1);
     fence_barrier_init();
+  }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (C::kGate) tma_prefetch_desc(&tmG);
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (warp == 0) {
+    int g, n0, n_end;
+    const bool ok = schedule_tile(p.offsets, p.num_groups, BN, blockIdx.y, g, n0, n_end);
+    if (lane == 0) {
+      s_sched[0] = ok ? g : -1;
+      s_sched[1] = n0;
+      s_sched[2] = min(n_end, p.max_rows);
+    }
   }
   __syncthreads();
   const int g = s_sched[0];
@@ -170,9 +182,6 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   if (warp == 4) {
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
-      tma_prefetch_desc(&tmA);
-      tma_prefetch_desc(&tmB);
-      if (C::kGate) tma_prefetch_desc(&tmG);
       constexpr uint32_t kTx = (C::kConvert ? C::kRawBytes : C::kABytes) * (C::kGate ? 2 : 1) + C::kBBytes;
       int issued = 0;
       for (int it = 0; it < nk; ++it) {
@@ -348,6 +357,8 @@ static int launch_tc(const sb_grouped_gemm_args& a, cudaStream_t st) {
   if (configured_device != dev) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (e != cudaSuccess) return cuda_status(e);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return cuda_status(e);
     configured_device = dev;
   }
   CUtensorMap ma, mg, mb;
@@ -358,8 +369,7 @@ static int launch_tc(const sb_grouped_gemm_args& a, cudaStream_t st) {
                 CU_TENSOR_MAP_SWIZZLE_128B))
     return SB_ERR_UNSUPPORTED;
   const dim3 grid((a.m_rows + kTcBM - 1) / kTcBM, (a.max_rows + BN - 1) / BN + a.num_groups, a.splits);
-  kern<<<grid, kTcThreads, C::kSmemBytes, st>>>(ma, mg, mb, a);
-  return sb_last_launch_status();
+  return launch(kern, grid, dim3(kTcThreads), C::kSmemBytes, st, ma, mg, mb, a);
 }
 
 template <int WFMT, int EPI>

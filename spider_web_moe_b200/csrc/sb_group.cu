@@ -41,13 +41,16 @@ group_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w, int n
   __shared__ int wcnt[32][kGroupMaxG];
   __shared__ int run_total[kGroupMaxG];
   __shared__ int s_off[kGroupMaxG + 1];
+  pdl_wait();
+  pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nthreads = blockDim.x, nwarps = nthreads >> 5;
   const int64_t total = static_cast<int64_t>(n_rows) * slots;
-  for (int g = tid; g < G; g += kGroupThreads) run_total[g] = 0;
+  for (int g = tid; g < G; g += nthreads) run_total[g] = 0;
   const unsigned lt_mask = (1u << lane) - 1u;
 
-  for (int64_t base = 0; base < total; base += kGroupThreads) {
-    for (int i = tid; i < 32 * kGroupMaxG; i += kGroupThreads) (&wcnt[0][0])[i] = 0;
+  for (int64_t base = 0; base < total; base += nthreads) {
+    for (int i = tid; i < nwarps * kGroupMaxG; i += nthreads) (&wcnt[0][0])[i] = 0;
     __syncthreads();
     const int64_t e = base + tid;
     float wsum = 0.f;
@@ -56,9 +59,9 @@ group_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w, int n
     const int rank_w = __popc(peers & lt_mask);
     if (g >= 0 && rank_w == 0) wcnt[warp][g] = __popc(peers);
     __syncthreads();
-    for (int gg = tid; gg < G; gg += kGroupThreads) {
+    for (int gg = tid; gg < G; gg += nthreads) {
       int acc = run_total[gg];
-      for (int ww = 0; ww < 32; ++ww) {
+      for (int ww = 0; ww < nwarps; ++ww) {
         const int c = wcnt[ww][gg];
         wcnt[ww][gg] = acc;
         acc += c;
@@ -81,8 +84,8 @@ group_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w, int n
     s_off[G] = acc;
   }
   __syncthreads();
-  for (int g = tid; g <= G; g += kGroupThreads) offsets[g] = s_off[g];
-  for (int64_t e = tid; e < total; e += kGroupThreads) {
+  for (int g = tid; g <= G; g += nthreads) offsets[g] = s_off[g];
+  for (int64_t e = tid; e < total; e += nthreads) {
     const int r = rank_scratch[e];
     if (r < 0) {
       inv[e] = -1;
@@ -102,6 +105,8 @@ __global__ void gather_rows_kernel(const V* __restrict__ src, int vec_per_row,
                                    const int32_t* __restrict__ perm_row,
                                    const int32_t* __restrict__ offsets, int G, int max_rows,
                                    V* __restrict__ dst) {
+  pdl_wait();
+  pdl_trigger();
   const int rows = min(offsets[G], max_rows);
   const int64_t n = static_cast<int64_t>(rows) * vec_per_row;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
@@ -136,10 +141,12 @@ extern "C" SB_API int sb_group(const int32_t* idx, const float* w, int n_rows, i
   const size_t total = static_cast<size_t>(n_rows) * slots;
   int32_t* rank_scratch = c.take<int32_t>(total);
   float* w_scratch = c.take<float>(total);
-  group_kernel<<<1, kGroupThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      idx, w, n_rows, slots, num_groups, flags, offsets, perm_row, perm_slot, perm_w, inv,
-      rank_scratch, w_scratch);
-  return sb_last_launch_status();
+  // One CTA; as many threads as entries (rounded to warps, 64..1024): fewer warps
+  // to synchronise and scan when a decode batch has only a few hundred entries.
+  int threads = static_cast<int>(((total + 31) / 32) * 32);
+  threads = threads < 64 ? 64 : (threads > kGroupThreads ? kGroupThreads : threads);
+  return launch(group_kernel, dim3(1), dim3(threads), 0, static_cast<cudaStream_t>(stream), idx, w, n_rows,
+                slots, num_groups, flags, offsets, perm_row, perm_slot, perm_w, inv, rank_scratch, w_scratch);
 }
 
 extern "C" SB_API int sb_gather_rows(const void* src, int act_dtype, int cols,
@@ -155,8 +162,6 @@ extern "C" SB_API int sb_gather_rows(const void* src, int act_dtype, int cols,
   int blocks = static_cast<int>((n + 255) / 256);
   const int cap = 8 * current_sm_count();
   blocks = blocks > cap ? cap : blocks;
-  gather_rows_kernel<uint4><<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint4*>(src), vpr, perm_row, offsets, num_groups, max_rows,
-      static_cast<uint4*>(dst));
-  return sb_last_launch_status();
+  return launch(gather_rows_kernel<uint4>, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                static_cast<const uint4*>(src), vpr, perm_row, offsets, num_groups, max_rows, static_cast<uint4*>(dst));
 }

@@ -40,6 +40,26 @@ int gemm_simt(const sb_grouped_gemm_args& a, cudaStream_t st);
 int gemm_tcgen05(const sb_grouped_gemm_args& a, cudaStream_t st);
 bool tcgen05_supported(const sb_grouped_gemm_args& a);
 
+// Kernel launch with programmatic stream serialization (PDL), unless disabled
+// by SPIDER_B200_PDL=0.  Kernels launched this way call pdl_wait() first.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                  Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
 // Device properties cached per device.
 int current_sm_count();
 int current_cc_major();

@@ -35,47 +35,80 @@ template <> struct Vec8<__nv_bfloat16> {
   }
 };
 
-// One warp per token.  Lane j owns 8-element chunks j, j+32, ... of the hidden
-// vector (kept in registers, H <= 32*8*kMaxChunks) and the logits of experts
-// j, j+32, ...
-template <typename T, int kMaxChunks>
+// One CTA per kRouterTok tokens.  Their hidden rows are staged in shared
+// memory; warp w computes the logits of experts w, w+8, ... for all of them,
+// four experts (and their weight loads) at a time, so the weight rows are read
+// once per CTA and many loads are in flight.  Warps 0..kRouterTok-1 then do the
+// softmax and top-k of one token each.
+constexpr int kRouterTok = 4;
+constexpr int kRouterEPI = 4;  // experts per iteration of a warp
+
+template <typename T>
 __global__ void __launch_bounds__(kRouterWarps * 32)
 router_kernel(const T* __restrict__ h, int n_tokens, int hidden, const T* __restrict__ wr,
               const float* __restrict__ bias, int E, int K, int32_t* __restrict__ top_idx,
               float* __restrict__ top_w, float* __restrict__ probs_out) {
-  const int lane = threadIdx.x & 31;
-  const int token = blockIdx.x * kRouterWarps + (threadIdx.x >> 5);
-  if (token >= n_tokens) return;
-  const int nchunks = hidden >> 3;  // hidden % 8 == 0 checked on the host
-  float hv[kMaxChunks][8];
-#pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
-    const int chunk = lane + 32 * c;
-    if (chunk < nchunks) Vec8<T>::load(h + static_cast<size_t>(token) * hidden + chunk * 8, hv[c]);
+  extern __shared__ __align__(16) uint8_t router_smem[];
+  T* sh = reinterpret_cast<T*>(router_smem);                                       // [kRouterTok][hidden]
+  float* slog = reinterpret_cast<float*>(router_smem + kRouterTok * hidden * sizeof(T));  // [kRouterTok][E]
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * kRouterTok;
+  const int ntok = min(kRouterTok, n_tokens - t0);
+  const int nchunks = hidden >> 3;  // 8 elements per 16-byte (bf16) / 32-byte (fp32) chunk
+  // stage the token rows (16-byte vectors)
+  {
+    const int vec_per_row = hidden * static_cast<int>(sizeof(T)) / 16;
+    const uint4* src = reinterpret_cast<const uint4*>(h + static_cast<size_t>(t0) * hidden);
+    uint4* dst = reinterpret_cast<uint4*>(sh);
+    for (int i = threadIdx.x; i < ntok * vec_per_row; i += blockDim.x) dst[i] = src[i];
   }
-  float logit[kRouterMaxE / 32];
+  __syncthreads();
+  for (int e0 = warp * kRouterEPI; e0 < E; e0 += kRouterWarps * kRouterEPI) {
+    float acc[kRouterEPI][kRouterTok];
 #pragma unroll
-  for (int i = 0; i < kRouterMaxE / 32; ++i) logit[i] = -INFINITY;
-  for (int e = 0; e < E; ++e) {
-    const T* row = wr + static_cast<size_t>(e) * hidden;
-    float acc = 0.f;
+    for (int j = 0; j < kRouterEPI; ++j)
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
-      const int chunk = lane + 32 * c;
-      if (chunk < nchunks) {
-        float wv[8];
-        Vec8<T>::load(row + chunk * 8, wv);
+      for (int t = 0; t < kRouterTok; ++t) acc[j][t] = 0.f;
+    for (int c = lane; c < nchunks; c += 32) {
+      float wv[kRouterEPI][8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc = fmaf(hv[c][i], wv[i], acc);
+      for (int j = 0; j < kRouterEPI; ++j)
+        if (e0 + j < E) Vec8<T>::load(wr + static_cast<size_t>(e0 + j) * hidden + c * 8, wv[j]);
+#pragma unroll
+      for (int t = 0; t < kRouterTok; ++t) {
+        if (t < ntok) {
+          float hv[8];
+          Vec8<T>::load(sh + t * hidden + c * 8, hv);
+#pragma unroll
+          for (int j = 0; j < kRouterEPI; ++j)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[j][t] = fmaf(hv[i], wv[j][i], acc[j][t]);
+        }
       }
     }
-    acc = warp_sum(acc);
-    const float lg = acc + bias[e];
 #pragma unroll
-    for (int i = 0; i < kRouterMaxE / 32; ++i)
-      if (e == lane + 32 * i) logit[i] = lg;
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int j = 0; j < kRouterEPI; ++j)
+#pragma unroll
+        for (int t = 0; t < kRouterTok; ++t) acc[j][t] += __shfl_xor_sync(0xffffffffu, acc[j][t], o);
+    if (lane == 0) {
+#pragma unroll
+      for (int j = 0; j < kRouterEPI; ++j)
+        if (e0 + j < E)
+#pragma unroll
+          for (int t = 0; t < kRouterTok; ++t) slog[t * E + e0 + j] = acc[j][t] + bias[e0 + j];
+    }
   }
-  // fp32 softmax over E.
+  __syncthreads();
+  if (warp >= ntok) return;
+  const int token = t0 + warp;
+  float logit[kRouterMaxE / 32];
+#pragma unroll
+  for (int i = 0; i < kRouterMaxE / 32; ++i) logit[i] = (lane + 32 * i < E) ? slog[warp * E + lane + 32 * i] : -INFINITY;
+  // fp32 softmax over E (spider_moe/model.py:256).
   float mx = -INFINITY;
 #pragma unroll
   for (int i = 0; i < kRouterMaxE / 32; ++i) mx = fmaxf(mx, logit[i]);
@@ -93,7 +126,8 @@ router_kernel(const T* __restrict__ h, int n_tokens, int hidden, const T* __rest
     p[i] = p[i] / s;
     if (probs_out && lane + 32 * i < E) probs_out[static_cast<size_t>(token) * E + lane + 32 * i] = p[i];
   }
-  // top-K by repeated arg-max; a taken expert is masked with -1 (probabilities are >= 0).
+  // top-K by repeated arg-max (model.py:257); a taken expert is masked with -1
+  // (probabilities are >= 0), equal values go to the smaller expert id.
   float sel_w = 0.f, sum_w = 0.f;
   int sel_i = -1;
   for (int k = 0; k < K; ++k) {
@@ -111,6 +145,7 @@ router_kernel(const T* __restrict__ h, int n_tokens, int hidden, const T* __rest
     sum_w += bv;
     if (lane == k) { sel_w = bv; sel_i = bi; }
   }
+  // renormalise (model.py:258)
   if (lane < K) {
     top_idx[static_cast<size_t>(token) * K + lane] = sel_i;
     top_w[static_cast<size_t>(token) * K + lane] = sel_w / fmaxf(sum_w, 1e-9f);
@@ -122,6 +157,8 @@ __global__ void __launch_bounds__(256)
 edge_topm_kernel(const float* __restrict__ logits, int64_t ld, int E, int M,
                  const int32_t* __restrict__ perm_slot, const int32_t* __restrict__ offsets,
                  int G, int max_rows, int32_t* __restrict__ edge_idx, float* __restrict__ edge_w) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
   const int rows = min(offsets[G], max_rows);
@@ -174,32 +211,34 @@ extern "C" SB_API int sb_router(const void* h, int act_dtype, int n_tokens, int 
       top_k <= 0 || top_k > num_experts || top_k > 32 || !router_w || !loop_bias_l || !top_idx ||
       !top_w || (n_tokens > 0 && !h))
     return SB_ERR_ARG;
-  if (hidden > 32 * 8 * 16) return SB_ERR_UNSUPPORTED;
   if (n_tokens == 0) return SB_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const dim3 grid((n_tokens + kRouterWarps - 1) / kRouterWarps), block(kRouterWarps * 32);
-  const int chunks = (hidden / 8 + 31) / 32;
-#define SB_ROUTER_LAUNCH(T, C)                                                                    \
-  router_kernel<T, C><<<grid, block, 0, st>>>(static_cast<const T*>(h), n_tokens, hidden,          \
-                                              static_cast<const T*>(router_w), loop_bias_l,        \
-                                              num_experts, top_k, top_idx, top_w, probs)
+  const dim3 grid((n_tokens + kRouterTok - 1) / kRouterTok), block(kRouterWarps * 32);
+  const int esize = act_dtype == SB_F32 ? 4 : 2;
+  const size_t smem = static_cast<size_t>(kRouterTok) * hidden * esize + static_cast<size_t>(kRouterTok) * num_experts * 4;
+  if (smem > 200 * 1024) return SB_ERR_UNSUPPORTED;
+  int rc = SB_OK;
   if (act_dtype == SB_F32) {
-    if (chunks <= 1) SB_ROUTER_LAUNCH(float, 1);
-    else if (chunks <= 2) SB_ROUTER_LAUNCH(float, 2);
-    else if (chunks <= 4) SB_ROUTER_LAUNCH(float, 4);
-    else if (chunks <= 8) SB_ROUTER_LAUNCH(float, 8);
-    else SB_ROUTER_LAUNCH(float, 16);
+    static bool attr_set = false;
+    if (!attr_set && smem > 48 * 1024) {
+      cudaFuncSetAttribute(router_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      attr_set = true;
+    }
+    rc = launch(router_kernel<float>, grid, block, smem, st, static_cast<const float*>(h), n_tokens, hidden,
+                static_cast<const float*>(router_w), loop_bias_l, num_experts, top_k, top_idx, top_w, probs);
   } else if (act_dtype == SB_BF16) {
-    if (chunks <= 1) SB_ROUTER_LAUNCH(__nv_bfloat16, 1);
-    else if (chunks <= 2) SB_ROUTER_LAUNCH(__nv_bfloat16, 2);
-    else if (chunks <= 4) SB_ROUTER_LAUNCH(__nv_bfloat16, 4);
-    else if (chunks <= 8) SB_ROUTER_LAUNCH(__nv_bfloat16, 8);
-    else SB_ROUTER_LAUNCH(__nv_bfloat16, 16);
+    static bool attr_set = false;
+    if (!attr_set && smem > 48 * 1024) {
+      cudaFuncSetAttribute(router_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      attr_set = true;
+    }
+    rc = launch(router_kernel<__nv_bfloat16>, grid, block, smem, st, static_cast<const __nv_bfloat16*>(h), n_tokens,
+                hidden, static_cast<const __nv_bfloat16*>(router_w), loop_bias_l, num_experts, top_k, top_idx, top_w,
+                probs);
   } else {
     return SB_ERR_ARG;
   }
-#undef SB_ROUTER_LAUNCH
-  return sb_last_launch_status();
+  return rc;
 }
 
 extern "C" SB_API int sb_edge_topm(const float* logits, int64_t ld, int num_experts, int edges,
@@ -213,7 +252,6 @@ extern "C" SB_API int sb_edge_topm(const float* logits, int64_t ld, int num_expe
   const int warps = 8;
   int blocks = (max_rows + warps - 1) / warps;
   blocks = blocks > 4 * 148 ? 4 * 148 : blocks;
-  edge_topm_kernel<<<blocks, warps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      logits, ld, num_experts, edges, perm_slot, offsets, num_groups, max_rows, edge_idx, edge_w);
-  return sb_last_launch_status();
+  return launch(edge_topm_kernel, dim3(blocks), dim3(warps * 32), 0, static_cast<cudaStream_t>(stream), logits, ld,
+                num_experts, edges, perm_slot, offsets, num_groups, max_rows, edge_idx, edge_w);
 }
