@@ -137,8 +137,14 @@ typedef struct sb_grouped_gemm_args {
   int64_t bias_group_stride;
   const void* x;
   int64_t ldx;
+  /* Optional gather: when x_row_index is not NULL, permuted row r of the B
+   * operand is row x_row_index[r] of x (x then has x_rows rows); otherwise x
+   * holds the permuted rows themselves. */
+  const int32_t* x_row_index;
+  int x_rows;
   int max_rows;           /* rows allocated in x / out (upper bound of offsets[G]) */
   int rows_hint;          /* host estimate of offsets[G] (tile shape choice only) */
+  int group_rows_bound;   /* upper bound of any one group's rows, 0 if unknown (tile choice only) */
   const int32_t* offsets; /* [G+1] device */
   const float* row_scale; /* [max_rows] per permuted row, SB_EPI_LINEAR only, may be NULL */
   void* out;
@@ -162,9 +168,9 @@ SB_API int sb_edge_topm(const float* logits, int64_t ld, int num_experts, int ed
 
 /* ------------------------------------------------------------------ combines
  * Row combine: out[t, :] = sum_{j<slots, inv[t*slots+j]>=0} sum_s y[s][inv[t*slots+j], :]
- * (fixed ascending order, no atomics).  out_f32 and/or out_act may be NULL;
- * scatter_inv (may be NULL) additionally writes the combined row, in act_dtype,
- * to rows scatter_inv[t*scatter_slots+k] >= 0 of scatter_out. */
+ * (fixed ascending order, no atomics).  out_f32 may be NULL.  If scatter_out is
+ * not NULL the combined row is also written there in act_dtype: to rows
+ * scatter_inv[t*scatter_slots+k] >= 0, or to row t when scatter_inv is NULL. */
 SB_API int sb_combine_rows(const float* y, int64_t ldy, int splits, int64_t split_stride,
                            const int32_t* inv, int slots, int n_tokens, int cols, float* out_f32,
                            const int32_t* scatter_inv, int scatter_slots, void* scatter_out,

@@ -42,7 +42,8 @@ class GemmArgs(C.Structure):
         ("a_group_rows", i64), ("lda", i64), ("a_rows_total", i64),
         ("a", vp), ("a_scale", vp), ("a_gate", vp), ("a_gate_scale", vp),
         ("bias", vp), ("bias_gate", vp), ("bias_group_stride", i64),
-        ("x", vp), ("ldx", i64), ("max_rows", i32), ("rows_hint", i32),
+        ("x", vp), ("ldx", i64), ("x_row_index", vp), ("x_rows", i32), ("max_rows", i32), ("rows_hint", i32),
+        ("group_rows_bound", i32),
         ("offsets", vp), ("row_scale", vp), ("out", vp), ("ldo", i64),
         ("splits", i32), ("split_stride", i64), ("status", vp),
     ]

@@ -117,6 +117,7 @@ struct BlockBuffers {
   int32_t *dst_off, *dst_row, *dst_slot, *dst_inv; float* dst_w;
   void* x_dst; float* y_msg;
   float* msg_f32;
+  void* msg_act;
   int32_t *ffn_off, *ffn_row, *ffn_slot, *ffn_inv; float* ffn_w;
   void* x_ffn; void* act; float* y_ffn;
   void* hbuf[2];
@@ -155,6 +156,7 @@ static size_t carve_block(const sb_block_dims& d, int n_cap, void* base, size_t 
   b->x_dst = c.take<char>(cap_dst * H * as);
   b->y_msg = c.take<float>(msg_rows * H);
   b->msg_f32 = c.take<float>(N * H);
+  b->msg_act = c.take<char>(N * H * as);
   b->ffn_off = c.take<int32_t>(E + 1);
   b->ffn_row = c.take<int32_t>(N * K);
   b->ffn_slot = c.take<int32_t>(N * K);
@@ -192,12 +194,24 @@ static int run_gemm(sb_grouped_gemm_args& a, int engine_pref, cudaStream_t st) {
   return tc_ok ? gemm_tcgen05(a, st) : gemm_simt(a, st);
 }
 
+// Whether a GEMM reads its token rows straight from the unpermuted matrix
+// (gather inside the GEMM) instead of from a permuted copy.  The CUDA-core
+// engine always can; the tcgen05 engine for column tiles up to 64.
+static bool gemm_gathers(const sb_grouped_gemm_args& a, int engine) {
+  if (engine == SB_ENGINE_SIMT) return true;
+  const bool tc = tcgen05_supported(a);
+  if (!tc) return engine == SB_ENGINE_AUTO;  // AUTO falls back to the CUDA-core engine
+  return tc_tile_n(a) <= 64;
+}
+
 // K-split factor for a LINEAR GEMM: spread small grids over the SMs.
-static int pick_splits(int m_rows, int k, int rows_hint, int groups, int max_splits, bool tc) {
+static int pick_splits(int m_rows, int k, int rows_hint, int groups, int max_splits, bool tc, int bound) {
   const int m_tiles = (m_rows + 127) / 128;
   const int per_group = (rows_hint + groups - 1) / (groups > 0 ? groups : 1);
-  const int bn = per_group <= 16 ? 16 : per_group <= 32 ? 32 : per_group <= 64 ? 64 : per_group <= 128 ? 128 : 256;
-  int tiles = m_tiles * (rows_hint / bn + (groups < rows_hint ? groups : rows_hint));
+  const bool fixed = bound > 0 && bound <= 64;
+  const int bn = fixed ? 64 : per_group <= 16 ? 16 : per_group <= 32 ? 32 : per_group <= 64 ? 64 : per_group <= 128 ? 128 : 256;
+  int tiles = fixed ? m_tiles * (groups < rows_hint ? groups : rows_hint)
+                    : m_tiles * (rows_hint / bn + (groups < rows_hint ? groups : rows_hint));
   if (tiles < 1) tiles = 1;
   // Small column tiles run two CTAs per SM: aim for about two CTAs per SM.
   const int target = (bn <= 64 ? 2 : 1) * current_sm_count();
@@ -330,10 +344,9 @@ extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block
     // 1. router
     { StageScope sc_(0, st); SB_TRY(sb_router(cur, d.act_dtype, N, H, w->router_w, w->loop_bias + static_cast<int64_t>(l) * E, E, K,
                      b.top_idx, b.top_w, nullptr, st)); }
-    // 2-3. rows grouped by selected source; gather h
+    // 2-3. rows grouped by selected source; gather h (inside the GEMM when it can)
     { StageScope sc_(1, st); SB_TRY(sb_group(b.top_idx, nullptr, N, K, E, 0, b.src_off, b.src_row, b.src_slot, b.src_w, b.src_inv,
                     b.group_ws, b.group_ws_bytes, st)); }
-    { StageScope sc_(2, st); SB_TRY(sb_gather_rows(cur, d.act_dtype, H, b.src_row, b.src_off, E, N * K, b.x_src, st)); }
     // 4. edge logits of the selected sources: rows [s*E, s*E+E) of the generator
     {
       sb_grouped_gemm_args a;
@@ -342,16 +355,21 @@ extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block
       a.num_groups = E; a.m_rows = E; a.k = H; a.a_group_rows = E; a.lda = H;
       a.a_rows_total = static_cast<int64_t>(E) * E; a.a = w->gen_w;
       a.bias = w->gen_bias + static_cast<int64_t>(l) * E * E; a.bias_group_stride = E;
-      a.x = b.x_src; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K; a.offsets = b.src_off;
+      a.x = b.x_src; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N; a.offsets = b.src_off;
       a.out = b.elog; a.ldo = E; a.splits = 1; a.status = b.status;
+      if (gemm_gathers(a, d.engine)) {
+        a.x = cur; a.x_row_index = b.src_row; a.x_rows = N;
+      } else {
+        StageScope sc_(2, st);
+        SB_TRY(sb_gather_rows(cur, d.act_dtype, H, b.src_row, b.src_off, E, N * K, b.x_src, st));
+      }
       { StageScope sc_(3, st); SB_TRY(run_gemm(a, d.engine, st)); }
     }
     // 5. top-M destinations per (token, source)
     { StageScope sc_(4, st); SB_TRY(sb_edge_topm(b.elog, E, E, M, b.src_slot, b.src_off, E, N * K, b.edge_idx, b.edge_w, st)); }
-    // 6-7. (token, destination) pairs with summed coefficients; gather h
+    // 6-7. (token, destination) pairs with summed coefficients
     { StageScope sc_(5, st); SB_TRY(sb_group(b.edge_idx, b.edge_w, N, KM, E, 0, b.dst_off, b.dst_row, b.dst_slot, b.dst_w, b.dst_inv,
                     b.group_ws, b.group_ws_bytes, st)); }
-    { StageScope sc_(6, st); SB_TRY(sb_gather_rows(cur, d.act_dtype, H, b.dst_row, b.dst_off, E, static_cast<int>(cap_dst), b.x_dst, st)); }
     // 8. c[t,d] * W_edge[d] h[t]
     int msg_splits = 1;
     {
@@ -361,26 +379,37 @@ extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block
       a.num_groups = E; a.m_rows = H; a.k = H; a.a_group_rows = H; a.lda = H;
       a.a_rows_total = static_cast<int64_t>(E) * H; a.a = w->edge_w;
       a.x = b.x_dst; a.ldx = H; a.max_rows = static_cast<int>(cap_dst);
-      a.rows_hint = static_cast<int>(cap_dst * 7 / 8); a.offsets = b.dst_off; a.row_scale = b.dst_w;
-      msg_splits = pick_splits(H, H, a.rows_hint, E, max_splits_for(N), tc_pref);
+      a.rows_hint = static_cast<int>(cap_dst * 7 / 8); a.group_rows_bound = N; a.offsets = b.dst_off; a.row_scale = b.dst_w;
+      msg_splits = pick_splits(H, H, a.rows_hint, E, max_splits_for(N), tc_pref, N);
       a.splits = msg_splits; a.split_stride = cap_dst * H;
       a.out = b.y_msg; a.ldo = H; a.status = b.status;
+      if (gemm_gathers(a, d.engine)) {
+        a.x = cur; a.x_row_index = b.dst_row; a.x_rows = N;
+      } else {
+        StageScope sc_(6, st);
+        SB_TRY(sb_gather_rows(cur, d.act_dtype, H, b.dst_row, b.dst_off, E, static_cast<int>(cap_dst), b.x_dst, st));
+      }
       { StageScope sc_(7, st); SB_TRY(run_gemm(a, d.engine, st)); }
     }
     // 9. dispatch plan of the expert FFN
     { StageScope sc_(8, st); SB_TRY(sb_group(b.top_idx, b.top_w, N, K, E, SB_GROUP_POSITIVE_ONLY, b.ffn_off, b.ffn_row, b.ffn_slot,
                     b.ffn_w, b.ffn_inv, b.group_ws, b.group_ws_bytes, st)); }
-    // 10. messages (sum over the token's destinations), scattered into expert order
-    { StageScope sc_(9, st); SB_TRY(sb_combine_rows(b.y_msg, H, msg_splits, cap_dst * H, b.dst_inv, KM, N, H,
-                           (taps && taps->messages) ? b.msg_f32 : nullptr, b.ffn_inv, K, b.x_ffn, d.act_dtype,
-                           st)); }
-    // 11. up projection + activation
+    // 10-11. messages (sum over the token's destinations), then up projection +
+    // activation with the message rows gathered in expert order.
     {
       sb_grouped_gemm_args a;
       fill_expert_gemm(a, d, true, w->w_up, w->s_up, w->b_up, w->w_gate, w->s_gate, w->b_gate);
       a.epilogue = d.activation == SB_ACT_SWIGLU ? SB_EPI_SWIGLU : SB_EPI_GELU;
-      a.num_groups = E; a.x = b.x_ffn; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K;
+      a.num_groups = E; a.x = b.x_ffn; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N;
       a.offsets = b.ffn_off; a.out = b.act; a.ldo = U; a.splits = 1; a.status = b.status;
+      const bool gather = gemm_gathers(a, d.engine);
+      float* msg_out = (taps && taps->messages) ? b.msg_f32 : nullptr;
+      { StageScope sc_(9, st); SB_TRY(sb_combine_rows(b.y_msg, H, msg_splits, cap_dst * H, b.dst_inv, KM, N, H, msg_out,
+                                                  gather ? nullptr : b.ffn_inv, K, gather ? b.msg_act : b.x_ffn,
+                                                  d.act_dtype, st)); }
+      if (gather) {
+        a.x = b.msg_act; a.x_row_index = b.ffn_row; a.x_rows = N;
+      }
       { StageScope sc_(10, st); SB_TRY(run_gemm(a, d.engine, st)); }
     }
     // 12. down projection, scaled by the routing weight
@@ -389,9 +418,9 @@ extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block
       sb_grouped_gemm_args a;
       fill_expert_gemm(a, d, false, w->w_down, w->s_down, w->b_down, nullptr, nullptr, nullptr);
       a.epilogue = SB_EPI_LINEAR;
-      a.num_groups = E; a.x = b.act; a.ldx = U; a.max_rows = N * K; a.rows_hint = N * K;
+      a.num_groups = E; a.x = b.act; a.ldx = U; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N;
       a.offsets = b.ffn_off; a.row_scale = b.ffn_w;
-      ffn_splits = pick_splits(H, U, N * K, E, max_splits_for(N), tc_pref);
+      ffn_splits = pick_splits(H, U, N * K, E, max_splits_for(N), tc_pref, N);
       a.splits = ffn_splits; a.split_stride = static_cast<int64_t>(N) * K * H;
       a.out = b.y_ffn; a.ldo = H; a.status = b.status;
       { StageScope sc_(11, st); SB_TRY(run_gemm(a, d.engine, st)); }
@@ -472,14 +501,18 @@ extern "C" SB_API int sb_expert_delta(const sb_block_dims* dims, const sb_block_
 #define SB_TRY(x) do { rc = (x); if (rc) return rc; } while (0)
   SB_TRY(sb_group(b.top_idx, top_w, N, K, G, SB_GROUP_POSITIVE_ONLY, b.ffn_off, b.ffn_row, b.ffn_slot, b.ffn_w,
                   b.ffn_inv, b.group_ws, b.group_ws_bytes, st));
-  SB_TRY(sb_gather_rows(messages, d.act_dtype, H, b.ffn_row, b.ffn_off, G, N * K, b.x_ffn, st));
   {
     sb_grouped_gemm_args a;
     fill_expert_gemm(a, d, true, w->w_up, w->s_up, w->b_up, w->w_gate, w->s_gate, w->b_gate);
     shard_expert_gemm(a, d, rank, world);
     a.epilogue = d.activation == SB_ACT_SWIGLU ? SB_EPI_SWIGLU : SB_EPI_GELU;
-    a.num_groups = G; a.x = b.x_ffn; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K;
+    a.num_groups = G; a.x = b.x_ffn; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N;
     a.offsets = b.ffn_off; a.out = b.act; a.ldo = U; a.splits = 1; a.status = b.status;
+    if (gemm_gathers(a, d.engine)) {
+      a.x = messages; a.x_row_index = b.ffn_row; a.x_rows = N;
+    } else {
+      SB_TRY(sb_gather_rows(messages, d.act_dtype, H, b.ffn_row, b.ffn_off, G, N * K, b.x_ffn, st));
+    }
     SB_TRY(run_gemm(a, d.engine, st));
   }
   int splits = 1;
@@ -488,9 +521,9 @@ extern "C" SB_API int sb_expert_delta(const sb_block_dims* dims, const sb_block_
     fill_expert_gemm(a, d, false, w->w_down, w->s_down, w->b_down, nullptr, nullptr, nullptr);
     shard_expert_gemm(a, d, rank, world);
     a.epilogue = SB_EPI_LINEAR;
-    a.num_groups = G; a.x = b.act; a.ldx = U; a.max_rows = N * K; a.rows_hint = N * K;
+    a.num_groups = G; a.x = b.act; a.ldx = U; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N;
     a.offsets = b.ffn_off; a.row_scale = b.ffn_w;
-    splits = pick_splits(H, U, N * K, G, 4, d.engine != SB_ENGINE_SIMT);
+    splits = pick_splits(H, U, N * K, G, 4, d.engine != SB_ENGINE_SIMT, N);
     a.splits = splits; a.split_stride = static_cast<int64_t>(N) * K * H;
     a.out = b.y_ffn; a.ldo = H; a.status = b.status;
     SB_TRY(run_gemm(a, d.engine, st));

@@ -68,6 +68,8 @@ combine_rows_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_
         if (q < 0) continue;
         Vec4<T>::store(scatter_out + static_cast<int64_t>(q) * cols + c, acc);
       }
+    } else if (scatter_out) {
+      Vec4<T>::store(scatter_out + static_cast<int64_t>(t) * cols + c, acc);
     }
   }
 }
@@ -182,7 +184,8 @@ extern "C" SB_API int sb_combine_rows(const float* y, int64_t ldy, int splits, i
                                       void* scatter_out, int act_dtype, void* stream) {
   if (n_tokens < 0 || cols <= 0 || cols % 4 || slots <= 0 || slots > kMaxSlots || splits <= 0 ||
       ldy < cols || (ldy % 4) || (split_stride % 4) || (scatter_inv && (scatter_slots <= 0 ||
-      scatter_slots > kMaxSlots || !scatter_out)) || (n_tokens > 0 && (!y || !inv)))
+      scatter_slots > kMaxSlots || !scatter_out)) || (n_tokens > 0 && (!y || !inv)) ||
+      (scatter_out && act_dtype != SB_F32 && act_dtype != SB_BF16))
     return SB_ERR_ARG;
   if (n_tokens == 0) return SB_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -90,6 +90,10 @@ SB_DEVINL void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
 }
+// Raise the expected transaction bytes of the current phase without arriving.
+SB_DEVINL void mbar_add_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
 SB_DEVINL void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -205,6 +209,17 @@ SB_DEVINL uint64_t smem_desc_k_sw128(uint32_t smem_addr) {
   d |= static_cast<uint64_t>(1) << 46;                      // descriptor version (sm_100)
   d |= static_cast<uint64_t>(2) << 61;                      // swizzle: 128 B
   return d;
+}
+
+// Four rows (row0..row3) x one box of columns starting at c0 gathered into
+// this CTA's shared memory (2-D tensor map with a one-row box).
+SB_DEVINL void tma_gather4(void* smem_dst, const void* desc, uint64_t* bar, int c0, int r0, int r1, int r2,
+                           int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(smem_u32(bar)), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+      : "memory");
 }
 
 // Instruction descriptor: bf16 x bf16 -> fp32, both K-major, M x N tile.

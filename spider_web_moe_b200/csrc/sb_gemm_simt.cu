@@ -80,7 +80,8 @@ simt_gemm_kernel(const sb_grouped_gemm_args p) {
       const int r = n0 + nn;
       float v = 0.f;
       if (r < n_end && (k0 + kk) < ke) {
-        const int64_t off = static_cast<int64_t>(r) * p.ldx + k0 + kk;
+        const int64_t src_row = p.x_row_index ? p.x_row_index[r] : r;
+        const int64_t off = src_row * p.ldx + k0 + kk;
         v = p.act_dtype == SB_F32 ? static_cast<const float*>(p.x)[off]
                                   : __bfloat162float(static_cast<const __nv_bfloat16*>(p.x)[off]);
       }

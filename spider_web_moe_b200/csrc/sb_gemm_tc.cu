@@ -54,7 +54,7 @@ struct TcCfg {
   static constexpr int kOffRaw = kOffB + kStages * kBBytes;
   static constexpr int kOffRawG = kOffRaw + kStages * kRawBytes;
   static constexpr int kOffBar = kOffRawG + (kGate ? kStages * kRawBytes : 0);
-  static constexpr int kOffMisc = kOffBar + (3 * kStages + 1) * 8;
+  static constexpr int kOffMisc = kOffBar + (3 * kStages + 2) * 8;
   static constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
   static_assert(kTmemCols <= 512, "TMEM holds 512 columns");
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "M=128 MMA needs N in [16, 256], N % 16 == 0");
@@ -118,30 +118,47 @@ SB_DEVINL void convert_tile(const uint8_t* raw, uint8_t* dst, const sb_grouped_g
   }
 }
 
-template <int BN, int WFMT, int EPI>
+// Modes.  kFixed (decode-size column tiles): CTA (m-tile, group) covers every
+// row tile of its group, and its first weight tiles are requested before the
+// dependency wait -- the weights do not depend on the preceding kernel, so
+// they stream in while that kernel finishes.  kGather: the token rows are
+// fetched with tile::gather4 straight from the unpermuted activation matrix
+// (no permuted copy in HBM): each gather writes four whole 128-byte rows
+// (512 bytes, 512-byte aligned) into the same 128-byte swizzled layout a tiled
+// load produces.  Otherwise (large tiles) a CTA takes one (group, row tile)
+// slot of the upper-bound grid and B is one tiled TMA load.
+template <int BN, int WFMT, int EPI, bool kFixed, bool kGather>
 __global__ void __launch_bounds__(kTcThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmG,
                const __grid_constant__ CUtensorMap tmB, const sb_grouped_gemm_args p) {
   using C = TcCfg<BN, WFMT, EPI>;
   constexpr int S = C::kStages;
+  static_assert(!kGather || BN <= 64, "gathers are issued by the lanes of one warp (BN/4 <= 32)");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
   uint64_t* empty = full + S;
   uint64_t* conv = empty + S;
-  uint64_t* done = conv + S;
+  uint64_t* acc_full = conv + S;
+  uint64_t* acc_empty = acc_full + 1;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
   int* s_sched = reinterpret_cast<int*>(smem + C::kOffMisc + 16);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // Set-up that reads no predecessor output runs before the dependency wait.
+  const int m0 = blockIdx.x * kTcBM;
+  const int ks = p.k / p.splits;
+  const int kb = blockIdx.z * ks;
+  const int nk = ks / kTcBK;
+
+  // ---- set-up that reads no predecessor output (runs before the dependency wait)
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
       mbar_init(&conv[s], 128);
     }
-    mbar_init(done, 1);
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 128);
     fence_barrier_init();
   }
   if (warp == 4 && lane == 0) {
@@ -149,25 +166,61 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tma_prefetch_desc(&tmB);
     if (C::kGate) tma_prefetch_desc(&tmG);
   }
+  __syncthreads();
+  int pre = 0;  // weight tiles requested before the wait (kFixed)
+  constexpr uint32_t kTxA = (C::kConvert ? C::kRawBytes : C::kABytes) * (C::kGate ? 2 : 1);
+  if (kFixed && warp == 4 && lane == 0) {
+    const int64_t arow = static_cast<int64_t>(blockIdx.y) * p.a_group_rows + m0;
+    pre = nk < S ? nk : S;
+    for (int it = 0; it < pre; ++it) {
+      mbar_add_tx(&full[it], kTxA);  // the stage's arrival (with its B bytes) comes after the wait
+      const int k0 = kb + it * kTcBK;
+      const int acol = WFMT == SB_W_INT4 ? k0 / 2 : k0;
+      uint8_t* adst = C::kConvert ? smem + C::kOffRaw + it * C::kRawBytes : smem + C::kOffA + it * C::kABytes;
+      tma_load_2d(adst, &tmA, &full[it], acol, static_cast<int>(arow));
+      if (C::kGate) {
+        uint8_t* gdst = C::kConvert ? smem + C::kOffRawG + it * C::kRawBytes : smem + C::kOffG + it * C::kABytes;
+        tma_load_2d(gdst, &tmG, &full[it], acol, static_cast<int>(arow));
+      }
+    }
+  }
   pdl_wait();
   pdl_trigger();
-  if (warp == 0) {
+
+  // ---- schedule
+  if (kFixed) {
+    if (tid == 0) {
+      const int g = blockIdx.y;
+      s_sched[0] = g;
+      s_sched[1] = p.offsets[g];
+      s_sched[2] = min(p.offsets[g + 1], p.max_rows);
+    }
+  } else if (warp == 0) {
     int g, n0, n_end;
     const bool ok = schedule_tile(p.offsets, p.num_groups, BN, blockIdx.y, g, n0, n_end);
     if (lane == 0) {
       s_sched[0] = ok ? g : -1;
       s_sched[1] = n0;
-      s_sched[2] = min(n_end, p.max_rows);
+      s_sched[2] = min(min(n_end, p.max_rows), n0 + BN);
     }
   }
   __syncthreads();
   const int g = s_sched[0];
-  if (g < 0) return;  // surplus CTA of the upper-bound grid
   const int n0 = s_sched[1], n_end = s_sched[2];
-  const int m0 = blockIdx.x * kTcBM;
-  const int ks = p.k / p.splits;
-  const int kb = blockIdx.z * ks;
-  const int nk = ks / kTcBK;
+  if (!kFixed && g < 0) return;  // surplus slot of the upper-bound grid
+  const int rows = n_end - n0;
+  if (kFixed && rows <= 0) {
+    // A group without rows: arrive on the stages whose weights were requested
+    // and let those copies land before exiting.
+    if (warp == 4 && lane == 0) {
+      for (int it = 0; it < pre; ++it) mbar_arrive(&full[it]);
+      for (int it = 0; it < pre; ++it)
+        if (!mbar_wait(&full[it], 0, p.status, SB_DEVERR_DRAIN)) break;
+    }
+    return;
+  }
+  const int ntile = kFixed ? (rows + BN - 1) / BN : 1;
+  const int total_it = ntile * nk;
   const int64_t arow0 = static_cast<int64_t>(g) * p.a_group_rows + m0;
 
   if (warp == 5) {
@@ -181,95 +234,140 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
   if (warp == 4) {
     // ---------------------------------------------------------------- producer
-    if (lane == 0) {
-      constexpr uint32_t kTx = (C::kConvert ? C::kRawBytes : C::kABytes) * (C::kGate ? 2 : 1) + C::kBBytes;
-      int issued = 0;
-      for (int it = 0; it < nk; ++it) {
-        const int s = it % S;
-        const uint32_t ph = (it / S) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, p.status, SB_DEVERR_MMA_WAIT)) break;
-        mbar_expect_tx(&full[s], kTx);
-        const int k0 = kb + it * kTcBK;
-        const int acol = WFMT == SB_W_INT4 ? k0 / 2 : k0;
-        uint8_t* adst = C::kConvert ? smem + C::kOffRaw + s * C::kRawBytes : smem + C::kOffA + s * C::kABytes;
-        tma_load_2d(adst, &tmA, &full[s], acol, static_cast<int>(arow0));
-        if (C::kGate) {
-          uint8_t* gdst = C::kConvert ? smem + C::kOffRawG + s * C::kRawBytes : smem + C::kOffG + s * C::kABytes;
-          tma_load_2d(gdst, &tmG, &full[s], acol, static_cast<int>(arow0));
-        }
-        tma_load_2d(smem + C::kOffB + s * C::kBBytes, &tmB, &full[s], k0, n0);
-        ++issued;
+    int issued = 0;
+    int rix[4] = {0, 0, 0, 0};  // kGather: the four token rows this lane gathers (lanes < BN/4)
+    for (int it = 0; it < total_it; ++it) {
+      const int t = it / nk, kk = it - t * nk;
+      const int s = it % S;
+      const uint32_t ph = (it / S) & 1;
+      const int k0 = kb + kk * kTcBK;
+      const int nrow = n0 + t * BN;
+      // Only the tile's valid rows are fetched: 4-row gathers, or 16-row tiled
+      // boxes on the fixed-group schedule; the rest of the tile is never read.
+      const int tval = min(BN, n_end - nrow);
+      const int nb = kGather ? (tval + 3) / 4 : (kFixed ? (tval + 15) / 16 : 1);
+      const uint32_t tx_b = kGather ? nb * 512u : (kFixed ? nb * 2048u : static_cast<uint32_t>(C::kBBytes));
+      if (kGather && kk == 0 && lane < nb) {
+        // token rows of this tile; rows past the group's end repeat its last row (discarded)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) rix[r] = p.x_row_index[min(nrow + 4 * lane + r, n_end - 1)];
       }
-      // Drain: every issued copy must have landed before the CTA may exit.
+      bool ok = true;
+      if (lane == 0) {
+        if (kFixed && it < pre) {
+          mbar_expect_tx(&full[s], tx_b);  // weights already requested before the wait
+        } else {
+          ok = mbar_wait(&empty[s], ph ^ 1, p.status, SB_DEVERR_MMA_WAIT);
+          if (ok) {
+            mbar_expect_tx(&full[s], kTxA + tx_b);
+            const int acol = WFMT == SB_W_INT4 ? k0 / 2 : k0;
+            uint8_t* adst = C::kConvert ? smem + C::kOffRaw + s * C::kRawBytes : smem + C::kOffA + s * C::kABytes;
+            tma_load_2d(adst, &tmA, &full[s], acol, static_cast<int>(arow0));
+            if (C::kGate) {
+              uint8_t* gdst = C::kConvert ? smem + C::kOffRawG + s * C::kRawBytes : smem + C::kOffG + s * C::kABytes;
+              tma_load_2d(gdst, &tmG, &full[s], acol, static_cast<int>(arow0));
+            }
+          }
+        }
+        if (ok && !kGather) {
+          if (kFixed)
+            for (int j = 0; j < nb; ++j)
+              tma_load_2d(smem + C::kOffB + s * C::kBBytes + j * 2048, &tmB, &full[s], k0, nrow + 16 * j);
+          else
+            tma_load_2d(smem + C::kOffB + s * C::kBBytes, &tmB, &full[s], k0, nrow);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      if (kGather) {
+        __syncwarp();
+        if (lane < nb)
+          tma_gather4(smem + C::kOffB + s * C::kBBytes + lane * 512, &tmB, &full[s], k0, rix[0], rix[1], rix[2], rix[3]);
+      }
+      ++issued;
+    }
+    // Drain: every issued copy must have landed before the CTA may exit.
+    if (lane == 0)
       for (int it = issued - S > 0 ? issued - S : 0; it < issued; ++it)
         if (!mbar_wait(&full[it % S], (it / S) & 1, p.status, SB_DEVERR_DRAIN)) break;
-    }
+    __syncwarp();
   } else if (warp == 5) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(kTcBM, BN);
-      for (int it = 0; it < nk; ++it) {
-        const int s = it % S;
-        const uint32_t ph = (it / S) & 1;
-        const bool ok = C::kConvert ? mbar_wait(&conv[s], ph, p.status, SB_DEVERR_CONV_WAIT)
-                                    : mbar_wait(&full[s], ph, p.status, SB_DEVERR_TMA_WAIT);
-        if (!ok) break;
+      bool ok = true;
+      for (int t = 0; t < ntile && ok; ++t) {
+        if (t > 0) ok = mbar_wait(acc_empty, (t - 1) & 1, p.status, SB_DEVERR_EPI_WAIT);
         tc_fence_after();
-        const uint32_t a_base = smem_u32(smem + C::kOffA + s * C::kABytes);
-        const uint32_t g_base = smem_u32(smem + C::kOffG + s * C::kABytes);
-        const uint32_t b_base = smem_u32(smem + C::kOffB + s * C::kBBytes);
+        for (int kk = 0; kk < nk && ok; ++kk) {
+          const int it = t * nk + kk;
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          ok = C::kConvert ? mbar_wait(&conv[s], ph, p.status, SB_DEVERR_CONV_WAIT)
+                           : mbar_wait(&full[s], ph, p.status, SB_DEVERR_TMA_WAIT);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + C::kOffA + s * C::kABytes);
+          const uint32_t g_base = smem_u32(smem + C::kOffG + s * C::kABytes);
+          const uint32_t b_base = smem_u32(smem + C::kOffB + s * C::kBBytes);
 #pragma unroll
-        for (int kk = 0; kk < kTcBK / 16; ++kk) {
-          const uint64_t bdesc = smem_desc_k_sw128(b_base + kk * 32);
-          const uint32_t accum = (it > 0 || kk > 0) ? 1u : 0u;
-          tc_mma_bf16(tmem, smem_desc_k_sw128(a_base + kk * 32), bdesc, idesc, accum);
-          if (C::kGate) tc_mma_bf16(tmem + BN, smem_desc_k_sw128(g_base + kk * 32), bdesc, idesc, accum);
+          for (int j = 0; j < kTcBK / 16; ++j) {
+            const uint64_t bdesc = smem_desc_k_sw128(b_base + j * 32);
+            const uint32_t accum = (kk > 0 || j > 0) ? 1u : 0u;
+            tc_mma_bf16(tmem, smem_desc_k_sw128(a_base + j * 32), bdesc, idesc, accum);
+            if (C::kGate) tc_mma_bf16(tmem + BN, smem_desc_k_sw128(g_base + j * 32), bdesc, idesc, accum);
+          }
+          tc_commit(&empty[s]);
         }
-        tc_commit(&empty[s]);
+        tc_commit(acc_full);
       }
-      tc_commit(done);
     }
     __syncwarp();
   } else {
     // ---------------------------------------------------------------- dequant + epilogue
-    if (C::kConvert) {
-      for (int it = 0; it < nk; ++it) {
-        const int s = it % S;
-        const uint32_t ph = (it / S) & 1;
-        if (!mbar_wait(&full[s], ph, p.status, SB_DEVERR_TMA_WAIT)) break;
-        const int k0 = kb + it * kTcBK;
-        convert_tile<WFMT>(smem + C::kOffRaw + s * C::kRawBytes, smem + C::kOffA + s * C::kABytes, p,
-                           p.a_scale, arow0, k0, tid);
-        if (C::kGate)
-          convert_tile<WFMT>(smem + C::kOffRawG + s * C::kRawBytes, smem + C::kOffG + s * C::kABytes, p,
-                             p.a_gate_scale, arow0, k0, tid);
-        fence_proxy_async_smem();
-        mbar_arrive(&conv[s]);
+    const int mloc = warp * 32 + lane;
+    const int m = m0 + mloc;
+    const int64_t arow = arow0 + mloc;
+    const bool mvalid = m < p.m_rows && arow < p.a_rows_total;
+    const float sa = (WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_scale)[arow] : 1.f;
+    const float sg = (C::kGate && WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_gate_scale)[arow] : 1.f;
+    const float bias = (p.bias && mvalid && blockIdx.z == 0) ? p.bias[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
+    const float bgate = (C::kGate && p.bias_gate && mvalid) ? p.bias_gate[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    bool live = true;
+    for (int t = 0; t < ntile && live; ++t) {
+      if (C::kConvert) {
+        for (int kk = 0; kk < nk; ++kk) {
+          const int it = t * nk + kk;
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait(&full[s], ph, p.status, SB_DEVERR_TMA_WAIT)) { live = false; break; }
+          const int k0 = kb + kk * kTcBK;
+          convert_tile<WFMT>(smem + C::kOffRaw + s * C::kRawBytes, smem + C::kOffA + s * C::kABytes, p,
+                             p.a_scale, arow0, k0, tid);
+          if (C::kGate)
+            convert_tile<WFMT>(smem + C::kOffRawG + s * C::kRawBytes, smem + C::kOffG + s * C::kABytes, p,
+                               p.a_gate_scale, arow0, k0, tid);
+          fence_proxy_async_smem();
+          mbar_arrive(&conv[s]);
+        }
       }
-    }
-    // tcgen05.ld is warp-collective: every lane must take the same branch.
-    const bool acc_ready = __all_sync(0xffffffffu, mbar_wait(done, 0, p.status, SB_DEVERR_EPI_WAIT));
-    tc_fence_after();
-    if (acc_ready) {
-      const int mloc = warp * 32 + lane;
-      const int m = m0 + mloc;
-      const int64_t arow = arow0 + mloc;
-      const bool mvalid = m < p.m_rows && arow < p.a_rows_total;
-      const float sa = (WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_scale)[arow] : 1.f;
-      const float sg = (C::kGate && WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_gate_scale)[arow] : 1.f;
-      const float bias = (p.bias && mvalid && blockIdx.z == 0) ? p.bias[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
-      const float bgate = (C::kGate && p.bias_gate && mvalid) ? p.bias_gate[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
-      const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+      // tcgen05.ld is warp-collective: every lane must take the same branch.
+      live = __all_sync(0xffffffffu, live && mbar_wait(acc_full, t & 1, p.status, SB_DEVERR_EPI_WAIT));
+      tc_fence_after();
+      if (!live) break;
+      const int tn0 = n0 + t * BN;
+      const int tend = min(tn0 + BN, n_end);
       for (int c0 = 0; c0 < BN; c0 += 16) {
-        if (n0 + c0 >= n_end) break;
+        if (tn0 + c0 >= tend) break;
         float v[16], vg[16];
         tmem_ld16(lane_addr + c0, v);
         if (C::kGate) tmem_ld16(lane_addr + BN + c0, vg);
         if (!mvalid) continue;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int r = n0 + c0 + j;
-          if (r >= n_end) break;
+          const int r = tn0 + c0 + j;
+          if (r >= tend) break;
           const float x = v[j] * sa + bias;
           if (EPI == SB_EPI_LINEAR) {
             const float rs = p.row_scale ? p.row_scale[r] : 1.f;
@@ -282,6 +380,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           }
         }
       }
+      tc_fence_before();
+      mbar_arrive(acc_empty);
     }
   }
   tc_fence_before();
@@ -344,13 +444,14 @@ bool tcgen05_supported(const sb_grouped_gemm_args& a) {
   if (reinterpret_cast<uintptr_t>(a.a) % 16 || reinterpret_cast<uintptr_t>(a.x) % 16) return false;
   if (a.epilogue == SB_EPI_SWIGLU && (!a.a_gate || reinterpret_cast<uintptr_t>(a.a_gate) % 16)) return false;
   if (a.a_rows_total > 0x7fffffffLL || a.max_rows <= 0) return false;
+  if (a.x_row_index && (tc_tile_n(a) > 64 || a.x_rows <= 0)) return false;
   return current_cc_major() == 10;
 }
 
-template <int BN, int WFMT, int EPI>
+template <int BN, int WFMT, int EPI, bool kFixed, bool kGather>
 static int launch_tc(const sb_grouped_gemm_args& a, cudaStream_t st) {
   using C = TcCfg<BN, WFMT, EPI>;
-  auto kern = tc_gemm_kernel<BN, WFMT, EPI>;
+  auto kern = tc_gemm_kernel<BN, WFMT, EPI, kFixed, kGather>;
   static int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -365,21 +466,36 @@ static int launch_tc(const sb_grouped_gemm_args& a, cudaStream_t st) {
   if (!weight_map(&ma, a, a.a)) return SB_ERR_UNSUPPORTED;
   mg = ma;
   if (C::kGate && !weight_map(&mg, a, a.a_gate)) return SB_ERR_UNSUPPORTED;
-  if (!make_map(&mb, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.k, a.max_rows, a.ldx * 2, kTcBK, BN,
-                CU_TENSOR_MAP_SWIZZLE_128B))
-    return SB_ERR_UNSUPPORTED;
-  const dim3 grid((a.m_rows + kTcBM - 1) / kTcBM, (a.max_rows + BN - 1) / BN + a.num_groups, a.splits);
+  bool ok_b;
+  if (kGather)  // source rows: a one-row box of 64 elements (128 bytes), 128-byte swizzle
+    ok_b = make_map(&mb, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.k, a.x_rows, a.ldx * 2, kTcBK, 1,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  else  // fixed-group schedule: 16-row boxes, only as many as the tile's valid rows need
+    ok_b = make_map(&mb, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.k, a.max_rows, a.ldx * 2, kTcBK,
+                    kFixed ? 16 : BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!ok_b) return SB_ERR_UNSUPPORTED;
+  const int m_tiles = (a.m_rows + kTcBM - 1) / kTcBM;
+  const dim3 grid(m_tiles, kFixed ? a.num_groups : (a.max_rows + BN - 1) / BN + a.num_groups, a.splits);
   return launch(kern, grid, dim3(kTcThreads), C::kSmemBytes, st, ma, mg, mb, a);
+}
+
+template <int BN, int WFMT, int EPI>
+static int launch_modes(const sb_grouped_gemm_args& a, cudaStream_t st) {
+  const bool g = a.x_row_index != nullptr;
+  if (tc_fixed_groups(a))
+    return g ? launch_tc<BN, WFMT, EPI, true, true>(a, st) : launch_tc<BN, WFMT, EPI, true, false>(a, st);
+  return g ? launch_tc<BN, WFMT, EPI, false, true>(a, st) : launch_tc<BN, WFMT, EPI, false, false>(a, st);
 }
 
 template <int WFMT, int EPI>
 static int launch_bn(const sb_grouped_gemm_args& a, cudaStream_t st, int bn) {
+  const bool g = a.x_row_index != nullptr;
   switch (bn) {
-    case 16: return launch_tc<16, WFMT, EPI>(a, st);
-    case 32: return launch_tc<32, WFMT, EPI>(a, st);
-    case 64: return launch_tc<64, WFMT, EPI>(a, st);
-    case 128: return launch_tc<128, WFMT, EPI>(a, st);
-    default: return launch_tc<256, WFMT, EPI>(a, st);
+    case 16: return launch_modes<16, WFMT, EPI>(a, st);
+    case 32: return launch_modes<32, WFMT, EPI>(a, st);
+    case 64: return launch_modes<64, WFMT, EPI>(a, st);
+    case 128: return g ? SB_ERR_UNSUPPORTED : launch_tc<128, WFMT, EPI, false, false>(a, st);
+    default: return g ? SB_ERR_UNSUPPORTED : launch_tc<256, WFMT, EPI, false, false>(a, st);
   }
 }
 
@@ -392,8 +508,16 @@ static int launch_epi(const sb_grouped_gemm_args& a, cudaStream_t st, int bn) {
   }
 }
 
-// Column tile: the smallest of 16..256 that covers the expected rows per group.
-static int choose_bn(const sb_grouped_gemm_args& a) {
+// Fixed-group schedule when one tile of <= 64 columns is known to hold every
+// group's rows: each CTA then streams its weights exactly once.
+bool tc_fixed_groups(const sb_grouped_gemm_args& a) {
+  return a.group_rows_bound > 0 && a.group_rows_bound <= 64;
+}
+
+// Column tile: the bound rounded up to 16 on the fixed-group schedule,
+// otherwise the smallest of 16..256 that covers the expected rows per group.
+int tc_tile_n(const sb_grouped_gemm_args& a) {
+  if (tc_fixed_groups(a)) return a.group_rows_bound <= 16 ? 16 : (a.group_rows_bound <= 32 ? 32 : 64);
   const int hint = a.rows_hint > 0 ? a.rows_hint : a.max_rows;
   const int per_group = (hint + a.num_groups - 1) / a.num_groups;
   if (per_group <= 16) return 16;
@@ -404,7 +528,7 @@ static int choose_bn(const sb_grouped_gemm_args& a) {
 }
 
 int gemm_tcgen05(const sb_grouped_gemm_args& a, cudaStream_t st) {
-  const int bn = choose_bn(a);
+  const int bn = tc_tile_n(a);
   switch (a.wfmt) {
     case SB_W_BF16: return launch_epi<SB_W_BF16>(a, st, bn);
     case SB_W_FP8: return launch_epi<SB_W_FP8>(a, st, bn);

@@ -129,19 +129,33 @@ def test_full_size_config_one_loop(name, tokens, engine, cuda_device):
 
 
 def test_engines_agree_and_are_deterministic(cuda_device):
+    """tcgen05 and CUDA-core engines agree loop by loop (same input to both); each
+    engine is bitwise deterministic across calls (no float atomics anywhere)."""
     cfg, spec, n = full_config("cfg2")
     sd = synth.synthetic_state_dict(cfg, seed=3, device=cuda_device, round_bf16=True)
     h, _ = synth.block_inputs(n, cfg.hidden_size, seed=4, device=cuda_device, dtype=torch.bfloat16)
-    outs = {}
-    for engine in ("tcgen05", "simt"):
-        eng = BlockEngine(cfg, sd, cuda_device, act_dtype=torch.bfloat16, max_tokens=n, engine=engine)
+    h = h.view(n, -1)
+    engs = {e: BlockEngine(cfg, sd, cuda_device, act_dtype=torch.bfloat16, max_tokens=n, engine=e)
+            for e in ("tcgen05", "simt")}
+    for name, eng in engs.items():
         a = eng.forward(h, h).clone()
         b = eng.forward(h, h).clone()
         torch.cuda.synchronize()
         eng.check_status()
-        assert torch.equal(a, b), f"{engine} not deterministic"
-        outs[engine] = a
-    assert rel_err(outs["tcgen05"], outs["simt"]) < 2e-2
+        assert torch.equal(a, b), f"{name} not deterministic"
+    cur = h
+    for l in range(cfg.num_loops):
+        outs, taps = {}, {}
+        for name, eng in engs.items():
+            taps[name] = eng.make_taps(n)
+            outs[name] = eng.forward(cur, h, l, l + 1, taps=taps[name]).clone()
+        same = (taps["tcgen05"]["top_idx"] == taps["simt"]["top_idx"]).all(-1) & \
+               (taps["tcgen05"]["edge_idx"] == taps["simt"]["edge_idx"]).reshape(n, -1).all(-1)
+        # rows whose routing differs can only be near-ties of the fp32 logits
+        assert int((~same).sum()) <= max(1, n // 32), f"loop {l}: {int((~same).sum())} rows route differently"
+        keep = same.cpu()
+        assert rel_err(outs["tcgen05"][same], outs["simt"][same]) < 2e-2
+        cur = outs["tcgen05"]
 
 
 def test_cuda_graph_replay_matches_eager(cuda_device):
