@@ -102,6 +102,22 @@ SB_API int sb_group(const int32_t* idx, const float* w, int n_rows, int slots, i
                     float* perm_w, int32_t* inv, void* workspace, size_t workspace_bytes,
                     void* stream);
 
+/* No reference counterpart: the grouping of sb_group for callers that cannot
+ * allocate device memory (a binding that only forwards pointers it was given,
+ * or code running during stream capture, where cudaMalloc is not allowed).
+ * Same arguments and results as sb_group, without the workspace: its scratch
+ * is a fixed device array of SB_GROUP_NOALLOC_MAX_ENTRIES entries (n_rows *
+ * slots) inside the library, held on every device that loads the library until
+ * the process exits.  Larger inputs return SB_ERR_WORKSPACE.  All calls on a
+ * device share the array (it keeps the last call's contents; nothing in it has
+ * to start at zero), so calls whose kernels can overlap on the GPU race.  The
+ * first call on a device looks up the array's address and should come before
+ * any stream capture.  Nothing is allocated. */
+#define SB_GROUP_NOALLOC_MAX_ENTRIES 65536
+SB_API int sb_group_noalloc(const int32_t* idx, const float* w, int n_rows, int slots, int num_groups,
+                            int flags, int32_t* offsets, int32_t* perm_row, int32_t* perm_slot,
+                            float* perm_w, int32_t* inv, void* stream);
+
 /* dst[p, :] = src[perm_row[p], :] for p < offsets[num_groups] (rows of `cols` elements). */
 SB_API int sb_gather_rows(const void* src, int act_dtype, int cols, const int32_t* perm_row,
                           const int32_t* offsets, int num_groups, int max_rows, void* dst,

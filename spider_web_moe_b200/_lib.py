@@ -83,6 +83,7 @@ SIGNATURES = {
     "sb_router": (i32, [vp, i32, i32, i32, vp, vp, i32, i32, vp, vp, vp, vp]),
     "sb_group_workspace_bytes": (sz, [i32, i32, i32]),
     "sb_group": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, sz, vp]),
+    "sb_group_noalloc": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]),
     "sb_gather_rows": (i32, [vp, i32, i32, vp, vp, i32, i32, vp, vp]),
     "sb_grouped_gemm": (i32, [C.POINTER(GemmArgs), vp]),
     "sb_edge_topm": (i32, [vp, i64, i32, i32, vp, vp, i32, i32, vp, vp, vp]),

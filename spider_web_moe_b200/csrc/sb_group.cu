@@ -149,6 +149,20 @@ extern "C" SB_API int sb_group(const int32_t* idx, const float* w, int n_rows, i
                 slots, num_groups, flags, offsets, perm_row, perm_slot, perm_w, inv, rank_scratch, w_scratch);
 }
 
+namespace sb {
+// Launch of the grouping kernel with caller-chosen scratch arrays (used by the
+// no-allocation entry point, whose scratch is a fixed device array).
+int group_launch_with_scratch(const int32_t* idx, const float* w, int n_rows, int slots, int num_groups, int flags,
+                              int32_t* offsets, int32_t* perm_row, int32_t* perm_slot, float* perm_w, int32_t* inv,
+                              int32_t* rank_scratch, float* w_scratch, cudaStream_t st) {
+  const int64_t total = static_cast<int64_t>(n_rows) * slots;
+  int threads = static_cast<int>(((total + 31) / 32) * 32);
+  threads = threads < 64 ? 64 : (threads > kGroupThreads ? kGroupThreads : threads);
+  return launch(group_kernel, dim3(1), dim3(threads), 0, st, idx, w, n_rows, slots, num_groups, flags, offsets,
+                perm_row, perm_slot, perm_w, inv, rank_scratch, w_scratch);
+}
+}  // namespace sb
+
 extern "C" SB_API int sb_gather_rows(const void* src, int act_dtype, int cols,
                                      const int32_t* perm_row, const int32_t* offsets, int num_groups,
                                      int max_rows, void* dst, void* stream) {

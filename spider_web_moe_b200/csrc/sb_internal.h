@@ -62,6 +62,11 @@ inline int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, 
   return cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
 }
 
+// Grouping kernel launch on caller-chosen scratch (sb_group.cu).
+int group_launch_with_scratch(const int32_t* idx, const float* w, int n_rows, int slots, int num_groups, int flags,
+                              int32_t* offsets, int32_t* perm_row, int32_t* perm_slot, float* perm_w, int32_t* inv,
+                              int32_t* rank_scratch, float* w_scratch, cudaStream_t st);
+
 // Device properties cached per device.
 int current_sm_count();
 int current_cc_major();
