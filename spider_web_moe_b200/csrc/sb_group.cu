@@ -14,6 +14,7 @@ namespace sb {
 
 constexpr int kGroupThreads = 1024;
 constexpr int kGroupMaxG = 256;
+constexpr size_t kGroupSingleCtaMax = 2048;  // entries up to which one CTA groups everything
 
 // Evaluate entry e = row*slots + s: returns its group (or -1) and summed weight.
 SB_DEVINL int entry_group(const int32_t* __restrict__ idx, const float* __restrict__ w, int slots,
@@ -100,6 +101,109 @@ group_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w, int n
   }
 }
 
+// ---------------------------------------------------------------------------
+// Multi-CTA grouping for large entry counts (prefill, many slots).
+//
+// Pass 1 (grid of CTAs, one chunk of kGroupThreads entries each): the same
+// per-warp match ranks and per-group warp scan as group_kernel, giving each
+// entry its rank inside its CTA's chunk and each CTA its per-group counts.
+// The last CTA to finish (ticket counter) scans the counts in (group, CTA)
+// order into per-(CTA, group) base positions and the group offsets.
+// Pass 2 scatters every entry to base + rank.  Positions are therefore the
+// same as the single-CTA kernel's: groups ascending, rows ascending.
+__global__ void __launch_bounds__(kGroupThreads, 1)
+group_rank_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w, int n_rows, int slots, int G,
+                  int flags, int32_t* __restrict__ offsets, int32_t* __restrict__ rank_scratch,
+                  float* __restrict__ w_scratch, int32_t* __restrict__ cta_base, unsigned* __restrict__ ticket) {
+  __shared__ int wcnt[32][kGroupMaxG];
+  __shared__ bool s_last;
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t total = static_cast<int64_t>(n_rows) * slots;
+  for (int i = tid; i < 32 * kGroupMaxG; i += kGroupThreads) (&wcnt[0][0])[i] = 0;
+  __syncthreads();
+  const int64_t e = static_cast<int64_t>(blockIdx.x) * kGroupThreads + tid;
+  float wsum = 0.f;
+  const int g = e < total ? entry_group(idx, w, slots, G, flags, e, wsum) : -1;
+  const unsigned peers = __match_any_sync(0xffffffffu, g);
+  const int rank_w = __popc(peers & ((1u << lane) - 1u));
+  if (g >= 0 && rank_w == 0) wcnt[warp][g] = __popc(peers);
+  __syncthreads();
+  for (int gg = tid; gg < G; gg += kGroupThreads) {
+    int acc = 0;
+    for (int ww = 0; ww < 32; ++ww) {
+      const int c = wcnt[ww][gg];
+      wcnt[ww][gg] = acc;
+      acc += c;
+    }
+    cta_base[static_cast<int64_t>(blockIdx.x) * G + gg] = acc;  // this CTA's count, made a base below
+  }
+  __syncthreads();
+  if (e < total) {
+    rank_scratch[e] = g >= 0 ? wcnt[warp][g] + rank_w : -1;
+    w_scratch[e] = wsum;
+  }
+  // last CTA: counts -> bases and offsets
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  __shared__ int s_tot[kGroupMaxG + 1];
+  const int nctas = gridDim.x;
+  for (int gg = tid; gg < G; gg += kGroupThreads) {
+    int acc = 0;
+    for (int c = 0; c < nctas; ++c) {
+      volatile int32_t* p = cta_base + static_cast<int64_t>(c) * G + gg;
+      const int v = *p;
+      *p = acc;
+      acc += v;
+    }
+    s_tot[gg] = acc;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int gg = 0; gg < G; ++gg) {
+      const int t = s_tot[gg];
+      s_tot[gg] = acc;
+      acc += t;
+    }
+    s_tot[G] = acc;
+  }
+  __syncthreads();
+  for (int gg = tid; gg <= G; gg += kGroupThreads) offsets[gg] = s_tot[gg];
+  for (int64_t i = tid; i < static_cast<int64_t>(nctas) * G; i += kGroupThreads)
+    cta_base[i] += s_tot[i % G];
+  if (tid == 0) *ticket = 0u;  // ready for the next call
+}
+
+__global__ void __launch_bounds__(256)
+group_scatter_kernel(const int32_t* __restrict__ idx, int n_rows, int slots, int G,
+                     const int32_t* __restrict__ rank_scratch, const float* __restrict__ w_scratch,
+                     const int32_t* __restrict__ cta_base, int32_t* __restrict__ perm_row,
+                     int32_t* __restrict__ perm_slot, float* __restrict__ perm_w, int32_t* __restrict__ inv) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t total = static_cast<int64_t>(n_rows) * slots;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int r = rank_scratch[e];
+    if (r < 0) {
+      inv[e] = -1;
+      continue;
+    }
+    const int g = idx[e];
+    const int pos = cta_base[(e / kGroupThreads) * G + g] + r;
+    perm_row[pos] = static_cast<int32_t>(e / slots);
+    perm_slot[pos] = static_cast<int32_t>(e);
+    perm_w[pos] = w_scratch[e];
+    inv[e] = pos;
+  }
+}
+
 template <typename V>
 __global__ void gather_rows_kernel(const V* __restrict__ src, int vec_per_row,
                                    const int32_t* __restrict__ perm_row,
@@ -122,9 +226,11 @@ __global__ void gather_rows_kernel(const V* __restrict__ src, int vec_per_row,
 using namespace sb;
 
 extern "C" SB_API size_t sb_group_workspace_bytes(int n_rows, int slots, int num_groups) {
-  (void)num_groups;
   const size_t total = static_cast<size_t>(n_rows > 0 ? n_rows : 0) * (slots > 0 ? slots : 0);
-  return kStatusBytes + align_up(total * sizeof(int32_t), 256) + align_up(total * sizeof(float), 256);
+  const size_t ctas = (total + kGroupThreads - 1) / kGroupThreads;
+  const size_t groups = num_groups > 0 ? static_cast<size_t>(num_groups) : 1;
+  return kStatusBytes + align_up(total * sizeof(int32_t), 256) + align_up(total * sizeof(float), 256) +
+         align_up(ctas * groups * sizeof(int32_t), 256) + 256;
 }
 
 extern "C" SB_API int sb_group(const int32_t* idx, const float* w, int n_rows, int slots,
@@ -141,12 +247,29 @@ extern "C" SB_API int sb_group(const int32_t* idx, const float* w, int n_rows, i
   const size_t total = static_cast<size_t>(n_rows) * slots;
   int32_t* rank_scratch = c.take<int32_t>(total);
   float* w_scratch = c.take<float>(total);
-  // One CTA; as many threads as entries (rounded to warps, 64..1024): fewer warps
-  // to synchronise and scan when a decode batch has only a few hundred entries.
-  int threads = static_cast<int>(((total + 31) / 32) * 32);
-  threads = threads < 64 ? 64 : (threads > kGroupThreads ? kGroupThreads : threads);
-  return launch(group_kernel, dim3(1), dim3(threads), 0, static_cast<cudaStream_t>(stream), idx, w, n_rows,
-                slots, num_groups, flags, offsets, perm_row, perm_slot, perm_w, inv, rank_scratch, w_scratch);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (total <= kGroupSingleCtaMax) {
+    // One CTA; as many threads as entries (rounded to warps, 64..1024): fewer warps
+    // to synchronise and scan when a decode batch has only a few hundred entries.
+    int threads = static_cast<int>(((total + 31) / 32) * 32);
+    threads = threads < 64 ? 64 : (threads > kGroupThreads ? kGroupThreads : threads);
+    return launch(group_kernel, dim3(1), dim3(threads), 0, st, idx, w, n_rows, slots, num_groups, flags, offsets,
+                  perm_row, perm_slot, perm_w, inv, rank_scratch, w_scratch);
+  }
+  const int ctas = static_cast<int>((total + kGroupThreads - 1) / kGroupThreads);
+  int32_t* cta_base = c.take<int32_t>(static_cast<size_t>(ctas) * num_groups);
+  unsigned* ticket = c.take<unsigned>(1);
+  int rc = cuda_status(cudaMemsetAsync(ticket, 0, sizeof(unsigned), st));
+  if (rc) return rc;
+  rc = launch(group_rank_kernel, dim3(ctas), dim3(kGroupThreads), 0, st, idx, w, n_rows, slots, num_groups, flags,
+              offsets, rank_scratch, w_scratch, cta_base, ticket);
+  if (rc) return rc;
+  int blocks = static_cast<int>((total + 255) / 256);
+  const int cap = 4 * current_sm_count();
+  blocks = blocks > cap ? cap : blocks;
+  return launch(group_scatter_kernel, dim3(blocks), dim3(256), 0, st, idx, n_rows, slots, num_groups,
+                static_cast<const int32_t*>(rank_scratch), static_cast<const float*>(w_scratch),
+                static_cast<const int32_t*>(cta_base), perm_row, perm_slot, perm_w, inv);
 }
 
 namespace sb {

@@ -170,7 +170,7 @@ def test_cuda_graph_replay_matches_eager(cuda_device):
     assert torch.equal(out.view_as(eager), eager)
 
 
-@pytest.mark.parametrize("n", [1, 7, 37, 130])
+@pytest.mark.parametrize("n", [1, 7, 37, 130, 1536])
 def test_ragged_token_counts(n, cuda_device):
     cfg = ModelConfig(hidden_size=256, num_heads=4, num_experts=16, top_k=2, edges_per_expert=2,
                       num_loops=2, expert_ffn_size=512).validate()
