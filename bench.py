@@ -41,9 +41,9 @@ import torch.distributed as dist  # noqa: E402
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
-# DRAM traffic per launch measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum)
-# for the grouped-GEMM launches of one cfg2 step; the capture and command are in
-# profiles/gemm_tcgen05_cfg2.md.  None until a capture exists for a config.
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum, one ncu capture) of the
+# grouped-GEMM launches of one step, per config; None where no capture of all of
+# them exists yet.
 NCU_TRAFFIC_PER_STEP = {"cfg2": None}
 
 
