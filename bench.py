@@ -18,9 +18,10 @@ Arms:
 * ``--impl reference``: the reference block's CPU algorithm (the oracle
   restatement, dense as the reference computes it) on all host threads, rank 0.
 
-With N > 1 (torchrun) every rank runs its own batch on its own GPU with the
-full block (replicas; the expert-parallel all-to-all path is measured by
-``spider_web_moe_b200.ep``), ``scaling`` = weak.
+With N > 1 (torchrun) every rank holds its own batch of the config's token
+count (weak scaling) and the experts are sharded e % N: the token-sharded
+expert-parallel block (spider_web_moe_b200.ep: NCCL all-to-all of message rows
+to expert owners and back every loop).
 """
 from __future__ import annotations
 
@@ -314,12 +315,92 @@ def run_reference(args):
         dist.destroy_process_group()
 
 
+def run_b200_ep(args, rank, world, local, device):
+    """N > 1: token-sharded expert parallelism, one batch per rank, experts e % N."""
+    from spider_web_moe_b200 import synth
+    from spider_web_moe_b200.ep import ExpertParallelBlock
+
+    cfg, spec = workload(args)
+    n = spec["tokens"]
+    zipf = 1.1 if spec["zipf"] else None
+    if spec["wfmt"] == "int4":
+        cfg.moe_int4_group_size = cfg.moe_int4_group_size or 128
+    sd = synth.synthetic_state_dict(cfg, seed=0, device=device, zipf=zipf, round_bf16=True)
+    ep = ExpertParallelBlock(cfg, sd, device, act_dtype=torch.bfloat16, max_tokens=n, weight_format=spec["wfmt"],
+                             engine=args.engine)
+    del sd
+    h, _ = synth.block_inputs(n, cfg.hidden_size, seed=1 + rank, device=device, dtype=torch.bfloat16)
+    h = h.view(n, -1).contiguous()
+    stream = torch.cuda.current_stream(device)
+    for _ in range(max(3, args.warmup)):
+        out = ep.forward(h, h)
+    torch.cuda.synchronize(device)
+    ep.dense.check_status()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for _ in range(args.steps):
+            out = ep.forward(h, h)
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    barrier(world)
+    ms_step = max_over_ranks(start.elapsed_time(end), world, device) / args.steps
+    # e2e through the public API: pinned host input in, output back, every step
+    h_host = h.cpu().pin_memory()
+    out_host = torch.empty(n, cfg.hidden_size, dtype=torch.bfloat16).pin_memory()
+    h_dev = torch.empty_like(h)
+    barrier(world)
+    torch.cuda.synchronize(device)
+    start.record(stream)
+    for _ in range(args.steps):
+        h_dev.copy_(h_host, non_blocking=True)
+        out = ep.forward(h_dev, h_dev)
+        out_host.copy_(out, non_blocking=True)
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    e2e_ms = max_over_ranks(start.elapsed_time(end), world, device) / args.steps
+    peaks, peak_kind = load_peaks()
+    per_rank_bytes = (ep.dense.weight_bytes() + (ep.local.weight_bytes() if ep.local else 0)) * cfg.num_loops
+    achieved = per_rank_bytes / (ms_step / 1e3) / 1e9
+    loop_launches = 7 + 3 + 5 + 1
+    line = {
+        "metric": "spider_moe_block_tokens_per_s", "value": n * world / (ms_step / 1e3), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) hidden states)",
+        "config": {"workload": args.config, "tokens_per_step_per_gpu": n, "num_loops": cfg.num_loops,
+                   "hidden": cfg.hidden_size, "experts": cfg.num_experts, "top_k": cfg.top_k,
+                   "edges_per_expert": cfg.edges_per_expert, "ffn": cfg.expert_ffn_size,
+                   "expert_activation": cfg.expert_activation, "expert_weights": spec["wfmt"],
+                   "parallelism": f"ep{world}: tokens sharded by rank, experts e % {world}, NCCL all-to-all",
+                   "l2": "not flushed: dense + local expert weights re-read every loop", "engine": args.engine},
+        "clocks": clk.summary(),
+        "e2e": {"value": n * world / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": n * cfg.hidden_size * 2,
+                "d2h_bytes_per_step": n * cfg.hidden_size * 2, "ms_per_step": e2e_ms},
+        "gpu_launches": loop_launches * cfg.num_loops * args.steps,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "peak_kind": f"{peak_kind} (STREAM copy)",
+                     "traffic": None, "kernel": "whole expert-parallel step per rank (dense + local expert weights)"},
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, spec, args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    barrier(world)
+    dist.destroy_process_group()
+
+
 def run_b200(args):
     rank, world, local = dist_setup(args)
     if not torch.cuda.is_available():
         raise SystemExit("bench.py --impl b200 needs a CUDA device")
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if world > 1 and not args.profile_only:
+        return run_b200_ep(args, rank, world, local, device)
     from spider_web_moe_b200 import synth
     from spider_web_moe_b200.engine import CapturedBlock
 

@@ -262,6 +262,35 @@ SB_API int sb_expert_delta(const sb_block_dims* dims, const sb_block_weights* w,
                            int n_tokens, int rank, int world, float* delta, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------ expert parallel
+ * Token-sharded expert parallelism.  Each rank routes its own tokens
+ * (sb_block_route), sends each token's message row once to every rank owning
+ * one of its experts (owner = e % world, spider_moe/expert_parallel.py:29-30)
+ * with a fixed-capacity all-to-all, the owners run their experts
+ * (sb_expert_delta on the received rows, local expert ids), the results come
+ * back with a second all-to-all and sb_combine_ln sums them (inv = ret_pos).
+ *
+ * sb_block_route replaces the router + graph part of SpiderMoELayer.forward
+ * (model.py:254-288) for loop loop_idx: messages [n, H] in act dtype (and
+ * optionally fp32), top_idx / top_w [n, K].  Uses the sb_block_forward
+ * workspace; needs no expert weights. */
+SB_API int sb_block_route(const sb_block_dims* dims, const sb_block_weights* w, const void* h, int n_tokens,
+                          int loop_idx, void* messages, float* messages_f32, int32_t* top_idx, float* top_w,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* Dispatch packing (no reference counterpart; the reference all-reduces the
+ * full delta instead, expert_parallel.py:33-37).  send_x [world, cap, hidden]
+ * (act dtype), send_idx / send_w [world, cap, K]: row (q, j) is the j-th token
+ * (ascending) that owner q must see; send_idx holds q's local expert id per
+ * slot (-1: not q's expert or unused row).  ret_pos [n, K]: position q*cap + j
+ * of the returned combined row for the first slot of each owner, else -1.
+ * cap >= n_tokens. */
+SB_API size_t sb_ep_pack_workspace_bytes(int n_tokens, int top_k, int world);
+SB_API int sb_ep_pack(const int32_t* top_idx, const float* top_w, const void* messages, int act_dtype,
+                      int n_tokens, int hidden, int top_k, int num_experts, int world, int cap, void* send_x,
+                      int32_t* send_idx, float* send_w, int32_t* ret_pos, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
 /* Byte offset of the device status word inside every workspace above. */
 SB_API size_t sb_status_offset(void);
 

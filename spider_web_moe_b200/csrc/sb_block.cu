@@ -175,8 +175,7 @@ static size_t carve_block(const sb_block_dims& d, int n_cap, void* base, size_t 
 
 static int check_dims(const sb_block_dims* d) {
   if (!d || d->hidden <= 0 || d->hidden % 8 || d->num_experts <= 0 || d->num_experts > 256 || d->top_k <= 0 ||
-      d->top_k > d->num_experts || d->edges_per_expert <= 0 || d->edges_per_expert > d->num_experts ||
-      d->top_k * d->edges_per_expert > 64 || d->ffn <= 0 || d->ffn % 8 || d->num_loops <= 0 ||
+      d->edges_per_expert <= 0 || d->top_k * d->edges_per_expert > 64 || d->ffn <= 0 || d->ffn % 8 || d->num_loops <= 0 ||
       d->max_tokens < 0 || (d->act_dtype != SB_F32 && d->act_dtype != SB_BF16) ||
       d->wfmt < SB_W_F32 || d->wfmt > SB_W_INT4 || (d->activation != SB_ACT_GELU && d->activation != SB_ACT_SWIGLU))
     return SB_ERR_ARG;
@@ -313,6 +312,84 @@ extern "C" SB_API size_t sb_block_workspace_bytes(const sb_block_dims* dims) {
   return carve_block(*dims, dims->max_tokens > 0 ? dims->max_tokens : 1, nullptr, ~size_t(0) >> 1, &b);
 }
 
+// Steps 1-8 of one loop: routing, edge graph and the edge-value GEMM.  Leaves
+// the routing in b.top_idx / b.top_w and the message partials in b.y_msg.
+static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBuffers& b, const void* cur, int N,
+                      int l, int* msg_splits_out, cudaStream_t st) {
+  int rc = SB_OK;
+  const int H = d.hidden, E = d.num_experts, K = d.top_k, M = d.edges_per_expert;
+  const int KM = K * M;
+  const int dense_fmt = d.act_dtype == SB_F32 ? SB_W_F32 : SB_W_BF16;
+  const int64_t cap_dst = static_cast<int64_t>(N) * (E < KM ? E : KM);
+  const bool tc_pref = d.engine != SB_ENGINE_SIMT;
+#define SB_TRY(x) do { rc = (x); if (rc) return rc; } while (0)
+  // 1. router
+  { StageScope sc_(0, st); SB_TRY(sb_router(cur, d.act_dtype, N, H, w->router_w, w->loop_bias + static_cast<int64_t>(l) * E, E, K,
+                                          b.top_idx, b.top_w, nullptr, st)); }
+  // 2-3. rows grouped by selected source; gather h (inside the GEMM when it can)
+  { StageScope sc_(1, st); SB_TRY(sb_group(b.top_idx, nullptr, N, K, E, 0, b.src_off, b.src_row, b.src_slot, b.src_w,
+                                         b.src_inv, b.group_ws, b.group_ws_bytes, st)); }
+  // 4. edge logits of the selected sources: rows [s*E, s*E+E) of the generator
+  {
+    sb_grouped_gemm_args a;
+    std::memset(&a, 0, sizeof(a));
+    a.engine = d.engine; a.wfmt = dense_fmt; a.act_dtype = d.act_dtype; a.epilogue = SB_EPI_LINEAR;
+    a.num_groups = E; a.m_rows = E; a.k = H; a.a_group_rows = E; a.lda = H;
+    a.a_rows_total = static_cast<int64_t>(E) * E; a.a = w->gen_w;
+    a.bias = w->gen_bias + static_cast<int64_t>(l) * E * E; a.bias_group_stride = E;
+    a.x = b.x_src; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N; a.offsets = b.src_off;
+    a.out = b.elog; a.ldo = E; a.splits = 1; a.status = b.status;
+    if (gemm_gathers(a, d.engine)) {
+      a.x = cur; a.x_row_index = b.src_row; a.x_rows = N;
+    } else {
+      StageScope sc_(2, st);
+      SB_TRY(sb_gather_rows(cur, d.act_dtype, H, b.src_row, b.src_off, E, N * K, b.x_src, st));
+    }
+    { StageScope sc_(3, st); SB_TRY(run_gemm(a, d.engine, st)); }
+  }
+  // 5. top-M destinations per (token, source)
+  { StageScope sc_(4, st); SB_TRY(sb_edge_topm(b.elog, E, E, M, b.src_slot, b.src_off, E, N * K, b.edge_idx, b.edge_w, st)); }
+  // 6-7. (token, destination) pairs with summed coefficients
+  { StageScope sc_(5, st); SB_TRY(sb_group(b.edge_idx, b.edge_w, N, KM, E, 0, b.dst_off, b.dst_row, b.dst_slot, b.dst_w,
+                                         b.dst_inv, b.group_ws, b.group_ws_bytes, st)); }
+  // 8. c[t,d] * W_edge[d] h[t]
+  {
+    sb_grouped_gemm_args a;
+    std::memset(&a, 0, sizeof(a));
+    a.engine = d.engine; a.wfmt = dense_fmt; a.act_dtype = d.act_dtype; a.epilogue = SB_EPI_LINEAR;
+    a.num_groups = E; a.m_rows = H; a.k = H; a.a_group_rows = H; a.lda = H;
+    a.a_rows_total = static_cast<int64_t>(E) * H; a.a = w->edge_w;
+    a.x = b.x_dst; a.ldx = H; a.max_rows = static_cast<int>(cap_dst);
+    a.rows_hint = static_cast<int>(cap_dst * 7 / 8); a.group_rows_bound = N; a.offsets = b.dst_off; a.row_scale = b.dst_w;
+    const int msg_splits = pick_splits(H, H, a.rows_hint, E, max_splits_for(N), tc_pref, N);
+    a.splits = msg_splits; a.split_stride = cap_dst * H;
+    a.out = b.y_msg; a.ldo = H; a.status = b.status;
+    if (gemm_gathers(a, d.engine)) {
+      a.x = cur; a.x_row_index = b.dst_row; a.x_rows = N;
+    } else {
+      StageScope sc_(6, st);
+      SB_TRY(sb_gather_rows(cur, d.act_dtype, H, b.dst_row, b.dst_off, E, static_cast<int>(cap_dst), b.x_dst, st));
+    }
+    { StageScope sc_(7, st); SB_TRY(run_gemm(a, d.engine, st)); }
+    *msg_splits_out = msg_splits;
+  }
+#undef SB_TRY
+  return SB_OK;
+}
+
+static int check_block_args(const sb_block_dims& d, const sb_block_weights* w, bool need_experts, bool need_dense) {
+  if (!w) return SB_ERR_ARG;
+  // routing picks top_k distinct experts and edges_per_expert distinct destinations
+  if (need_dense && (d.top_k > d.num_experts || d.edges_per_expert > d.num_experts)) return SB_ERR_ARG;
+  if (need_dense && (!w->router_w || !w->loop_bias || !w->gen_w || !w->gen_bias || !w->edge_w || !w->ln_w || !w->ln_b))
+    return SB_ERR_ARG;
+  if (need_experts && (!w->w_up || !w->b_up || !w->w_down || !w->b_down ||
+                       (d.activation == SB_ACT_SWIGLU && (!w->w_gate || !w->b_gate)) ||
+                       ((d.wfmt == SB_W_FP8 || d.wfmt == SB_W_INT4) && (!w->s_up || !w->s_down))))
+    return SB_ERR_ARG;
+  return SB_OK;
+}
+
 extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block_weights* w, const void* h_in,
                                        const void* x0, void* h_out, int n_tokens, int loop_begin, int loop_end,
                                        void* workspace, size_t workspace_bytes, const sb_block_taps* taps,
@@ -320,11 +397,8 @@ extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block
   int rc = check_dims(dims);
   if (rc) return rc;
   const sb_block_dims& d = *dims;
-  if (!w || !w->router_w || !w->loop_bias || !w->gen_w || !w->gen_bias || !w->edge_w || !w->w_up || !w->b_up ||
-      !w->w_down || !w->b_down || !w->ln_w || !w->ln_b || n_tokens < 0 || n_tokens > d.max_tokens ||
-      loop_begin < 0 || loop_end > d.num_loops || loop_begin > loop_end ||
-      (d.activation == SB_ACT_SWIGLU && (!w->w_gate || !w->b_gate)) ||
-      ((d.wfmt == SB_W_FP8 || d.wfmt == SB_W_INT4) && (!w->s_up || !w->s_down)))
+  if (check_block_args(d, w, true, true) || n_tokens < 0 || n_tokens > d.max_tokens || loop_begin < 0 ||
+      loop_end > d.num_loops || loop_begin > loop_end)
     return SB_ERR_ARG;
   if (n_tokens == 0 || loop_begin == loop_end) return SB_OK;
   if (!h_in || !x0 || !h_out) return SB_ERR_ARG;
@@ -334,66 +408,17 @@ extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int N = n_tokens, H = d.hidden, E = d.num_experts, K = d.top_k, M = d.edges_per_expert, U = d.ffn;
   const int KM = K * M;
-  const int dense_fmt = d.act_dtype == SB_F32 ? SB_W_F32 : SB_W_BF16;
   const int64_t cap_dst = static_cast<int64_t>(N) * (E < KM ? E : KM);
   const bool tc_pref = d.engine != SB_ENGINE_SIMT;
   const void* cur = h_in;
 #define SB_TRY(x) do { rc = (x); if (rc) return rc; } while (0)
   for (int l = loop_begin; l < loop_end; ++l) {
     void* next = (l == loop_end - 1) ? h_out : b.hbuf[(l - loop_begin) & 1];
-    // 1. router
-    { StageScope sc_(0, st); SB_TRY(sb_router(cur, d.act_dtype, N, H, w->router_w, w->loop_bias + static_cast<int64_t>(l) * E, E, K,
-                     b.top_idx, b.top_w, nullptr, st)); }
-    // 2-3. rows grouped by selected source; gather h (inside the GEMM when it can)
-    { StageScope sc_(1, st); SB_TRY(sb_group(b.top_idx, nullptr, N, K, E, 0, b.src_off, b.src_row, b.src_slot, b.src_w, b.src_inv,
-                    b.group_ws, b.group_ws_bytes, st)); }
-    // 4. edge logits of the selected sources: rows [s*E, s*E+E) of the generator
-    {
-      sb_grouped_gemm_args a;
-      std::memset(&a, 0, sizeof(a));
-      a.engine = d.engine; a.wfmt = dense_fmt; a.act_dtype = d.act_dtype; a.epilogue = SB_EPI_LINEAR;
-      a.num_groups = E; a.m_rows = E; a.k = H; a.a_group_rows = E; a.lda = H;
-      a.a_rows_total = static_cast<int64_t>(E) * E; a.a = w->gen_w;
-      a.bias = w->gen_bias + static_cast<int64_t>(l) * E * E; a.bias_group_stride = E;
-      a.x = b.x_src; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N; a.offsets = b.src_off;
-      a.out = b.elog; a.ldo = E; a.splits = 1; a.status = b.status;
-      if (gemm_gathers(a, d.engine)) {
-        a.x = cur; a.x_row_index = b.src_row; a.x_rows = N;
-      } else {
-        StageScope sc_(2, st);
-        SB_TRY(sb_gather_rows(cur, d.act_dtype, H, b.src_row, b.src_off, E, N * K, b.x_src, st));
-      }
-      { StageScope sc_(3, st); SB_TRY(run_gemm(a, d.engine, st)); }
-    }
-    // 5. top-M destinations per (token, source)
-    { StageScope sc_(4, st); SB_TRY(sb_edge_topm(b.elog, E, E, M, b.src_slot, b.src_off, E, N * K, b.edge_idx, b.edge_w, st)); }
-    // 6-7. (token, destination) pairs with summed coefficients
-    { StageScope sc_(5, st); SB_TRY(sb_group(b.edge_idx, b.edge_w, N, KM, E, 0, b.dst_off, b.dst_row, b.dst_slot, b.dst_w, b.dst_inv,
-                    b.group_ws, b.group_ws_bytes, st)); }
-    // 8. c[t,d] * W_edge[d] h[t]
     int msg_splits = 1;
-    {
-      sb_grouped_gemm_args a;
-      std::memset(&a, 0, sizeof(a));
-      a.engine = d.engine; a.wfmt = dense_fmt; a.act_dtype = d.act_dtype; a.epilogue = SB_EPI_LINEAR;
-      a.num_groups = E; a.m_rows = H; a.k = H; a.a_group_rows = H; a.lda = H;
-      a.a_rows_total = static_cast<int64_t>(E) * H; a.a = w->edge_w;
-      a.x = b.x_dst; a.ldx = H; a.max_rows = static_cast<int>(cap_dst);
-      a.rows_hint = static_cast<int>(cap_dst * 7 / 8); a.group_rows_bound = N; a.offsets = b.dst_off; a.row_scale = b.dst_w;
-      msg_splits = pick_splits(H, H, a.rows_hint, E, max_splits_for(N), tc_pref, N);
-      a.splits = msg_splits; a.split_stride = cap_dst * H;
-      a.out = b.y_msg; a.ldo = H; a.status = b.status;
-      if (gemm_gathers(a, d.engine)) {
-        a.x = cur; a.x_row_index = b.dst_row; a.x_rows = N;
-      } else {
-        StageScope sc_(6, st);
-        SB_TRY(sb_gather_rows(cur, d.act_dtype, H, b.dst_row, b.dst_off, E, static_cast<int>(cap_dst), b.x_dst, st));
-      }
-      { StageScope sc_(7, st); SB_TRY(run_gemm(a, d.engine, st)); }
-    }
+    SB_TRY(route_loop(d, w, b, cur, N, l, &msg_splits, st));
     // 9. dispatch plan of the expert FFN
-    { StageScope sc_(8, st); SB_TRY(sb_group(b.top_idx, b.top_w, N, K, E, SB_GROUP_POSITIVE_ONLY, b.ffn_off, b.ffn_row, b.ffn_slot,
-                    b.ffn_w, b.ffn_inv, b.group_ws, b.group_ws_bytes, st)); }
+    { StageScope sc_(8, st); SB_TRY(sb_group(b.top_idx, b.top_w, N, K, E, SB_GROUP_POSITIVE_ONLY, b.ffn_off, b.ffn_row,
+                                           b.ffn_slot, b.ffn_w, b.ffn_inv, b.group_ws, b.group_ws_bytes, st)); }
     // 10-11. messages (sum over the token's destinations), then up projection +
     // activation with the message rows gathered in expert order.
     {
@@ -426,9 +451,11 @@ extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block
       { StageScope sc_(11, st); SB_TRY(run_gemm(a, d.engine, st)); }
     }
     // 13. delta + LayerNorm epilogue
-    { StageScope sc_(12, st); SB_TRY(sb_combine_ln(b.y_ffn, H, ffn_splits, static_cast<int64_t>(N) * K * H, b.ffn_inv, K, nullptr, cur, x0,
-                         d.act_dtype, N, H, w->ln_w, w->ln_b, d.residual_scale, d.reinject, d.ln_eps, next,
-                         (taps && taps->delta && l == loop_end - 1) ? taps->delta : nullptr, st)); }
+    { StageScope sc_(12, st); SB_TRY(sb_combine_ln(b.y_ffn, H, ffn_splits, static_cast<int64_t>(N) * K * H, b.ffn_inv, K,
+                                                nullptr, cur, x0, d.act_dtype, N, H, w->ln_w, w->ln_b, d.residual_scale,
+                                                d.reinject, d.ln_eps, next,
+                                                (taps && taps->delta && l == loop_end - 1) ? taps->delta : nullptr,
+                                                st)); }
     if (taps && l == loop_end - 1) {
       auto cp = [&](void* dst, const void* src, size_t bytes) -> int {
         return dst ? cuda_status(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, st)) : SB_OK;
@@ -446,6 +473,33 @@ extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block
   }
 #undef SB_TRY
   return SB_OK;
+}
+
+extern "C" SB_API int sb_block_route(const sb_block_dims* dims, const sb_block_weights* w, const void* h, int n_tokens,
+                                     int loop_idx, void* messages, float* messages_f32, int32_t* top_idx, float* top_w,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_dims(dims);
+  if (rc) return rc;
+  const sb_block_dims& d = *dims;
+  if (check_block_args(d, w, false, true) || n_tokens < 0 || n_tokens > d.max_tokens || loop_idx < 0 ||
+      loop_idx >= d.num_loops)
+    return SB_ERR_ARG;
+  if (n_tokens == 0) return SB_OK;
+  if (!h || !messages || !top_idx || !top_w) return SB_ERR_ARG;
+  BlockBuffers b;
+  const size_t need = carve_block(d, d.max_tokens, workspace, workspace_bytes, &b);
+  if (!workspace || need == static_cast<size_t>(-1) || workspace_bytes < need) return SB_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int N = n_tokens, H = d.hidden, E = d.num_experts, K = d.top_k, KM = K * d.edges_per_expert;
+  const int64_t cap_dst = static_cast<int64_t>(N) * (E < KM ? E : KM);
+  int msg_splits = 1;
+  if ((rc = route_loop(d, w, b, h, N, loop_idx, &msg_splits, st))) return rc;
+  if ((rc = sb_combine_rows(b.y_msg, H, msg_splits, cap_dst * H, b.dst_inv, KM, N, H, messages_f32, nullptr, K,
+                            messages, d.act_dtype, st)))
+    return rc;
+  if ((rc = cuda_status(cudaMemcpyAsync(top_idx, b.top_idx, sizeof(int32_t) * N * K, cudaMemcpyDeviceToDevice, st))))
+    return rc;
+  return cuda_status(cudaMemcpyAsync(top_w, b.top_w, sizeof(float) * N * K, cudaMemcpyDeviceToDevice, st));
 }
 
 // ------------------------------------------------------------------ sparse expert delta

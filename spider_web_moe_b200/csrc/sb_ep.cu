@@ -1,0 +1,144 @@
+// Expert-parallel dispatch packing for the token-sharded block.
+//
+// Rank r owns the experts e with e % world == r (spider_moe/expert_parallel.py:
+// 29-30).  Each token is sent once to every rank that owns at least one of its
+// routed experts: send row (q, j) of the fixed-capacity buffer [world, cap, H]
+// carries the token's message row and, for each of its K slots, the owner's
+// local expert id (e / world, or -1 when q does not own e) and the routing
+// weight.  Rows are ordered by token inside each destination (a stable
+// grouping by owner), unused rows carry id -1.  ret_pos[t, k] is where the
+// owner's combined result for (token t, owner of slot k) comes back in the
+// return buffer [world, cap, H] (first slot per owner; -1 for the others), so
+// the epilogue sums exactly one returned row per (token, owner).
+#include "sb_common.cuh"
+#include "sb_internal.h"
+
+namespace sb {
+
+__global__ void __launch_bounds__(256)
+ep_owner_kernel(const int32_t* __restrict__ top_idx, int n, int E, int world, int32_t* __restrict__ owner) {
+  pdl_wait();
+  pdl_trigger();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int e = top_idx[i];
+    owner[i] = (e >= 0 && e < E) ? e % world : -1;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+ep_pack_kernel(const T* __restrict__ msgs, const int32_t* __restrict__ top_idx, const float* __restrict__ top_w,
+               int n_tokens, int K, int E, int world, int cap, int H, const int32_t* __restrict__ off,
+               const int32_t* __restrict__ prow, const int32_t* __restrict__ owner, const int32_t* __restrict__ inv,
+               T* __restrict__ send_x, int32_t* __restrict__ send_idx, float* __restrict__ send_w,
+               int32_t* __restrict__ ret_pos) {
+  pdl_wait();
+  pdl_trigger();
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int vec = H * static_cast<int>(sizeof(T)) / 16;
+  // send rows, one warp per row
+  for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < world * cap; row += warps) {
+    const int q = row / cap, j = row - q * cap;
+    const int cnt = off[q + 1] - off[q];
+    int t = -1;
+    if (j < cnt) t = prow[off[q] + j];
+    if (lane < K) {
+      int lid = -1;
+      float wk = 0.f;
+      if (t >= 0) {
+        const int e = top_idx[static_cast<int64_t>(t) * K + lane];
+        if (e >= 0 && e < E && e % world == q) lid = e / world;
+        wk = top_w[static_cast<int64_t>(t) * K + lane];
+      }
+      send_idx[static_cast<int64_t>(row) * K + lane] = lid;
+      send_w[static_cast<int64_t>(row) * K + lane] = wk;
+    }
+    if (t >= 0) {
+      const uint4* src = reinterpret_cast<const uint4*>(msgs + static_cast<int64_t>(t) * H);
+      uint4* dst = reinterpret_cast<uint4*>(send_x + static_cast<int64_t>(row) * H);
+      for (int v = lane; v < vec; v += 32) dst[v] = src[v];
+    }
+  }
+  // return positions, one thread per (token, slot)
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_tokens * K; i += gridDim.x * blockDim.x) {
+    const int p = inv[i];
+    const int q = owner[i];
+    ret_pos[i] = (p >= 0 && q >= 0) ? q * cap + (p - off[q]) : -1;
+  }
+}
+
+struct EpBuffers {
+  int32_t *owner, *off, *prow, *pslot, *inv;
+  float* pw;
+  void* group_ws;
+  size_t group_ws_bytes;
+};
+
+static size_t carve_ep(int n, int K, int world, void* base, size_t size, EpBuffers* b) {
+  Carver c(base, size);
+  c.take<char>(kStatusBytes);
+  const size_t e = static_cast<size_t>(n) * K;
+  b->owner = c.take<int32_t>(e);
+  b->off = c.take<int32_t>(world + 1);
+  b->prow = c.take<int32_t>(e);
+  b->pslot = c.take<int32_t>(e);
+  b->pw = c.take<float>(e);
+  b->inv = c.take<int32_t>(e);
+  b->group_ws_bytes = sb_group_workspace_bytes(n, K, world);
+  b->group_ws = c.take<char>(b->group_ws_bytes);
+  return c.overflow ? static_cast<size_t>(-1) : align_up(c.used, 256);
+}
+
+}  // namespace sb
+
+using namespace sb;
+
+extern "C" SB_API size_t sb_ep_pack_workspace_bytes(int n_tokens, int top_k, int world) {
+  if (n_tokens < 0 || top_k <= 0 || world <= 0) return 0;
+  EpBuffers b;
+  return carve_ep(n_tokens > 0 ? n_tokens : 1, top_k, world, nullptr, ~size_t(0) >> 1, &b);
+}
+
+extern "C" SB_API int sb_ep_pack(const int32_t* top_idx, const float* top_w, const void* messages, int act_dtype,
+                                 int n_tokens, int hidden, int top_k, int num_experts, int world, int cap,
+                                 void* send_x, int32_t* send_idx, float* send_w, int32_t* ret_pos, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  const int esize = act_dtype == SB_F32 ? 4 : (act_dtype == SB_BF16 ? 2 : 0);
+  if (n_tokens < 0 || hidden <= 0 || !esize || (hidden * esize) % 16 || top_k <= 0 || top_k > 32 ||
+      num_experts <= 0 || world <= 0 || world > 256 || cap < n_tokens || cap <= 0)
+    return SB_ERR_ARG;
+  if (world * static_cast<int64_t>(cap) > 0x7fffffff) return SB_ERR_UNSUPPORTED;
+  if (!send_x || !send_idx || !send_w || (n_tokens > 0 && (!top_idx || !top_w || !messages || !ret_pos)))
+    return SB_ERR_ARG;
+  EpBuffers b;
+  const size_t need = carve_ep(n_tokens, top_k, world, workspace, workspace_bytes, &b);
+  if (!workspace || need == static_cast<size_t>(-1) || workspace_bytes < need) return SB_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int entries = n_tokens * top_k;
+  int rc = SB_OK;
+  if (n_tokens > 0) {
+    rc = launch(ep_owner_kernel, dim3((entries + 255) / 256), dim3(256), 0, st, top_idx, entries, num_experts, world,
+                b.owner);
+    if (rc) return rc;
+    rc = sb_group(b.owner, nullptr, n_tokens, top_k, world, 0, b.off, b.prow, b.pslot, b.pw, b.inv, b.group_ws,
+                  b.group_ws_bytes, st);
+  } else {
+    rc = cuda_status(cudaMemsetAsync(b.off, 0, sizeof(int32_t) * (world + 1), st));
+  }
+  if (rc) return rc;
+  const int rows = world * cap;
+  int blocks = (rows * 32 + 255) / 256;
+  const int lim = 4 * current_sm_count();
+  blocks = blocks > lim ? lim : (blocks < 1 ? 1 : blocks);
+  if (act_dtype == SB_BF16)
+    return launch(ep_pack_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st,
+                  static_cast<const __nv_bfloat16*>(messages), top_idx, top_w, n_tokens, top_k, num_experts, world,
+                  cap, hidden, static_cast<const int32_t*>(b.off), static_cast<const int32_t*>(b.prow),
+                  static_cast<const int32_t*>(b.owner), static_cast<const int32_t*>(b.inv),
+                  static_cast<__nv_bfloat16*>(send_x), send_idx, send_w, ret_pos);
+  return launch(ep_pack_kernel<float>, dim3(blocks), dim3(256), 0, st, static_cast<const float*>(messages), top_idx,
+                top_w, n_tokens, top_k, num_experts, world, cap, hidden, static_cast<const int32_t*>(b.off),
+                static_cast<const int32_t*>(b.prow), static_cast<const int32_t*>(b.owner),
+                static_cast<const int32_t*>(b.inv), static_cast<float*>(send_x), send_idx, send_w, ret_pos);
+}

@@ -85,14 +85,16 @@ class BlockEngine:
             t["edge_w"] = stacked(state, "edge_value.{}.weight", E).to(dev, dt).contiguous()
             t["ln_w"] = g("norm.weight").to(f32).contiguous()
             t["ln_b"] = g("norm.bias").to(f32).contiguous()
-        t["b_up"] = stacked(state, "experts.{}.0.bias", E).to(dev, f32).contiguous()
-        t["b_down"] = stacked(state, "experts.{}.2.bias", E).to(dev, f32).contiguous()
         swiglu = cfg.expert_activation == "swiglu"
-        if swiglu:
-            t["b_gate"] = stacked(state, "expert_gates.{}.bias", E).to(dev, f32).contiguous()
         self.group_size = 0
-        names = [("up", "experts.{}.0.weight")] + ([("gate", "expert_gates.{}.weight")] if swiglu else []) \
-            + [("down", "experts.{}.2.weight")]
+        has_experts = "experts.0.0.weight" in state or int4 is not None or fp8 is not None
+        if has_experts:  # dense-only engines (routing of an expert-parallel rank) skip the experts
+            t["b_up"] = stacked(state, "experts.{}.0.bias", E).to(dev, f32).contiguous()
+            t["b_down"] = stacked(state, "experts.{}.2.bias", E).to(dev, f32).contiguous()
+            if swiglu:
+                t["b_gate"] = stacked(state, "expert_gates.{}.bias", E).to(dev, f32).contiguous()
+        names = ([("up", "experts.{}.0.weight")] + ([("gate", "expert_gates.{}.weight")] if swiglu else [])
+                 + [("down", "experts.{}.2.weight")]) if has_experts else []
         for short, key in names:
             if fmt in ("f32", "bf16"):
                 t["w_" + short] = stacked(state, key, E).to(dev, f32 if fmt == "f32" else torch.bfloat16).contiguous()
@@ -183,6 +185,62 @@ class BlockEngine:
         if os.environ.get("SPIDER_B200_CHECK"):
             self.check_status()
         return out.view(h.shape)
+
+    def route(self, h: torch.Tensor, loop_idx: int, stream=None):
+        """Router + edge graph + messages of one loop (sb_block_route): returns
+        (messages [n, H] act dtype, top_idx [n, K] int32, top_w [n, K] fp32)."""
+        H, K = self.cfg.hidden_size, self.cfg.top_k
+        n = h.numel() // H
+        self._ensure_workspace(n)
+        h2 = h.reshape(n, H)
+        if h2.dtype != self.act_dtype or not h2.is_contiguous():
+            h2 = h2.to(self.act_dtype).contiguous()
+        msgs = torch.empty((n, H), dtype=self.act_dtype, device=self.device)
+        top_idx = torch.empty((n, K), dtype=torch.int32, device=self.device)
+        top_w = torch.empty((n, K), dtype=torch.float32, device=self.device)
+        rc = self.lib.sb_block_route(C.byref(self.dims), C.byref(self.weights), h2.data_ptr(), n, int(loop_idx),
+                                     msgs.data_ptr(), None, top_idx.data_ptr(), top_w.data_ptr(),
+                                     self.workspace.data_ptr(), self.workspace.numel(), _stream_ptr(stream))
+        L.check(rc, "sb_block_route")
+        return msgs, top_idx, top_w
+
+    def epilogue(self, rows: torch.Tensor, inv: torch.Tensor, h: torch.Tensor, x0: torch.Tensor, stream=None):
+        """h_out = LayerNorm(h + a*delta + b*x0) with delta[t] = sum of rows[inv[t, k]] (sb_combine_ln)."""
+        H = self.cfg.hidden_size
+        n = h.numel() // H
+        slots = inv.shape[-1]
+        h2 = h.reshape(n, H).to(self.act_dtype).contiguous()
+        x2 = x0.reshape(n, H).to(self.act_dtype).contiguous()
+        out = torch.empty((n, H), dtype=self.act_dtype, device=self.device)
+        rc = self.lib.sb_combine_ln(rows.data_ptr(), H, 1, 0, inv.data_ptr(), slots, None, h2.data_ptr(),
+                                    x2.data_ptr(), self.dims.act_dtype, n, H, self.t["ln_w"].data_ptr(),
+                                    self.t["ln_b"].data_ptr(), self.dims.residual_scale, self.dims.reinject,
+                                    self.dims.ln_eps, out.data_ptr(), None, _stream_ptr(stream))
+        L.check(rc, "sb_combine_ln")
+        return out.view(h.shape)
+
+    def ep_pack(self, top_idx, top_w, msgs, world: int, cap: int, stream=None):
+        """Per-owner send buffers for the all-to-all (sb_ep_pack)."""
+        H, K, E = self.cfg.hidden_size, self.cfg.top_k, self.cfg.num_experts
+        n = msgs.shape[0]
+        send_x = torch.empty((world, cap, H), dtype=self.act_dtype, device=self.device)
+        send_idx = torch.empty((world, cap, K), dtype=torch.int32, device=self.device)
+        send_w = torch.empty((world, cap, K), dtype=torch.float32, device=self.device)
+        ret_pos = torch.empty((n, K), dtype=torch.int32, device=self.device)
+        nbytes = self.lib.sb_ep_pack_workspace_bytes(n, K, world)
+        ws = self._ep_ws(nbytes)
+        rc = self.lib.sb_ep_pack(top_idx.data_ptr(), top_w.data_ptr(), msgs.data_ptr(), self.dims.act_dtype, n, H,
+                                 K, E, world, cap, send_x.data_ptr(), send_idx.data_ptr(), send_w.data_ptr(),
+                                 ret_pos.data_ptr(), ws.data_ptr(), ws.numel(), _stream_ptr(stream))
+        L.check(rc, "sb_ep_pack")
+        return send_x, send_idx, send_w, ret_pos
+
+    def _ep_ws(self, nbytes: int) -> torch.Tensor:
+        ws = getattr(self, "_epws", None)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+            self._epws = ws
+        return ws
 
     def make_taps(self, n: int) -> dict:
         cfg = self.cfg

@@ -1,0 +1,135 @@
+"""Token-sharded expert parallelism for the recurrent Spider-MoE block.
+
+Every rank holds its own batch of tokens and the block's dense weights
+(router, edge generator, edge values, LayerNorm); the experts are sharded the
+reference's way, rank ``r`` owning the experts ``e % world == r``
+(spider_moe/expert_parallel.py:29-30).  One loop on a rank:
+
+1. route: router, edge graph and messages of its own tokens (sb_block_route);
+2. pack: each token's message row once per owner of one of its experts, into a
+   fixed-capacity buffer [world, cap, H] with the owner's local expert ids and
+   routing weights (sb_ep_pack; cap = tokens per rank, so no host round trip
+   is needed to size the exchange);
+3. all-to-all of rows, ids and weights (NCCL over NVLink);
+4. experts: the owner runs its local experts on the received rows and sums
+   each row's weighted outputs (sb_expert_delta);
+5. all-to-all back;
+6. epilogue: per token, the sum of the rows returned by its owners is the
+   expert delta, then LayerNorm(h + 0.5 delta + 0.1 x0) (sb_combine_ln).
+
+The reference instead replicates all tokens on every rank and all-reduces the
+full delta (expert_parallel.py:33-37); ``SpiderMoELayer`` keeps that contract,
+this module is the sharded path measured by ``bench.py --gpus N``.
+
+The loop is written against an ``ops`` object (route / pack / experts /
+epilogue) so that the exchange logic itself can be checked on CPU ranks with
+the gloo backend; ``CudaOps`` is the implementation that runs the kernels.
+"""
+from __future__ import annotations
+
+import dataclasses
+
+import torch
+import torch.distributed as dist
+
+from .config import from_any
+from .engine import BlockEngine
+
+
+def local_expert_ids(num_experts: int, rank: int, world: int) -> list[int]:
+    return [e for e in range(num_experts) if e % world == rank]
+
+
+def local_expert_state(state: dict, num_experts: int, rank: int, world: int) -> dict:
+    """The rank's experts renamed to local ids j (global id rank + world*j)."""
+    out = {}
+    for j, e in enumerate(local_expert_ids(num_experts, rank, world)):
+        for pre in ("experts", "expert_gates"):
+            for k, v in state.items():
+                head = f"{pre}.{e}."
+                if k.startswith(head):
+                    out[f"{pre}.{j}." + k[len(head):]] = v
+    return out
+
+
+class CudaOps:
+    """The EP loop's compute steps on one GPU (libspider_b200)."""
+
+    def __init__(self, dense: BlockEngine, local: BlockEngine | None, world: int):
+        self.dense, self.local, self.world = dense, local, world
+
+    def route(self, h, loop_idx):
+        return self.dense.route(h, loop_idx)
+
+    def pack(self, top_idx, top_w, msgs, cap):
+        return self.dense.ep_pack(top_idx, top_w, msgs, self.world, cap)
+
+    def experts(self, rows, ids, weights):
+        n = rows.shape[0] * rows.shape[1]
+        H = rows.shape[-1]
+        if self.local is None:
+            return torch.zeros(rows.shape[0], rows.shape[1], H, dtype=torch.float32, device=rows.device)
+        out = self.local.expert_delta(rows.reshape(n, H), ids.reshape(n, -1), weights.reshape(n, -1), 0, 1)
+        return out.view(rows.shape[0], rows.shape[1], H)
+
+    def epilogue(self, ret, ret_pos, h, x0):
+        return self.dense.epilogue(ret.reshape(-1, ret.shape[-1]), ret_pos, h, x0)
+
+
+def ep_loop(ops, h, x0, loop_idx: int, world: int, cap: int, group=None):
+    """One loop of the token-sharded block on this rank (see the module docstring)."""
+    msgs, top_idx, top_w = ops.route(h, loop_idx)
+    send_x, send_idx, send_w, ret_pos = ops.pack(top_idx, top_w, msgs, cap)
+    if world > 1:
+        recv_x, recv_idx, recv_w = (torch.empty_like(t) for t in (send_x, send_idx, send_w))
+        dist.all_to_all_single(recv_x, send_x, group=group)
+        dist.all_to_all_single(recv_idx, send_idx, group=group)
+        dist.all_to_all_single(recv_w, send_w, group=group)
+    else:
+        recv_x, recv_idx, recv_w = send_x, send_idx, send_w
+    rows = ops.experts(recv_x, recv_idx, recv_w)
+    if world > 1:
+        ret = torch.empty_like(rows)
+        dist.all_to_all_single(ret, rows, group=group)
+    else:
+        ret = rows
+    return ops.epilogue(ret, ret_pos, h, x0)
+
+
+class ExpertParallelBlock:
+    """The block on one rank of a token-sharded expert-parallel group."""
+
+    def __init__(self, cfg, state: dict, device, group=None, act_dtype=torch.bfloat16, max_tokens: int = 64,
+                 weight_format: str | None = None, engine: str = "auto"):
+        self.cfg = from_any(cfg)
+        self.group = group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        E = self.cfg.num_experts
+        dense_state = {k: v for k, v in state.items() if not k.startswith(("experts.", "expert_gates."))}
+        self.dense = BlockEngine(self.cfg, dense_state, device, act_dtype=act_dtype, max_tokens=max_tokens,
+                                 weight_format="bf16" if act_dtype == torch.bfloat16 else "native", engine=engine)
+        ids = local_expert_ids(E, self.rank, self.world)
+        self.local = None
+        if ids:
+            lcfg = dataclasses.replace(self.cfg, num_experts=len(ids))
+            self.local = BlockEngine(lcfg, local_expert_state(state, E, self.rank, self.world), device,
+                                     act_dtype=act_dtype, max_tokens=1, weight_format=weight_format, engine=engine)
+        self.ops = CudaOps(self.dense, self.local, self.world)
+        self.max_tokens = max_tokens
+
+    def loop(self, h, x0, loop_idx: int):
+        """One loop; every rank must call it (the exchange is collective).  The
+        exchange capacity is max_tokens on every rank, so ranks may hold
+        different token counts up to that."""
+        n = h.numel() // self.cfg.hidden_size
+        if n > self.max_tokens:
+            raise ValueError(f"{n} tokens exceed max_tokens={self.max_tokens} of the expert-parallel block")
+        return ep_loop(self.ops, h.reshape(n, -1), x0.reshape(n, -1), loop_idx, self.world, self.max_tokens,
+                       self.group).view(h.shape)
+
+    def forward(self, h, x0, loop_begin: int = 0, loop_end: int | None = None):
+        loop_end = self.cfg.num_loops if loop_end is None else loop_end
+        for l in range(loop_begin, loop_end):
+            h = self.loop(h, x0, l)
+        return h

@@ -1,0 +1,60 @@
+"""Two-or-more-GPU check of the token-sharded expert-parallel block (run by torchrun).
+
+Each rank holds its own slice of the tokens; experts are owned by e % world.
+Loop by loop (same input to both), the rank's EP output must match a full
+single-GPU block on the same tokens: routing identical, h_out within the bf16
+tolerance.  Exits non-zero on a mismatch.
+"""
+import datetime
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from spider_web_moe_b200 import synth  # noqa: E402
+from spider_web_moe_b200.config import ModelConfig, benchmark_configs  # noqa: E402
+from spider_web_moe_b200.engine import BlockEngine  # noqa: E402
+from spider_web_moe_b200.ep import ExpertParallelBlock  # noqa: E402
+
+
+def main():
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", local)
+    name = os.environ.get("EP_CONFIG", "cfg2")
+    spec = benchmark_configs()[name]
+    cfg = ModelConfig(**spec["model"]).validate()
+    n = 48
+    sd = synth.synthetic_state_dict(cfg, seed=31, device=dev, zipf=1.1 if spec["zipf"] else None, round_bf16=True)
+    ep = ExpertParallelBlock(cfg, sd, dev, act_dtype=torch.bfloat16, max_tokens=n, weight_format=spec["wfmt"])
+    full = BlockEngine(cfg, sd, dev, act_dtype=torch.bfloat16, max_tokens=n, weight_format=spec["wfmt"])
+    h, _ = synth.block_inputs(n * world, cfg.hidden_size, seed=32, device=dev, dtype=torch.bfloat16)
+    h = h.view(-1, cfg.hidden_size)[rank * n:(rank + 1) * n].contiguous()
+    x0 = h.clone()
+    worst = 0.0
+    ok = True
+    for l in range(cfg.num_loops):
+        out_ep = ep.loop(h, x0, l)
+        out_full = full.forward(h, x0, l, l + 1)
+        torch.cuda.synchronize()
+        num = (out_ep.float() - out_full.float()).abs().amax(-1)
+        den = out_full.float().abs().amax(-1).clamp_min(1e-30)
+        err = float((num / den).max())
+        worst = max(worst, err)
+        ok &= err < 2e-2
+        h = out_full
+    full.check_status()
+    print(f"rank {rank}/{world} {name}: worst relative error {worst:.3e} {'ok' if ok else 'MISMATCH'}", flush=True)
+    flag = torch.tensor([0 if ok else 1], device=dev)
+    dist.all_reduce(flag)
+    dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(0 if int(flag.item()) == 0 else 1)
+
+
+if __name__ == "__main__":
+    main()

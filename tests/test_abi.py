@@ -44,8 +44,12 @@ def test_argument_validation_without_device():
     assert lib.sb_grouped_gemm(None, None) == L.SB_ERR_ARG
     a = L.GemmArgs()
     assert lib.sb_grouped_gemm(C.byref(a), None) == L.SB_ERR_ARG
-    d = L.BlockDims(hidden=64, num_experts=4, top_k=5, edges_per_expert=2, ffn=128, num_loops=2)
-    assert lib.sb_block_workspace_bytes(C.byref(d)) == 0  # top_k > num_experts
+    d = L.BlockDims(hidden=60, num_experts=4, top_k=2, edges_per_expert=2, ffn=128, num_loops=2)
+    assert lib.sb_block_workspace_bytes(C.byref(d)) == 0  # hidden not a multiple of 8
+    d.hidden = 64
+    d.top_k = 5  # routing needs top_k <= num_experts: rejected before any launch
+    wts = L.BlockWeights()
+    assert lib.sb_block_forward(C.byref(d), C.byref(wts), None, None, None, 4, 0, 1, None, 0, None, None) == L.SB_ERR_ARG
     d.top_k = 2
     d.max_tokens = 64
     assert lib.sb_block_workspace_bytes(C.byref(d)) > 0

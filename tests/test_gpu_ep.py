@@ -1,0 +1,58 @@
+"""Token-sharded expert-parallel block on the GPU.
+
+On one GPU the EP path (route, pack, owner-side experts, combine) runs with a
+world of one and must match the full block loop by loop.  With two or more
+GPUs, tests/ep_worker.py runs under torchrun (NCCL) and checks every rank
+against a full single-GPU block on its own tokens.
+"""
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+import torch
+
+from spider_web_moe_b200 import synth
+from spider_web_moe_b200.config import ModelConfig, benchmark_configs
+from spider_web_moe_b200.engine import BlockEngine
+from spider_web_moe_b200.ep import ExpertParallelBlock
+
+from helpers import rel_err
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+@pytest.mark.parametrize("name", ["cfg2", "cfg5"])
+def test_ep_path_single_gpu_matches_block(name, cuda_device):
+    spec = benchmark_configs()[name]
+    cfg = ModelConfig(**spec["model"]).validate()
+    n = 40
+    sd = synth.synthetic_state_dict(cfg, seed=41, device=cuda_device, zipf=1.1 if spec["zipf"] else None,
+                                    round_bf16=True)
+    ep = ExpertParallelBlock(cfg, sd, cuda_device, act_dtype=torch.bfloat16, max_tokens=n, weight_format=spec["wfmt"])
+    full = BlockEngine(cfg, sd, cuda_device, act_dtype=torch.bfloat16, max_tokens=n, weight_format=spec["wfmt"])
+    h, _ = synth.block_inputs(n, cfg.hidden_size, seed=42, device=cuda_device, dtype=torch.bfloat16)
+    h = h.view(n, -1)
+    for l in range(cfg.num_loops):
+        a = ep.loop(h, h, l)
+        b = full.forward(h, h, l, l + 1)
+        torch.cuda.synchronize()
+        assert rel_err(a, b) < 2e-2, f"loop {l}"
+        h = b
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_ep_two_gpus_nccl():
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={free_port()}", os.path.join(HERE, "ep_worker.py")]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600,
+                       env=dict(os.environ, NCCL_NVLS_ENABLE="0"))
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
