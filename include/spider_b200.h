@@ -279,17 +279,26 @@ SB_API int sb_block_route(const sb_block_dims* dims, const sb_block_weights* w, 
                           void* workspace, size_t workspace_bytes, void* stream);
 
 /* Dispatch packing (no reference counterpart; the reference all-reduces the
- * full delta instead, expert_parallel.py:33-37).  send_x [world, cap, hidden]
- * (act dtype), send_idx / send_w [world, cap, K]: row (q, j) is the j-th token
- * (ascending) that owner q must see; send_idx holds q's local expert id per
- * slot (-1: not q's expert or unused row).  ret_pos [n, K]: position q*cap + j
- * of the returned combined row for the first slot of each owner, else -1.
- * cap >= n_tokens. */
+ * full delta instead, expert_parallel.py:33-37).  send [world, cap] rows of
+ * sb_ep_row_pitch() bytes: [message row (hidden x act dtype) | K int32 | K fp32].
+ * Row (q, j) is the j-th token (ascending) that owner q must see, with q's
+ * local expert id per slot (-1: not q's expert, or an unused row) and the
+ * routing weight.  ret_pos [n, K]: position q*cap + j of the returned combined
+ * row for the first slot of each owner, else -1.  cap >= n_tokens. */
+SB_API size_t sb_ep_row_pitch(int hidden, int act_dtype, int top_k);
 SB_API size_t sb_ep_pack_workspace_bytes(int n_tokens, int top_k, int world);
 SB_API int sb_ep_pack(const int32_t* top_idx, const float* top_w, const void* messages, int act_dtype,
-                      int n_tokens, int hidden, int top_k, int num_experts, int world, int cap, void* send_x,
-                      int32_t* send_idx, float* send_w, int32_t* ret_pos, void* workspace,
-                      size_t workspace_bytes, void* stream);
+                      int n_tokens, int hidden, int top_k, int num_experts, int world, int cap, void* send,
+                      int32_t* ret_pos, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Owner side: rows in the packed layout above (n_rows of row_pitch bytes, ids
+ * are local expert ids in [0, dims->num_experts)); out[r] = sum over the row's
+ * slots of w * ffn_id(row message), fp32 [n_rows, hidden].  The expert part of
+ * sparse_expert_delta (sparse_experts.py:51-63) for received rows. */
+SB_API size_t sb_expert_rows_workspace_bytes(const sb_block_dims* dims, int n_rows);
+SB_API int sb_expert_rows(const sb_block_dims* dims, const sb_block_weights* w, const void* rows,
+                          int64_t row_pitch, int n_rows, float* out, void* workspace, size_t workspace_bytes,
+                          void* stream);
 
 /* Byte offset of the device status word inside every workspace above. */
 SB_API size_t sb_status_offset(void);

@@ -106,6 +106,20 @@ struct StageScope {
   }
 };
 
+// Packed expert-parallel rows -> contiguous local ids (out of range -> -1) and weights.
+__global__ void unpack_meta_kernel(const uint8_t* __restrict__ rows, int64_t pitch, int64_t meta_off, int n, int K,
+                                   int G, int32_t* __restrict__ ids, float* __restrict__ w) {
+  pdl_wait();
+  pdl_trigger();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n * K; i += gridDim.x * blockDim.x) {
+    const int r = i / K, k = i - r * K;
+    const uint8_t* m = rows + static_cast<int64_t>(r) * pitch + meta_off;
+    const int e = reinterpret_cast<const int32_t*>(m)[k];
+    ids[i] = (e >= 0 && e < G) ? e : -1;
+    w[i] = reinterpret_cast<const float*>(m + static_cast<int64_t>(K) * 4)[k];
+  }
+}
+
 // ------------------------------------------------------------------ workspace layout
 
 struct BlockBuffers {
@@ -516,11 +530,81 @@ static size_t carve_delta(const sb_block_dims& d, int n, void* base, size_t size
   b->ffn_w = c.take<float>(N * K);
   b->ffn_inv = c.take<int32_t>(N * K);
   b->x_ffn = c.take<char>(N * K * H * as);
+  b->msg_act = c.take<char>(N * H * as);
   b->act = c.take<char>(N * K * U * as);
   b->y_ffn = c.take<float>(4 * N * K * H);
   b->group_ws_bytes = sb_group_workspace_bytes(static_cast<int>(N), static_cast<int>(K), static_cast<int>(E));
   b->group_ws = c.take<char>(b->group_ws_bytes);
   return c.overflow ? static_cast<size_t>(-1) : align_up(c.used, 256);
+}
+
+extern "C" SB_API size_t sb_expert_rows_workspace_bytes(const sb_block_dims* dims, int n_rows) {
+  if (check_dims(dims) != SB_OK || n_rows < 0) return 0;
+  BlockBuffers b;
+  return carve_delta(*dims, n_rows > 0 ? n_rows : 1, nullptr, ~size_t(0) >> 1, &b) +
+         align_up(static_cast<size_t>(n_rows > 0 ? n_rows : 1) * dims->top_k * 4, 256);
+}
+
+extern "C" SB_API int sb_expert_rows(const sb_block_dims* dims, const sb_block_weights* w, const void* rows,
+                                     int64_t row_pitch, int n_rows, float* out, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  int rc = check_dims(dims);
+  if (rc) return rc;
+  const sb_block_dims& d = *dims;
+  const int es = d.act_dtype == SB_F32 ? 4 : 2;
+  const int64_t meta_off = static_cast<int64_t>(d.hidden) * es;
+  if (check_block_args(d, w, true, false) || n_rows < 0 || row_pitch % 16 ||
+      row_pitch < meta_off + 8LL * d.top_k)
+    return SB_ERR_ARG;
+  if (n_rows == 0) return SB_OK;
+  if (!rows || !out) return SB_ERR_ARG;
+  BlockBuffers b;
+  const size_t need = carve_delta(d, n_rows, workspace, workspace_bytes, &b);
+  const size_t wbytes = align_up(static_cast<size_t>(n_rows) * d.top_k * 4, 256);
+  if (!workspace || need == static_cast<size_t>(-1) || workspace_bytes < need + wbytes) return SB_ERR_WORKSPACE;
+  float* top_w = reinterpret_cast<float*>(static_cast<char*>(workspace) + need);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int N = n_rows, H = d.hidden, K = d.top_k, U = d.ffn, G = d.num_experts;
+  const int ldx = static_cast<int>(row_pitch / es);
+#define SB_TRY(x) do { rc = (x); if (rc) return rc; } while (0)
+  SB_TRY(launch(unpack_meta_kernel, dim3((N * K + 255) / 256), dim3(256), 0, st, static_cast<const uint8_t*>(rows),
+                row_pitch, meta_off, N, K, G, b.top_idx, top_w));
+  SB_TRY(sb_group(b.top_idx, top_w, N, K, G, SB_GROUP_POSITIVE_ONLY, b.ffn_off, b.ffn_row, b.ffn_slot, b.ffn_w,
+                  b.ffn_inv, b.group_ws, b.group_ws_bytes, st));
+  {
+    sb_grouped_gemm_args a;
+    fill_expert_gemm(a, d, true, w->w_up, w->s_up, w->b_up, w->w_gate, w->s_gate, w->b_gate);
+    a.epilogue = d.activation == SB_ACT_SWIGLU ? SB_EPI_SWIGLU : SB_EPI_GELU;
+    a.num_groups = G; a.x = b.x_ffn; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N;
+    a.offsets = b.ffn_off; a.out = b.act; a.ldo = U; a.splits = 1; a.status = b.status;
+    sb_grouped_gemm_args g = a;
+    g.x = rows; g.ldx = ldx; g.x_row_index = b.ffn_row; g.x_rows = N;
+    if (gemm_gathers(g, d.engine)) {
+      a = g;
+    } else {
+      // materialise the message rows (first hidden columns of each packed row), then in expert order
+      SB_TRY(cuda_status(cudaMemcpy2DAsync(b.msg_act, static_cast<size_t>(H) * es, rows, row_pitch,
+                                           static_cast<size_t>(H) * es, N, cudaMemcpyDeviceToDevice, st)));
+      SB_TRY(sb_gather_rows(b.msg_act, d.act_dtype, H, b.ffn_row, b.ffn_off, G, N * K, b.x_ffn, st));
+    }
+    SB_TRY(run_gemm(a, d.engine, st));
+  }
+  int splits = 1;
+  {
+    sb_grouped_gemm_args a;
+    fill_expert_gemm(a, d, false, w->w_down, w->s_down, w->b_down, nullptr, nullptr, nullptr);
+    a.epilogue = SB_EPI_LINEAR;
+    a.num_groups = G; a.x = b.act; a.ldx = U; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N;
+    a.offsets = b.ffn_off; a.row_scale = b.ffn_w;
+    splits = pick_splits(H, U, N * K, G, 4, d.engine != SB_ENGINE_SIMT, N);
+    a.splits = splits; a.split_stride = static_cast<int64_t>(N) * K * H;
+    a.out = b.y_ffn; a.ldo = H; a.status = b.status;
+    SB_TRY(run_gemm(a, d.engine, st));
+  }
+  SB_TRY(sb_combine_rows(b.y_ffn, H, splits, static_cast<int64_t>(N) * K * H, b.ffn_inv, K, N, H, out, nullptr, 0,
+                         nullptr, d.act_dtype, st));
+#undef SB_TRY
+  return SB_OK;
 }
 
 extern "C" SB_API size_t sb_expert_delta_workspace_bytes(const sb_block_dims* dims, int n_tokens) {

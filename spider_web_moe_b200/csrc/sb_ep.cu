@@ -25,24 +25,27 @@ ep_owner_kernel(const int32_t* __restrict__ top_idx, int n, int E, int world, in
   }
 }
 
+// Packed send row: [message row: H x act dtype | K int32 local ids | K fp32 weights | pad],
+// row_pitch bytes (a multiple of 16).
 template <typename T>
 __global__ void __launch_bounds__(256)
 ep_pack_kernel(const T* __restrict__ msgs, const int32_t* __restrict__ top_idx, const float* __restrict__ top_w,
-               int n_tokens, int K, int E, int world, int cap, int H, const int32_t* __restrict__ off,
-               const int32_t* __restrict__ prow, const int32_t* __restrict__ owner, const int32_t* __restrict__ inv,
-               T* __restrict__ send_x, int32_t* __restrict__ send_idx, float* __restrict__ send_w,
-               int32_t* __restrict__ ret_pos) {
+               int n_tokens, int K, int E, int world, int cap, int H, int64_t row_pitch,
+               const int32_t* __restrict__ off, const int32_t* __restrict__ prow, const int32_t* __restrict__ owner,
+               const int32_t* __restrict__ inv, uint8_t* __restrict__ send, int32_t* __restrict__ ret_pos) {
   pdl_wait();
   pdl_trigger();
   const int warps = (gridDim.x * blockDim.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int vec = H * static_cast<int>(sizeof(T)) / 16;
+  const int64_t meta = static_cast<int64_t>(H) * sizeof(T);
   // send rows, one warp per row
   for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < world * cap; row += warps) {
     const int q = row / cap, j = row - q * cap;
     const int cnt = off[q + 1] - off[q];
     int t = -1;
     if (j < cnt) t = prow[off[q] + j];
+    uint8_t* dst_row = send + static_cast<int64_t>(row) * row_pitch;
     if (lane < K) {
       int lid = -1;
       float wk = 0.f;
@@ -51,12 +54,12 @@ ep_pack_kernel(const T* __restrict__ msgs, const int32_t* __restrict__ top_idx, 
         if (e >= 0 && e < E && e % world == q) lid = e / world;
         wk = top_w[static_cast<int64_t>(t) * K + lane];
       }
-      send_idx[static_cast<int64_t>(row) * K + lane] = lid;
-      send_w[static_cast<int64_t>(row) * K + lane] = wk;
+      reinterpret_cast<int32_t*>(dst_row + meta)[lane] = lid;
+      reinterpret_cast<float*>(dst_row + meta + K * 4)[lane] = wk;
     }
     if (t >= 0) {
       const uint4* src = reinterpret_cast<const uint4*>(msgs + static_cast<int64_t>(t) * H);
-      uint4* dst = reinterpret_cast<uint4*>(send_x + static_cast<int64_t>(row) * H);
+      uint4* dst = reinterpret_cast<uint4*>(dst_row);
       for (int v = lane; v < vec; v += 32) dst[v] = src[v];
     }
   }
@@ -100,17 +103,21 @@ extern "C" SB_API size_t sb_ep_pack_workspace_bytes(int n_tokens, int top_k, int
   return carve_ep(n_tokens > 0 ? n_tokens : 1, top_k, world, nullptr, ~size_t(0) >> 1, &b);
 }
 
+extern "C" SB_API size_t sb_ep_row_pitch(int hidden, int act_dtype, int top_k) {
+  const size_t es = act_dtype == SB_F32 ? 4 : 2;
+  return align_up(static_cast<size_t>(hidden) * es + static_cast<size_t>(top_k) * 8, 16);
+}
+
 extern "C" SB_API int sb_ep_pack(const int32_t* top_idx, const float* top_w, const void* messages, int act_dtype,
                                  int n_tokens, int hidden, int top_k, int num_experts, int world, int cap,
-                                 void* send_x, int32_t* send_idx, float* send_w, int32_t* ret_pos, void* workspace,
-                                 size_t workspace_bytes, void* stream) {
+                                 void* send, int32_t* ret_pos, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
   const int esize = act_dtype == SB_F32 ? 4 : (act_dtype == SB_BF16 ? 2 : 0);
   if (n_tokens < 0 || hidden <= 0 || !esize || (hidden * esize) % 16 || top_k <= 0 || top_k > 32 ||
       num_experts <= 0 || world <= 0 || world > 256 || cap < n_tokens || cap <= 0)
     return SB_ERR_ARG;
   if (world * static_cast<int64_t>(cap) > 0x7fffffff) return SB_ERR_UNSUPPORTED;
-  if (!send_x || !send_idx || !send_w || (n_tokens > 0 && (!top_idx || !top_w || !messages || !ret_pos)))
-    return SB_ERR_ARG;
+  if (!send || (n_tokens > 0 && (!top_idx || !top_w || !messages || !ret_pos))) return SB_ERR_ARG;
   EpBuffers b;
   const size_t need = carve_ep(n_tokens, top_k, world, workspace, workspace_bytes, &b);
   if (!workspace || need == static_cast<size_t>(-1) || workspace_bytes < need) return SB_ERR_WORKSPACE;
@@ -127,6 +134,7 @@ extern "C" SB_API int sb_ep_pack(const int32_t* top_idx, const float* top_w, con
     rc = cuda_status(cudaMemsetAsync(b.off, 0, sizeof(int32_t) * (world + 1), st));
   }
   if (rc) return rc;
+  const int64_t pitch = static_cast<int64_t>(sb_ep_row_pitch(hidden, act_dtype, top_k));
   const int rows = world * cap;
   int blocks = (rows * 32 + 255) / 256;
   const int lim = 4 * current_sm_count();
@@ -134,11 +142,11 @@ extern "C" SB_API int sb_ep_pack(const int32_t* top_idx, const float* top_w, con
   if (act_dtype == SB_BF16)
     return launch(ep_pack_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st,
                   static_cast<const __nv_bfloat16*>(messages), top_idx, top_w, n_tokens, top_k, num_experts, world,
-                  cap, hidden, static_cast<const int32_t*>(b.off), static_cast<const int32_t*>(b.prow),
+                  cap, hidden, pitch, static_cast<const int32_t*>(b.off), static_cast<const int32_t*>(b.prow),
                   static_cast<const int32_t*>(b.owner), static_cast<const int32_t*>(b.inv),
-                  static_cast<__nv_bfloat16*>(send_x), send_idx, send_w, ret_pos);
+                  static_cast<uint8_t*>(send), ret_pos);
   return launch(ep_pack_kernel<float>, dim3(blocks), dim3(256), 0, st, static_cast<const float*>(messages), top_idx,
-                top_w, n_tokens, top_k, num_experts, world, cap, hidden, static_cast<const int32_t*>(b.off),
+                top_w, n_tokens, top_k, num_experts, world, cap, hidden, pitch, static_cast<const int32_t*>(b.off),
                 static_cast<const int32_t*>(b.prow), static_cast<const int32_t*>(b.owner),
-                static_cast<const int32_t*>(b.inv), static_cast<float*>(send_x), send_idx, send_w, ret_pos);
+                static_cast<const int32_t*>(b.inv), static_cast<uint8_t*>(send), ret_pos);
 }

@@ -220,20 +220,34 @@ class BlockEngine:
         return out.view(h.shape)
 
     def ep_pack(self, top_idx, top_w, msgs, world: int, cap: int, stream=None):
-        """Per-owner send buffers for the all-to-all (sb_ep_pack)."""
+        """Packed per-owner send rows for the all-to-all (sb_ep_pack): a uint8
+        tensor [world, cap, pitch] and the return positions [n, K]."""
         H, K, E = self.cfg.hidden_size, self.cfg.top_k, self.cfg.num_experts
         n = msgs.shape[0]
-        send_x = torch.empty((world, cap, H), dtype=self.act_dtype, device=self.device)
-        send_idx = torch.empty((world, cap, K), dtype=torch.int32, device=self.device)
-        send_w = torch.empty((world, cap, K), dtype=torch.float32, device=self.device)
+        pitch = self.lib.sb_ep_row_pitch(H, self.dims.act_dtype, K)
+        send = torch.empty((world, cap, pitch), dtype=torch.uint8, device=self.device)
         ret_pos = torch.empty((n, K), dtype=torch.int32, device=self.device)
         nbytes = self.lib.sb_ep_pack_workspace_bytes(n, K, world)
         ws = self._ep_ws(nbytes)
         rc = self.lib.sb_ep_pack(top_idx.data_ptr(), top_w.data_ptr(), msgs.data_ptr(), self.dims.act_dtype, n, H,
-                                 K, E, world, cap, send_x.data_ptr(), send_idx.data_ptr(), send_w.data_ptr(),
-                                 ret_pos.data_ptr(), ws.data_ptr(), ws.numel(), _stream_ptr(stream))
+                                 K, E, world, cap, send.data_ptr(), ret_pos.data_ptr(), ws.data_ptr(), ws.numel(),
+                                 _stream_ptr(stream))
         L.check(rc, "sb_ep_pack")
-        return send_x, send_idx, send_w, ret_pos
+        return send, ret_pos
+
+    def expert_rows(self, rows: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """Owner side: packed rows [R, pitch] (uint8) -> fp32 [R, H] weighted sums of this
+        engine's (local) experts (sb_expert_rows)."""
+        H = self.cfg.hidden_size
+        r, pitch = rows.shape[0], rows.shape[-1]
+        if out is None:
+            out = torch.empty((r, H), dtype=torch.float32, device=self.device)
+        nbytes = self.lib.sb_expert_rows_workspace_bytes(C.byref(self.dims), r)
+        ws = self._delta_ws(nbytes)
+        rc = self.lib.sb_expert_rows(C.byref(self.dims), C.byref(self.weights), rows.data_ptr(), pitch, r,
+                                     out.data_ptr(), ws.data_ptr(), ws.numel(), _stream_ptr(stream))
+        L.check(rc, "sb_expert_rows")
+        return out
 
     def _ep_ws(self, nbytes: int) -> torch.Tensor:
         ws = getattr(self, "_epws", None)

@@ -7,12 +7,12 @@ reference's way, rank ``r`` owning the experts ``e % world == r``
 
 1. route: router, edge graph and messages of its own tokens (sb_block_route);
 2. pack: each token's message row once per owner of one of its experts, into a
-   fixed-capacity buffer [world, cap, H] with the owner's local expert ids and
-   routing weights (sb_ep_pack; cap = tokens per rank, so no host round trip
-   is needed to size the exchange);
-3. all-to-all of rows, ids and weights (NCCL over NVLink);
+   fixed-capacity buffer [world, cap] of packed rows (message, the owner's local
+   expert ids, routing weights; sb_ep_pack; cap = the agreed tokens per rank,
+   so no host round trip is needed to size the exchange);
+3. all-to-all of the packed rows (NCCL over NVLink);
 4. experts: the owner runs its local experts on the received rows and sums
-   each row's weighted outputs (sb_expert_delta);
+   each row's weighted outputs (sb_expert_rows);
 5. all-to-all back;
 6. epilogue: per token, the sum of the rows returned by its owners is the
    expert delta, then LayerNorm(h + 0.5 delta + 0.1 x0) (sb_combine_ln).
@@ -64,30 +64,28 @@ class CudaOps:
     def pack(self, top_idx, top_w, msgs, cap):
         return self.dense.ep_pack(top_idx, top_w, msgs, self.world, cap)
 
-    def experts(self, rows, ids, weights):
-        n = rows.shape[0] * rows.shape[1]
-        H = rows.shape[-1]
+    def experts(self, rows):
+        W, cap, pitch = rows.shape
+        H = self.dense.cfg.hidden_size
         if self.local is None:
-            return torch.zeros(rows.shape[0], rows.shape[1], H, dtype=torch.float32, device=rows.device)
-        out = self.local.expert_delta(rows.reshape(n, H), ids.reshape(n, -1), weights.reshape(n, -1), 0, 1)
-        return out.view(rows.shape[0], rows.shape[1], H)
+            return torch.zeros(W, cap, H, dtype=torch.float32, device=rows.device)
+        return self.local.expert_rows(rows.view(W * cap, pitch)).view(W, cap, H)
 
     def epilogue(self, ret, ret_pos, h, x0):
         return self.dense.epilogue(ret.reshape(-1, ret.shape[-1]), ret_pos, h, x0)
 
 
 def ep_loop(ops, h, x0, loop_idx: int, world: int, cap: int, group=None):
-    """One loop of the token-sharded block on this rank (see the module docstring)."""
+    """One loop of the token-sharded block on this rank (see the module docstring).
+    Two collectives: the packed dispatch rows out, the owners' combined rows back."""
     msgs, top_idx, top_w = ops.route(h, loop_idx)
-    send_x, send_idx, send_w, ret_pos = ops.pack(top_idx, top_w, msgs, cap)
+    send, ret_pos = ops.pack(top_idx, top_w, msgs, cap)
     if world > 1:
-        recv_x, recv_idx, recv_w = (torch.empty_like(t) for t in (send_x, send_idx, send_w))
-        dist.all_to_all_single(recv_x, send_x, group=group)
-        dist.all_to_all_single(recv_idx, send_idx, group=group)
-        dist.all_to_all_single(recv_w, send_w, group=group)
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=group)
     else:
-        recv_x, recv_idx, recv_w = send_x, send_idx, send_w
-    rows = ops.experts(recv_x, recv_idx, recv_w)
+        recv = send
+    rows = ops.experts(recv)
     if world > 1:
         ret = torch.empty_like(rows)
         dist.all_to_all_single(ret, rows, group=group)
@@ -133,3 +131,37 @@ class ExpertParallelBlock:
         for l in range(loop_begin, loop_end):
             h = self.loop(h, x0, l)
         return h
+
+    # ------------------------------------------------------------------ CUDA graph
+    def capture(self, n_tokens: int):
+        """Capture all loops (kernels and the NCCL exchanges) of one step for a fixed
+        token count in one CUDA graph.  Every rank must call it.  Release the graph
+        (``release_graph``) before destroying the process group."""
+        H = self.cfg.hidden_size
+        dev = self.dense.device
+        dt = self.dense.act_dtype
+        self.g_h = torch.zeros(n_tokens, H, dtype=dt, device=dev)
+        self.g_x0 = torch.zeros(n_tokens, H, dtype=dt, device=dev)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):  # sizes every workspace and warms the communicator up
+                self.g_out = self.forward(self.g_h, self.g_x0)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.g_out = self.forward(self.g_h, self.g_x0)
+        torch.cuda.synchronize(dev)
+
+    def replay(self, h=None, x0=None):
+        if h is not None:
+            self.g_h.copy_(h.reshape(self.g_h.shape), non_blocking=True)
+        if x0 is not None:
+            self.g_x0.copy_(x0.reshape(self.g_x0.shape), non_blocking=True)
+        self.graph.replay()
+        return self.g_out
+
+    def release_graph(self):
+        self.graph = None
+

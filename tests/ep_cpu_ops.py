@@ -46,11 +46,16 @@ class CpuOps:
                     send_idx[q, j, kk] = e // W if e % W == q else -1
                     send_w[q, j, kk] = top_w[t, kk]
                 ret_pos[t, k] = q * cap + j
-        return send_x, send_idx, send_w, ret_pos
+        # one packed fp32 tensor per row: [message | ids | weights], as the device layout
+        packed = torch.cat([send_x, send_idx.float(), send_w], dim=-1)
+        return packed, ret_pos
 
-    def experts(self, rows, ids, weights):
+    def experts(self, packed):
         p = self.p
-        W, cap, H = rows.shape
+        K = self.cfg.top_k
+        H = packed.shape[-1] - 2 * K
+        rows, ids, weights = packed[..., :H], packed[..., H:H + K].long(), packed[..., H + K:]
+        W, cap, _ = rows.shape
         out = torch.zeros(W, cap, H)
         for q in range(W):
             for j in range(cap):
