@@ -160,7 +160,8 @@ typedef struct sb_grouped_gemm_args {
   int x_rows;
   int max_rows;           /* rows allocated in x / out (upper bound of offsets[G]) */
   int rows_hint;          /* host estimate of offsets[G] (tile shape choice only) */
-  int group_rows_bound;   /* upper bound of any one group's rows, 0 if unknown (tile choice only) */
+  int group_rows_bound;   /* rows per group the tile is planned for: an upper bound, or 0 if unknown
+                             (tile choice only; larger groups are still computed correctly) */
   const int32_t* offsets; /* [G+1] device */
   const float* row_scale; /* [max_rows] per permuted row, SB_EPI_LINEAR only, may be NULL */
   void* out;
@@ -294,11 +295,13 @@ SB_API int sb_ep_pack(const int32_t* top_idx, const float* top_w, const void* me
 /* Owner side: rows in the packed layout above (n_rows of row_pitch bytes, ids
  * are local expert ids in [0, dims->num_experts)); out[r] = sum over the row's
  * slots of w * ffn_id(row message), fp32 [n_rows, hidden].  The expert part of
- * sparse_expert_delta (sparse_experts.py:51-63) for received rows. */
+ * sparse_expert_delta (sparse_experts.py:51-63) for received rows.
+ * expected_pairs (0: n_rows * K) is the number of (row, expert) pairs the caller
+ * expects -- most received rows are padding -- and only steers tile shapes. */
 SB_API size_t sb_expert_rows_workspace_bytes(const sb_block_dims* dims, int n_rows);
 SB_API int sb_expert_rows(const sb_block_dims* dims, const sb_block_weights* w, const void* rows,
-                          int64_t row_pitch, int n_rows, float* out, void* workspace, size_t workspace_bytes,
-                          void* stream);
+                          int64_t row_pitch, int n_rows, int expected_pairs, float* out, void* workspace,
+                          size_t workspace_bytes, void* stream);
 
 /* Byte offset of the device status word inside every workspace above. */
 SB_API size_t sb_status_offset(void);

@@ -102,7 +102,7 @@ SIGNATURES = {
     "sb_ep_pack_workspace_bytes": (sz, [i32, i32, i32]),
     "sb_ep_pack": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, sz, vp]),
     "sb_expert_rows_workspace_bytes": (sz, [C.POINTER(BlockDims), i32]),
-    "sb_expert_rows": (i32, [C.POINTER(BlockDims), C.POINTER(BlockWeights), vp, i64, i32, vp, vp, sz, vp]),
+    "sb_expert_rows": (i32, [C.POINTER(BlockDims), C.POINTER(BlockWeights), vp, i64, i32, i32, vp, vp, sz, vp]),
     "sb_status_offset": (sz, []),
     "sb_num_stages": (i32, []),
     "sb_stage_name": (C.c_char_p, [i32]),

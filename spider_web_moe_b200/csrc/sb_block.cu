@@ -546,7 +546,7 @@ extern "C" SB_API size_t sb_expert_rows_workspace_bytes(const sb_block_dims* dim
 }
 
 extern "C" SB_API int sb_expert_rows(const sb_block_dims* dims, const sb_block_weights* w, const void* rows,
-                                     int64_t row_pitch, int n_rows, float* out, void* workspace,
+                                     int64_t row_pitch, int n_rows, int expected_pairs, float* out, void* workspace,
                                      size_t workspace_bytes, void* stream) {
   int rc = check_dims(dims);
   if (rc) return rc;
@@ -566,6 +566,11 @@ extern "C" SB_API int sb_expert_rows(const sb_block_dims* dims, const sb_block_w
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int N = n_rows, H = d.hidden, K = d.top_k, U = d.ffn, G = d.num_experts;
   const int ldx = static_cast<int>(row_pitch / es);
+  // Most received rows are padding: tile choices follow the expected real pairs.
+  // When those average at most 32 per expert, a 64-row tile per expert is
+  // planned (an expert with more rows is covered by its CTA looping).
+  const int hint = expected_pairs > 0 ? expected_pairs : N * K;
+  const int row_plan = hint <= 32 * G ? (N < 64 ? N : 64) : N;
 #define SB_TRY(x) do { rc = (x); if (rc) return rc; } while (0)
   SB_TRY(launch(unpack_meta_kernel, dim3((N * K + 255) / 256), dim3(256), 0, st, static_cast<const uint8_t*>(rows),
                 row_pitch, meta_off, N, K, G, b.top_idx, top_w));
@@ -575,7 +580,7 @@ extern "C" SB_API int sb_expert_rows(const sb_block_dims* dims, const sb_block_w
     sb_grouped_gemm_args a;
     fill_expert_gemm(a, d, true, w->w_up, w->s_up, w->b_up, w->w_gate, w->s_gate, w->b_gate);
     a.epilogue = d.activation == SB_ACT_SWIGLU ? SB_EPI_SWIGLU : SB_EPI_GELU;
-    a.num_groups = G; a.x = b.x_ffn; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N;
+    a.num_groups = G; a.x = b.x_ffn; a.ldx = H; a.max_rows = N * K; a.rows_hint = hint; a.group_rows_bound = row_plan;
     a.offsets = b.ffn_off; a.out = b.act; a.ldo = U; a.splits = 1; a.status = b.status;
     sb_grouped_gemm_args g = a;
     g.x = rows; g.ldx = ldx; g.x_row_index = b.ffn_row; g.x_rows = N;
@@ -594,9 +599,9 @@ extern "C" SB_API int sb_expert_rows(const sb_block_dims* dims, const sb_block_w
     sb_grouped_gemm_args a;
     fill_expert_gemm(a, d, false, w->w_down, w->s_down, w->b_down, nullptr, nullptr, nullptr);
     a.epilogue = SB_EPI_LINEAR;
-    a.num_groups = G; a.x = b.act; a.ldx = U; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N;
+    a.num_groups = G; a.x = b.act; a.ldx = U; a.max_rows = N * K; a.rows_hint = hint; a.group_rows_bound = row_plan;
     a.offsets = b.ffn_off; a.row_scale = b.ffn_w;
-    splits = pick_splits(H, U, N * K, G, 4, d.engine != SB_ENGINE_SIMT, N);
+    splits = pick_splits(H, U, hint, G, 4, d.engine != SB_ENGINE_SIMT, row_plan);
     a.splits = splits; a.split_stride = static_cast<int64_t>(N) * K * H;
     a.out = b.y_ffn; a.ldo = H; a.status = b.status;
     SB_TRY(run_gemm(a, d.engine, st));

@@ -508,8 +508,9 @@ static int launch_epi(const sb_grouped_gemm_args& a, cudaStream_t st, int bn) {
   }
 }
 
-// Fixed-group schedule when one tile of <= 64 columns is known to hold every
-// group's rows: each CTA then streams its weights exactly once.
+// Fixed-group schedule when the caller expects every group's rows to fit one
+// tile of <= 64 columns (each CTA then streams its weights once; a group with
+// more rows is still covered: its CTA loops over the row tiles).
 bool tc_fixed_groups(const sb_grouped_gemm_args& a) {
   return a.group_rows_bound > 0 && a.group_rows_bound <= 64;
 }

@@ -235,7 +235,8 @@ class BlockEngine:
         L.check(rc, "sb_ep_pack")
         return send, ret_pos
 
-    def expert_rows(self, rows: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    def expert_rows(self, rows: torch.Tensor, out: torch.Tensor | None = None, expected_pairs: int = 0,
+                    stream=None) -> torch.Tensor:
         """Owner side: packed rows [R, pitch] (uint8) -> fp32 [R, H] weighted sums of this
         engine's (local) experts (sb_expert_rows)."""
         H = self.cfg.hidden_size
@@ -245,7 +246,8 @@ class BlockEngine:
         nbytes = self.lib.sb_expert_rows_workspace_bytes(C.byref(self.dims), r)
         ws = self._delta_ws(nbytes)
         rc = self.lib.sb_expert_rows(C.byref(self.dims), C.byref(self.weights), rows.data_ptr(), pitch, r,
-                                     out.data_ptr(), ws.data_ptr(), ws.numel(), _stream_ptr(stream))
+                                     int(expected_pairs), out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                     _stream_ptr(stream))
         L.check(rc, "sb_expert_rows")
         return out
 

@@ -69,7 +69,9 @@ class CudaOps:
         H = self.dense.cfg.hidden_size
         if self.local is None:
             return torch.zeros(W, cap, H, dtype=torch.float32, device=rows.device)
-        return self.local.expert_rows(rows.view(W * cap, pitch)).view(W, cap, H)
+        # each source rank sends on average cap*K/world (row, expert) pairs per owner
+        expected = cap * self.dense.cfg.top_k
+        return self.local.expert_rows(rows.view(W * cap, pitch), expected_pairs=expected).view(W, cap, H)
 
     def epilogue(self, ret, ret_pos, h, x0):
         return self.dense.epilogue(ret.reshape(-1, ret.shape[-1]), ret_pos, h, x0)

@@ -193,14 +193,17 @@ def test_zero_tokens_is_a_noop(cuda_device):
     assert out.shape == h.shape
 
 
-def test_all_tokens_on_one_expert(cuda_device):
-    """A dominant loop bias sends every token to the same experts (one huge group)."""
+@pytest.mark.parametrize("n", [200, 300])
+def test_all_tokens_on_one_expert(n, cuda_device):
+    """A dominant loop bias sends every token to the same experts (one huge group).
+    With 200 tokens the expected rows per expert stay small, so the hot expert's
+    rows are covered by one CTA looping over several row tiles; with 300 the
+    row tiles are spread over CTAs."""
     cfg = ModelConfig(hidden_size=256, num_heads=4, num_experts=16, top_k=2, edges_per_expert=2,
                       num_loops=1, expert_ffn_size=512).validate()
     sd = synth.synthetic_state_dict(cfg, seed=9, device=cuda_device, round_bf16=True)
     sd["loop_bias"][0, 3] = 40.0
     sd["loop_bias"][0, 11] = 30.0
-    n = 300
     eng = BlockEngine(cfg, sd, cuda_device, act_dtype=torch.bfloat16, max_tokens=n)
     p = O.params_from_state_dict({k: v.cpu() for k, v in sd.items()}, cfg.num_experts)
     h, _ = synth.block_inputs(n, cfg.hidden_size, seed=10)
