@@ -43,6 +43,27 @@ def test_ep_path_single_gpu_matches_block(name, cuda_device):
         h = b
 
 
+def test_ep_owner_hot_expert_loops_row_tiles(cuda_device):
+    """200 tokens with two experts taking every token: the owner plans 64-row tiles
+    per expert (32 expected pairs per expert on average), so each hot expert's
+    CTA loops over four row tiles."""
+    cfg = ModelConfig(hidden_size=256, num_heads=4, num_experts=16, top_k=2, edges_per_expert=2,
+                      num_loops=1, expert_ffn_size=512).validate()
+    n = 200
+    sd = synth.synthetic_state_dict(cfg, seed=43, device=cuda_device, round_bf16=True)
+    sd["loop_bias"][0, 5] = 40.0
+    sd["loop_bias"][0, 9] = 30.0
+    ep = ExpertParallelBlock(cfg, sd, cuda_device, act_dtype=torch.bfloat16, max_tokens=n, weight_format="bf16")
+    full = BlockEngine(cfg, sd, cuda_device, act_dtype=torch.bfloat16, max_tokens=n)
+    h, _ = synth.block_inputs(n, cfg.hidden_size, seed=44, device=cuda_device, dtype=torch.bfloat16)
+    h = h.view(n, -1)
+    a = ep.loop(h, h, 0)
+    b = full.forward(h, h, 0, 1)
+    torch.cuda.synchronize()
+    ep.local.check_status()
+    assert rel_err(a, b) < 2e-2
+
+
 def free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
