@@ -18,6 +18,7 @@
 // No load in this file uses cluster multicast: every CTA fetches its own tiles,
 // so the kernel is safe on expert-parallel runs where operands may live in
 // buffers filled by other GPUs.
+#include <cstdlib>
 #include <unordered_map>
 #include <mutex>
 #include <tuple>
@@ -392,6 +393,275 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   }
 }
 
+// ------------------------------------------------------------------ persistent large-tile GEMM
+//
+// Prefill-size problems (many row tiles per group): one CTA per SM walks the
+// tile list (group, row tile, 128-feature tile; feature tile fastest so a token
+// tile is reused from L2 by all feature tiles), with the TMA pipeline running
+// continuously across tiles and two TMEM accumulators, so the epilogue of tile
+// i overlaps the MMAs of tile i+1.  fp8 / int4 tiles are dequantised by four
+// dedicated warps.  Warps: 0-3 epilogue, 4 TMA, 5 MMA (+TMEM), 6-9 dequant.
+template <int BN, int WFMT, int EPI>
+struct PCfg {
+  static constexpr bool kGate = EPI == SB_EPI_SWIGLU;
+  static constexpr bool kConvert = WFMT != SB_W_BF16;
+  static constexpr int kABytes = kTcBM * kTcBK * 2;
+  static constexpr int kBBytes = BN * kTcBK * 2;
+  static constexpr int kRawBytes = WFMT == SB_W_FP8 ? kTcBM * kTcBK : (WFMT == SB_W_INT4 ? kTcBM * kTcBK / 2 : 0);
+  static constexpr int kStageBytes = kABytes * (kGate ? 2 : 1) + kBBytes + kRawBytes * (kGate ? 2 : 1);
+  static constexpr int kStagesRaw = (212 * 1024) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 6 ? 6 : (kStagesRaw < 2 ? 2 : kStagesRaw);
+  static constexpr int kAccCols = BN * (kGate ? 2 : 1);
+  static constexpr int kTmemCols = 2 * kAccCols;
+  static constexpr int kThreads = kConvert ? 320 : 192;
+  static constexpr int kOffA = 0;
+  static constexpr int kOffG = kOffA + kStages * kABytes;
+  static constexpr int kOffB = kOffG + (kGate ? kStages * kABytes : 0);
+  static constexpr int kOffRaw = kOffB + kStages * kBBytes;
+  static constexpr int kOffRawG = kOffRaw + kStages * kRawBytes;
+  static constexpr int kOffBar = kOffRawG + (kGate ? kStages * kRawBytes : 0);
+  static constexpr int kOffMisc = kOffBar + (3 * kStages + 4) * 8;
+  static constexpr int kOffPrefix = kOffMisc + 64;                  // int[kMaxG + 1]
+  static constexpr int kMaxG = 256;
+  static constexpr int kSmemBytes = kOffPrefix + (kMaxG + 1) * 4 + 1024;
+  static_assert(kTmemCols <= 512, "two accumulators must fit the 512 TMEM columns");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+};
+
+// Tile t -> (group, row tile, feature tile) from the per-group tile prefix.
+SB_DEVINL void decode_tile(const int* prefix, int G, int m_tiles, int t, int& g, int& nt, int& mt) {
+  int lo = 0, hi = G - 1;
+  while (lo < hi) {  // largest g with prefix[g] <= t
+    const int mid = (lo + hi + 1) >> 1;
+    if (prefix[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  g = lo;
+  const int local = t - prefix[g];
+  nt = local / m_tiles;
+  mt = local - nt * m_tiles;
+}
+
+template <int BN, int WFMT, int EPI>
+__global__ void __launch_bounds__(PCfg<BN, WFMT, EPI>::kThreads, 1)
+tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmG,
+                          const __grid_constant__ CUtensorMap tmB, const sb_grouped_gemm_args p) {
+  using C = PCfg<BN, WFMT, EPI>;
+  constexpr int S = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* empty = full + S;
+  uint64_t* conv = empty + S;
+  uint64_t* acc_full = conv + S;     // [2]
+  uint64_t* acc_empty = acc_full + 2;  // [2]
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
+  int* s_total = reinterpret_cast<int*>(smem + C::kOffMisc + 16);
+  int* prefix = reinterpret_cast<int*>(smem + C::kOffPrefix);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = p.num_groups;
+  const int m_tiles = (p.m_rows + kTcBM - 1) / kTcBM;
+  const int nk = p.k / kTcBK;
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 128);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (C::kGate) tma_prefetch_desc(&tmG);
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (warp == 0) {
+    // per-group tile counts -> exclusive prefix (warp scan, 32 groups at a time)
+    int seen = 0;
+    for (int base = 0; base < G; base += 32) {
+      const int gi = base + lane;
+      int tiles = 0;
+      if (gi < G) {
+        const int lo = min(p.offsets[gi], p.max_rows), hi = min(p.offsets[gi + 1], p.max_rows);
+        tiles = hi > lo ? (hi - lo + BN - 1) / BN * m_tiles : 0;
+      }
+      int incl = tiles;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += t;
+      }
+      if (gi < G) prefix[gi] = seen + incl - tiles;
+      seen += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      prefix[G] = seen;
+      *s_total = seen;
+    }
+  }
+  __syncthreads();
+  const int total = *s_total;
+  if (static_cast<int>(blockIdx.x) >= total) return;  // no tile for this CTA
+  const int my_tiles = (total - static_cast<int>(blockIdx.x) + gridDim.x - 1) / gridDim.x;
+
+  if (warp == 5) {
+    tmem_alloc(s_tmem, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      constexpr uint32_t kTx = (C::kConvert ? C::kRawBytes : C::kABytes) * (C::kGate ? 2 : 1) + C::kBBytes;
+      int it = 0;
+      bool ok = true;
+      for (int j = 0; j < my_tiles && ok; ++j) {
+        int g, nt, mt;
+        decode_tile(prefix, G, m_tiles, blockIdx.x + j * gridDim.x, g, nt, mt);
+        const int64_t arow = static_cast<int64_t>(g) * p.a_group_rows + mt * kTcBM;
+        const int nrow = p.offsets[g] + nt * BN;
+        for (int kk = 0; kk < nk; ++kk, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, p.status, SB_DEVERR_MMA_WAIT)) { ok = false; break; }
+          mbar_expect_tx(&full[s], kTx);
+          const int k0 = kk * kTcBK;
+          const int acol = WFMT == SB_W_INT4 ? k0 / 2 : k0;
+          uint8_t* adst = C::kConvert ? smem + C::kOffRaw + s * C::kRawBytes : smem + C::kOffA + s * C::kABytes;
+          tma_load_2d(adst, &tmA, &full[s], acol, static_cast<int>(arow));
+          if (C::kGate) {
+            uint8_t* gdst = C::kConvert ? smem + C::kOffRawG + s * C::kRawBytes : smem + C::kOffG + s * C::kABytes;
+            tma_load_2d(gdst, &tmG, &full[s], acol, static_cast<int>(arow));
+          }
+          tma_load_2d(smem + C::kOffB + s * C::kBBytes, &tmB, &full[s], k0, nrow);
+        }
+      }
+      for (int i = it - S > 0 ? it - S : 0; i < it; ++i)  // drain
+        if (!mbar_wait(&full[i % S], (i / S) & 1, p.status, SB_DEVERR_DRAIN)) break;
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kTcBM, BN);
+      int it = 0;
+      bool ok = true;
+      for (int j = 0; j < my_tiles && ok; ++j) {
+        const int buf = j & 1;
+        if (!mbar_wait(&acc_empty[buf], ((j >> 1) & 1) ^ 1, p.status, SB_DEVERR_EPI_WAIT)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + buf * C::kAccCols;
+        for (int kk = 0; kk < nk; ++kk, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          ok = C::kConvert ? mbar_wait(&conv[s], ph, p.status, SB_DEVERR_CONV_WAIT)
+                           : mbar_wait(&full[s], ph, p.status, SB_DEVERR_TMA_WAIT);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + C::kOffA + s * C::kABytes);
+          const uint32_t g_base = smem_u32(smem + C::kOffG + s * C::kABytes);
+          const uint32_t b_base = smem_u32(smem + C::kOffB + s * C::kBBytes);
+#pragma unroll
+          for (int q = 0; q < kTcBK / 16; ++q) {
+            const uint64_t bdesc = smem_desc_k_sw128(b_base + q * 32);
+            const uint32_t accum = (kk > 0 || q > 0) ? 1u : 0u;
+            tc_mma_bf16(acc, smem_desc_k_sw128(a_base + q * 32), bdesc, idesc, accum);
+            if (C::kGate) tc_mma_bf16(acc + BN, smem_desc_k_sw128(g_base + q * 32), bdesc, idesc, accum);
+          }
+          tc_commit(&empty[s]);
+        }
+        tc_commit(&acc_full[buf]);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 6) {
+    // ---------------------------------------------------------------- dequant (fp8 / int4)
+    if (C::kConvert) {
+      const int ctid = tid - 192;
+      int it = 0;
+      for (int j = 0; j < my_tiles; ++j) {
+        int g, nt, mt;
+        decode_tile(prefix, G, m_tiles, blockIdx.x + j * gridDim.x, g, nt, mt);
+        const int64_t arow0 = static_cast<int64_t>(g) * p.a_group_rows + mt * kTcBM;
+        bool ok = true;
+        for (int kk = 0; kk < nk; ++kk, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&full[s], (it / S) & 1, p.status, SB_DEVERR_TMA_WAIT)) { ok = false; break; }
+          const int k0 = kk * kTcBK;
+          convert_tile<WFMT>(smem + C::kOffRaw + s * C::kRawBytes, smem + C::kOffA + s * C::kABytes, p,
+                             p.a_scale, arow0, k0, ctid);
+          if (C::kGate)
+            convert_tile<WFMT>(smem + C::kOffRawG + s * C::kRawBytes, smem + C::kOffG + s * C::kABytes, p,
+                               p.a_gate_scale, arow0, k0, ctid);
+          fence_proxy_async_smem();
+          mbar_arrive(&conv[s]);
+        }
+        if (!ok) break;
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 0-3)
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    for (int j = 0; j < my_tiles; ++j) {
+      int g, nt, mt;
+      decode_tile(prefix, G, m_tiles, blockIdx.x + j * gridDim.x, g, nt, mt);
+      const int buf = j & 1;
+      const bool ready = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (j >> 1) & 1, p.status, SB_DEVERR_EPI_WAIT));
+      tc_fence_after();
+      if (!ready) break;
+      const int m = mt * kTcBM + warp * 32 + lane;
+      const int64_t arow = static_cast<int64_t>(g) * p.a_group_rows + m;
+      const bool mvalid = m < p.m_rows && arow < p.a_rows_total;
+      const float sa = (WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_scale)[arow] : 1.f;
+      const float sg = (C::kGate && WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_gate_scale)[arow] : 1.f;
+      const float bias = (p.bias && mvalid) ? p.bias[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
+      const float bgate = (C::kGate && p.bias_gate && mvalid) ? p.bias_gate[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
+      const int tn0 = p.offsets[g] + nt * BN;
+      const int tend = min(min(tn0 + BN, p.offsets[g + 1]), p.max_rows);
+      const uint32_t acc_addr = lane_addr + buf * C::kAccCols;
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        if (tn0 + c0 >= tend) break;
+        float v[16], vg[16];
+        tmem_ld16(acc_addr + c0, v);
+        if (C::kGate) tmem_ld16(acc_addr + BN + c0, vg);
+        if (!mvalid) continue;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const int r = tn0 + c0 + q;
+          if (r >= tend) break;
+          const float x = v[q] * sa + bias;
+          if (EPI == SB_EPI_LINEAR) {
+            const float rs = p.row_scale ? p.row_scale[r] : 1.f;
+            static_cast<float*>(p.out)[static_cast<int64_t>(r) * p.ldo + m] = x * rs;
+          } else if (EPI == SB_EPI_GELU) {
+            static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(r) * p.ldo + m] = __float2bfloat16_rn(gelu_erf(x));
+          } else {
+            const float gx = vg[q] * sg + bgate;
+            static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(r) * p.ldo + m] = __float2bfloat16_rn(silu(gx) * x);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -479,6 +749,46 @@ static int launch_tc(const sb_grouped_gemm_args& a, cudaStream_t st) {
   return launch(kern, grid, dim3(kTcThreads), C::kSmemBytes, st, ma, mg, mb, a);
 }
 
+constexpr int kPersistentMaxGroups = 256;
+
+// SPIDER_B200_PERSISTENT=0 selects the one-tile-per-CTA kernel for large tiles
+// (for comparisons); the default is the persistent kernel.
+static bool use_persistent(const sb_grouped_gemm_args& a) {
+  static const bool enabled = [] {
+    const char* e = std::getenv("SPIDER_B200_PERSISTENT");
+    return !(e && e[0] == '0');
+  }();
+  return enabled && a.splits == 1 && a.num_groups <= kPersistentMaxGroups;
+}
+
+template <int BN, int WFMT, int EPI>
+static int launch_persistent(const sb_grouped_gemm_args& a, cudaStream_t st) {
+  using C = PCfg<BN, WFMT, EPI>;
+  auto kern = tc_gemm_persistent_kernel<BN, WFMT, EPI>;
+  static int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e);
+    configured_device = dev;
+  }
+  static_assert(C::kMaxG == kPersistentMaxGroups, "tile table size");
+  if (a.num_groups > C::kMaxG || a.splits != 1) return SB_ERR_UNSUPPORTED;
+  CUtensorMap ma, mg, mb;
+  if (!weight_map(&ma, a, a.a)) return SB_ERR_UNSUPPORTED;
+  mg = ma;
+  if (C::kGate && !weight_map(&mg, a, a.a_gate)) return SB_ERR_UNSUPPORTED;
+  if (!make_map(&mb, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.k, a.max_rows, a.ldx * 2, kTcBK, BN,
+                CU_TENSOR_MAP_SWIZZLE_128B))
+    return SB_ERR_UNSUPPORTED;
+  const int m_tiles = (a.m_rows + kTcBM - 1) / kTcBM;
+  const int64_t bound = static_cast<int64_t>(m_tiles) * ((a.max_rows + BN - 1) / BN + a.num_groups);
+  const int sms = current_sm_count();
+  const int grid = static_cast<int>(bound < sms ? bound : sms);
+  return launch(kern, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, ma, mg, mb, a);
+}
+
 template <int BN, int WFMT, int EPI>
 static int launch_modes(const sb_grouped_gemm_args& a, cudaStream_t st) {
   const bool g = a.x_row_index != nullptr;
@@ -494,8 +804,18 @@ static int launch_bn(const sb_grouped_gemm_args& a, cudaStream_t st, int bn) {
     case 16: return launch_modes<16, WFMT, EPI>(a, st);
     case 32: return launch_modes<32, WFMT, EPI>(a, st);
     case 64: return launch_modes<64, WFMT, EPI>(a, st);
-    case 128: return g ? SB_ERR_UNSUPPORTED : launch_tc<128, WFMT, EPI, false, false>(a, st);
-    default: return g ? SB_ERR_UNSUPPORTED : launch_tc<256, WFMT, EPI, false, false>(a, st);
+    // Large tiles: the persistent kernel (two TMEM accumulators; SwiGLU's two
+    // accumulator sets fit only at 128 columns) unless the problem is K-split
+    // or has more groups than its tile table holds.
+    case 128:
+      if (g) return SB_ERR_UNSUPPORTED;
+      if (!use_persistent(a)) return launch_tc<128, WFMT, EPI, false, false>(a, st);
+      return launch_persistent<128, WFMT, EPI>(a, st);
+    default:
+      if (g) return SB_ERR_UNSUPPORTED;
+      if (!use_persistent(a)) return launch_tc<256, WFMT, EPI, false, false>(a, st);
+      if constexpr (EPI == SB_EPI_SWIGLU) return launch_persistent<128, WFMT, EPI>(a, st);
+      else return launch_persistent<256, WFMT, EPI>(a, st);
   }
 }
 
