@@ -46,6 +46,21 @@ template <> SB_DEVINL __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __
 SB_DEVINL float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 SB_DEVINL float silu(float x) { return x / (1.0f + expf(-x)); }
 
+// erf by Abramowitz & Stegun, Handbook of Mathematical Functions (1964), formula
+// 7.1.26: erf(x) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-x^2) with
+// t = 1 / (1 + p x) for x >= 0, |error| <= 1.5e-7; odd in x.  About half the
+// instructions of erff, for epilogues whose result is rounded to bf16 (relative
+// step 2^-8), where the approximation error is invisible.
+SB_DEVINL float erf_as7126(float x) {
+  const float ax = fabsf(x);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, ax, 1.0f));
+  const float poly =
+      fmaf(fmaf(fmaf(fmaf(1.061405429f, t, -1.453152027f), t, 1.421413741f), t, -0.284496736f), t, 0.254829592f) * t;
+  return copysignf(1.0f - poly * __expf(-ax * ax), x);
+}
+SB_DEVINL float gelu_bf16out(float x) { return 0.5f * x * (1.0f + erf_as7126(x * 0.70710678118654752f)); }
+SB_DEVINL float silu_bf16out(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
 SB_DEVINL float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -374,10 +374,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const float rs = p.row_scale ? p.row_scale[r] : 1.f;
             static_cast<float*>(p.out)[blockIdx.z * p.split_stride + static_cast<int64_t>(r) * p.ldo + m] = x * rs;
           } else if (EPI == SB_EPI_GELU) {
-            static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(r) * p.ldo + m] = __float2bfloat16_rn(gelu_erf(x));
+            static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(r) * p.ldo + m] = __float2bfloat16_rn(gelu_bf16out(x));
           } else {
             const float gx = vg[j] * sg + bgate;
-            static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(r) * p.ldo + m] = __float2bfloat16_rn(silu(gx) * x);
+            static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(r) * p.ldo + m] = __float2bfloat16_rn(silu_bf16out(gx) * x);
           }
         }
       }
@@ -399,8 +399,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // tile list (group, row tile, 128-feature tile; feature tile fastest so a token
 // tile is reused from L2 by all feature tiles), with the TMA pipeline running
 // continuously across tiles and two TMEM accumulators, so the epilogue of tile
-// i overlaps the MMAs of tile i+1.  fp8 / int4 tiles are dequantised by four
-// dedicated warps.  Warps: 0-3 epilogue, 4 TMA, 5 MMA (+TMEM), 6-9 dequant.
+// i overlaps the MMAs of tile i+1.  Eight epilogue warps, two per TMEM lane
+// quarter (one per half of the tile's columns), keep the epilogue shorter than
+// a tile's MMAs; fp8 / int4 tiles are dequantised by four dedicated warps.
+// Warps: 0-3 and 6-9 epilogue, 4 TMA, 5 MMA (+TMEM), 10-13 dequant.
 template <int BN, int WFMT, int EPI>
 struct PCfg {
   static constexpr bool kGate = EPI == SB_EPI_SWIGLU;
@@ -413,7 +415,8 @@ struct PCfg {
   static constexpr int kStages = kStagesRaw > 6 ? 6 : (kStagesRaw < 2 ? 2 : kStagesRaw);
   static constexpr int kAccCols = BN * (kGate ? 2 : 1);
   static constexpr int kTmemCols = 2 * kAccCols;
-  static constexpr int kThreads = kConvert ? 320 : 192;
+  static constexpr int kEpiThreads = 256;
+  static constexpr int kThreads = kConvert ? 448 : 320;
   static constexpr int kOffA = 0;
   static constexpr int kOffG = kOffA + kStages * kABytes;
   static constexpr int kOffB = kOffG + (kGate ? kStages * kABytes : 0);
@@ -423,7 +426,8 @@ struct PCfg {
   static constexpr int kOffMisc = kOffBar + (3 * kStages + 4) * 8;
   static constexpr int kOffPrefix = kOffMisc + 64;                  // int[kMaxG + 1]
   static constexpr int kMaxG = 256;
-  static constexpr int kSmemBytes = kOffPrefix + (kMaxG + 1) * 4 + 1024;
+  static constexpr int kOffOffsets = kOffPrefix + (kMaxG + 1) * 4;  // int[kMaxG + 1]: group row offsets
+  static constexpr int kSmemBytes = kOffOffsets + (kMaxG + 1) * 4 + 1024;
   static_assert(kTmemCols <= 512, "two accumulators must fit the 512 TMEM columns");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 };
@@ -457,6 +461,7 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
   int* s_total = reinterpret_cast<int*>(smem + C::kOffMisc + 16);
   int* prefix = reinterpret_cast<int*>(smem + C::kOffPrefix);
+  int* s_off = reinterpret_cast<int*>(smem + C::kOffOffsets);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = p.num_groups;
@@ -470,7 +475,7 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], C::kEpiThreads);
     }
     fence_barrier_init();
   }
@@ -488,7 +493,10 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
       const int gi = base + lane;
       int tiles = 0;
       if (gi < G) {
-        const int lo = min(p.offsets[gi], p.max_rows), hi = min(p.offsets[gi + 1], p.max_rows);
+        const int o0 = p.offsets[gi], o1 = p.offsets[gi + 1];
+        s_off[gi] = o0;
+        if (gi == G - 1) s_off[G] = o1;
+        const int lo = min(o0, p.max_rows), hi = min(o1, p.max_rows);
         tiles = hi > lo ? (hi - lo + BN - 1) / BN * m_tiles : 0;
       }
       int incl = tiles;
@@ -529,7 +537,7 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
         int g, nt, mt;
         decode_tile(prefix, G, m_tiles, blockIdx.x + j * gridDim.x, g, nt, mt);
         const int64_t arow = static_cast<int64_t>(g) * p.a_group_rows + mt * kTcBM;
-        const int nrow = p.offsets[g] + nt * BN;
+        const int nrow = s_off[g] + nt * BN;
         for (int kk = 0; kk < nk; ++kk, ++it) {
           const int s = it % S;
           if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, p.status, SB_DEVERR_MMA_WAIT)) { ok = false; break; }
@@ -583,10 +591,10 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
       }
     }
     __syncwarp();
-  } else if (warp >= 6) {
+  } else if (warp >= 10) {
     // ---------------------------------------------------------------- dequant (fp8 / int4)
     if (C::kConvert) {
-      const int ctid = tid - 192;
+      const int ctid = tid - 320;
       int it = 0;
       for (int j = 0; j < my_tiles; ++j) {
         int g, nt, mt;
@@ -609,45 +617,64 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
       }
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 0-3)
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    // ---------------------------------------------------------------- epilogue (warps 0-3, 6-9)
+    // A warp reads the TMEM lane quarter warp % 4 (output features) and one half
+    // of the tile's columns (tokens).
+    constexpr int HB = BN / 2;
+    const int quarter = warp & 3;
+    const int half = warp < 4 ? 0 : 1;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + half * HB;
     for (int j = 0; j < my_tiles; ++j) {
       int g, nt, mt;
       decode_tile(prefix, G, m_tiles, blockIdx.x + j * gridDim.x, g, nt, mt);
       const int buf = j & 1;
-      const bool ready = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (j >> 1) & 1, p.status, SB_DEVERR_EPI_WAIT));
-      tc_fence_after();
-      if (!ready) break;
-      const int m = mt * kTcBM + warp * 32 + lane;
+      // per-tile operands first: their loads overlap the wait for the accumulator
+      const int m = mt * kTcBM + quarter * 32 + lane;
       const int64_t arow = static_cast<int64_t>(g) * p.a_group_rows + m;
       const bool mvalid = m < p.m_rows && arow < p.a_rows_total;
       const float sa = (WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_scale)[arow] : 1.f;
       const float sg = (C::kGate && WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_gate_scale)[arow] : 1.f;
       const float bias = (p.bias && mvalid) ? p.bias[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
       const float bgate = (C::kGate && p.bias_gate && mvalid) ? p.bias_gate[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
-      const int tn0 = p.offsets[g] + nt * BN;
-      const int tend = min(min(tn0 + BN, p.offsets[g + 1]), p.max_rows);
+      const int tn0 = s_off[g] + nt * BN + half * HB;
+      const int tend = min(min(s_off[g] + nt * BN + BN, s_off[g + 1]), p.max_rows);
+      // LINEAR: the half's row scales, one per lane and 32 columns
+      float rsv[HB / 32];
+#pragma unroll
+      for (int i = 0; i < HB / 32; ++i) {
+        const int r = tn0 + i * 32 + lane;
+        rsv[i] = (EPI == SB_EPI_LINEAR && p.row_scale && r < tend) ? p.row_scale[r] : 1.f;
+      }
+      const bool ready = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (j >> 1) & 1, p.status, SB_DEVERR_EPI_WAIT));
+      tc_fence_after();
+      if (!ready) break;
       const uint32_t acc_addr = lane_addr + buf * C::kAccCols;
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        if (tn0 + c0 >= tend) break;
-        float v[16], vg[16];
+#pragma unroll
+      for (int c0 = 0; c0 < HB; c0 += 16) {
+        if (tn0 + c0 >= tend) break;  // warp-uniform
+        float v[16], vg[16], o[16];
         tmem_ld16(acc_addr + c0, v);
         if (C::kGate) tmem_ld16(acc_addr + BN + c0, vg);
-        if (!mvalid) continue;
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
-          const int r = tn0 + c0 + q;
-          if (r >= tend) break;
           const float x = v[q] * sa + bias;
-          if (EPI == SB_EPI_LINEAR) {
-            const float rs = p.row_scale ? p.row_scale[r] : 1.f;
-            static_cast<float*>(p.out)[static_cast<int64_t>(r) * p.ldo + m] = x * rs;
-          } else if (EPI == SB_EPI_GELU) {
-            static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(r) * p.ldo + m] = __float2bfloat16_rn(gelu_erf(x));
-          } else {
-            const float gx = vg[q] * sg + bgate;
-            static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(r) * p.ldo + m] = __float2bfloat16_rn(silu(gx) * x);
-          }
+          if (EPI == SB_EPI_LINEAR)
+            o[q] = x * __shfl_sync(0xffffffffu, rsv[(c0 + q) >> 5], (c0 + q) & 31);
+          else if (EPI == SB_EPI_GELU)
+            o[q] = gelu_bf16out(x);
+          else
+            o[q] = silu_bf16out(vg[q] * sg + bgate) * x;
+        }
+        if (!mvalid) continue;
+        const int nvalid = tend - (tn0 + c0);
+        const int64_t base = static_cast<int64_t>(tn0 + c0) * p.ldo + m;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          if (nvalid < 16 && q >= nvalid) break;
+          if (EPI == SB_EPI_LINEAR)
+            static_cast<float*>(p.out)[base + static_cast<int64_t>(q) * p.ldo] = o[q];
+          else
+            static_cast<__nv_bfloat16*>(p.out)[base + static_cast<int64_t>(q) * p.ldo] = __float2bfloat16_rn(o[q]);
         }
       }
       tc_fence_before();

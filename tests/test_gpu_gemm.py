@@ -1,0 +1,198 @@
+"""sb_grouped_gemm against a plain PyTorch fp32 statement of the same op.
+
+out[r] = epilogue(W_g x[r] * s_g + b_g) for every row r of group g (rows
+offsets[g] .. offsets[g+1]); LINEAR scales by row_scale[r] and writes fp32
+(K-split partials summed by the caller), GELU / SwiGLU write bf16.  The cases
+cover every tcgen05 schedule the library picks from the row counts (fixed
+groups with 16-row boxes or 4-row gathers, the slot grid for mid-size tiles,
+the persistent kernel for 128 / 256-column tiles), each weight format, and the
+CUDA-core engine.  The weights are the device operands dequantised on the host
+(fp8 -> bf16 with the per-row scale applied in fp32; int4 -> q * bf16 group
+scale rounded to bf16), so the tolerance measures the GEMM alone: fp32
+accumulation order and the bf16 rounding of the output.
+"""
+import ctypes as C
+
+import pytest
+import torch
+
+from spider_web_moe_b200 import _lib as L
+from spider_web_moe_b200.quant import quantize_fp8_per_channel, quantize_int4
+
+pytestmark = pytest.mark.gpu
+
+EPI = {"linear": L.SB_EPI_LINEAR, "gelu": L.SB_EPI_GELU, "swiglu": L.SB_EPI_SWIGLU}
+WFMT = {"bf16": L.SB_W_BF16, "fp8": L.SB_W_FP8, "int4": L.SB_W_INT4}
+ENGINE = {"tcgen05": L.SB_ENGINE_TCGEN05, "simt": L.SB_ENGINE_SIMT}
+
+
+def device_weight(w, wfmt, group_size, dev):
+    """(device operand, device scale, fp32 weights the device multiplies by)."""
+    G, m, k = w.shape
+    if wfmt == "bf16":
+        wb = w.to(torch.bfloat16)
+        return wb.to(dev), None, wb.float(), None
+    if wfmt == "fp8":
+        q = quantize_fp8_per_channel(w)
+        return q.q.to(dev), q.scale.float().to(dev), q.q.float(), q.scale.float()
+    t = quantize_int4(w, group_size)
+    s_bf = t.scales.to(torch.bfloat16)
+    packed = t.packed
+    lo = (packed & 0x0F).to(torch.int8)
+    hi = (packed >> 4).to(torch.int8)
+    lo = torch.where(lo > 7, lo - 16, lo)
+    hi = torch.where(hi > 7, hi - 16, hi)
+    q = torch.stack([lo, hi], dim=-1).reshape(G, m, k).float()
+    deq = (q * s_bf.float().repeat_interleave(group_size, dim=-1)).to(torch.bfloat16).float()
+    return packed.to(dev), s_bf.to(dev), deq, None
+
+
+def run_case(rows, m, k, wfmt, epi, engine, dev, bound=0, splits=1, gather=False, group_size=128, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    G = len(rows)
+    total = sum(rows)
+    off = torch.tensor([0] + list(torch.tensor(rows).cumsum(0)), dtype=torch.int32)
+    w = torch.randn(G, m, k, generator=g) * 0.05
+    wg = torch.randn(G, m, k, generator=g) * 0.05
+    bias = torch.randn(G, m, generator=g) * 0.1
+    bias_g = torch.randn(G, m, generator=g) * 0.1
+    x = torch.randn(total, k, generator=g).to(torch.bfloat16)
+    row_scale = torch.rand(total, generator=g) + 0.5
+    a, a_s, deq, s_row = device_weight(w, wfmt, group_size, dev)
+    ag, ag_s, deq_g, s_row_g = device_weight(wg, wfmt, group_size, dev) if epi == "swiglu" else (None, None, None, None)
+
+    # torch fp32 statement
+    want = torch.zeros(total, m)
+    for gi in range(G):
+        lo, hi = int(off[gi]), int(off[gi + 1])
+        if hi == lo:
+            continue
+        y = x[lo:hi].float() @ deq[gi].T
+        if s_row is not None:
+            y = y * s_row[gi]
+        y = y + bias[gi]
+        if epi == "linear":
+            y = y * row_scale[lo:hi, None]
+        elif epi == "gelu":
+            y = torch.nn.functional.gelu(y)
+        else:
+            z = x[lo:hi].float() @ deq_g[gi].T
+            if s_row_g is not None:
+                z = z * s_row_g[gi]
+            y = torch.nn.functional.silu(z + bias_g[gi]) * y
+        want[lo:hi] = y
+
+    # the GEMM's token rows: contiguous, or gathered from a permuted source
+    perm = torch.randperm(total, generator=g)
+    src = torch.empty_like(x)
+    src[perm] = x
+    d_x = (src if gather else x).to(dev)
+    d_idx = perm.to(torch.int32).to(dev)
+    d_off = off.to(dev)
+    out_dtype = torch.float32 if epi == "linear" else torch.bfloat16
+    out = torch.full((splits, total, m), float("nan"), dtype=out_dtype, device=dev)
+    status = torch.zeros(64, dtype=torch.int32, device=dev)
+    keep = [a, a_s, ag, ag_s, d_x, d_idx, d_off, out, status]
+    d_bias, d_bias_g, d_rs = bias.to(dev), bias_g.to(dev), row_scale.to(dev)
+    keep += [d_bias, d_bias_g, d_rs]
+
+    args = L.GemmArgs()
+    args.engine = ENGINE[engine]
+    args.wfmt = WFMT[wfmt]
+    args.act_dtype = L.SB_BF16
+    args.epilogue = EPI[epi]
+    args.num_groups = G
+    args.m_rows = m
+    args.k = k
+    args.group_size = group_size
+    args.a_group_rows = m
+    args.lda = k
+    args.a_rows_total = G * m
+    args.a = a.data_ptr()
+    args.a_scale = a_s.data_ptr() if a_s is not None else None
+    if epi == "swiglu":
+        args.a_gate = ag.data_ptr()
+        args.a_gate_scale = ag_s.data_ptr() if ag_s is not None else None
+        args.bias_gate = d_bias_g.data_ptr()
+    args.bias = d_bias.data_ptr()
+    args.bias_group_stride = m
+    args.x = d_x.data_ptr()
+    args.ldx = k
+    if gather:
+        args.x_row_index = d_idx.data_ptr()
+        args.x_rows = total
+    args.max_rows = total
+    args.rows_hint = total
+    args.group_rows_bound = bound
+    args.offsets = d_off.data_ptr()
+    args.row_scale = d_rs.data_ptr() if epi == "linear" else None
+    args.out = out.data_ptr()
+    args.ldo = m
+    args.splits = splits
+    args.split_stride = total * m
+    args.status = status.data_ptr()
+    lib = L.load()
+    L.check(lib.sb_grouped_gemm(C.byref(args), C.c_void_p(torch.cuda.current_stream().cuda_stream)), "sb_grouped_gemm")
+    torch.cuda.synchronize()
+    assert int(status.abs().sum()) == 0, status[:8].tolist()
+    got = out.float().sum(0).cpu() if epi == "linear" else out[0].float().cpu()
+    assert not torch.isnan(got).any()
+    del keep
+    return got, want
+
+
+def check(got, want, epi):
+    err = (got - want).abs()
+    # fp32 accumulation order (LINEAR), plus bf16 rounding of the output (GELU / SwiGLU)
+    tol = (1e-4 if epi == "linear" else 8e-3) * want.abs() + 2e-4 * want.abs().max()
+    bad = err > tol
+    assert not bad.any(), f"{int(bad.sum())} of {bad.numel()} outside tolerance, max err {float(err.max()):.3e}"
+
+
+# (rows per group, bound, splits, gather): which schedule the library takes
+SCHEDULES = {
+    "fixed16_gather": ([5, 0, 16, 9, 1], 16, 1, True),
+    "fixed64": ([40, 64, 3, 0, 57], 64, 1, False),
+    "fixed_multi_tile": ([150, 7, 0, 70], 64, 1, False),   # groups beyond the bound loop over row tiles
+    "slot64": ([70, 40, 90, 1], 0, 1, False),
+    "slot64_split2": ([70, 40, 90, 1], 0, 2, False),
+    "persistent128": ([100, 130, 0, 90, 120], 0, 1, False),
+    "persistent256": ([300, 0, 517, 129], 0, 1, False),
+    "tile256_split2": ([300, 0, 517, 129], 0, 2, False),
+}
+
+
+@pytest.mark.parametrize("sched", sorted(SCHEDULES))
+@pytest.mark.parametrize("wfmt", ["bf16", "fp8", "int4"])
+def test_tcgen05_linear_and_gelu(sched, wfmt, cuda_device):
+    rows, bound, splits, gather = SCHEDULES[sched]
+    for epi in (["linear"] if splits > 1 else ["linear", "gelu"]):
+        got, want = run_case(rows, 256, 512, wfmt, epi, "tcgen05", cuda_device, bound=bound, splits=splits,
+                             gather=gather, seed=len(sched) + len(wfmt))
+        check(got, want, epi)
+
+
+@pytest.mark.parametrize("sched", ["fixed64", "slot64", "persistent128", "persistent256"])
+@pytest.mark.parametrize("wfmt", ["bf16", "fp8", "int4"])
+def test_tcgen05_swiglu(sched, wfmt, cuda_device):
+    rows, bound, splits, gather = SCHEDULES[sched]
+    got, want = run_case(rows, 256, 384, wfmt, "swiglu", "tcgen05", cuda_device, bound=bound, splits=splits,
+                         gather=gather, seed=7)
+    check(got, want, "swiglu")
+
+
+def test_persistent_many_tiles_and_groups(cuda_device):
+    """More tiles than SMs (each CTA loops, both TMEM accumulators turn over many
+    times) and 200 groups of ragged sizes, zeros included."""
+    g = torch.Generator().manual_seed(5)
+    rows = [int(v) for v in torch.randint(0, 400, (200,), generator=g)]
+    rows[3] = rows[50] = 0
+    got, want = run_case(rows, 384, 256, "bf16", "gelu", "tcgen05", cuda_device, seed=11)
+    check(got, want, "gelu")
+
+
+@pytest.mark.parametrize("epi", ["linear", "gelu", "swiglu"])
+@pytest.mark.parametrize("wfmt", ["bf16", "fp8", "int4"])
+def test_simt_engine(epi, wfmt, cuda_device):
+    got, want = run_case([33, 0, 70, 5], 160, 256, wfmt, epi, "simt", cuda_device, seed=3)
+    check(got, want, epi)
