@@ -689,6 +689,309 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
   }
 }
 
+// ------------------------------------------------------------------ persistent CTA-pair GEMM
+//
+// The persistent schedule of the kernel above on CTA pairs (clusters of two):
+// a pair computes a 256-feature x BN-token tile with tcgen05.mma.cta_group::2,
+// each CTA holding 128 weight rows and BN/2 token rows of every K stage, so a
+// CTA moves 32 KB of operands per 64-deep K step instead of 48 KB for the same
+// work per SM.  The leader (cluster rank 0) issues the MMAs; commits arrive in
+// both CTAs.  bf16 weights: each CTA's loads count on the leader's stage
+// barrier.  fp8 / int4: loads count on the CTA's own barrier, its dequant warps
+// convert and then arrive on the leader's conversion barrier.
+// Warps as in the one-CTA kernel: 0-3, 6-9 epilogue, 4 TMA, 5 MMA, 10-13 dequant.
+template <int BN, int WFMT, int EPI>
+struct PairCfg {
+  static constexpr bool kGate = EPI == SB_EPI_SWIGLU;
+  static constexpr bool kConvert = WFMT != SB_W_BF16;
+  static constexpr int kBH = BN / 2;  // token rows of B per CTA
+  static constexpr int kABytes = kTcBM * kTcBK * 2;
+  static constexpr int kBBytes = kBH * kTcBK * 2;
+  static constexpr int kRawBytes = WFMT == SB_W_FP8 ? kTcBM * kTcBK : (WFMT == SB_W_INT4 ? kTcBM * kTcBK / 2 : 0);
+  static constexpr int kStageBytes = kABytes * (kGate ? 2 : 1) + kBBytes + kRawBytes * (kGate ? 2 : 1);
+  static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
+  static constexpr int kAccCols = BN * (kGate ? 2 : 1);
+  static constexpr int kTmemCols = 2 * kAccCols;
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kConvWarps = 4;
+  static constexpr int kThreads = kConvert ? 448 : 320;
+  // B stages first: every operand read stays inside the allocation
+  static constexpr int kOffB = 0;
+  static constexpr int kOffA = kOffB + kStages * kBBytes;
+  static constexpr int kOffG = kOffA + kStages * kABytes;
+  static constexpr int kOffRaw = kOffG + (kGate ? kStages * kABytes : 0);
+  static constexpr int kOffRawG = kOffRaw + kStages * kRawBytes;
+  static constexpr int kOffBar = kOffRawG + (kGate ? kStages * kRawBytes : 0);
+  static constexpr int kOffMisc = kOffBar + (3 * kStages + 4) * 8;
+  static constexpr int kOffPrefix = kOffMisc + 64;
+  static constexpr int kMaxG = 256;
+  static constexpr int kOffOffsets = kOffPrefix + (kMaxG + 1) * 4;
+  static constexpr int kSmemBytes = kOffOffsets + (kMaxG + 1) * 4 + 1024;
+  static_assert(kTmemCols <= 512, "two accumulators must fit the 512 TMEM columns");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+  static_assert(kBBytes % 1024 == 0 && kABytes % 1024 == 0, "1024-byte aligned swizzled stages");
+  static_assert(BN == 128 || BN == 256, "pair tiles are 128 or 256 tokens wide");
+};
+
+template <int BN, int WFMT, int EPI>
+__global__ void __launch_bounds__(PairCfg<BN, WFMT, EPI>::kThreads, 1)
+tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmG,
+                    const __grid_constant__ CUtensorMap tmB, const sb_grouped_gemm_args p) {
+  using C = PairCfg<BN, WFMT, EPI>;
+  constexpr int S = C::kStages;
+  constexpr int kPairM = 2 * kTcBM;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* empty = full + S;
+  uint64_t* conv = empty + S;
+  uint64_t* acc_full = conv + S;       // [2]
+  uint64_t* acc_empty = acc_full + 2;  // [2]
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
+  int* prefix = reinterpret_cast<int*>(smem + C::kOffPrefix);
+  int* s_off = reinterpret_cast<int*>(smem + C::kOffOffsets);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+  const int G = p.num_groups;
+  const int m_tiles = (p.m_rows + kPairM - 1) / kPairM;
+  const int nk = p.k / kTcBK;
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 2 * C::kConvWarps);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * C::kEpiWarps);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (C::kGate) tma_prefetch_desc(&tmG);
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (warp == 0) {
+    int seen = 0;
+    for (int base = 0; base < G; base += 32) {
+      const int gi = base + lane;
+      int tiles = 0;
+      if (gi < G) {
+        const int o0 = p.offsets[gi], o1 = p.offsets[gi + 1];
+        s_off[gi] = o0;
+        if (gi == G - 1) s_off[G] = o1;
+        const int lo = min(o0, p.max_rows), hi = min(o1, p.max_rows);
+        tiles = hi > lo ? (hi - lo + BN - 1) / BN * m_tiles : 0;
+      }
+      int incl = tiles;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += t;
+      }
+      if (gi < G) prefix[gi] = seen + incl - tiles;
+      seen += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) prefix[G] = seen;
+  }
+  // both CTAs' barriers initialised (and this CTA's tile table written) before
+  // any CTA of the pair signals the other
+  __syncwarp();
+  cluster_sync();
+  const int total = prefix[G];
+  if (pair >= total) return;  // both CTAs of the pair leave: nothing to do
+  const int my_tiles = (total - pair + npairs - 1) / npairs;
+  const uint32_t full_lead = mapa_shared(smem_u32(full), 0);
+  const uint32_t conv_lead = mapa_shared(smem_u32(conv), 0);
+  const uint32_t acc_empty_lead = mapa_shared(smem_u32(acc_empty), 0);
+
+  if (warp == 5) {
+    tmem_alloc_pair(s_tmem, C::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- producer (both CTAs)
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int j = 0; j < my_tiles && ok; ++j) {
+        int g, nt, mt;
+        decode_tile(prefix, G, m_tiles, pair + j * npairs, g, nt, mt);
+        const int arow = static_cast<int>(static_cast<int64_t>(g) * p.a_group_rows) + mt * kPairM + static_cast<int>(rank) * kTcBM;
+        const int nrow = s_off[g] + nt * BN + static_cast<int>(rank) * C::kBH;
+        for (int kk = 0; kk < nk; ++kk, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, p.status, SB_DEVERR_MMA_WAIT)) { ok = false; break; }
+          const int k0 = kk * kTcBK;
+          if (C::kConvert) {
+            // raw weights + this CTA's token rows on its own barrier (dequant warps wait on it)
+            mbar_expect_tx(&full[s], C::kRawBytes * (C::kGate ? 2 : 1) + C::kBBytes);
+            const int acol = WFMT == SB_W_INT4 ? k0 / 2 : k0;
+            tma_load_2d(smem + C::kOffRaw + s * C::kRawBytes, &tmA, &full[s], acol, arow);
+            if (C::kGate) tma_load_2d(smem + C::kOffRawG + s * C::kRawBytes, &tmG, &full[s], acol, arow);
+            tma_load_2d(smem + C::kOffB + s * C::kBBytes, &tmB, &full[s], k0, nrow);
+          } else {
+            // both CTAs' bytes count on the leader's barrier; the leader arrives once
+            if (leader) mbar_expect_tx(&full[s], 2 * (C::kABytes * (C::kGate ? 2 : 1) + C::kBBytes));
+            const uint32_t bar = full_lead + 8u * s;
+            tma_load_2d_pair(smem + C::kOffA + s * C::kABytes, &tmA, bar, k0, arow);
+            if (C::kGate) tma_load_2d_pair(smem + C::kOffG + s * C::kABytes, &tmG, bar, k0, arow);
+            tma_load_2d_pair(smem + C::kOffB + s * C::kBBytes, &tmB, bar, k0, nrow);
+          }
+        }
+      }
+      // Drain: the MMAs released every stage (all copies landed, all commit
+      // arrivals on this CTA's barriers done) before the CTA may exit.
+      for (int i = it - S > 0 ? it - S : 0; i < it; ++i)
+        if (!mbar_wait(&empty[i % S], (i / S) & 1, p.status, SB_DEVERR_DRAIN)) break;
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA issuer (leader)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kPairM, BN);
+      int it = 0;
+      bool ok = true;
+      for (int j = 0; j < my_tiles && ok; ++j) {
+        const int buf = j & 1;
+        if (!mbar_wait_cluster(&acc_empty[buf], ((j >> 1) & 1) ^ 1, p.status, SB_DEVERR_EPI_WAIT)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + buf * C::kAccCols;
+        for (int kk = 0; kk < nk; ++kk, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          ok = C::kConvert ? mbar_wait_cluster(&conv[s], ph, p.status, SB_DEVERR_CONV_WAIT)
+                           : mbar_wait(&full[s], ph, p.status, SB_DEVERR_TMA_WAIT);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + C::kOffA + s * C::kABytes);
+          const uint32_t g_base = smem_u32(smem + C::kOffG + s * C::kABytes);
+          const uint32_t b_base = smem_u32(smem + C::kOffB + s * C::kBBytes);
+#pragma unroll
+          for (int q = 0; q < kTcBK / 16; ++q) {
+            const uint64_t bdesc = smem_desc_k_sw128(b_base + q * 32);
+            const uint32_t accum = (kk > 0 || q > 0) ? 1u : 0u;
+            tc_mma_bf16_pair(acc, smem_desc_k_sw128(a_base + q * 32), bdesc, idesc, accum);
+            if (C::kGate) tc_mma_bf16_pair(acc + BN, smem_desc_k_sw128(g_base + q * 32), bdesc, idesc, accum);
+          }
+          tc_commit_pair(&empty[s]);
+        }
+        tc_commit_pair(&acc_full[buf]);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 10) {
+    // ---------------------------------------------------------------- dequant (fp8 / int4, both CTAs)
+    if (C::kConvert) {
+      const int ctid = tid - 320;
+      int it = 0;
+      for (int j = 0; j < my_tiles; ++j) {
+        int g, nt, mt;
+        decode_tile(prefix, G, m_tiles, pair + j * npairs, g, nt, mt);
+        const int64_t arow0 = static_cast<int64_t>(g) * p.a_group_rows + mt * kPairM + rank * kTcBM;
+        bool ok = true;
+        for (int kk = 0; kk < nk; ++kk, ++it) {
+          const int s = it % S;
+          if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (it / S) & 1, p.status, SB_DEVERR_TMA_WAIT))) {
+            ok = false;
+            break;
+          }
+          const int k0 = kk * kTcBK;
+          convert_tile<WFMT>(smem + C::kOffRaw + s * C::kRawBytes, smem + C::kOffA + s * C::kABytes, p,
+                             p.a_scale, arow0, k0, ctid);
+          if (C::kGate)
+            convert_tile<WFMT>(smem + C::kOffRawG + s * C::kRawBytes, smem + C::kOffG + s * C::kABytes, p,
+                               p.a_gate_scale, arow0, k0, ctid);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(conv_lead + 8u * s);
+        }
+        if (!ok) break;
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 0-3, 6-9; both CTAs)
+    constexpr int HB = BN / 2;
+    const int quarter = warp & 3;
+    const int half = warp < 4 ? 0 : 1;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + half * HB;
+    for (int j = 0; j < my_tiles; ++j) {
+      int g, nt, mt;
+      decode_tile(prefix, G, m_tiles, pair + j * npairs, g, nt, mt);
+      const int buf = j & 1;
+      const int m = mt * kPairM + static_cast<int>(rank) * kTcBM + quarter * 32 + lane;
+      const int64_t arow = static_cast<int64_t>(g) * p.a_group_rows + m;
+      const bool mvalid = m < p.m_rows && arow < p.a_rows_total;
+      const float sa = (WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_scale)[arow] : 1.f;
+      const float sg = (C::kGate && WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_gate_scale)[arow] : 1.f;
+      const float bias = (p.bias && mvalid) ? p.bias[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
+      const float bgate = (C::kGate && p.bias_gate && mvalid) ? p.bias_gate[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
+      const int tn0 = s_off[g] + nt * BN + half * HB;
+      const int tend = min(min(s_off[g] + nt * BN + BN, s_off[g + 1]), p.max_rows);
+      float rsv[HB / 32];
+#pragma unroll
+      for (int i = 0; i < HB / 32; ++i) {
+        const int r = tn0 + i * 32 + lane;
+        rsv[i] = (EPI == SB_EPI_LINEAR && p.row_scale && r < tend) ? p.row_scale[r] : 1.f;
+      }
+      const bool ready = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (j >> 1) & 1, p.status, SB_DEVERR_EPI_WAIT));
+      tc_fence_after();
+      if (!ready) break;
+      const uint32_t acc_addr = lane_addr + buf * C::kAccCols;
+#pragma unroll
+      for (int c0 = 0; c0 < HB; c0 += 16) {
+        if (tn0 + c0 >= tend) break;  // warp-uniform
+        float v[16], vg[16], o[16];
+        tmem_ld16(acc_addr + c0, v);
+        if (C::kGate) tmem_ld16(acc_addr + BN + c0, vg);
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const float x = v[q] * sa + bias;
+          if (EPI == SB_EPI_LINEAR)
+            o[q] = x * __shfl_sync(0xffffffffu, rsv[(c0 + q) >> 5], (c0 + q) & 31);
+          else if (EPI == SB_EPI_GELU)
+            o[q] = gelu_bf16out(x);
+          else
+            o[q] = silu_bf16out(vg[q] * sg + bgate) * x;
+        }
+        if (!mvalid) continue;
+        const int nvalid = tend - (tn0 + c0);
+        const int64_t base = static_cast<int64_t>(tn0 + c0) * p.ldo + m;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          if (nvalid < 16 && q >= nvalid) break;
+          if (EPI == SB_EPI_LINEAR)
+            static_cast<float*>(p.out)[base + static_cast<int64_t>(q) * p.ldo] = o[q];
+          else
+            static_cast<__nv_bfloat16*>(p.out)[base + static_cast<int64_t>(q) * p.ldo] = __float2bfloat16_rn(o[q]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty_lead + 8u * buf);
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // neither CTA leaves while the other may still touch its shared memory
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, C::kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -816,6 +1119,68 @@ static int launch_persistent(const sb_grouped_gemm_args& a, cudaStream_t st) {
   return launch(kern, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, ma, mg, mb, a);
 }
 
+// SPIDER_B200_PAIR=0 keeps large tiles on one-CTA tiles (for comparisons).
+static bool use_pair(const sb_grouped_gemm_args& a) {
+  static const bool enabled = [] {
+    const char* e = std::getenv("SPIDER_B200_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  // fp8 / int4 weights stay on one-CTA tiles: their dequant-then-signal path
+  // measured slower on pairs than the one-CTA kernel.
+  return enabled && a.m_rows > kTcBM && a.wfmt == SB_W_BF16;
+}
+
+template <int BN, int WFMT, int EPI>
+static int launch_pair(const sb_grouped_gemm_args& a, cudaStream_t st) {
+  using C = PairCfg<BN, WFMT, EPI>;
+  static_assert(C::kMaxG == kPersistentMaxGroups, "tile table size");
+  auto kern = tc_gemm_pair_kernel<BN, WFMT, EPI>;
+  static int configured_device = -1;
+  static int max_pairs = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e);
+    cfg.gridDim = dim3(2 * current_sm_count());
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = current_sm_count() / 2;
+    }
+    max_pairs = n;
+    configured_device = dev;
+  }
+  if (a.num_groups > C::kMaxG || a.splits != 1) return SB_ERR_UNSUPPORTED;
+  CUtensorMap ma, mg, mb;
+  if (!weight_map(&ma, a, a.a)) return SB_ERR_UNSUPPORTED;
+  mg = ma;
+  if (C::kGate && !weight_map(&mg, a, a.a_gate)) return SB_ERR_UNSUPPORTED;
+  if (!make_map(&mb, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.k, a.max_rows, a.ldx * 2, kTcBK, C::kBH,
+                CU_TENSOR_MAP_SWIZZLE_128B))
+    return SB_ERR_UNSUPPORTED;
+  const int m_tiles = (a.m_rows + 2 * kTcBM - 1) / (2 * kTcBM);
+  const int64_t bound = static_cast<int64_t>(m_tiles) * ((a.max_rows + BN - 1) / BN + a.num_groups);
+  const int pairs = static_cast<int>(bound < max_pairs ? bound : max_pairs);
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, ma, mg, mb, a));
+}
+
 template <int BN, int WFMT, int EPI>
 static int launch_modes(const sb_grouped_gemm_args& a, cudaStream_t st) {
   const bool g = a.x_row_index != nullptr;
@@ -837,12 +1202,18 @@ static int launch_bn(const sb_grouped_gemm_args& a, cudaStream_t st, int bn) {
     case 128:
       if (g) return SB_ERR_UNSUPPORTED;
       if (!use_persistent(a)) return launch_tc<128, WFMT, EPI, false, false>(a, st);
+      if (use_pair(a)) return launch_pair<128, WFMT, EPI>(a, st);
       return launch_persistent<128, WFMT, EPI>(a, st);
     default:
       if (g) return SB_ERR_UNSUPPORTED;
       if (!use_persistent(a)) return launch_tc<256, WFMT, EPI, false, false>(a, st);
-      if constexpr (EPI == SB_EPI_SWIGLU) return launch_persistent<128, WFMT, EPI>(a, st);
-      else return launch_persistent<256, WFMT, EPI>(a, st);
+      if constexpr (EPI == SB_EPI_SWIGLU) {
+        if (use_pair(a)) return launch_pair<128, WFMT, EPI>(a, st);
+        return launch_persistent<128, WFMT, EPI>(a, st);
+      } else {
+        if (use_pair(a)) return launch_pair<256, WFMT, EPI>(a, st);
+        return launch_persistent<256, WFMT, EPI>(a, st);
+      }
   }
 }
 
