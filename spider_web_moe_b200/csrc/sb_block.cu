@@ -133,6 +133,7 @@ struct BlockBuffers {
   float* msg_f32;
   void* msg_act;
   int32_t *ffn_off, *ffn_row, *ffn_slot, *ffn_inv; float* ffn_w;
+  int32_t *dst_rank, *ffn_rank; float *dst_wsc, *ffn_wsc;  // scratch of the two-plan grouping launch
   void* x_ffn; void* act; float* y_ffn;
   void* hbuf[2];
   void* group_ws; size_t group_ws_bytes;
@@ -181,6 +182,10 @@ static size_t carve_block(const sb_block_dims& d, int n_cap, void* base, size_t 
   b->y_ffn = c.take<float>(ffn_rows * H);
   b->hbuf[0] = c.take<char>(N * H * as);
   b->hbuf[1] = c.take<char>(N * H * as);
+  b->dst_rank = c.take<int32_t>(N * K * M);
+  b->dst_wsc = c.take<float>(N * K * M);
+  b->ffn_rank = c.take<int32_t>(N * K);
+  b->ffn_wsc = c.take<float>(N * K);
   b->group_ws_bytes = sb_group_workspace_bytes(static_cast<int>(N), static_cast<int>(K * M), static_cast<int>(E));
   b->group_ws = c.take<char>(b->group_ws_bytes);
   b->cap_dst = cap_dst;
@@ -326,10 +331,25 @@ extern "C" SB_API size_t sb_block_workspace_bytes(const sb_block_dims* dims) {
   return carve_block(*dims, dims->max_tokens > 0 ? dims->max_tokens : 1, nullptr, ~size_t(0) >> 1, &b);
 }
 
+// The fused router + edge-generator kernel re-reads a selected source's E
+// generator rows for every token: it is used while those reads (N*K*E*H
+// elements) stay within this many bytes, a few microseconds of L2 traffic
+// (SPIDER_B200_FUSED_ROUTE_BYTES overrides; 0 disables the fused kernel).
+static double fused_route_max_bytes() {
+  static const double v = [] {
+    const char* e = std::getenv("SPIDER_B200_FUSED_ROUTE_BYTES");
+    return e ? std::atof(e) : 32.0 * 1024 * 1024;
+  }();
+  return v;
+}
+
 // Steps 1-8 of one loop: routing, edge graph and the edge-value GEMM.  Leaves
 // the routing in b.top_idx / b.top_w and the message partials in b.y_msg.
+// With `ffn_planned` non-null the expert dispatch plan (step 9) is built in
+// the same launch as the destination plan when both fit one CTA each, and
+// *ffn_planned says whether that happened.
 static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBuffers& b, const void* cur, int N,
-                      int l, int* msg_splits_out, cudaStream_t st) {
+                      int l, int* msg_splits_out, bool* ffn_planned, cudaStream_t st) {
   int rc = SB_OK;
   const int H = d.hidden, E = d.num_experts, K = d.top_k, M = d.edges_per_expert;
   const int KM = K * M;
@@ -337,35 +357,61 @@ static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBu
   const int64_t cap_dst = static_cast<int64_t>(N) * (E < KM ? E : KM);
   const bool tc_pref = d.engine != SB_ENGINE_SIMT;
 #define SB_TRY(x) do { rc = (x); if (rc) return rc; } while (0)
-  // 1. router
-  { StageScope sc_(0, st); SB_TRY(sb_router(cur, d.act_dtype, N, H, w->router_w, w->loop_bias + static_cast<int64_t>(l) * E, E, K,
-                                          b.top_idx, b.top_w, nullptr, st)); }
-  // 2-3. rows grouped by selected source; gather h (inside the GEMM when it can)
-  { StageScope sc_(1, st); SB_TRY(sb_group(b.top_idx, nullptr, N, K, E, 0, b.src_off, b.src_row, b.src_slot, b.src_w,
-                                         b.src_inv, b.group_ws, b.group_ws_bytes, st)); }
-  // 4. edge logits of the selected sources: rows [s*E, s*E+E) of the generator
-  {
-    sb_grouped_gemm_args a;
-    std::memset(&a, 0, sizeof(a));
-    a.engine = d.engine; a.wfmt = dense_fmt; a.act_dtype = d.act_dtype; a.epilogue = SB_EPI_LINEAR;
-    a.num_groups = E; a.m_rows = E; a.k = H; a.a_group_rows = E; a.lda = H;
-    a.a_rows_total = static_cast<int64_t>(E) * E; a.a = w->gen_w;
-    a.bias = w->gen_bias + static_cast<int64_t>(l) * E * E; a.bias_group_stride = E;
-    a.x = b.x_src; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N; a.offsets = b.src_off;
-    a.out = b.elog; a.ldo = E; a.splits = 1; a.status = b.status;
-    if (gemm_gathers(a, d.engine)) {
-      a.x = cur; a.x_row_index = b.src_row; a.x_rows = N;
-    } else {
-      StageScope sc_(2, st);
-      SB_TRY(sb_gather_rows(cur, d.act_dtype, H, b.src_row, b.src_off, E, N * K, b.x_src, st));
+  const double gen_bytes = static_cast<double>(N) * K * E * H * act_size(d.act_dtype);
+  const bool fused = gen_bytes <= fused_route_max_bytes() && route_edges_smem(d.act_dtype, H, E, K) <= kRouteEdgesMaxSmem;
+  if (fused) {
+    // 1-5 in one kernel: router, edge logits of the selected sources, top-M
+    StageScope sc_(0, st);
+    SB_TRY(route_edges(cur, d.act_dtype, N, H, w->router_w, w->loop_bias + static_cast<int64_t>(l) * E, E, K, w->gen_w,
+                       w->gen_bias + static_cast<int64_t>(l) * E * E, M, b.top_idx, b.top_w, b.edge_idx, b.edge_w,
+                       st));
+  } else {
+    // 1. router
+    { StageScope sc_(0, st); SB_TRY(sb_router(cur, d.act_dtype, N, H, w->router_w, w->loop_bias + static_cast<int64_t>(l) * E, E, K,
+                                            b.top_idx, b.top_w, nullptr, st)); }
+    // 2-3. rows grouped by selected source; gather h (inside the GEMM when it can)
+    { StageScope sc_(1, st); SB_TRY(sb_group(b.top_idx, nullptr, N, K, E, 0, b.src_off, b.src_row, b.src_slot, b.src_w,
+                                           b.src_inv, b.group_ws, b.group_ws_bytes, st)); }
+    // 4. edge logits of the selected sources: rows [s*E, s*E+E) of the generator
+    {
+      sb_grouped_gemm_args a;
+      std::memset(&a, 0, sizeof(a));
+      a.engine = d.engine; a.wfmt = dense_fmt; a.act_dtype = d.act_dtype; a.epilogue = SB_EPI_LINEAR;
+      a.num_groups = E; a.m_rows = E; a.k = H; a.a_group_rows = E; a.lda = H;
+      a.a_rows_total = static_cast<int64_t>(E) * E; a.a = w->gen_w;
+      a.bias = w->gen_bias + static_cast<int64_t>(l) * E * E; a.bias_group_stride = E;
+      a.x = b.x_src; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N; a.offsets = b.src_off;
+      a.out = b.elog; a.ldo = E; a.splits = 1; a.status = b.status;
+      if (gemm_gathers(a, d.engine)) {
+        a.x = cur; a.x_row_index = b.src_row; a.x_rows = N;
+      } else {
+        StageScope sc_(2, st);
+        SB_TRY(sb_gather_rows(cur, d.act_dtype, H, b.src_row, b.src_off, E, N * K, b.x_src, st));
+      }
+      { StageScope sc_(3, st); SB_TRY(run_gemm(a, d.engine, st)); }
     }
-    { StageScope sc_(3, st); SB_TRY(run_gemm(a, d.engine, st)); }
+    // 5. top-M destinations per (token, source)
+    { StageScope sc_(4, st); SB_TRY(sb_edge_topm(b.elog, E, E, M, b.src_slot, b.src_off, E, N * K, b.edge_idx, b.edge_w, st)); }
   }
-  // 5. top-M destinations per (token, source)
-  { StageScope sc_(4, st); SB_TRY(sb_edge_topm(b.elog, E, E, M, b.src_slot, b.src_off, E, N * K, b.edge_idx, b.edge_w, st)); }
-  // 6-7. (token, destination) pairs with summed coefficients
-  { StageScope sc_(5, st); SB_TRY(sb_group(b.edge_idx, b.edge_w, N, KM, E, 0, b.dst_off, b.dst_row, b.dst_slot, b.dst_w,
-                                         b.dst_inv, b.group_ws, b.group_ws_bytes, st)); }
+  // 6-7. (token, destination) pairs with summed coefficients (and, when asked,
+  // the expert dispatch plan of step 9 in the same launch)
+  bool both = false;
+  if (ffn_planned) {
+    const GroupJob jd{b.edge_idx, b.edge_w, N, KM, E, 0, b.dst_off, b.dst_row, b.dst_slot, b.dst_w, b.dst_inv,
+                      b.dst_rank, b.dst_wsc};
+    const GroupJob jf{b.top_idx, b.top_w, N, K, E, SB_GROUP_POSITIVE_ONLY, b.ffn_off, b.ffn_row, b.ffn_slot, b.ffn_w,
+                      b.ffn_inv, b.ffn_rank, b.ffn_wsc};
+    StageScope sc_(5, st);
+    rc = group_pair_launch(jd, jf, st);
+    if (rc != SB_OK && rc != SB_ERR_UNSUPPORTED) return rc;
+    both = rc == SB_OK;
+    *ffn_planned = both;
+  }
+  if (!both) {
+    StageScope sc_(5, st);
+    SB_TRY(sb_group(b.edge_idx, b.edge_w, N, KM, E, 0, b.dst_off, b.dst_row, b.dst_slot, b.dst_w, b.dst_inv,
+                    b.group_ws, b.group_ws_bytes, st));
+  }
   // 8. c[t,d] * W_edge[d] h[t]
   {
     sb_grouped_gemm_args a;
@@ -429,10 +475,14 @@ extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block
   for (int l = loop_begin; l < loop_end; ++l) {
     void* next = (l == loop_end - 1) ? h_out : b.hbuf[(l - loop_begin) & 1];
     int msg_splits = 1;
-    SB_TRY(route_loop(d, w, b, cur, N, l, &msg_splits, st));
-    // 9. dispatch plan of the expert FFN
-    { StageScope sc_(8, st); SB_TRY(sb_group(b.top_idx, b.top_w, N, K, E, SB_GROUP_POSITIVE_ONLY, b.ffn_off, b.ffn_row,
-                                           b.ffn_slot, b.ffn_w, b.ffn_inv, b.group_ws, b.group_ws_bytes, st)); }
+    bool ffn_planned = false;
+    SB_TRY(route_loop(d, w, b, cur, N, l, &msg_splits, &ffn_planned, st));
+    // 9. dispatch plan of the expert FFN (unless built with the destination plan)
+    if (!ffn_planned) {
+      StageScope sc_(8, st);
+      SB_TRY(sb_group(b.top_idx, b.top_w, N, K, E, SB_GROUP_POSITIVE_ONLY, b.ffn_off, b.ffn_row, b.ffn_slot, b.ffn_w,
+                      b.ffn_inv, b.group_ws, b.group_ws_bytes, st));
+    }
     // 10-11. messages (sum over the token's destinations), then up projection +
     // activation with the message rows gathered in expert order.
     {
@@ -507,7 +557,7 @@ extern "C" SB_API int sb_block_route(const sb_block_dims* dims, const sb_block_w
   const int N = n_tokens, H = d.hidden, E = d.num_experts, K = d.top_k, KM = K * d.edges_per_expert;
   const int64_t cap_dst = static_cast<int64_t>(N) * (E < KM ? E : KM);
   int msg_splits = 1;
-  if ((rc = route_loop(d, w, b, h, N, loop_idx, &msg_splits, st))) return rc;
+  if ((rc = route_loop(d, w, b, h, N, loop_idx, &msg_splits, nullptr, st))) return rc;
   if ((rc = sb_combine_rows(b.y_msg, H, msg_splits, cap_dst * H, b.dst_inv, KM, N, H, messages_f32, nullptr, K,
                             messages, d.act_dtype, st)))
     return rc;

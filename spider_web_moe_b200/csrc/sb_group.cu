@@ -34,16 +34,14 @@ SB_DEVINL int entry_group(const int32_t* __restrict__ idx, const float* __restri
   return g;
 }
 
-__global__ void __launch_bounds__(kGroupThreads, 1)
-group_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w, int n_rows, int slots,
-             int G, int flags, int32_t* __restrict__ offsets, int32_t* __restrict__ perm_row,
-             int32_t* __restrict__ perm_slot, float* __restrict__ perm_w, int32_t* __restrict__ inv,
-             int32_t* __restrict__ rank_scratch, float* __restrict__ w_scratch) {
+// The whole grouping in one CTA (any block size that is a multiple of 32).
+SB_DEVINL void group_one_cta(const int32_t* __restrict__ idx, const float* __restrict__ w, int n_rows, int slots,
+                             int G, int flags, int32_t* __restrict__ offsets, int32_t* __restrict__ perm_row,
+                             int32_t* __restrict__ perm_slot, float* __restrict__ perm_w, int32_t* __restrict__ inv,
+                             int32_t* __restrict__ rank_scratch, float* __restrict__ w_scratch) {
   __shared__ int wcnt[32][kGroupMaxG];
   __shared__ int run_total[kGroupMaxG];
   __shared__ int s_off[kGroupMaxG + 1];
-  pdl_wait();
-  pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nthreads = blockDim.x, nwarps = nthreads >> 5;
   const int64_t total = static_cast<int64_t>(n_rows) * slots;
@@ -99,6 +97,25 @@ group_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w, int n
     perm_w[pos] = w_scratch[e];
     inv[e] = pos;
   }
+}
+
+__global__ void __launch_bounds__(kGroupThreads, 1)
+group_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w, int n_rows, int slots,
+             int G, int flags, int32_t* __restrict__ offsets, int32_t* __restrict__ perm_row,
+             int32_t* __restrict__ perm_slot, float* __restrict__ perm_w, int32_t* __restrict__ inv,
+             int32_t* __restrict__ rank_scratch, float* __restrict__ w_scratch) {
+  pdl_wait();
+  pdl_trigger();
+  group_one_cta(idx, w, n_rows, slots, G, flags, offsets, perm_row, perm_slot, perm_w, inv, rank_scratch, w_scratch);
+}
+
+// Two independent groupings in one launch, one CTA each.
+__global__ void __launch_bounds__(kGroupThreads, 1) group_pair_kernel(const GroupJob j0, const GroupJob j1) {
+  pdl_wait();
+  pdl_trigger();
+  const GroupJob& j = blockIdx.x == 0 ? j0 : j1;
+  group_one_cta(j.idx, j.w, j.n_rows, j.slots, j.num_groups, j.flags, j.offsets, j.perm_row, j.perm_slot, j.perm_w,
+                j.inv, j.rank_scratch, j.w_scratch);
 }
 
 // ---------------------------------------------------------------------------
@@ -273,6 +290,16 @@ extern "C" SB_API int sb_group(const int32_t* idx, const float* w, int n_rows, i
 }
 
 namespace sb {
+int group_pair_launch(const GroupJob& j0, const GroupJob& j1, cudaStream_t st) {
+  const int64_t t0 = static_cast<int64_t>(j0.n_rows) * j0.slots, t1 = static_cast<int64_t>(j1.n_rows) * j1.slots;
+  const int64_t tmax = t0 > t1 ? t0 : t1;
+  if (tmax > static_cast<int64_t>(kGroupSingleCtaMax) || j0.num_groups > kGroupMaxG || j1.num_groups > kGroupMaxG)
+    return SB_ERR_UNSUPPORTED;
+  int threads = static_cast<int>(((tmax + 31) / 32) * 32);
+  threads = threads < 64 ? 64 : (threads > kGroupThreads ? kGroupThreads : threads);
+  return launch(group_pair_kernel, dim3(2), dim3(threads), 0, st, j0, j1);
+}
+
 // Launch of the grouping kernel with caller-chosen scratch arrays (used by the
 // no-allocation entry point, whose scratch is a fixed device array).
 int group_launch_with_scratch(const int32_t* idx, const float* w, int n_rows, int slots, int num_groups, int flags,

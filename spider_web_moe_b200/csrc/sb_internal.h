@@ -67,6 +67,32 @@ int group_launch_with_scratch(const int32_t* idx, const float* w, int n_rows, in
                               int32_t* offsets, int32_t* perm_row, int32_t* perm_slot, float* perm_w, int32_t* inv,
                               int32_t* rank_scratch, float* w_scratch, cudaStream_t st);
 
+// One grouping (sb_group's arguments with explicit scratch of n_rows*slots
+// entries each); two of them run as one launch of two CTAs (sb_group.cu).
+struct GroupJob {
+  const int32_t* idx;
+  const float* w;
+  int n_rows, slots, num_groups, flags;
+  int32_t* offsets;
+  int32_t* perm_row;
+  int32_t* perm_slot;
+  float* perm_w;
+  int32_t* inv;
+  int32_t* rank_scratch;
+  float* w_scratch;
+};
+// SB_ERR_UNSUPPORTED when either grouping is too large for one CTA.
+int group_pair_launch(const GroupJob& j0, const GroupJob& j1, cudaStream_t st);
+
+// Router + edge generator + edge top-M of small batches in one kernel
+// (sb_router.cu); SB_ERR_UNSUPPORTED when its shared memory would exceed
+// kRouteEdgesMaxSmem.
+constexpr size_t kRouteEdgesMaxSmem = 160 * 1024;
+size_t route_edges_smem(int act_dtype, int hidden, int E, int K);
+int route_edges(const void* h, int act_dtype, int n_tokens, int hidden, const void* router_w, const float* rbias,
+                int E, int K, const void* gen_w, const float* gen_bias, int M, int32_t* top_idx, float* top_w,
+                int32_t* edge_idx, float* edge_w, cudaStream_t st);
+
 // Device properties cached per device.
 int current_sm_count();
 int current_cc_major();

@@ -35,6 +35,88 @@ template <> struct Vec8<__nv_bfloat16> {
   }
 };
 
+// Softmax over one token's E router logits (fp32, spider_moe/model.py:256),
+// top-K by repeated arg-max (model.py:257; a taken expert is masked with -1
+// since probabilities are >= 0, equal values go to the smaller id) and the
+// renormalisation of model.py:258.  One warp; lane k < K returns slot k.
+SB_DEVINL void router_select(const float* logits, int E, int K, int lane, float* probs_out, int& sel_i,
+                             float& sel_w) {
+  float logit[kRouterMaxE / 32];
+#pragma unroll
+  for (int i = 0; i < kRouterMaxE / 32; ++i) logit[i] = (lane + 32 * i < E) ? logits[lane + 32 * i] : -INFINITY;
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kRouterMaxE / 32; ++i) mx = fmaxf(mx, logit[i]);
+  mx = warp_max(mx);
+  float p[kRouterMaxE / 32];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRouterMaxE / 32; ++i) {
+    p[i] = (lane + 32 * i < E) ? expf(logit[i] - mx) : 0.f;
+    s += p[i];
+  }
+  s = warp_sum(s);
+#pragma unroll
+  for (int i = 0; i < kRouterMaxE / 32; ++i) {
+    p[i] = p[i] / s;
+    if (probs_out && lane + 32 * i < E) probs_out[lane + 32 * i] = p[i];
+  }
+  float w = 0.f, sum_w = 0.f;
+  int idx = -1;
+  for (int k = 0; k < K; ++k) {
+    float bv = -1.f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kRouterMaxE / 32; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && (p[i] > bv || (p[i] == bv && e < bi))) { bv = p[i]; bi = e; }
+    }
+    warp_argmax(bv, bi);
+#pragma unroll
+    for (int i = 0; i < kRouterMaxE / 32; ++i)
+      if (lane + 32 * i == bi) p[i] = -1.f;
+    sum_w += bv;
+    if (lane == k) { w = bv; idx = bi; }
+  }
+  sel_i = idx;
+  sel_w = w / fmaxf(sum_w, 1e-9f);
+}
+
+// Top-M of one source's E destination logits (spider_moe/model.py:264-266):
+// repeated arg-max with a taken mask (equal values to the smaller id), then an
+// fp32 softmax over the M selected values.  One warp; lane m < M returns slot m.
+SB_DEVINL void topm_select(const float* logits, int E, int M, int lane, int& sel_i, float& sel_w) {
+  float v[kRouterMaxE / 32];
+#pragma unroll
+  for (int i = 0; i < kRouterMaxE / 32; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < E ? logits[e] : -INFINITY;
+  }
+  uint32_t taken = 0;  // bit i: destination lane + 32*i already selected
+  float sel_v = -INFINITY, first = -INFINITY;
+  int idx = -1;
+  for (int m = 0; m < M; ++m) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kRouterMaxE / 32; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && !(taken & (1u << i)) && (bi == 0x7fffffff || v[i] > bv || (v[i] == bv && e < bi))) {
+        bv = v[i];
+        bi = e;
+      }
+    }
+    warp_argmax(bv, bi);
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    if (m == 0) first = bv;  // the largest selected value
+    if (lane == m) { sel_v = bv; idx = bi; }
+  }
+  const float ex = (lane < M) ? expf(sel_v - first) : 0.f;
+  const float s = warp_sum(ex);
+  sel_i = idx;
+  sel_w = ex / s;
+}
+
 // One CTA per kRouterTok tokens.  Their hidden rows are staged in shared
 // memory; warp w computes the logits of experts w, w+8, ... for all of them,
 // four experts (and their weight loads) at a time, so the weight rows are read
@@ -104,51 +186,13 @@ router_kernel(const T* __restrict__ h, int n_tokens, int hidden, const T* __rest
   }
   __syncthreads();
   if (warp >= ntok) return;
-  const int token = t0 + warp;
-  float logit[kRouterMaxE / 32];
-#pragma unroll
-  for (int i = 0; i < kRouterMaxE / 32; ++i) logit[i] = (lane + 32 * i < E) ? slog[warp * E + lane + 32 * i] : -INFINITY;
-  // fp32 softmax over E (spider_moe/model.py:256).
-  float mx = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < kRouterMaxE / 32; ++i) mx = fmaxf(mx, logit[i]);
-  mx = warp_max(mx);
-  float p[kRouterMaxE / 32];
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < kRouterMaxE / 32; ++i) {
-    p[i] = (lane + 32 * i < E) ? expf(logit[i] - mx) : 0.f;
-    s += p[i];
-  }
-  s = warp_sum(s);
-#pragma unroll
-  for (int i = 0; i < kRouterMaxE / 32; ++i) {
-    p[i] = p[i] / s;
-    if (probs_out && lane + 32 * i < E) probs_out[static_cast<size_t>(token) * E + lane + 32 * i] = p[i];
-  }
-  // top-K by repeated arg-max (model.py:257); a taken expert is masked with -1
-  // (probabilities are >= 0), equal values go to the smaller expert id.
-  float sel_w = 0.f, sum_w = 0.f;
-  int sel_i = -1;
-  for (int k = 0; k < K; ++k) {
-    float bv = -1.f;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < kRouterMaxE / 32; ++i) {
-      const int e = lane + 32 * i;
-      if (e < E && (p[i] > bv || (p[i] == bv && e < bi))) { bv = p[i]; bi = e; }
-    }
-    warp_argmax(bv, bi);
-#pragma unroll
-    for (int i = 0; i < kRouterMaxE / 32; ++i)
-      if (lane + 32 * i == bi) p[i] = -1.f;
-    sum_w += bv;
-    if (lane == k) { sel_w = bv; sel_i = bi; }
-  }
-  // renormalise (model.py:258)
+  int sel_i;
+  float sel_w;
+  router_select(slog + warp * E, E, K, lane, probs_out ? probs_out + static_cast<size_t>(t0 + warp) * E : nullptr,
+                sel_i, sel_w);
   if (lane < K) {
-    top_idx[static_cast<size_t>(token) * K + lane] = sel_i;
-    top_w[static_cast<size_t>(token) * K + lane] = sel_w / fmaxf(sum_w, 1e-9f);
+    top_idx[static_cast<size_t>(t0 + warp) * K + lane] = sel_i;
+    top_w[static_cast<size_t>(t0 + warp) * K + lane] = sel_w;
   }
 }
 
@@ -163,40 +207,165 @@ edge_topm_kernel(const float* __restrict__ logits, int64_t ld, int E, int M,
   const int warps = (gridDim.x * blockDim.x) >> 5;
   const int rows = min(offsets[G], max_rows);
   for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
-    float v[kRouterMaxE / 32];
-#pragma unroll
-    for (int i = 0; i < kRouterMaxE / 32; ++i) {
-      const int e = lane + 32 * i;
-      v[i] = e < E ? logits[static_cast<int64_t>(r) * ld + e] : -INFINITY;
-    }
     const int slot = perm_slot[r];
-    uint32_t taken = 0;  // bit i: destination lane + 32*i already selected
-    float sel_v = -INFINITY, first = -INFINITY;
-    int sel_i = -1;
-    for (int m = 0; m < M; ++m) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int i = 0; i < kRouterMaxE / 32; ++i) {
-        const int e = lane + 32 * i;
-        if (e < E && !(taken & (1u << i)) && (bi == 0x7fffffff || v[i] > bv || (v[i] == bv && e < bi))) {
-          bv = v[i];
-          bi = e;
-        }
-      }
-      warp_argmax(bv, bi);
-      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-      if (m == 0) first = bv;  // the largest selected value
-      if (lane == m) { sel_v = bv; sel_i = bi; }
-    }
-    // softmax over the M selected values (fp32): exp(v - max) / sum.
-    float ex = (lane < M) ? expf(sel_v - first) : 0.f;
-    const float s = warp_sum(ex);
+    int sel_i;
+    float sel_w;
+    topm_select(logits + static_cast<int64_t>(r) * ld, E, M, lane, sel_i, sel_w);
     if (lane < M) {
       edge_idx[static_cast<int64_t>(slot) * M + lane] = sel_i;
-      edge_w[static_cast<int64_t>(slot) * M + lane] = ex / s;
+      edge_w[static_cast<int64_t>(slot) * M + lane] = sel_w;
     }
   }
+}
+
+// Router, edge generator and edge top-M of one token per CTA, for small
+// batches (decode), where recomputing a selected source's E generator rows
+// per token costs less than grouping tokens by source for a GEMM.  The
+// hidden row is staged in shared memory; every warp keeps the loads of four
+// weight rows (two chunk steps each) in flight.  The router logits use the
+// same per-lane accumulation order and tree reduction as router_kernel; the
+// edge logits of a selected source s are its generator rows s*E .. s*E+E-1
+// (spider_moe/model.py:260-263) dotted with the hidden row in fp32.
+constexpr int kRouteRows = 4;
+
+template <typename T>
+SB_DEVINL void dot_rows4(const T* __restrict__ sh, const T* const* rows, int nrows, int nchunks, int lane,
+                         float* acc) {
+#pragma unroll
+  for (int j = 0; j < kRouteRows; ++j) acc[j] = 0.f;
+#pragma unroll 2
+  for (int c = lane; c < nchunks; c += 32) {
+    float hv[8];
+    Vec8<T>::load(sh + c * 8, hv);
+#pragma unroll
+    for (int j = 0; j < kRouteRows; ++j) {
+      if (j < nrows) {
+        float wv[8];
+        Vec8<T>::load(rows[j] + c * 8, wv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[j] = fmaf(hv[i], wv[i], acc[j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kRouteRows; ++j) acc[j] = warp_sum(acc[j]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kRouterWarps * 32)
+route_edges_kernel(const T* __restrict__ h, int hidden, const T* __restrict__ wr, const float* __restrict__ rbias,
+                   int E, int K, const T* __restrict__ gen_w, const float* __restrict__ gen_bias, int M,
+                   int32_t* __restrict__ top_idx, float* __restrict__ top_w, int32_t* __restrict__ edge_idx,
+                   float* __restrict__ edge_w) {
+  extern __shared__ __align__(16) uint8_t route_smem[];
+  T* sh = reinterpret_cast<T*>(route_smem);                                                      // [hidden]
+  float* slog = reinterpret_cast<float*>(route_smem + ((hidden * sizeof(T) + 15) & ~size_t(15)));  // [E]
+  float* selog = slog + E;                                                                        // [K][E]
+  int* ssel = reinterpret_cast<int*>(selog + K * E);                                              // [K]
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.x;
+  const int nchunks = hidden >> 3;
+  {
+    const int vec_per_row = hidden * static_cast<int>(sizeof(T)) / 16;
+    const uint4* src = reinterpret_cast<const uint4*>(h + static_cast<size_t>(t) * hidden);
+    uint4* dst = reinterpret_cast<uint4*>(sh);
+    for (int i = threadIdx.x; i < vec_per_row; i += blockDim.x) dst[i] = src[i];
+  }
+  __syncthreads();
+  // router logits: warp w takes rows w*4 .. w*4+3, then + 32 ...
+  for (int r0 = warp * kRouteRows; r0 < E; r0 += kRouterWarps * kRouteRows) {
+    const T* rows[kRouteRows];
+    const int nr = min(kRouteRows, E - r0);
+#pragma unroll
+    for (int j = 0; j < kRouteRows; ++j) rows[j] = wr + static_cast<size_t>(min(r0 + j, E - 1)) * hidden;
+    float acc[kRouteRows];
+    dot_rows4<T>(sh, rows, nr, nchunks, lane, acc);
+    if (lane == 0)
+#pragma unroll
+      for (int j = 0; j < kRouteRows; ++j)
+        if (j < nr) slog[r0 + j] = acc[j] + rbias[r0 + j];
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int sel_i;
+    float sel_w;
+    router_select(slog, E, K, lane, nullptr, sel_i, sel_w);
+    if (lane < K) {
+      top_idx[static_cast<size_t>(t) * K + lane] = sel_i;
+      top_w[static_cast<size_t>(t) * K + lane] = sel_w;
+      ssel[lane] = sel_i;
+    }
+  }
+  __syncthreads();
+  // edge logits: row r = k*E + j is generator row ssel[k]*E + j
+  const int KE = K * E;
+  for (int r0 = warp * kRouteRows; r0 < KE; r0 += kRouterWarps * kRouteRows) {
+    const T* rows[kRouteRows];
+    const int nr = min(kRouteRows, KE - r0);
+#pragma unroll
+    for (int j = 0; j < kRouteRows; ++j) {
+      const int r = min(r0 + j, KE - 1);
+      rows[j] = gen_w + (static_cast<size_t>(ssel[r / E]) * E + r % E) * hidden;
+    }
+    float acc[kRouteRows];
+    dot_rows4<T>(sh, rows, nr, nchunks, lane, acc);
+    if (lane == 0)
+#pragma unroll
+      for (int j = 0; j < kRouteRows; ++j)
+        if (j < nr) {
+          const int r = r0 + j;
+          selog[r] = acc[j] + gen_bias[static_cast<size_t>(ssel[r / E]) * E + r % E];
+        }
+  }
+  __syncthreads();
+  for (int k = warp; k < K; k += kRouterWarps) {
+    int sel_i;
+    float sel_w;
+    topm_select(selog + k * E, E, M, lane, sel_i, sel_w);
+    if (lane < M) {
+      const int64_t slot = static_cast<int64_t>(t) * K + k;
+      edge_idx[slot * M + lane] = sel_i;
+      edge_w[slot * M + lane] = sel_w;
+    }
+  }
+}
+
+size_t route_edges_smem(int act_dtype, int hidden, int E, int K) {
+  const size_t esize = act_dtype == SB_F32 ? 4 : 2;
+  return ((hidden * esize + 15) & ~size_t(15)) + static_cast<size_t>(E) * 4 + static_cast<size_t>(K) * E * 4 +
+         static_cast<size_t>(K) * 4;
+}
+
+int route_edges(const void* h, int act_dtype, int n_tokens, int hidden, const void* router_w, const float* rbias,
+                int E, int K, const void* gen_w, const float* gen_bias, int M, int32_t* top_idx, float* top_w,
+                int32_t* edge_idx, float* edge_w, cudaStream_t st) {
+  if (n_tokens <= 0) return SB_OK;
+  if (E > kRouterMaxE || K > 32 || M > 32 || K > E || M > E || hidden % 8) return SB_ERR_ARG;
+  const size_t smem = route_edges_smem(act_dtype, hidden, E, K);
+  if (smem > kRouteEdgesMaxSmem) return SB_ERR_UNSUPPORTED;
+  const dim3 grid(n_tokens), block(kRouterWarps * 32);
+  if (act_dtype == SB_F32) {
+    static bool attr_set = false;
+    if (!attr_set) {
+      cudaFuncSetAttribute(route_edges_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRouteEdgesMaxSmem);
+      attr_set = true;
+    }
+    return launch(route_edges_kernel<float>, grid, block, smem, st, static_cast<const float*>(h), hidden,
+                  static_cast<const float*>(router_w), rbias, E, K, static_cast<const float*>(gen_w), gen_bias, M,
+                  top_idx, top_w, edge_idx, edge_w);
+  }
+  if (act_dtype != SB_BF16) return SB_ERR_ARG;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(route_edges_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kRouteEdgesMaxSmem);
+    attr_set = true;
+  }
+  return launch(route_edges_kernel<__nv_bfloat16>, grid, block, smem, st, static_cast<const __nv_bfloat16*>(h),
+                hidden, static_cast<const __nv_bfloat16*>(router_w), rbias, E, K,
+                static_cast<const __nv_bfloat16*>(gen_w), gen_bias, M, top_idx, top_w, edge_idx, edge_w);
 }
 
 }  // namespace sb
