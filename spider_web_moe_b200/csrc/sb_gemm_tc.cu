@@ -353,32 +353,46 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           mbar_arrive(&conv[s]);
         }
       }
+      const int tn0 = n0 + t * BN;
+      const int tend = min(tn0 + BN, n_end);
+      // LINEAR row scales of the tile, one per lane and 32 columns, read before
+      // the accumulator wait so their latency overlaps the MMAs
+      float rsv[BN >= 32 ? BN / 32 : 1];
+#pragma unroll
+      for (int i = 0; i < (BN >= 32 ? BN / 32 : 1); ++i) {
+        const int r = tn0 + i * 32 + lane;
+        rsv[i] = (EPI == SB_EPI_LINEAR && p.row_scale && r < tend && i * 32 + lane < BN) ? p.row_scale[r] : 1.f;
+      }
       // tcgen05.ld is warp-collective: every lane must take the same branch.
       live = __all_sync(0xffffffffu, live && mbar_wait(acc_full, t & 1, p.status, SB_DEVERR_EPI_WAIT));
       tc_fence_after();
       if (!live) break;
-      const int tn0 = n0 + t * BN;
-      const int tend = min(tn0 + BN, n_end);
+#pragma unroll
       for (int c0 = 0; c0 < BN; c0 += 16) {
-        if (tn0 + c0 >= tend) break;
-        float v[16], vg[16];
+        if (tn0 + c0 >= tend) break;  // warp-uniform
+        float v[16], vg[16], o[16];
         tmem_ld16(lane_addr + c0, v);
         if (C::kGate) tmem_ld16(lane_addr + BN + c0, vg);
-        if (!mvalid) continue;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int r = tn0 + c0 + j;
-          if (r >= tend) break;
           const float x = v[j] * sa + bias;
-          if (EPI == SB_EPI_LINEAR) {
-            const float rs = p.row_scale ? p.row_scale[r] : 1.f;
-            static_cast<float*>(p.out)[blockIdx.z * p.split_stride + static_cast<int64_t>(r) * p.ldo + m] = x * rs;
-          } else if (EPI == SB_EPI_GELU) {
-            static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(r) * p.ldo + m] = __float2bfloat16_rn(gelu_bf16out(x));
-          } else {
-            const float gx = vg[j] * sg + bgate;
-            static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(r) * p.ldo + m] = __float2bfloat16_rn(silu_bf16out(gx) * x);
-          }
+          if (EPI == SB_EPI_LINEAR)
+            o[j] = x * __shfl_sync(0xffffffffu, rsv[(c0 + j) >> 5], (c0 + j) & 31);
+          else if (EPI == SB_EPI_GELU)
+            o[j] = gelu_bf16out(x);
+          else
+            o[j] = silu_bf16out(vg[j] * sg + bgate) * x;
+        }
+        if (!mvalid) continue;
+        const int nvalid = tend - (tn0 + c0);
+        const int64_t base = static_cast<int64_t>(tn0 + c0) * p.ldo + m;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (nvalid < 16 && j >= nvalid) break;
+          if (EPI == SB_EPI_LINEAR)
+            static_cast<float*>(p.out)[blockIdx.z * p.split_stride + base + static_cast<int64_t>(j) * p.ldo] = o[j];
+          else
+            static_cast<__nv_bfloat16*>(p.out)[base + static_cast<int64_t>(j) * p.ldo] = __float2bfloat16_rn(o[j]);
         }
       }
       tc_fence_before();
