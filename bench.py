@@ -368,7 +368,6 @@ def run_b200_ep(args, rank, world, local, device):
     peaks, peak_kind = load_peaks()
     per_rank_bytes = (ep.dense.weight_bytes() + (ep.local.weight_bytes() if ep.local else 0)) * cfg.num_loops
     achieved = per_rank_bytes / (ms_step / 1e3) / 1e9
-    loop_launches = 7 + 3 + 5 + 1
     line = {
         "metric": "spider_moe_block_tokens_per_s", "value": n * world / (ms_step / 1e3), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
@@ -383,7 +382,7 @@ def run_b200_ep(args, rank, world, local, device):
         "clocks": clk.summary(),
         "e2e": {"value": n * world / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 2 * n * cfg.hidden_size * 2,
                 "d2h_bytes_per_step": n * cfg.hidden_size * 2, "ms_per_step": e2e_ms},
-        "gpu_launches": loop_launches * cfg.num_loops * args.steps,
+        "gpu_launches": ep.kernels_per_replay * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_kind": f"{peak_kind} (STREAM copy)",
                      "traffic": None, "kernel": "whole expert-parallel step per rank (dense + local expert weights)"},
@@ -447,7 +446,7 @@ def run_b200(args):
     ms = max_over_ranks(ms, world, device)
     ms_step = ms / args.steps
     value = n * world / (ms_step / 1e3)
-    gpu_launches = 13 * cfg.num_loops * args.steps
+    gpu_launches = g.kernels_per_replay * args.steps  # libspider_b200 kernels counted at capture
 
     # e2e: host (pinned) input -> device, all loops, device -> host output, every step
     h_host = h.cpu().pin_memory()

@@ -317,6 +317,12 @@ SB_API const char* sb_stage_name(int stage);
 SB_API int sb_stage_timing(int enable);
 SB_API int sb_stage_timing_read(double* ms, int* launches, int n_stages);
 
+/* Kernel launches this library has enqueued since it was loaded, counting
+ * those recorded into a CUDA graph during stream capture (no reference
+ * counterpart): the difference around one captured forward is the number of
+ * kernels each replay runs. */
+SB_API unsigned long long sb_kernel_launches(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -108,6 +108,7 @@ SIGNATURES = {
     "sb_stage_name": (C.c_char_p, [i32]),
     "sb_stage_timing": (i32, [i32]),
     "sb_stage_timing_read": (i32, [C.POINTER(C.c_double), C.POINTER(i32), i32]),
+    "sb_kernel_launches": (C.c_ulonglong, []),
 }
 
 

@@ -19,6 +19,7 @@
 //  11  grouped GEMM         up projection + GELU / SwiGLU            (sparse_experts.py:60-61)
 //  12  grouped GEMM         down projection * routing weight         (sparse_experts.py:62-63)
 //  13  sb_combine_ln        delta + LayerNorm epilogue               (model.py:317)
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -51,6 +52,9 @@ int current_cc_major() {
   }
   return cached[dev];
 }
+
+static std::atomic<unsigned long long> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 bool pdl_enabled() {
   static int cached = -1;
@@ -762,5 +766,7 @@ extern "C" SB_API int sb_stage_timing_read(double* ms, int* launches, int n_stag
 extern "C" SB_API const char* sb_stage_name(int stage) {
   return (stage >= 0 && stage < kNumStages) ? kStageNames[stage] : "";
 }
+
+extern "C" SB_API unsigned long long sb_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 extern "C" SB_API int sb_num_stages(void) { return kNumStages; }

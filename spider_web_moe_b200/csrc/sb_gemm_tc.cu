@@ -1192,6 +1192,7 @@ static int launch_pair(const sb_grouped_gemm_args& a, cudaStream_t st) {
   const int pairs = static_cast<int>(bound < max_pairs ? bound : max_pairs);
   cfg.gridDim = dim3(2 * pairs);
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  note_launch();
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, ma, mg, mb, a));
 }
 

@@ -46,9 +46,14 @@ bool tc_fixed_groups(const sb_grouped_gemm_args& a);
 // by SPIDER_B200_PDL=0.  Kernels launched this way call pdl_wait() first.
 bool pdl_enabled();
 
+// Kernel launches enqueued by this library (also those recorded into a CUDA
+// graph while capturing); read by sb_kernel_launches().
+void note_launch();
+
 template <typename... KArgs, typename... Args>
 inline int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                   Args&&... args) {
+  note_launch();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;

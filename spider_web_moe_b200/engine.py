@@ -312,8 +312,11 @@ class CapturedBlock:
         torch.cuda.current_stream(dev).wait_stream(s)
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
+        lib = L.load()
+        before = lib.sb_kernel_launches()
         with torch.cuda.graph(self.graph):
             engine.forward(self.h, self.x0, loop_begin, loop_end, out=self.out)
+        self.kernels_per_replay = int(lib.sb_kernel_launches() - before)
 
     def __call__(self, h=None, x0=None):
         if h is not None:

@@ -32,6 +32,7 @@ import dataclasses
 import torch
 import torch.distributed as dist
 
+from . import _lib as L
 from .config import from_any
 from .engine import BlockEngine
 
@@ -152,8 +153,11 @@ class ExpertParallelBlock:
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
+        lib = L.load()
+        before = lib.sb_kernel_launches()
         with torch.cuda.graph(self.graph):
             self.g_out = self.forward(self.g_h, self.g_x0)
+        self.kernels_per_replay = int(lib.sb_kernel_launches() - before)  # library kernels (NCCL not counted)
         torch.cuda.synchronize(dev)
 
     def replay(self, h=None, x0=None):

@@ -81,3 +81,10 @@ def test_product_path_refuses_cpu_tensors():
     with pytest.raises(RuntimeError):
         sparse_expert_delta(h, torch.zeros(1, 4, 2, dtype=torch.long), torch.ones(1, 4, 2),
                             torch.zeros(4, 8, 64), torch.zeros(4, 8), torch.zeros(4, 64, 8), torch.zeros(4, 64), 4, 2)
+    from spider_web_moe_b200 import forge_ep
+    with pytest.raises(RuntimeError):
+        forge_ep.build_dispatch_plan(torch.zeros(1, 4, 2, dtype=torch.long), torch.ones(1, 4, 2), num_experts=4)
+    with pytest.raises(RuntimeError):
+        forge_ep.ForgeEP().run_dispatched_ffn(h, torch.zeros(1, 4, 2, dtype=torch.long), torch.ones(1, 4, 2),
+                                              w_up=torch.zeros(4, 8, 64), b_up=torch.zeros(4, 8),
+                                              w_down=torch.zeros(4, 64, 8), b_down=torch.zeros(4, 64), num_experts=4)
