@@ -33,10 +33,18 @@ constexpr int kTcBK = 64;
 constexpr int kTcThreads = 192;
 // Shared memory for the pipeline stages: small column tiles (decode) keep two
 // CTAs per SM (two independent TMA/MMA latency chains), large ones take one.
-constexpr int kTcSmemBudgetSmallN = 110 * 1024;
+// Shared-memory budgets of the one-tile kernel (they set the stage count and
+// so the CTAs per SM), measured on B200: the fixed-group schedule streams a
+// whole expert per CTA and is fastest with 4 stages and 2 CTAs per SM (bf16
+// decode, cfg2); one-tile slots (<= 64 columns) and fp8 / int4 tiles, whose
+// dequant runs in the CTA's own epilogue warps, are fastest with 2 stages and
+// 3-4 CTAs per SM (cfg5: +20% on the edge-value and expert GEMMs).
+constexpr int kTcSmemBudgetFixed = 110 * 1024;
+constexpr int kTcSmemBudgetSmallN = 50 * 1024;
+constexpr int kTcSmemBudgetSmallNConvert = 64 * 1024;
 constexpr int kTcSmemBudgetLargeN = 200 * 1024;
 
-template <int BN, int WFMT, int EPI>
+template <int BN, int WFMT, int EPI, bool kFixed>
 struct TcCfg {
   static constexpr bool kGate = EPI == SB_EPI_SWIGLU;
   static constexpr bool kConvert = WFMT != SB_W_BF16;
@@ -44,7 +52,9 @@ struct TcCfg {
   static constexpr int kBBytes = BN * kTcBK * 2;
   static constexpr int kRawBytes = WFMT == SB_W_FP8 ? kTcBM * kTcBK : (WFMT == SB_W_INT4 ? kTcBM * kTcBK / 2 : 0);
   static constexpr int kStageBytes = kABytes * (kGate ? 2 : 1) + kBBytes + kRawBytes * (kGate ? 2 : 1);
-  static constexpr int kBudget = BN <= 64 ? kTcSmemBudgetSmallN : kTcSmemBudgetLargeN;
+  static constexpr int kBudget =
+      BN > 64 ? kTcSmemBudgetLargeN
+              : (kConvert ? kTcSmemBudgetSmallNConvert : (kFixed ? kTcSmemBudgetFixed : kTcSmemBudgetSmallN));
   static constexpr int kStagesRaw = kBudget / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
   static constexpr int kTmemCols = (BN * (kGate ? 2 : 1)) <= 32 ? 32 : BN * (kGate ? 2 : 1);
@@ -56,15 +66,35 @@ struct TcCfg {
   static constexpr int kOffRawG = kOffRaw + kStages * kRawBytes;
   static constexpr int kOffBar = kOffRawG + (kGate ? kStages * kRawBytes : 0);
   static constexpr int kOffMisc = kOffBar + (3 * kStages + 2) * 8;
-  static constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
+  // int4: the CTA's group scales (128 rows x up to 32 groups of its K range)
+  static constexpr int kScaleBytes = WFMT == SB_W_INT4 ? 8192 : 0;
+  static constexpr int kOffScale = kOffMisc + 64;
+  static constexpr int kSmemBytes = kOffScale + kScaleBytes + 1024;  // + alignment slack
   static_assert(kTmemCols <= 512, "TMEM holds 512 columns");
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "M=128 MMA needs N in [16, 256], N % 16 == 0");
 };
 
+// Two int4 weights (the nibbles at bit `lo` and bit lo + 4 of x, where x is
+// the packed word with bit 3 of every nibble flipped) as bf16x2 bit patterns
+// of 128 + (nibble ^ 8): exponent 2^7 with the unsigned value in the low
+// mantissa bits, exact for values below 128.
+template <int kLo>
+SB_DEVINL uint32_t int4x2_biased_bf16x2(uint32_t x) {
+  const uint32_t lo = (x >> kLo) & 0xFu;
+  const uint32_t hi = kLo + 4 <= 16 ? (x << (16 - kLo - 4)) & 0xF0000u : (x >> (kLo + 4 - 16)) & 0xF0000u;
+  return lo | hi | 0x43004300u;
+}
+
 // Convert the raw fp8 / int4 tile of this stage into the swizzled bf16 tile.
+// int4: the group scale of (row, k0) comes from `s_scale[row * s_ngr + k0 /
+// group_size - s_g0]` in shared memory when s_scale is given, else from global
+// memory.  Each weight is bf16(q * s) with one rounding, as the CUDA-core
+// engine and the oracle compute it: (128 + u) - 136 is exact in bf16 and the
+// bf16x2 multiply rounds the exact product once.
 template <int WFMT>
 SB_DEVINL void convert_tile(const uint8_t* raw, uint8_t* dst, const sb_grouped_gemm_args& p,
-                            const void* scales, int64_t arow0, int k0, int tid) {
+                            const void* scales, int64_t arow0, int k0, int tid,
+                            const __nv_bfloat16* s_scale = nullptr, int s_ngr = 0, int s_g0 = 0) {
   if (WFMT == SB_W_FP8) {
     // 128 rows x 64 bytes; item = (row, 16-byte chunk): 512 items over 128 threads.
 #pragma unroll
@@ -92,22 +122,33 @@ SB_DEVINL void convert_tile(const uint8_t* raw, uint8_t* dst, const sb_grouped_g
   } else {
     // 128 rows x 32 bytes; item = (row, 16-byte chunk): 256 items over 128 threads.
     const int groups = static_cast<int>(p.lda / p.group_size);
+    const int gk = k0 / p.group_size;
+    const __nv_bfloat162 bias = __float2bfloat162_rn(136.f);
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const int item = tid + 128 * q;
       const int row = item >> 1, c16 = item & 1;
       const int64_t arow = arow0 + row;
-      const float s = arow < p.a_rows_total
-                          ? __bfloat162float(static_cast<const __nv_bfloat16*>(scales)[arow * groups + k0 / p.group_size])
-                          : 0.f;
+      __nv_bfloat16 sb;
+      if (s_scale)
+        sb = s_scale[row * s_ngr + gk - s_g0];
+      else
+        sb = arow < p.a_rows_total ? static_cast<const __nv_bfloat16*>(scales)[arow * groups + gk]
+                                   : __float2bfloat16_rn(0.f);
+      const __nv_bfloat162 s2 = __bfloat162bfloat162(sb);
       const uint4 v = *reinterpret_cast<const uint4*>(raw + row * 32 + c16 * 16);
-      const uint8_t* b = reinterpret_cast<const uint8_t*>(&v);
+      const uint32_t w[4] = {v.x ^ 0x88888888u, v.y ^ 0x88888888u, v.z ^ 0x88888888u, v.w ^ 0x88888888u};
       uint32_t out[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const __nv_bfloat162 bb = __floats2bfloat162_rn(static_cast<float>(int4_nibble(b[j], 0)) * s,
-                                                        static_cast<float>(int4_nibble(b[j], 1)) * s);
-        out[j] = *reinterpret_cast<const uint32_t*>(&bb);
+      for (int i = 0; i < 4; ++i) {
+        uint32_t pr[4] = {int4x2_biased_bf16x2<0>(w[i]), int4x2_biased_bf16x2<8>(w[i]),
+                          int4x2_biased_bf16x2<16>(w[i]), int4x2_biased_bf16x2<24>(w[i])};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const __nv_bfloat162 qv = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&pr[j]), bias);
+          const __nv_bfloat162 r = __hmul2(qv, s2);
+          out[4 * i + j] = *reinterpret_cast<const uint32_t*>(&r);
+        }
       }
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
@@ -132,7 +173,7 @@ template <int BN, int WFMT, int EPI, bool kFixed, bool kGather>
 __global__ void __launch_bounds__(kTcThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmG,
                const __grid_constant__ CUtensorMap tmB, const sb_grouped_gemm_args p) {
-  using C = TcCfg<BN, WFMT, EPI>;
+  using C = TcCfg<BN, WFMT, EPI, kFixed>;
   constexpr int S = C::kStages;
   static_assert(!kGather || BN <= 64, "gathers are issued by the lanes of one warp (BN/4 <= 32)");
   extern __shared__ uint8_t smem_raw[];
@@ -182,6 +223,28 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (C::kGate) {
         uint8_t* gdst = C::kConvert ? smem + C::kOffRawG + it * C::kRawBytes : smem + C::kOffG + it * C::kABytes;
         tma_load_2d(gdst, &tmG, &full[it], acol, static_cast<int>(arow));
+      }
+    }
+  }
+  // int4, fixed schedule: this CTA's group scales into shared memory, also
+  // before the wait (weights and scales do not depend on the previous kernel)
+  __nv_bfloat16* s_scale = nullptr;
+  int s_ngr = 0, s_g0 = 0;
+  if (kFixed && WFMT == SB_W_INT4) {
+    const int gs = p.group_size;
+    s_g0 = kb / gs;
+    s_ngr = (kb + ks + gs - 1) / gs - s_g0;
+    if (s_ngr * kTcBM * 2 <= C::kScaleBytes) {
+      s_scale = reinterpret_cast<__nv_bfloat16*>(smem + C::kOffScale);
+      if (warp < 4) {
+        const int groups = static_cast<int>(p.lda / gs);
+        const int64_t arow0s = static_cast<int64_t>(blockIdx.y) * p.a_group_rows + m0;
+        const __nv_bfloat16* sc = static_cast<const __nv_bfloat16*>(p.a_scale);
+        for (int i = tid; i < s_ngr * kTcBM; i += 128) {
+          const int row = i / s_ngr, gi = i - row * s_ngr;
+          const int64_t arow = arow0s + row;
+          s_scale[i] = arow < p.a_rows_total ? sc[arow * groups + s_g0 + gi] : __float2bfloat16_rn(0.f);
+        }
       }
     }
   }
@@ -345,7 +408,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (!mbar_wait(&full[s], ph, p.status, SB_DEVERR_TMA_WAIT)) { live = false; break; }
           const int k0 = kb + kk * kTcBK;
           convert_tile<WFMT>(smem + C::kOffRaw + s * C::kRawBytes, smem + C::kOffA + s * C::kABytes, p,
-                             p.a_scale, arow0, k0, tid);
+                             p.a_scale, arow0, k0, tid, s_scale, s_ngr, s_g0);
           if (C::kGate)
             convert_tile<WFMT>(smem + C::kOffRawG + s * C::kRawBytes, smem + C::kOffG + s * C::kABytes, p,
                                p.a_gate_scale, arow0, k0, tid);
@@ -1064,7 +1127,7 @@ bool tcgen05_supported(const sb_grouped_gemm_args& a) {
 
 template <int BN, int WFMT, int EPI, bool kFixed, bool kGather>
 static int launch_tc(const sb_grouped_gemm_args& a, cudaStream_t st) {
-  using C = TcCfg<BN, WFMT, EPI>;
+  using C = TcCfg<BN, WFMT, EPI, kFixed>;
   auto kern = tc_gemm_kernel<BN, WFMT, EPI, kFixed, kGather>;
   static int configured_device = -1;
   int dev = 0;
