@@ -162,7 +162,7 @@ typedef struct sb_grouped_gemm_args {
   int rows_hint;          /* host estimate of offsets[G] (tile shape choice only) */
   int group_rows_bound;   /* rows per group the tile is planned for: an upper bound, or 0 if unknown
                              (tile choice only; larger groups are still computed correctly) */
-  const int32_t* offsets; /* [G+1] device */
+  const int32_t* offsets; /* [G+1] device; NULL with num_groups == 1: one group of all max_rows rows */
   const float* row_scale; /* [max_rows] per permuted row, SB_EPI_LINEAR only, may be NULL */
   void* out;
   int64_t ldo;

@@ -319,7 +319,8 @@ extern "C" SB_API size_t sb_status_offset(void) { return 0; }
 extern "C" SB_API int sb_grouped_gemm(const sb_grouped_gemm_args* args, void* stream) {
   if (!args) return SB_ERR_ARG;
   const sb_grouped_gemm_args& a = *args;
-  if (!a.a || !a.x || !a.out || !a.offsets || a.num_groups <= 0 || a.m_rows <= 0 || a.k <= 0 || a.lda < a.k ||
+  if (!a.a || !a.x || !a.out || (!a.offsets && a.num_groups != 1) || a.num_groups <= 0 || a.m_rows <= 0 ||
+      a.k <= 0 || a.lda < a.k ||
       a.ldx < a.k || a.max_rows < 0 || a.splits <= 0 || a.a_rows_total <= 0 ||
       (a.epilogue != SB_EPI_LINEAR && a.splits != 1) || (a.epilogue == SB_EPI_SWIGLU && !a.a_gate) ||
       (a.wfmt != SB_W_BF16 && a.wfmt != SB_W_F32 && !a.a_scale) || a.epilogue < 0 || a.epilogue > 2)
@@ -334,6 +335,10 @@ extern "C" SB_API size_t sb_block_workspace_bytes(const sb_block_dims* dims) {
   BlockBuffers b;
   return carve_block(*dims, dims->max_tokens > 0 ? dims->max_tokens : 1, nullptr, ~size_t(0) >> 1, &b);
 }
+
+// Batches from this many tokens compute the router logits with the grouped
+// GEMM (tensor cores) instead of the CUDA-core router kernel.
+constexpr int kRouterGemmMinTokens = 1024;
 
 // The fused router + edge-generator kernel re-reads a selected source's E
 // generator rows for every token: it is used while those reads (N*K*E*H
@@ -370,9 +375,24 @@ static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBu
                        w->gen_bias + static_cast<int64_t>(l) * E * E, M, b.top_idx, b.top_w, b.edge_idx, b.edge_w,
                        st));
   } else {
-    // 1. router
-    { StageScope sc_(0, st); SB_TRY(sb_router(cur, d.act_dtype, N, H, w->router_w, w->loop_bias + static_cast<int64_t>(l) * E, E, K,
-                                            b.top_idx, b.top_w, nullptr, st)); }
+    // 1. router: large batches as a one-group GEMM (logits into the edge-logit
+    // buffer, free until step 4) and a top-K kernel; small ones in one kernel
+    if (N >= kRouterGemmMinTokens && d.engine != SB_ENGINE_SIMT) {
+      StageScope sc_(0, st);
+      sb_grouped_gemm_args a;
+      std::memset(&a, 0, sizeof(a));
+      a.engine = d.engine; a.wfmt = dense_fmt; a.act_dtype = d.act_dtype; a.epilogue = SB_EPI_LINEAR;
+      a.num_groups = 1; a.m_rows = E; a.k = H; a.a_group_rows = E; a.lda = H; a.a_rows_total = E;
+      a.a = w->router_w; a.bias = w->loop_bias + static_cast<int64_t>(l) * E; a.bias_group_stride = E;
+      a.x = cur; a.ldx = H; a.max_rows = N; a.rows_hint = N; a.offsets = nullptr;
+      a.out = b.elog; a.ldo = E; a.splits = 1; a.status = b.status;
+      SB_TRY(run_gemm(a, d.engine, st));
+      SB_TRY(router_from_logits(b.elog, E, 1, 0, N, E, K, b.top_idx, b.top_w, st));
+    } else {
+      StageScope sc_(0, st);
+      SB_TRY(sb_router(cur, d.act_dtype, N, H, w->router_w, w->loop_bias + static_cast<int64_t>(l) * E, E, K, b.top_idx,
+                       b.top_w, nullptr, st));
+    }
     // 2-3. rows grouped by selected source; gather h (inside the GEMM when it can)
     { StageScope sc_(1, st); SB_TRY(sb_group(b.top_idx, nullptr, N, K, E, 0, b.src_off, b.src_row, b.src_slot, b.src_w,
                                            b.src_inv, b.group_ws, b.group_ws_bytes, st)); }

@@ -174,9 +174,170 @@ combine_ln_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t 
   }
 }
 
+// ------------------------------------------------------------------ warp-per-token variants
+//
+// Large batches: one warp per token (8 per CTA), lane L owning float4 chunks
+// L, L+32, ... of the row (NV chunks, cols = 128 NV), every reduction inside
+// the warp: no shared memory and no block barriers, and all of a lane's
+// loads in flight at once.  The slot indices of a token are loaded by lanes
+// 0..slots-1 and broadcast.
+constexpr int kWarpRowsPerCta = 8;
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(kWarpRowsPerCta * 32)
+combine_rows_warp_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t split_stride,
+                         const int32_t* __restrict__ inv, int slots, int n_tokens, float* __restrict__ out_f32,
+                         const int32_t* __restrict__ scatter_inv, int scatter_slots, T* __restrict__ scatter_out) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * kWarpRowsPerCta + (threadIdx.x >> 5);
+  if (t >= n_tokens) return;
+  constexpr int cols = NV * 128;
+  const int my_inv0 = lane < slots ? inv[t * slots + lane] : -1;
+  const int my_inv1 = lane + 32 < slots ? inv[t * slots + lane + 32] : -1;
+  float4 acc[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = 0; j < slots; ++j) {
+    const int r = __shfl_sync(0xffffffffu, j < 32 ? my_inv0 : my_inv1, j & 31);
+    if (r < 0) continue;  // warp-uniform
+    for (int s = 0; s < splits; ++s) {
+      const float* row = y + s * split_stride + static_cast<int64_t>(r) * ldy;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const float4 v = *reinterpret_cast<const float4*>(row + 4 * (lane + 32 * i));
+        acc[i].x += v.x; acc[i].y += v.y; acc[i].z += v.z; acc[i].w += v.w;
+      }
+    }
+  }
+  if (out_f32)
+#pragma unroll
+    for (int i = 0; i < NV; ++i) *reinterpret_cast<float4*>(out_f32 + t * cols + 4 * (lane + 32 * i)) = acc[i];
+  if (scatter_inv) {
+    const int my_q0 = lane < scatter_slots ? scatter_inv[t * scatter_slots + lane] : -1;
+    const int my_q1 = lane + 32 < scatter_slots ? scatter_inv[t * scatter_slots + lane + 32] : -1;
+    for (int k = 0; k < scatter_slots; ++k) {
+      const int q = __shfl_sync(0xffffffffu, k < 32 ? my_q0 : my_q1, k & 31);
+      if (q < 0) continue;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) Vec4<T>::store(scatter_out + static_cast<int64_t>(q) * cols + 4 * (lane + 32 * i), acc[i]);
+    }
+  } else if (scatter_out) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) Vec4<T>::store(scatter_out + t * cols + 4 * (lane + 32 * i), acc[i]);
+  }
+}
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(kWarpRowsPerCta * 32)
+combine_ln_warp_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t split_stride,
+                       const int32_t* __restrict__ inv, int slots, const float* __restrict__ delta_in,
+                       const T* __restrict__ h, const T* __restrict__ x0, int n_tokens,
+                       const float* __restrict__ ln_w, const float* __restrict__ ln_b, float alpha, float beta,
+                       float eps, T* __restrict__ out, float* __restrict__ delta_out) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * kWarpRowsPerCta + (threadIdx.x >> 5);
+  if (t >= n_tokens) return;
+  constexpr int cols = NV * 128;
+  float4 u[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) u[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (y) {
+    const int my_inv0 = lane < slots ? inv[t * slots + lane] : -1;
+    const int my_inv1 = lane + 32 < slots ? inv[t * slots + lane + 32] : -1;
+    for (int j = 0; j < slots; ++j) {
+      const int r = __shfl_sync(0xffffffffu, j < 32 ? my_inv0 : my_inv1, j & 31);
+      if (r < 0) continue;  // warp-uniform
+      for (int s = 0; s < splits; ++s) {
+        const float* row = y + s * split_stride + static_cast<int64_t>(r) * ldy;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const float4 v = *reinterpret_cast<const float4*>(row + 4 * (lane + 32 * i));
+          u[i].x += v.x; u[i].y += v.y; u[i].z += v.z; u[i].w += v.w;
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) u[i] = *reinterpret_cast<const float4*>(delta_in + t * cols + 4 * (lane + 32 * i));
+  }
+  float local = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = 4 * (lane + 32 * i);
+    if (delta_out) *reinterpret_cast<float4*>(delta_out + t * cols + c) = u[i];
+    const float4 hv = Vec4<T>::load(h + t * cols + c), xv = Vec4<T>::load(x0 + t * cols + c);
+    u[i].x = (hv.x + alpha * u[i].x) + beta * xv.x;
+    u[i].y = (hv.y + alpha * u[i].y) + beta * xv.y;
+    u[i].z = (hv.z + alpha * u[i].z) + beta * xv.z;
+    u[i].w = (hv.w + alpha * u[i].w) + beta * xv.w;
+    local += (u[i].x + u[i].y) + (u[i].z + u[i].w);
+  }
+  const float mean = warp_sum(local) / static_cast<float>(cols);
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float a = u[i].x - mean, b = u[i].y - mean, c = u[i].z - mean, e = u[i].w - mean;
+    sq += (a * a + b * b) + (c * c + e * e);
+  }
+  const float rstd = rsqrtf(warp_sum(sq) / static_cast<float>(cols) + eps);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = 4 * (lane + 32 * i);
+    const float4 g = *reinterpret_cast<const float4*>(ln_w + c);
+    const float4 b = *reinterpret_cast<const float4*>(ln_b + c);
+    float4 o;
+    o.x = (u[i].x - mean) * rstd * g.x + b.x;
+    o.y = (u[i].y - mean) * rstd * g.y + b.y;
+    o.z = (u[i].z - mean) * rstd * g.z + b.z;
+    o.w = (u[i].w - mean) * rstd * g.w + b.w;
+    Vec4<T>::store(out + t * cols + c, o);
+  }
+}
+
 }  // namespace sb
 
 using namespace sb;
+
+namespace {
+// Warp-per-token variants for large batches (from 512 tokens): cols a
+// multiple of 128 up to 2048 (NV float4 chunks per lane).
+bool use_warp_rows(int n_tokens, int cols) { return n_tokens >= 512 && cols % 128 == 0 && cols <= 2048; }
+
+template <typename T>
+int launch_combine_rows_warp(const float* y, int64_t ldy, int splits, int64_t split_stride, const int32_t* inv,
+                             int slots, int n_tokens, int cols, float* out_f32, const int32_t* scatter_inv,
+                             int scatter_slots, T* scatter_out, cudaStream_t st) {
+  const dim3 grid((n_tokens + kWarpRowsPerCta - 1) / kWarpRowsPerCta), block(kWarpRowsPerCta * 32);
+  switch (cols / 128) {
+    case 1: return launch(combine_rows_warp_kernel<T, 1>, grid, block, 0, st, y, ldy, splits, split_stride, inv, slots, n_tokens, out_f32, scatter_inv, scatter_slots, scatter_out);
+    case 2: return launch(combine_rows_warp_kernel<T, 2>, grid, block, 0, st, y, ldy, splits, split_stride, inv, slots, n_tokens, out_f32, scatter_inv, scatter_slots, scatter_out);
+    case 4: return launch(combine_rows_warp_kernel<T, 4>, grid, block, 0, st, y, ldy, splits, split_stride, inv, slots, n_tokens, out_f32, scatter_inv, scatter_slots, scatter_out);
+    case 8: return launch(combine_rows_warp_kernel<T, 8>, grid, block, 0, st, y, ldy, splits, split_stride, inv, slots, n_tokens, out_f32, scatter_inv, scatter_slots, scatter_out);
+    case 16: return launch(combine_rows_warp_kernel<T, 16>, grid, block, 0, st, y, ldy, splits, split_stride, inv, slots, n_tokens, out_f32, scatter_inv, scatter_slots, scatter_out);
+    default: return SB_ERR_UNSUPPORTED;
+  }
+}
+
+template <typename T>
+int launch_combine_ln_warp(const float* y, int64_t ldy, int splits, int64_t split_stride, const int32_t* inv,
+                           int slots, const float* delta_in, const T* h, const T* x0, int n_tokens, int cols,
+                           const float* ln_w, const float* ln_b, float alpha, float beta, float eps, T* out,
+                           float* delta_out, cudaStream_t st) {
+  const dim3 grid((n_tokens + kWarpRowsPerCta - 1) / kWarpRowsPerCta), block(kWarpRowsPerCta * 32);
+  switch (cols / 128) {
+    case 1: return launch(combine_ln_warp_kernel<T, 1>, grid, block, 0, st, y, ldy, splits, split_stride, inv, slots, delta_in, h, x0, n_tokens, ln_w, ln_b, alpha, beta, eps, out, delta_out);
+    case 2: return launch(combine_ln_warp_kernel<T, 2>, grid, block, 0, st, y, ldy, splits, split_stride, inv, slots, delta_in, h, x0, n_tokens, ln_w, ln_b, alpha, beta, eps, out, delta_out);
+    case 4: return launch(combine_ln_warp_kernel<T, 4>, grid, block, 0, st, y, ldy, splits, split_stride, inv, slots, delta_in, h, x0, n_tokens, ln_w, ln_b, alpha, beta, eps, out, delta_out);
+    case 8: return launch(combine_ln_warp_kernel<T, 8>, grid, block, 0, st, y, ldy, splits, split_stride, inv, slots, delta_in, h, x0, n_tokens, ln_w, ln_b, alpha, beta, eps, out, delta_out);
+    case 16: return launch(combine_ln_warp_kernel<T, 16>, grid, block, 0, st, y, ldy, splits, split_stride, inv, slots, delta_in, h, x0, n_tokens, ln_w, ln_b, alpha, beta, eps, out, delta_out);
+    default: return SB_ERR_UNSUPPORTED;
+  }
+}
+}  // namespace
 
 extern "C" SB_API int sb_combine_rows(const float* y, int64_t ldy, int splits, int64_t split_stride,
                                       const int32_t* inv, int slots, int n_tokens, int cols,
@@ -189,6 +350,14 @@ extern "C" SB_API int sb_combine_rows(const float* y, int64_t ldy, int splits, i
     return SB_ERR_ARG;
   if (n_tokens == 0) return SB_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (use_warp_rows(n_tokens, cols)) {
+    if (act_dtype == SB_BF16 || !scatter_out)
+      return launch_combine_rows_warp<__nv_bfloat16>(y, ldy, splits, split_stride, inv, slots, n_tokens, cols, out_f32,
+                                                     scatter_inv, scatter_slots,
+                                                     static_cast<__nv_bfloat16*>(scatter_out), st);
+    return launch_combine_rows_warp<float>(y, ldy, splits, split_stride, inv, slots, n_tokens, cols, out_f32,
+                                           scatter_inv, scatter_slots, static_cast<float*>(scatter_out), st);
+  }
   if (act_dtype == SB_F32)
     return launch(combine_rows_kernel<float>, dim3(n_tokens), dim3(kCombineThreads), 0, st, y, ldy, splits,
                   split_stride, inv, slots, cols, out_f32, scatter_inv, scatter_slots, static_cast<float*>(scatter_out));
@@ -211,6 +380,16 @@ extern "C" SB_API int sb_combine_ln(const float* y, int64_t ldy, int splits, int
     return SB_ERR_ARG;
   if (n_tokens == 0) return SB_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (use_warp_rows(n_tokens, cols) && (!y || ldy % 4 == 0) && (act_dtype == SB_F32 || act_dtype == SB_BF16)) {
+    if (act_dtype == SB_F32)
+      return launch_combine_ln_warp<float>(y, ldy, splits, split_stride, inv, slots, delta_in,
+                                           static_cast<const float*>(h), static_cast<const float*>(x0), n_tokens, cols,
+                                           ln_w, ln_b, alpha, beta, eps, static_cast<float*>(out), delta_out, st);
+    return launch_combine_ln_warp<__nv_bfloat16>(y, ldy, splits, split_stride, inv, slots, delta_in,
+                                                 static_cast<const __nv_bfloat16*>(h),
+                                                 static_cast<const __nv_bfloat16*>(x0), n_tokens, cols, ln_w, ln_b,
+                                                 alpha, beta, eps, static_cast<__nv_bfloat16*>(out), delta_out, st);
+  }
   if (act_dtype == SB_F32)
     return launch(combine_ln_kernel<float>, dim3(n_tokens), dim3(kLnThreads), 0, st, y, ldy, splits, split_stride,
                   inv, slots, delta_in, static_cast<const float*>(h), static_cast<const float*>(x0), cols, ln_w,

@@ -9,8 +9,13 @@ namespace sb {
 // group.  Executed by one full warp; returns false (uniformly) when `slot` is
 // beyond the last tile.  No host synchronisation is needed: the launch grid is
 // an upper bound and surplus CTAs leave at once.
+// Row offset of group g; offsets == nullptr means one dense group of max_rows rows.
+SB_DEVINL int group_offset(const int32_t* __restrict__ offsets, int g, int max_rows) {
+  return offsets ? offsets[g] : (g == 0 ? 0 : max_rows);
+}
+
 SB_DEVINL bool schedule_tile(const int32_t* __restrict__ offsets, int G, int BN, int slot, int& g,
-                             int& n0, int& n_end) {
+                             int& n0, int& n_end, int max_rows) {
   const int lane = threadIdx.x & 31;
   int seen = 0;
   int found_g = -1, found_n0 = 0, found_end = 0;
@@ -18,8 +23,8 @@ SB_DEVINL bool schedule_tile(const int32_t* __restrict__ offsets, int G, int BN,
     const int gi = base + lane;
     int lo = 0, hi = 0;
     if (gi < G) {
-      lo = offsets[gi];
-      hi = offsets[gi + 1];
+      lo = group_offset(offsets, gi, max_rows);
+      hi = group_offset(offsets, gi + 1, max_rows);
     }
     const int cnt = hi > lo ? hi - lo : 0;
     const int tiles = (cnt + BN - 1) / BN;

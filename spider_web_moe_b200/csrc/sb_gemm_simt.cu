@@ -49,7 +49,7 @@ simt_gemm_kernel(const sb_grouped_gemm_args p) {
   const int tid = threadIdx.x;
   if (tid < 32) {
     int g, n0, n_end;
-    const bool ok = schedule_tile(p.offsets, p.num_groups, kSimtBN, blockIdx.y, g, n0, n_end);
+    const bool ok = schedule_tile(p.offsets, p.num_groups, kSimtBN, blockIdx.y, g, n0, n_end, p.max_rows);
     if (tid == 0) {
       s_sched[0] = ok ? g : -1;
       s_sched[1] = n0;

@@ -256,12 +256,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (tid == 0) {
       const int g = blockIdx.y;
       s_sched[0] = g;
-      s_sched[1] = p.offsets[g];
-      s_sched[2] = min(p.offsets[g + 1], p.max_rows);
+      s_sched[1] = group_offset(p.offsets, g, p.max_rows);
+      s_sched[2] = min(group_offset(p.offsets, g + 1, p.max_rows), p.max_rows);
     }
   } else if (warp == 0) {
     int g, n0, n_end;
-    const bool ok = schedule_tile(p.offsets, p.num_groups, BN, blockIdx.y, g, n0, n_end);
+    const bool ok = schedule_tile(p.offsets, p.num_groups, BN, blockIdx.y, g, n0, n_end, p.max_rows);
     if (lane == 0) {
       s_sched[0] = ok ? g : -1;
       s_sched[1] = n0;
@@ -570,7 +570,7 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
       const int gi = base + lane;
       int tiles = 0;
       if (gi < G) {
-        const int o0 = p.offsets[gi], o1 = p.offsets[gi + 1];
+        const int o0 = group_offset(p.offsets, gi, p.max_rows), o1 = group_offset(p.offsets, gi + 1, p.max_rows);
         s_off[gi] = o0;
         if (gi == G - 1) s_off[G] = o1;
         const int lo = min(o0, p.max_rows), hi = min(o1, p.max_rows);
@@ -861,7 +861,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       const int gi = base + lane;
       int tiles = 0;
       if (gi < G) {
-        const int o0 = p.offsets[gi], o1 = p.offsets[gi + 1];
+        const int o0 = group_offset(p.offsets, gi, p.max_rows), o1 = group_offset(p.offsets, gi + 1, p.max_rows);
         s_off[gi] = o0;
         if (gi == G - 1) s_off[G] = o1;
         const int lo = min(o0, p.max_rows), hi = min(o1, p.max_rows);

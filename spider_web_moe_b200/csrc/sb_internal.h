@@ -98,6 +98,10 @@ int route_edges(const void* h, int act_dtype, int n_tokens, int hidden, const vo
                 int E, int K, const void* gen_w, const float* gen_bias, int M, int32_t* top_idx, float* top_w,
                 int32_t* edge_idx, float* edge_w, cudaStream_t st);
 
+// Top-K routing of router logits that a grouped GEMM computed (sb_router.cu).
+int router_from_logits(const float* logits, int ld, int splits, int64_t split_stride, int n_tokens, int E, int K,
+                       int32_t* top_idx, float* top_w, cudaStream_t st);
+
 // Device properties cached per device.
 int current_sm_count();
 int current_cc_major();

@@ -196,6 +196,123 @@ router_kernel(const T* __restrict__ h, int n_tokens, int hidden, const T* __rest
   }
 }
 
+// Sum over the 32 lanes of 32 values per lane, returned transposed: lane L
+// gets the total of v[L].  Five butterfly steps, each halving the values a
+// lane keeps (31 shuffles instead of 32 x 5).
+SB_DEVINL float warp_transpose_sum32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) {
+    const bool upper = lane & d;
+#pragma unroll
+    for (int i = 0; i < d; ++i) {
+      const float send = upper ? v[i] : v[i + d];
+      const float keep = upper ? v[i + d] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+    }
+  }
+  return v[0];
+}
+
+// Router for large batches: a CTA stages `tok` (multiple of 8) hidden rows in
+// shared memory and reuses every router weight chunk it loads across 8 of
+// them; a warp task is 4 experts x 8 tokens (32 fp32 dot products, lanes
+// strided over the hidden dimension), reduced with one transpose-sum.  The
+// softmax / top-K / renormalisation is router_select, as in router_kernel.
+constexpr int kRouterTileMaxTok = 32;
+
+template <typename T>
+__global__ void __launch_bounds__(kRouterWarps * 32)
+router_tile_kernel(const T* __restrict__ h, int n_tokens, int hidden, int tok, const T* __restrict__ wr,
+                   const float* __restrict__ bias, int E, int K, int32_t* __restrict__ top_idx,
+                   float* __restrict__ top_w, float* __restrict__ probs_out) {
+  extern __shared__ __align__(16) uint8_t tile_smem[];
+  T* sh = reinterpret_cast<T*>(tile_smem);                                               // [tok][hidden]
+  float* slog = reinterpret_cast<float*>(tile_smem + static_cast<size_t>(tok) * hidden * sizeof(T));  // [tok][E]
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * tok;
+  const int ntok = min(tok, n_tokens - t0);
+  const int nchunks = hidden >> 3;
+  {
+    const int vec_per_row = hidden * static_cast<int>(sizeof(T)) / 16;
+    const uint4* src = reinterpret_cast<const uint4*>(h + static_cast<size_t>(t0) * hidden);
+    uint4* dst = reinterpret_cast<uint4*>(sh);
+    for (int i = threadIdx.x; i < ntok * vec_per_row; i += blockDim.x) dst[i] = src[i];
+  }
+  __syncthreads();
+  const int e_steps = (E + 3) / 4, t_steps = (ntok + 7) / 8;
+  for (int task = warp; task < e_steps * t_steps; task += kRouterWarps) {
+    const int e0 = (task % e_steps) * 4, tt0 = (task / e_steps) * 8;
+    float acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+    for (int c = lane; c < nchunks; c += 32) {
+      float wv[4][8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) Vec8<T>::load(wr + static_cast<size_t>(min(e0 + j, E - 1)) * hidden + c * 8, wv[j]);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        float hv[8];
+        Vec8<T>::load(sh + static_cast<size_t>(min(tt0 + t, ntok - 1)) * hidden + c * 8, hv);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[j * 8 + t] = fmaf(hv[i], wv[j][i], acc[j * 8 + t]);
+      }
+    }
+    const float sum = warp_transpose_sum32(acc, lane);  // lane = expert j * 8 + token t
+    const int e = e0 + (lane >> 3), t = tt0 + (lane & 7);
+    if (e < E && t < ntok) slog[t * E + e] = sum + bias[e];
+  }
+  __syncthreads();
+  for (int t = warp; t < ntok; t += kRouterWarps) {
+    int sel_i;
+    float sel_w;
+    router_select(slog + t * E, E, K, lane, probs_out ? probs_out + static_cast<size_t>(t0 + t) * E : nullptr,
+                  sel_i, sel_w);
+    if (lane < K) {
+      top_idx[static_cast<size_t>(t0 + t) * K + lane] = sel_i;
+      top_w[static_cast<size_t>(t0 + t) * K + lane] = sel_w;
+    }
+  }
+}
+
+// Softmax / top-K / renormalisation (router_select) of router logits computed
+// by the grouped GEMM: one warp per token, the logits the sum of `splits`
+// partial rows `split_stride` apart.
+__global__ void __launch_bounds__(kRouterWarps * 32)
+router_select_kernel(const float* __restrict__ logits, int ld, int splits, int64_t split_stride, int n_tokens, int E,
+                     int K, int32_t* __restrict__ top_idx, float* __restrict__ top_w) {
+  __shared__ float srow[kRouterWarps][kRouterMaxE];
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * kRouterWarps + warp;
+  if (t >= n_tokens) return;
+  for (int e = lane; e < E; e += 32) {
+    float v = 0.f;
+    for (int s = 0; s < splits; ++s) v += logits[s * split_stride + t * ld + e];
+    srow[warp][e] = v;
+  }
+  __syncwarp();
+  int sel_i;
+  float sel_w;
+  router_select(srow[warp], E, K, lane, nullptr, sel_i, sel_w);
+  if (lane < K) {
+    top_idx[t * K + lane] = sel_i;
+    top_w[t * K + lane] = sel_w;
+  }
+}
+
+int router_from_logits(const float* logits, int ld, int splits, int64_t split_stride, int n_tokens, int E, int K,
+                       int32_t* top_idx, float* top_w, cudaStream_t st) {
+  if (n_tokens <= 0) return SB_OK;
+  if (E > kRouterMaxE || K > 32 || K > E) return SB_ERR_ARG;
+  return launch(router_select_kernel, dim3((n_tokens + kRouterWarps - 1) / kRouterWarps), dim3(kRouterWarps * 32), 0,
+                st, logits, ld, splits, split_stride, n_tokens, E, K, top_idx, top_w);
+}
+
 // One warp per permuted (token, source) row: top-M over E destination logits.
 __global__ void __launch_bounds__(256)
 edge_topm_kernel(const float* __restrict__ logits, int64_t ld, int E, int M,
@@ -375,8 +492,36 @@ extern "C" SB_API int sb_router(const void* h, int act_dtype, int n_tokens, int 
     return SB_ERR_ARG;
   if (n_tokens == 0) return SB_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const dim3 grid((n_tokens + kRouterTok - 1) / kRouterTok), block(kRouterWarps * 32);
   const int esize = act_dtype == SB_F32 ? 4 : 2;
+  if (act_dtype != SB_F32 && act_dtype != SB_BF16) return SB_ERR_ARG;
+  const dim3 block(kRouterWarps * 32);
+  // Large batches: the tiled kernel (weights reused across 8 staged tokens),
+  // as many tokens per CTA (a multiple of 8, <= 32) as 128 KB of rows allow.
+  int tile_tok = static_cast<int>((128 * 1024) / (static_cast<size_t>(hidden) * esize)) / 8 * 8;
+  tile_tok = tile_tok > kRouterTileMaxTok ? kRouterTileMaxTok : tile_tok;
+  if (n_tokens >= 4 * current_sm_count() && tile_tok >= 8) {
+    const size_t smem = static_cast<size_t>(tile_tok) * hidden * esize + static_cast<size_t>(tile_tok) * num_experts * 4;
+    const dim3 grid((n_tokens + tile_tok - 1) / tile_tok);
+    if (act_dtype == SB_F32) {
+      static bool attr_set = false;
+      if (!attr_set) {
+        cudaFuncSetAttribute(router_tile_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr_set = true;
+      }
+      return launch(router_tile_kernel<float>, grid, block, smem, st, static_cast<const float*>(h), n_tokens, hidden,
+                    tile_tok, static_cast<const float*>(router_w), loop_bias_l, num_experts, top_k, top_idx, top_w,
+                    probs);
+    }
+    static bool attr_set = false;
+    if (!attr_set) {
+      cudaFuncSetAttribute(router_tile_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      attr_set = true;
+    }
+    return launch(router_tile_kernel<__nv_bfloat16>, grid, block, smem, st, static_cast<const __nv_bfloat16*>(h),
+                  n_tokens, hidden, tile_tok, static_cast<const __nv_bfloat16*>(router_w), loop_bias_l, num_experts,
+                  top_k, top_idx, top_w, probs);
+  }
+  const dim3 grid((n_tokens + kRouterTok - 1) / kRouterTok);
   const size_t smem = static_cast<size_t>(kRouterTok) * hidden * esize + static_cast<size_t>(kRouterTok) * num_experts * 4;
   if (smem > 200 * 1024) return SB_ERR_UNSUPPORTED;
   int rc = SB_OK;
@@ -388,7 +533,7 @@ extern "C" SB_API int sb_router(const void* h, int act_dtype, int n_tokens, int 
     }
     rc = launch(router_kernel<float>, grid, block, smem, st, static_cast<const float*>(h), n_tokens, hidden,
                 static_cast<const float*>(router_w), loop_bias_l, num_experts, top_k, top_idx, top_w, probs);
-  } else if (act_dtype == SB_BF16) {
+  } else {
     static bool attr_set = false;
     if (!attr_set && smem > 48 * 1024) {
       cudaFuncSetAttribute(router_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
@@ -397,8 +542,6 @@ extern "C" SB_API int sb_router(const void* h, int act_dtype, int n_tokens, int 
     rc = launch(router_kernel<__nv_bfloat16>, grid, block, smem, st, static_cast<const __nv_bfloat16*>(h), n_tokens,
                 hidden, static_cast<const __nv_bfloat16*>(router_w), loop_bias_l, num_experts, top_k, top_idx, top_w,
                 probs);
-  } else {
-    return SB_ERR_ARG;
   }
   return rc;
 }
@@ -411,9 +554,10 @@ extern "C" SB_API int sb_edge_topm(const float* logits, int64_t ld, int num_expe
       ld < num_experts || num_groups <= 0 || max_rows < 0)
     return SB_ERR_ARG;
   if (max_rows == 0) return SB_OK;
+  // one (token, source) row per warp: rows are independent and short, so
+  // more warps in flight rather than a loop per warp
   const int warps = 8;
-  int blocks = (max_rows + warps - 1) / warps;
-  blocks = blocks > 4 * 148 ? 4 * 148 : blocks;
+  const int blocks = (max_rows + warps - 1) / warps;
   return launch(edge_topm_kernel, dim3(blocks), dim3(warps * 32), 0, static_cast<cudaStream_t>(stream), logits, ld,
                 num_experts, edges, perm_slot, offsets, num_groups, max_rows, edge_idx, edge_w);
 }

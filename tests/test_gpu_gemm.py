@@ -47,7 +47,8 @@ def device_weight(w, wfmt, group_size, dev):
     return packed.to(dev), s_bf.to(dev), deq, None
 
 
-def run_case(rows, m, k, wfmt, epi, engine, dev, bound=0, splits=1, gather=False, group_size=128, seed=0):
+def run_case(rows, m, k, wfmt, epi, engine, dev, bound=0, splits=1, gather=False, group_size=128, seed=0,
+             null_offsets=False):
     g = torch.Generator().manual_seed(seed)
     G = len(rows)
     total = sum(rows)
@@ -124,7 +125,7 @@ def run_case(rows, m, k, wfmt, epi, engine, dev, bound=0, splits=1, gather=False
     args.max_rows = total
     args.rows_hint = total
     args.group_rows_bound = bound
-    args.offsets = d_off.data_ptr()
+    args.offsets = None if null_offsets else d_off.data_ptr()  # NULL: one dense group (G == 1)
     args.row_scale = d_rs.data_ptr() if epi == "linear" else None
     args.out = out.data_ptr()
     args.ldo = m
@@ -196,3 +197,11 @@ def test_persistent_many_tiles_and_groups(cuda_device):
 def test_simt_engine(epi, wfmt, cuda_device):
     got, want = run_case([33, 0, 70, 5], 160, 256, wfmt, epi, "simt", cuda_device, seed=3)
     check(got, want, epi)
+
+
+@pytest.mark.parametrize("engine", ["tcgen05", "simt"])
+@pytest.mark.parametrize("n", [40, 300, 2000])
+def test_single_dense_group_without_offsets(engine, n, cuda_device):
+    """offsets = NULL with num_groups = 1 (the router-logit GEMM): one group of all rows."""
+    got, want = run_case([n], 64, 512, "bf16", "linear", engine, cuda_device, seed=n, null_offsets=True)
+    check(got, want, "linear")
