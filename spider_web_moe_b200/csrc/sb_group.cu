@@ -36,106 +36,111 @@ __global__ void __launch_bounds__(kGroupThreads, 1) group_pair_kernel(const Grou
 }
 
 // ---------------------------------------------------------------------------
-// Multi-CTA grouping for large entry counts (prefill, many slots).
-//
-// Pass 1 (grid of CTAs, one chunk of kGroupThreads entries each): the same
-// per-warp match ranks and per-group warp scan as group_kernel, giving each
-// entry its rank inside its CTA's chunk and each CTA its per-group counts.
-// The last CTA to finish (ticket counter) scans the counts in (group, CTA)
-// order into per-(CTA, group) base positions and the group offsets.
-// Pass 2 scatters every entry to base + rank.  Positions are therefore the
-// same as the single-CTA kernel's: groups ascending, rows ascending.
-__global__ void __launch_bounds__(kGroupThreads, 1)
-group_rank_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w, int n_rows, int slots, int G,
-                  int flags, int32_t* __restrict__ offsets, int32_t* __restrict__ rank_scratch,
-                  float* __restrict__ w_scratch, int32_t* __restrict__ cta_base, unsigned* __restrict__ ticket) {
-  __shared__ int wcnt[32][kGroupMaxG];
-  __shared__ bool s_last;
+// Two-pass multi-CTA grouping (large entry counts), 256-entry chunks, no
+// serial step: pass 1 ranks each entry inside its chunk (warp match masks,
+// then the 8 warps' counts scanned in warp order) and stores the chunk's
+// per-group counts; pass 2 gives every chunk its base per group -- the counts
+// of all earlier chunks plus all smaller groups -- straight from the count
+// matrix, and scatters.  Positions equal the single-CTA kernel's.
+constexpr int kChunk = 256;
+
+__global__ void __launch_bounds__(kChunk)
+group_count_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w, int n_rows, int slots, int G,
+                   int flags, int32_t* __restrict__ rank_scratch, float* __restrict__ w_scratch,
+                   int32_t* __restrict__ chunk_count) {
+  __shared__ int wcnt[kChunk / 32][kGroupMaxG];
   pdl_wait();
   pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t total = static_cast<int64_t>(n_rows) * slots;
-  for (int i = tid; i < 32 * kGroupMaxG; i += kGroupThreads) (&wcnt[0][0])[i] = 0;
+  for (int i = tid; i < (kChunk / 32) * G; i += kChunk) (&wcnt[0][0])[(i / G) * kGroupMaxG + i % G] = 0;
   __syncthreads();
-  const int64_t e = static_cast<int64_t>(blockIdx.x) * kGroupThreads + tid;
+  const int64_t e = static_cast<int64_t>(blockIdx.x) * kChunk + tid;
   float wsum = 0.f;
   const int g = e < total ? entry_group(idx, w, slots, G, flags, e, wsum) : -1;
   const unsigned peers = __match_any_sync(0xffffffffu, g);
   const int rank_w = __popc(peers & ((1u << lane) - 1u));
   if (g >= 0 && rank_w == 0) wcnt[warp][g] = __popc(peers);
   __syncthreads();
-  for (int gg = tid; gg < G; gg += kGroupThreads) {
+  for (int gg = tid; gg < G; gg += kChunk) {
     int acc = 0;
-    for (int ww = 0; ww < 32; ++ww) {
+#pragma unroll
+    for (int ww = 0; ww < kChunk / 32; ++ww) {
       const int c = wcnt[ww][gg];
       wcnt[ww][gg] = acc;
       acc += c;
     }
-    cta_base[static_cast<int64_t>(blockIdx.x) * G + gg] = acc;  // this CTA's count, made a base below
+    chunk_count[static_cast<int64_t>(blockIdx.x) * G + gg] = acc;
   }
   __syncthreads();
   if (e < total) {
     rank_scratch[e] = g >= 0 ? wcnt[warp][g] + rank_w : -1;
     w_scratch[e] = wsum;
   }
-  // last CTA: counts -> bases and offsets
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  __shared__ int s_tot[kGroupMaxG + 1];
-  const int nctas = gridDim.x;
-  for (int gg = tid; gg < G; gg += kGroupThreads) {
-    int acc = 0;
-    for (int c = 0; c < nctas; ++c) {
-      volatile int32_t* p = cta_base + static_cast<int64_t>(c) * G + gg;
-      const int v = *p;
-      *p = acc;
-      acc += v;
+}
+
+__global__ void __launch_bounds__(kChunk)
+group_place_kernel(const int32_t* __restrict__ idx, int n_rows, int slots, int G, int nchunks,
+                   const int32_t* __restrict__ rank_scratch, const float* __restrict__ w_scratch,
+                   const int32_t* __restrict__ chunk_count, int32_t* __restrict__ offsets,
+                   int32_t* __restrict__ perm_row, int32_t* __restrict__ perm_slot, float* __restrict__ perm_w,
+                   int32_t* __restrict__ inv) {
+  __shared__ int s_before[kChunk];      // per (group, thread-slice) partial sums, then per group
+  __shared__ int s_total[kChunk];
+  __shared__ int s_base[kGroupMaxG + 1];
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x;
+  const int me = blockIdx.x;
+  // thread t sums chunks c = t / G, t / G + step, ... of group t % G
+  const int per_g = kChunk / G > 0 ? kChunk / G : 1;
+  const int gq = tid % G, sl = tid / G;
+  int before = 0, all = 0;
+  if (tid < per_g * G) {
+    for (int c = sl; c < nchunks; c += per_g) {
+      const int v = chunk_count[static_cast<int64_t>(c) * G + gq];
+      all += v;
+      if (c < me) before += v;
     }
-    s_tot[gg] = acc;
+  }
+  s_before[tid] = before;
+  s_total[tid] = all;
+  __syncthreads();
+  if (tid < G) {
+    int b = 0, a = 0;
+    for (int j = 0; j < per_g; ++j) {
+      b += s_before[j * G + tid];
+      a += s_total[j * G + tid];
+    }
+    s_before[tid] = b;  // earlier chunks' entries of group tid
+    s_total[tid] = a;   // all entries of group tid
   }
   __syncthreads();
   if (tid == 0) {
     int acc = 0;
     for (int gg = 0; gg < G; ++gg) {
-      const int t = s_tot[gg];
-      s_tot[gg] = acc;
-      acc += t;
+      s_base[gg] = acc;
+      acc += s_total[gg];
     }
-    s_tot[G] = acc;
+    s_base[G] = acc;
   }
   __syncthreads();
-  for (int gg = tid; gg <= G; gg += kGroupThreads) offsets[gg] = s_tot[gg];
-  for (int64_t i = tid; i < static_cast<int64_t>(nctas) * G; i += kGroupThreads)
-    cta_base[i] += s_tot[i % G];
-  if (tid == 0) *ticket = 0u;  // ready for the next call
-}
-
-__global__ void __launch_bounds__(256)
-group_scatter_kernel(const int32_t* __restrict__ idx, int n_rows, int slots, int G,
-                     const int32_t* __restrict__ rank_scratch, const float* __restrict__ w_scratch,
-                     const int32_t* __restrict__ cta_base, int32_t* __restrict__ perm_row,
-                     int32_t* __restrict__ perm_slot, float* __restrict__ perm_w, int32_t* __restrict__ inv) {
-  pdl_wait();
-  pdl_trigger();
+  if (me == 0)
+    for (int gg = tid; gg <= G; gg += kChunk) offsets[gg] = s_base[gg];
   const int64_t total = static_cast<int64_t>(n_rows) * slots;
-  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
-       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int r = rank_scratch[e];
-    if (r < 0) {
-      inv[e] = -1;
-      continue;
-    }
-    const int g = idx[e];
-    const int pos = cta_base[(e / kGroupThreads) * G + g] + r;
-    perm_row[pos] = static_cast<int32_t>(e / slots);
-    perm_slot[pos] = static_cast<int32_t>(e);
-    perm_w[pos] = w_scratch[e];
-    inv[e] = pos;
+  const int64_t e = static_cast<int64_t>(me) * kChunk + tid;
+  if (e >= total) return;
+  const int r = rank_scratch[e];
+  if (r < 0) {
+    inv[e] = -1;
+    return;
   }
+  const int g = idx[e];
+  const int pos = s_base[g] + s_before[g] + r;
+  perm_row[pos] = static_cast<int32_t>(e / slots);
+  perm_slot[pos] = static_cast<int32_t>(e);
+  perm_w[pos] = w_scratch[e];
+  inv[e] = pos;
 }
 
 template <typename V>
@@ -161,7 +166,7 @@ using namespace sb;
 
 extern "C" SB_API size_t sb_group_workspace_bytes(int n_rows, int slots, int num_groups) {
   const size_t total = static_cast<size_t>(n_rows > 0 ? n_rows : 0) * (slots > 0 ? slots : 0);
-  const size_t ctas = (total + kGroupThreads - 1) / kGroupThreads;
+  const size_t ctas = (total + kChunk - 1) / kChunk;  // chunks of the two-pass path (>= the rank path's CTAs)
   const size_t groups = num_groups > 0 ? static_cast<size_t>(num_groups) : 1;
   return kStatusBytes + align_up(total * sizeof(int32_t), 256) + align_up(total * sizeof(float), 256) +
          align_up(ctas * groups * sizeof(int32_t), 256) + 256;
@@ -190,20 +195,14 @@ extern "C" SB_API int sb_group(const int32_t* idx, const float* w, int n_rows, i
     return launch(group_kernel, dim3(1), dim3(threads), 0, st, idx, w, n_rows, slots, num_groups, flags, offsets,
                   perm_row, perm_slot, perm_w, inv, rank_scratch, w_scratch);
   }
-  const int ctas = static_cast<int>((total + kGroupThreads - 1) / kGroupThreads);
-  int32_t* cta_base = c.take<int32_t>(static_cast<size_t>(ctas) * num_groups);
-  unsigned* ticket = c.take<unsigned>(1);
-  int rc = cuda_status(cudaMemsetAsync(ticket, 0, sizeof(unsigned), st));
+  const int nchunks = static_cast<int>((total + kChunk - 1) / kChunk);
+  int32_t* chunk_count = c.take<int32_t>(static_cast<size_t>(nchunks) * num_groups);
+  int rc = launch(group_count_kernel, dim3(nchunks), dim3(kChunk), 0, st, idx, w, n_rows, slots, num_groups, flags,
+                  rank_scratch, w_scratch, chunk_count);
   if (rc) return rc;
-  rc = launch(group_rank_kernel, dim3(ctas), dim3(kGroupThreads), 0, st, idx, w, n_rows, slots, num_groups, flags,
-              offsets, rank_scratch, w_scratch, cta_base, ticket);
-  if (rc) return rc;
-  int blocks = static_cast<int>((total + 255) / 256);
-  const int cap = 4 * current_sm_count();
-  blocks = blocks > cap ? cap : blocks;
-  return launch(group_scatter_kernel, dim3(blocks), dim3(256), 0, st, idx, n_rows, slots, num_groups,
+  return launch(group_place_kernel, dim3(nchunks), dim3(kChunk), 0, st, idx, n_rows, slots, num_groups, nchunks,
                 static_cast<const int32_t*>(rank_scratch), static_cast<const float*>(w_scratch),
-                static_cast<const int32_t*>(cta_base), perm_row, perm_slot, perm_w, inv);
+                static_cast<const int32_t*>(chunk_count), offsets, perm_row, perm_slot, perm_w, inv);
 }
 
 namespace sb {

@@ -39,25 +39,26 @@ template <> struct Vec8<__nv_bfloat16> {
 // top-K by repeated arg-max (model.py:257; a taken expert is masked with -1
 // since probabilities are >= 0, equal values go to the smaller id) and the
 // renormalisation of model.py:258.  One warp; lane k < K returns slot k.
-SB_DEVINL void router_select(const float* logits, int E, int K, int lane, float* probs_out, int& sel_i,
-                             float& sel_w) {
-  float logit[kRouterMaxE / 32];
+template <int R>  // registers per lane: E <= 32 R
+SB_DEVINL void router_select_r(const float* logits, int E, int K, int lane, float* probs_out, int& sel_i,
+                               float& sel_w) {
+  float logit[R];
 #pragma unroll
-  for (int i = 0; i < kRouterMaxE / 32; ++i) logit[i] = (lane + 32 * i < E) ? logits[lane + 32 * i] : -INFINITY;
+  for (int i = 0; i < R; ++i) logit[i] = (lane + 32 * i < E) ? logits[lane + 32 * i] : -INFINITY;
   float mx = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < kRouterMaxE / 32; ++i) mx = fmaxf(mx, logit[i]);
+  for (int i = 0; i < R; ++i) mx = fmaxf(mx, logit[i]);
   mx = warp_max(mx);
-  float p[kRouterMaxE / 32];
+  float p[R];
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < kRouterMaxE / 32; ++i) {
+  for (int i = 0; i < R; ++i) {
     p[i] = (lane + 32 * i < E) ? expf(logit[i] - mx) : 0.f;
     s += p[i];
   }
   s = warp_sum(s);
 #pragma unroll
-  for (int i = 0; i < kRouterMaxE / 32; ++i) {
+  for (int i = 0; i < R; ++i) {
     p[i] = p[i] / s;
     if (probs_out && lane + 32 * i < E) probs_out[lane + 32 * i] = p[i];
   }
@@ -67,13 +68,13 @@ SB_DEVINL void router_select(const float* logits, int E, int K, int lane, float*
     float bv = -1.f;
     int bi = 0x7fffffff;
 #pragma unroll
-    for (int i = 0; i < kRouterMaxE / 32; ++i) {
+    for (int i = 0; i < R; ++i) {
       const int e = lane + 32 * i;
       if (e < E && (p[i] > bv || (p[i] == bv && e < bi))) { bv = p[i]; bi = e; }
     }
     warp_argmax(bv, bi);
 #pragma unroll
-    for (int i = 0; i < kRouterMaxE / 32; ++i)
+    for (int i = 0; i < R; ++i)
       if (lane + 32 * i == bi) p[i] = -1.f;
     sum_w += bv;
     if (lane == k) { w = bv; idx = bi; }
@@ -85,10 +86,11 @@ SB_DEVINL void router_select(const float* logits, int E, int K, int lane, float*
 // Top-M of one source's E destination logits (spider_moe/model.py:264-266):
 // repeated arg-max with a taken mask (equal values to the smaller id), then an
 // fp32 softmax over the M selected values.  One warp; lane m < M returns slot m.
-SB_DEVINL void topm_select(const float* logits, int E, int M, int lane, int& sel_i, float& sel_w) {
-  float v[kRouterMaxE / 32];
+template <int R>
+SB_DEVINL void topm_select_r(const float* logits, int E, int M, int lane, int& sel_i, float& sel_w) {
+  float v[R];
 #pragma unroll
-  for (int i = 0; i < kRouterMaxE / 32; ++i) {
+  for (int i = 0; i < R; ++i) {
     const int e = lane + 32 * i;
     v[i] = e < E ? logits[e] : -INFINITY;
   }
@@ -99,7 +101,7 @@ SB_DEVINL void topm_select(const float* logits, int E, int M, int lane, int& sel
     float bv = -INFINITY;
     int bi = 0x7fffffff;
 #pragma unroll
-    for (int i = 0; i < kRouterMaxE / 32; ++i) {
+    for (int i = 0; i < R; ++i) {
       const int e = lane + 32 * i;
       if (e < E && !(taken & (1u << i)) && (bi == 0x7fffffff || v[i] > bv || (v[i] == bv && e < bi))) {
         bv = v[i];
@@ -115,6 +117,22 @@ SB_DEVINL void topm_select(const float* logits, int E, int M, int lane, int& sel
   const float s = warp_sum(ex);
   sel_i = idx;
   sel_w = ex / s;
+}
+
+// Warp-uniform dispatch on E: only ceil(E/32) (rounded to a power of two)
+// values per lane are carried through the selection loops.
+SB_DEVINL void router_select(const float* logits, int E, int K, int lane, float* probs_out, int& sel_i,
+                             float& sel_w) {
+  if (E <= 32) router_select_r<1>(logits, E, K, lane, probs_out, sel_i, sel_w);
+  else if (E <= 64) router_select_r<2>(logits, E, K, lane, probs_out, sel_i, sel_w);
+  else if (E <= 128) router_select_r<4>(logits, E, K, lane, probs_out, sel_i, sel_w);
+  else router_select_r<8>(logits, E, K, lane, probs_out, sel_i, sel_w);
+}
+SB_DEVINL void topm_select(const float* logits, int E, int M, int lane, int& sel_i, float& sel_w) {
+  if (E <= 32) topm_select_r<1>(logits, E, M, lane, sel_i, sel_w);
+  else if (E <= 64) topm_select_r<2>(logits, E, M, lane, sel_i, sel_w);
+  else if (E <= 128) topm_select_r<4>(logits, E, M, lane, sel_i, sel_w);
+  else topm_select_r<8>(logits, E, M, lane, sel_i, sel_w);
 }
 
 // One CTA per kRouterTok tokens.  Their hidden rows are staged in shared
