@@ -338,7 +338,7 @@ extern "C" SB_API size_t sb_block_workspace_bytes(const sb_block_dims* dims) {
 
 // Batches from this many tokens compute the router logits with the grouped
 // GEMM (tensor cores) instead of the CUDA-core router kernel.
-constexpr int kRouterGemmMinTokens = 1024;
+constexpr int kRouterGemmMinTokens = 128;
 
 // The fused router + edge-generator kernel re-reads a selected source's E
 // generator rows for every token: it is used while those reads (N*K*E*H
@@ -385,9 +385,13 @@ static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBu
       a.num_groups = 1; a.m_rows = E; a.k = H; a.a_group_rows = E; a.lda = H; a.a_rows_total = E;
       a.a = w->router_w; a.bias = w->loop_bias + static_cast<int64_t>(l) * E; a.bias_group_stride = E;
       a.x = cur; a.ldx = H; a.max_rows = N; a.rows_hint = N; a.offsets = nullptr;
-      a.out = b.elog; a.ldo = E; a.splits = 1; a.status = b.status;
+      // K-split to spread small batches over the SMs; the partials must fit
+      // the edge-logit buffer (N*K*E floats)
+      int rs = pick_splits(E, H, N, 1, max_splits_for(N), tc_pref, 0);
+      while (rs > 1 && rs > K) rs >>= 1;
+      a.out = b.elog; a.ldo = E; a.splits = rs; a.split_stride = static_cast<int64_t>(N) * E; a.status = b.status;
       SB_TRY(run_gemm(a, d.engine, st));
-      SB_TRY(router_from_logits(b.elog, E, 1, 0, N, E, K, b.top_idx, b.top_w, st));
+      SB_TRY(router_from_logits(b.elog, E, rs, static_cast<int64_t>(N) * E, N, E, K, b.top_idx, b.top_w, st));
     } else {
       StageScope sc_(0, st);
       SB_TRY(sb_router(cur, d.act_dtype, N, H, w->router_w, w->loop_bias + static_cast<int64_t>(l) * E, E, K, b.top_idx,

@@ -14,7 +14,13 @@
 namespace sb {
 
 constexpr int kGroupThreads = 1024;
-constexpr size_t kGroupSingleCtaMax = 2048;  // entries up to which one CTA groups everything
+// Entries up to which one CTA groups everything; above it the two-pass
+// kernels (measured faster from a few hundred entries: one CTA's scans over
+// G groups and 32 warps serialise).
+constexpr size_t kGroupSingleCtaMax = 512;
+// The two-plan launch (decode) keeps one CTA per plan up to this many
+// entries: one launch instead of four.
+constexpr size_t kGroupPairMax = 2048;
 
 __global__ void __launch_bounds__(kGroupThreads, 1)
 group_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w, int n_rows, int slots,
@@ -209,7 +215,7 @@ namespace sb {
 int group_pair_launch(const GroupJob& j0, const GroupJob& j1, cudaStream_t st) {
   const int64_t t0 = static_cast<int64_t>(j0.n_rows) * j0.slots, t1 = static_cast<int64_t>(j1.n_rows) * j1.slots;
   const int64_t tmax = t0 > t1 ? t0 : t1;
-  if (tmax > static_cast<int64_t>(kGroupSingleCtaMax) || j0.num_groups > kGroupMaxG || j1.num_groups > kGroupMaxG)
+  if (tmax > static_cast<int64_t>(kGroupPairMax) || j0.num_groups > kGroupMaxG || j1.num_groups > kGroupMaxG)
     return SB_ERR_UNSUPPORTED;
   int threads = static_cast<int>(((tmax + 31) / 32) * 32);
   threads = threads < 64 ? 64 : (threads > kGroupThreads ? kGroupThreads : threads);
