@@ -185,7 +185,7 @@ SB_API int sb_edge_topm(const float* logits, int64_t ld, int num_experts, int ed
 
 /* ------------------------------------------------------------------ combines
  * Row combine: out[t, :] = sum_{j<slots, inv[t*slots+j]>=0} sum_s y[s][inv[t*slots+j], :]
- * (fixed ascending order, no atomics).  out_f32 may be NULL.  If scatter_out is
+ * (fixed ascending order, no atomics; slots <= 64, splits <= 8).  out_f32 may be NULL.  If scatter_out is
  * not NULL the combined row is also written there in act_dtype: to rows
  * scatter_inv[t*scatter_slots+k] >= 0, or to row t when scatter_inv is NULL. */
 SB_API int sb_combine_rows(const float* y, int64_t ldy, int splits, int64_t split_stride,

@@ -34,6 +34,46 @@ template <> struct Vec4<__nv_bfloat16> {
 };
 
 constexpr int kMaxSlots = 64;
+constexpr int kMaxSplits = 8;
+constexpr int kMaxTerms = kMaxSlots * kMaxSplits;  // (slot, split) rows summed per token
+constexpr int kTermUnroll = 8;                       // row loads in flight per thread
+
+// Offsets (elements from y) of the rows summed for token t, in the fixed
+// order (slot ascending, split ascending) every sum of this file uses;
+// filled by one warp, returns the count.
+SB_DEVINL int build_terms(const int32_t* __restrict__ inv, int64_t t, int slots, int splits, int64_t ldy,
+                          int64_t split_stride, int64_t* terms) {
+  const int lane = threadIdx.x & 31;
+  int n = 0;
+  for (int j0 = 0; j0 < slots; j0 += 32) {
+    const int j = j0 + lane;
+    const int r = j < slots ? inv[t * slots + j] : -1;
+    const unsigned valid = __ballot_sync(0xffffffffu, r >= 0);
+    const int before = __popc(valid & ((1u << lane) - 1u));
+    if (r >= 0)
+      for (int s = 0; s < splits; ++s) terms[(n + before) * splits + s] = s * split_stride + static_cast<int64_t>(r) * ldy;
+    n += __popc(valid);
+  }
+  return n * splits;
+}
+
+// acc += y[terms[e] + c] for e in order, kTermUnroll loads issued before their adds.
+SB_DEVINL void sum_terms(const float* __restrict__ y, const int64_t* terms, int n, int c, float4& acc) {
+  int e = 0;
+  for (; e + kTermUnroll <= n; e += kTermUnroll) {
+    float4 v[kTermUnroll];
+#pragma unroll
+    for (int q = 0; q < kTermUnroll; ++q) v[q] = *reinterpret_cast<const float4*>(y + terms[e + q] + c);
+#pragma unroll
+    for (int q = 0; q < kTermUnroll; ++q) {
+      acc.x += v[q].x; acc.y += v[q].y; acc.z += v[q].z; acc.w += v[q].w;
+    }
+  }
+  for (; e < n; ++e) {
+    const float4 v = *reinterpret_cast<const float4*>(y + terms[e] + c);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kCombineThreads)
@@ -41,26 +81,23 @@ combine_rows_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_
                     const int32_t* __restrict__ inv, int slots, int cols,
                     float* __restrict__ out_f32, const int32_t* __restrict__ scatter_inv,
                     int scatter_slots, T* __restrict__ scatter_out) {
-  __shared__ int s_rows[kMaxSlots];
+  __shared__ int64_t s_terms[kMaxTerms];
   __shared__ int s_dst[kMaxSlots];
+  __shared__ int s_n;
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;
-  if (threadIdx.x < slots) s_rows[threadIdx.x] = inv[static_cast<int64_t>(t) * slots + threadIdx.x];
+  if (threadIdx.x < 32) {
+    const int n = build_terms(inv, t, slots, splits, ldy, split_stride, s_terms);
+    if (threadIdx.x == 0) s_n = n;
+  }
   if (scatter_inv && threadIdx.x < scatter_slots)
     s_dst[threadIdx.x] = scatter_inv[static_cast<int64_t>(t) * scatter_slots + threadIdx.x];
   __syncthreads();
+  const int n = s_n;
   for (int c = threadIdx.x * 4; c < cols; c += kCombineThreads * 4) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = 0; j < slots; ++j) {
-      const int r = s_rows[j];
-      if (r < 0) continue;
-      for (int s = 0; s < splits; ++s) {
-        const float4 v =
-            *reinterpret_cast<const float4*>(y + s * split_stride + static_cast<int64_t>(r) * ldy + c);
-        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-      }
-    }
+    sum_terms(y, s_terms, n, c, acc);
     if (out_f32) *reinterpret_cast<float4*>(out_f32 + static_cast<int64_t>(t) * cols + c) = acc;
     if (scatter_inv) {
       for (int k = 0; k < scatter_slots; ++k) {
@@ -115,14 +152,14 @@ combine_ln_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t 
       xv[i] = Vec4<T>::load(x0 + t * cols + 4 * v);
     }
   }
-  int rows[kMaxSlots];
-  int nrows = 0;
-  if (y) {
-    for (int j = 0; j < slots; ++j) {
-      const int r = inv[t * slots + j];
-      if (r >= 0) rows[nrows++] = r;
-    }
+  __shared__ int64_t s_terms[kMaxTerms];
+  __shared__ int s_n;
+  if (y && threadIdx.x < 32) {
+    const int n = build_terms(inv, t, slots, splits, ldy, split_stride, s_terms);
+    if (threadIdx.x == 0) s_n = n;
   }
+  __syncthreads();
+  const int nterms = y ? s_n : 0;
   float local = 0.f;
 #pragma unroll
   for (int i = 0; i < kLnMaxVec; ++i) {
@@ -131,11 +168,7 @@ combine_ln_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t 
     if (v < nvec) {
       float4 d = make_float4(0.f, 0.f, 0.f, 0.f);
       if (y) {
-        for (int j = 0; j < nrows; ++j)
-          for (int s = 0; s < splits; ++s) {
-            const float4 a = *reinterpret_cast<const float4*>(y + s * split_stride + static_cast<int64_t>(rows[j]) * ldy + 4 * v);
-            d.x += a.x; d.y += a.y; d.z += a.z; d.w += a.w;
-          }
+        sum_terms(y, s_terms, nterms, 4 * v, d);
       } else {
         d = *reinterpret_cast<const float4*>(delta_in + t * cols + 4 * v);
       }
@@ -343,7 +376,7 @@ extern "C" SB_API int sb_combine_rows(const float* y, int64_t ldy, int splits, i
                                       const int32_t* inv, int slots, int n_tokens, int cols,
                                       float* out_f32, const int32_t* scatter_inv, int scatter_slots,
                                       void* scatter_out, int act_dtype, void* stream) {
-  if (n_tokens < 0 || cols <= 0 || cols % 4 || slots <= 0 || slots > kMaxSlots || splits <= 0 ||
+  if (n_tokens < 0 || cols <= 0 || cols % 4 || slots <= 0 || slots > kMaxSlots || splits <= 0 || splits > kMaxSplits ||
       ldy < cols || (ldy % 4) || (split_stride % 4) || (scatter_inv && (scatter_slots <= 0 ||
       scatter_slots > kMaxSlots || !scatter_out)) || (n_tokens > 0 && (!y || !inv)) ||
       (scatter_out && act_dtype != SB_F32 && act_dtype != SB_BF16))
@@ -375,7 +408,7 @@ extern "C" SB_API int sb_combine_ln(const float* y, int64_t ldy, int splits, int
                                     float beta, float eps, void* out, float* delta_out,
                                     void* stream) {
   if (n_tokens < 0 || cols <= 0 || cols > kLnThreads * kLnMaxVec * 4 || cols % 4 || !ln_w || !ln_b ||
-      (y && (!inv || slots <= 0 || slots > kMaxSlots || splits <= 0 || ldy < cols)) ||
+      (y && (!inv || slots <= 0 || slots > kMaxSlots || splits <= 0 || splits > kMaxSplits || ldy < cols)) ||
       (!y && !delta_in) || (n_tokens > 0 && (!h || !x0 || !out)))
     return SB_ERR_ARG;
   if (n_tokens == 0) return SB_OK;
