@@ -45,7 +45,10 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum, one ncu capture) of the
 # grouped-GEMM launches of one step, per config; None where no capture of all of
 # them exists yet.
-NCU_TRAFFIC_PER_STEP = {"cfg2": None}
+# DRAM bytes (read + write) of the edge-value, expert-up and expert-down GEMM
+# launches of one step, from ncu (dram__bytes_read.sum + dram__bytes_write.sum
+# over the 18 launches of one cfg2 replay; profiles/gemm_tcgen05_cfg2.txt).
+NCU_TRAFFIC_PER_STEP = {"cfg2": 1013465344}
 
 
 def parse():
