@@ -357,8 +357,25 @@ static double fused_route_max_bytes() {
 // With `ffn_planned` non-null the expert dispatch plan (step 9) is built in
 // the same launch as the destination plan when both fit one CTA each, and
 // *ffn_planned says whether that happened.
+static bool fuse_ln_route_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("SPIDER_B200_FUSE_LN_ROUTE");
+    return !(e && e[0] == '0');
+  }();
+  return v;
+}
+
+// Whether a batch of N tokens takes the fused per-token route kernel.
+static bool use_fused_route(const sb_block_dims& d, int N) {
+  const double gen_bytes = static_cast<double>(N) * d.top_k * d.num_experts * d.hidden * act_size(d.act_dtype);
+  return gen_bytes <= fused_route_max_bytes() &&
+         route_edges_smem(d.act_dtype, d.hidden, d.num_experts, d.top_k) <= kRouteEdgesMaxSmem;
+}
+
+// `routed`: the fused route of this loop already ran (inside the previous
+// loop's LayerNorm kernel); steps 1-5 are skipped.
 static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBuffers& b, const void* cur, int N,
-                      int l, int* msg_splits_out, bool* ffn_planned, cudaStream_t st) {
+                      int l, int* msg_splits_out, bool* ffn_planned, bool routed, cudaStream_t st) {
   int rc = SB_OK;
   const int H = d.hidden, E = d.num_experts, K = d.top_k, M = d.edges_per_expert;
   const int KM = K * M;
@@ -366,9 +383,10 @@ static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBu
   const int64_t cap_dst = static_cast<int64_t>(N) * (E < KM ? E : KM);
   const bool tc_pref = d.engine != SB_ENGINE_SIMT;
 #define SB_TRY(x) do { rc = (x); if (rc) return rc; } while (0)
-  const double gen_bytes = static_cast<double>(N) * K * E * H * act_size(d.act_dtype);
-  const bool fused = gen_bytes <= fused_route_max_bytes() && route_edges_smem(d.act_dtype, H, E, K) <= kRouteEdgesMaxSmem;
-  if (fused) {
+  const bool fused = use_fused_route(d, N);
+  if (fused && routed) {
+    // router, edge logits and top-M already in b.top_* / b.edge_*
+  } else if (fused) {
     // 1-5 in one kernel: router, edge logits of the selected sources, top-M
     StageScope sc_(0, st);
     SB_TRY(route_edges(cur, d.act_dtype, N, H, w->router_w, w->loop_bias + static_cast<int64_t>(l) * E, E, K, w->gen_w,
@@ -500,11 +518,14 @@ extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block
   const bool tc_pref = d.engine != SB_ENGINE_SIMT;
   const void* cur = h_in;
 #define SB_TRY(x) do { rc = (x); if (rc) return rc; } while (0)
+  // decode: loop l's LayerNorm kernel also routes loop l+1 (SPIDER_B200_FUSE_LN_ROUTE=0 disables)
+  const bool fuse_next = use_fused_route(d, N) && fuse_ln_route_enabled();
+  bool routed = false;
   for (int l = loop_begin; l < loop_end; ++l) {
     void* next = (l == loop_end - 1) ? h_out : b.hbuf[(l - loop_begin) & 1];
     int msg_splits = 1;
     bool ffn_planned = false;
-    SB_TRY(route_loop(d, w, b, cur, N, l, &msg_splits, &ffn_planned, st));
+    SB_TRY(route_loop(d, w, b, cur, N, l, &msg_splits, &ffn_planned, routed, st));
     // 9. dispatch plan of the expert FFN (unless built with the destination plan)
     if (!ffn_planned) {
       StageScope sc_(8, st);
@@ -542,12 +563,25 @@ extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block
       a.out = b.y_ffn; a.ldo = H; a.status = b.status;
       { StageScope sc_(11, st); SB_TRY(run_gemm(a, d.engine, st)); }
     }
-    // 13. delta + LayerNorm epilogue
-    { StageScope sc_(12, st); SB_TRY(sb_combine_ln(b.y_ffn, H, ffn_splits, static_cast<int64_t>(N) * K * H, b.ffn_inv, K,
-                                                nullptr, cur, x0, d.act_dtype, N, H, w->ln_w, w->ln_b, d.residual_scale,
-                                                d.reinject, d.ln_eps, next,
-                                                (taps && taps->delta && l == loop_end - 1) ? taps->delta : nullptr,
-                                                st)); }
+    // 13. delta + LayerNorm epilogue; in decode also the next loop's routing
+    // (steps 1-5 of loop l+1) in the same kernel
+    routed = false;
+    if (l + 1 < loop_end && fuse_next) {
+      StageScope sc_(12, st);
+      const RouteArgs ra{w->router_w, w->loop_bias + static_cast<int64_t>(l + 1) * E, w->gen_w,
+                         w->gen_bias + static_cast<int64_t>(l + 1) * E * E, E, K, M, b.top_idx, b.top_w, b.edge_idx,
+                         b.edge_w};
+      rc = combine_ln_route(b.y_ffn, H, ffn_splits, static_cast<int64_t>(N) * K * H, b.ffn_inv, K, cur, x0,
+                            d.act_dtype, N, H, w->ln_w, w->ln_b, d.residual_scale, d.reinject, d.ln_eps, next, ra, st);
+      if (rc != SB_OK && rc != SB_ERR_UNSUPPORTED) return rc;
+      routed = rc == SB_OK;
+    }
+    if (!routed) {
+      StageScope sc_(12, st);
+      SB_TRY(sb_combine_ln(b.y_ffn, H, ffn_splits, static_cast<int64_t>(N) * K * H, b.ffn_inv, K, nullptr, cur, x0,
+                           d.act_dtype, N, H, w->ln_w, w->ln_b, d.residual_scale, d.reinject, d.ln_eps, next,
+                           (taps && taps->delta && l == loop_end - 1) ? taps->delta : nullptr, st));
+    }
     if (taps && l == loop_end - 1) {
       auto cp = [&](void* dst, const void* src, size_t bytes) -> int {
         return dst ? cuda_status(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, st)) : SB_OK;
@@ -585,7 +619,7 @@ extern "C" SB_API int sb_block_route(const sb_block_dims* dims, const sb_block_w
   const int N = n_tokens, H = d.hidden, E = d.num_experts, K = d.top_k, KM = K * d.edges_per_expert;
   const int64_t cap_dst = static_cast<int64_t>(N) * (E < KM ? E : KM);
   int msg_splits = 1;
-  if ((rc = route_loop(d, w, b, h, N, loop_idx, &msg_splits, nullptr, st))) return rc;
+  if ((rc = route_loop(d, w, b, h, N, loop_idx, &msg_splits, nullptr, false, st))) return rc;
   if ((rc = sb_combine_rows(b.y_msg, H, msg_splits, cap_dst * H, b.dst_inv, KM, N, H, messages_f32, nullptr, K,
                             messages, d.act_dtype, st)))
     return rc;

@@ -7,6 +7,7 @@
 // epilogue (model.py:317).
 #include "sb_common.cuh"
 #include "sb_internal.h"
+#include "sb_route_dev.cuh"
 
 namespace sb {
 
@@ -131,16 +132,15 @@ SB_DEVINL float block_sum(float v, float* red) {
 }
 
 // One CTA per token; thread t owns float4 chunks t, t+256, ... of the row.
+// With row_copy the output row (rounded to T, as written) is also left in
+// shared memory.
 template <typename T>
-__global__ void __launch_bounds__(kLnThreads)
-combine_ln_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t split_stride,
-                  const int32_t* __restrict__ inv, int slots, const float* __restrict__ delta_in,
-                  const T* __restrict__ h, const T* __restrict__ x0, int cols,
-                  const float* __restrict__ ln_w, const float* __restrict__ ln_b, float alpha,
-                  float beta, float eps, T* __restrict__ out, float* __restrict__ delta_out) {
+SB_DEVINL void ln_token(const float* __restrict__ y, int64_t ldy, int splits, int64_t split_stride,
+                        const int32_t* __restrict__ inv, int slots, const float* __restrict__ delta_in,
+                        const T* __restrict__ h, const T* __restrict__ x0, int cols,
+                        const float* __restrict__ ln_w, const float* __restrict__ ln_b, float alpha,
+                        float beta, float eps, T* __restrict__ out, float* __restrict__ delta_out, T* row_copy) {
   __shared__ float red[32];
-  pdl_wait();
-  pdl_trigger();
   const int64_t t = blockIdx.x;
   const int nvec = cols >> 2;
   float4 u[kLnMaxVec], hv[kLnMaxVec], xv[kLnMaxVec];
@@ -203,8 +203,43 @@ combine_ln_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t 
       o.z = (u[i].z - mean) * rstd * g.z + b.z;
       o.w = (u[i].w - mean) * rstd * g.w + b.w;
       Vec4<T>::store(out + t * cols + 4 * v, o);
+      if (row_copy) Vec4<T>::store(row_copy + 4 * v, o);
     }
   }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kLnThreads)
+combine_ln_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t split_stride,
+                  const int32_t* __restrict__ inv, int slots, const float* __restrict__ delta_in,
+                  const T* __restrict__ h, const T* __restrict__ x0, int cols,
+                  const float* __restrict__ ln_w, const float* __restrict__ ln_b, float alpha,
+                  float beta, float eps, T* __restrict__ out, float* __restrict__ delta_out) {
+  pdl_wait();
+  pdl_trigger();
+  ln_token<T>(y, ldy, splits, split_stride, inv, slots, delta_in, h, x0, cols, ln_w, ln_b, alpha, beta, eps, out,
+              delta_out, nullptr);
+}
+
+// Decode: the loop's LayerNorm epilogue and the next loop's routing of the
+// same token in one CTA -- the new hidden row goes from the LayerNorm straight
+// into shared memory for route_token (the values written to `out`).
+template <typename T>
+__global__ void __launch_bounds__(kLnThreads)
+combine_ln_route_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t split_stride,
+                        const int32_t* __restrict__ inv, int slots, const T* __restrict__ h,
+                        const T* __restrict__ x0, int cols, const float* __restrict__ ln_w,
+                        const float* __restrict__ ln_b, float alpha, float beta, float eps, T* __restrict__ out,
+                        const RouteArgs r) {
+  extern __shared__ __align__(16) uint8_t route_smem[];
+  T* sh = reinterpret_cast<T*>(route_smem);
+  pdl_wait();
+  pdl_trigger();
+  ln_token<T>(y, ldy, splits, split_stride, inv, slots, nullptr, h, x0, cols, ln_w, ln_b, alpha, beta, eps, out,
+              nullptr, sh);
+  __syncthreads();
+  route_token(sh, static_cast<int>(blockIdx.x), cols, static_cast<const T*>(r.router_w), r.router_bias, r.E, r.K,
+              static_cast<const T*>(r.gen_w), r.gen_bias, r.M, r.top_idx, r.top_w, r.edge_idx, r.edge_w, route_smem);
 }
 
 // ------------------------------------------------------------------ warp-per-token variants
@@ -434,3 +469,40 @@ extern "C" SB_API int sb_combine_ln(const float* y, int64_t ldy, int splits, int
                   static_cast<__nv_bfloat16*>(out), delta_out);
   return SB_ERR_ARG;
 }
+
+namespace sb {
+int combine_ln_route(const float* y, int64_t ldy, int splits, int64_t split_stride, const int32_t* inv, int slots,
+                     const void* h, const void* x0, int act_dtype, int n_tokens, int cols, const float* ln_w,
+                     const float* ln_b, float alpha, float beta, float eps, void* out, const RouteArgs& r,
+                     cudaStream_t st) {
+  if (n_tokens <= 0) return SB_OK;
+  if (!y || !inv || slots <= 0 || slots > kMaxSlots || splits <= 0 || splits > kMaxSplits || ldy < cols ||
+      cols % 4 || cols > kLnThreads * kLnMaxVec * 4 || cols % 8 || r.E > kRouterMaxE || r.K > 32 || r.M > 32 ||
+      r.K > r.E || r.M > r.E)
+    return SB_ERR_ARG;
+  const size_t smem = route_smem_bytes(act_dtype, cols, r.E, r.K);
+  if (smem > kRouteEdgesMaxSmem) return SB_ERR_UNSUPPORTED;
+  if (act_dtype == SB_F32) {
+    static bool attr_set = false;
+    if (!attr_set) {
+      cudaFuncSetAttribute(combine_ln_route_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kRouteEdgesMaxSmem);
+      attr_set = true;
+    }
+    return launch(combine_ln_route_kernel<float>, dim3(n_tokens), dim3(kLnThreads), smem, st, y, ldy, splits,
+                  split_stride, inv, slots, static_cast<const float*>(h), static_cast<const float*>(x0), cols, ln_w,
+                  ln_b, alpha, beta, eps, static_cast<float*>(out), r);
+  }
+  if (act_dtype != SB_BF16) return SB_ERR_ARG;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(combine_ln_route_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kRouteEdgesMaxSmem);
+    attr_set = true;
+  }
+  return launch(combine_ln_route_kernel<__nv_bfloat16>, dim3(n_tokens), dim3(kLnThreads), smem, st, y, ldy, splits,
+                split_stride, inv, slots, static_cast<const __nv_bfloat16*>(h),
+                static_cast<const __nv_bfloat16*>(x0), cols, ln_w, ln_b, alpha, beta, eps,
+                static_cast<__nv_bfloat16*>(out), r);
+}
+}  // namespace sb

@@ -98,6 +98,26 @@ int route_edges(const void* h, int act_dtype, int n_tokens, int hidden, const vo
                 int E, int K, const void* gen_w, const float* gen_bias, int M, int32_t* top_idx, float* top_w,
                 int32_t* edge_idx, float* edge_w, cudaStream_t st);
 
+// Routing operands of one loop (fused route kernels).
+struct RouteArgs {
+  const void* router_w;
+  const float* router_bias;  // loop_bias of the loop routed
+  const void* gen_w;
+  const float* gen_bias;     // per-loop generator bias of the loop routed
+  int E, K, M;
+  int32_t* top_idx;
+  float* top_w;
+  int32_t* edge_idx;
+  float* edge_w;
+};
+// LayerNorm epilogue of one loop and routing of the next in one kernel (one
+// CTA per token, decode sizes; sb_combine.cu); SB_ERR_UNSUPPORTED when the
+// routing's shared memory exceeds kRouteEdgesMaxSmem.
+int combine_ln_route(const float* y, int64_t ldy, int splits, int64_t split_stride, const int32_t* inv, int slots,
+                     const void* h, const void* x0, int act_dtype, int n_tokens, int cols, const float* ln_w,
+                     const float* ln_b, float alpha, float beta, float eps, void* out, const RouteArgs& r,
+                     cudaStream_t st);
+
 // Top-K routing of router logits that a grouped GEMM computed (sb_router.cu).
 int router_from_logits(const float* logits, int ld, int splits, int64_t split_stride, int n_tokens, int E, int K,
                        int32_t* top_idx, float* top_w, cudaStream_t st);
