@@ -60,6 +60,9 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--engine", default="auto", choices=["auto", "tcgen05", "simt"])
     ap.add_argument("--activation", default="gelu", choices=["gelu", "swiglu"])
+    ap.add_argument("--transport", default="nccl", choices=["nccl", "peer"],
+                    help="N > 1 expert-parallel exchange: NCCL all-to-all, or stores into the peers' memory over "
+                         "NVLink (peer; measured at parity on 2 GPUs)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-only", action="store_true",
@@ -330,7 +333,7 @@ def run_b200_ep(args, rank, world, local, device):
         cfg.moe_int4_group_size = cfg.moe_int4_group_size or 128
     sd = synth.synthetic_state_dict(cfg, seed=0, device=device, zipf=zipf, round_bf16=True)
     ep = ExpertParallelBlock(cfg, sd, device, act_dtype=torch.bfloat16, max_tokens=n, weight_format=spec["wfmt"],
-                             engine=args.engine)
+                             engine=args.engine, transport=args.transport)
     del sd
     h, _ = synth.block_inputs(n, cfg.hidden_size, seed=1 + rank, device=device, dtype=torch.bfloat16)
     h = h.view(n, -1).contiguous()
@@ -380,7 +383,9 @@ def run_b200_ep(args, rank, world, local, device):
                    "hidden": cfg.hidden_size, "experts": cfg.num_experts, "top_k": cfg.top_k,
                    "edges_per_expert": cfg.edges_per_expert, "ffn": cfg.expert_ffn_size,
                    "expert_activation": cfg.expert_activation, "expert_weights": spec["wfmt"],
-                   "parallelism": f"ep{world}: tokens sharded by rank, experts e % {world}, NCCL all-to-all",
+                   "parallelism": f"ep{world}: tokens sharded by rank, experts e % {world}, "
+                                  + ("dispatch/combine stored into peer memory over NVLink" if args.transport == "peer"
+                                     else "NCCL all-to-all"),
                    "l2": "not flushed: dense + local expert weights re-read every loop", "engine": args.engine},
         "clocks": clk.summary(),
         "e2e": {"value": n * world / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 2 * n * cfg.hidden_size * 2,
@@ -394,8 +399,8 @@ def run_b200_ep(args, rank, world, local, device):
         line["cpu_baseline"] = cpu_baseline(cfg, spec, args.cpu_seconds)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    ep.release_graph()  # a graph holding NCCL work must go before the process group
     torch.cuda.synchronize(device)
+    ep.close()  # the graph (NCCL work) and the peer regions go before the process group
     barrier(world)
     dist.destroy_process_group()
 

@@ -292,6 +292,39 @@ SB_API int sb_ep_pack(const int32_t* top_idx, const float* top_w, const void* me
                       int n_tokens, int hidden, int top_k, int num_experts, int world, int cap, void* send,
                       int32_t* ret_pos, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Peer-memory exchange of the same rows (no reference counterpart: it replaces
+ * the all-to-all pair of the token-sharded step with stores into the peers'
+ * memory over NVLink).  Each rank owns one region of sb_ep_peer_region_bytes():
+ * recv rows [world][cap][row_pitch] | returned rows [world][cap][hidden] fp32 at
+ * the next 256-byte boundary | flags.  sb_ep_peer_create allocates and zeroes it
+ * (cudaMalloc: set-up only, never on the per-step path) and writes its 64-byte
+ * CUDA IPC handle; every rank maps the others' handles with sb_ep_peer_map.
+ * `regions` is a DEVICE array of world region pointers as mapped in this process
+ * (its own region at index rank).
+ *   sb_ep_dispatch: sb_ep_pack, but row (q, j) goes straight to rank q's recv
+ *     row [rank][j], then rank's dispatch flag is raised in every region.
+ *   sb_ep_wait(kind 0 dispatch / 1 return): waits (on the device, bounded: about
+ *     2 s, then SB_DEVERR_PEER_WAIT in *status) until every rank has raised this
+ *     rank's flag once more than this rank has waited before.
+ *   sb_ep_return: rows [q][cap][hidden] of this owner's results to rank q's
+ *     returned rows [rank][cap], then the return flag is raised in every region.
+ * One step per loop: dispatch -> wait(0) -> sb_expert_rows on the recv rows ->
+ * return -> wait(1) -> sb_combine_ln on the returned rows with ret_pos.  All
+ * ranks must take the same steps; regions must not be shared between blocks. */
+SB_API size_t sb_ep_peer_region_bytes(int world, int cap, int64_t row_pitch, int hidden);
+SB_API int sb_ep_peer_create(int world, int cap, int64_t row_pitch, int hidden, void** region, void* ipc_handle);
+SB_API int sb_ep_peer_map(const void* ipc_handle, void** region);
+SB_API int sb_ep_peer_unmap(void* region);
+SB_API int sb_ep_peer_destroy(void* region);
+SB_API int sb_ep_dispatch(const int32_t* top_idx, const float* top_w, const void* messages, int act_dtype,
+                          int n_tokens, int hidden, int top_k, int num_experts, int world, int rank, int cap,
+                          void* const* regions, int32_t* ret_pos, void* workspace, size_t workspace_bytes,
+                          void* stream);
+SB_API int sb_ep_wait(void* region, int world, int cap, int64_t row_pitch, int hidden, int kind, int* status,
+                      void* stream);
+SB_API int sb_ep_return(const float* rows_out, int world, int rank, int cap, int64_t row_pitch, int hidden,
+                        void* const* regions, void* stream);
+
 /* Owner side: rows in the packed layout above (n_rows of row_pitch bytes, ids
  * are local expert ids in [0, dims->num_experts)); out[r] = sum over the row's
  * slots of w * ffn_id(row message), fp32 [n_rows, hidden].  The expert part of

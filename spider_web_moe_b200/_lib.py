@@ -109,6 +109,14 @@ SIGNATURES = {
     "sb_stage_timing": (i32, [i32]),
     "sb_stage_timing_read": (i32, [C.POINTER(C.c_double), C.POINTER(i32), i32]),
     "sb_kernel_launches": (C.c_ulonglong, []),
+    "sb_ep_peer_region_bytes": (sz, [i32, i32, i64, i32]),
+    "sb_ep_peer_create": (i32, [i32, i32, i64, i32, C.POINTER(vp), vp]),
+    "sb_ep_peer_map": (i32, [vp, C.POINTER(vp)]),
+    "sb_ep_peer_unmap": (i32, [vp]),
+    "sb_ep_peer_destroy": (i32, [vp]),
+    "sb_ep_dispatch": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, sz, vp]),
+    "sb_ep_wait": (i32, [vp, i32, i32, i64, i32, i32, vp, vp]),
+    "sb_ep_return": (i32, [vp, i32, i32, i32, i64, i32, vp, vp]),
 }
 
 

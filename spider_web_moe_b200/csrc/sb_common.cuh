@@ -25,6 +25,7 @@ enum {
   SB_DEVERR_EPI_WAIT = 1 << 3,     // epilogue gave up on the accumulator barrier
   SB_DEVERR_BAD_INDEX = 1 << 4,    // an index outside its range was met and skipped
   SB_DEVERR_DRAIN = 1 << 5,        // in-flight copies not drained before exit
+  SB_DEVERR_PEER_WAIT = 1 << 6,    // gave up waiting for a peer rank's exchange flag
 };
 
 namespace sb {

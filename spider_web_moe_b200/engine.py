@@ -235,6 +235,25 @@ class BlockEngine:
         L.check(rc, "sb_ep_pack")
         return send, ret_pos
 
+    def ep_dispatch(self, top_idx, top_w, msgs, world: int, rank: int, cap: int, regions: torch.Tensor,
+                    stream=None) -> torch.Tensor:
+        """sb_ep_dispatch: the packed rows go straight into the owners' exchange
+        regions (`regions`: int64 device tensor of the mapped region pointers);
+        returns the return positions [n, K]."""
+        H, K, E = self.cfg.hidden_size, self.cfg.top_k, self.cfg.num_experts
+        n = msgs.shape[0]
+        ret_pos = torch.empty((n, K), dtype=torch.int32, device=self.device)
+        ws = self._ep_ws(self.lib.sb_ep_pack_workspace_bytes(n, K, world))
+        rc = self.lib.sb_ep_dispatch(top_idx.data_ptr(), top_w.data_ptr(), msgs.data_ptr(), self.dims.act_dtype, n, H,
+                                     K, E, world, rank, cap, regions.data_ptr(), ret_pos.data_ptr(), ws.data_ptr(),
+                                     ws.numel(), _stream_ptr(stream))
+        L.check(rc, "sb_ep_dispatch")
+        return ret_pos
+
+    def status_ptr(self) -> int:
+        """Device address of the status word (kernels outside the block record there)."""
+        return self.workspace.data_ptr() + self.lib.sb_status_offset()
+
     def expert_rows(self, rows: torch.Tensor, out: torch.Tensor | None = None, expected_pairs: int = 0,
                     stream=None) -> torch.Tensor:
         """Owner side: packed rows [R, pitch] (uint8) -> fp32 [R, H] weighted sums of this

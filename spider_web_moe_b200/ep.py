@@ -27,6 +27,7 @@ the gloo backend; ``CudaOps`` is the implementation that runs the kernels.
 """
 from __future__ import annotations
 
+import ctypes as C
 import dataclasses
 
 import torch
@@ -97,11 +98,92 @@ def ep_loop(ops, h, x0, loop_idx: int, world: int, cap: int, group=None):
     return ops.epilogue(ret, ret_pos, h, x0)
 
 
+class _DeviceBuffer:
+    """A raw device allocation seen by torch.as_tensor (no copy, no ownership)."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+class PeerExchange:
+    """Exchange regions of the peer-memory transport (sb_ep_peer_*): this rank's
+    region is created here and every other rank's mapped through CUDA IPC, over
+    NVLink on one node.  Set-up only; the per-step calls only read and write the
+    regions.  Every rank must construct it (the IPC handles are all-gathered)."""
+
+    def __init__(self, world: int, rank: int, cap: int, pitch: int, hidden: int, device, group=None):
+        self.lib = L.load()
+        self.world, self.rank, self.cap, self.pitch, self.hidden = world, rank, cap, pitch, hidden
+        region = C.c_void_p()
+        handle = (C.c_uint8 * 64)()
+        L.check(self.lib.sb_ep_peer_create(world, cap, pitch, hidden, C.byref(region), handle), "sb_ep_peer_create")
+        self.region = int(region.value)
+        handles = [bytes(handle)]
+        if world > 1:
+            mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=device)
+            gathered = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(gathered, mine, group=group)
+            handles = [bytes(t.cpu().tolist()) for t in gathered]
+        ptrs, self.mapped = [], []
+        for q in range(world):
+            if q == rank:
+                ptrs.append(self.region)
+                continue
+            p = C.c_void_p()
+            buf = (C.c_uint8 * 64).from_buffer_copy(handles[q])
+            L.check(self.lib.sb_ep_peer_map(buf, C.byref(p)), "sb_ep_peer_map")
+            ptrs.append(int(p.value))
+            self.mapped.append(int(p.value))
+        self.regions = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        ret_off = (world * cap * pitch + 255) // 256 * 256
+        self.recv = torch.as_tensor(_DeviceBuffer(self.region, (world, cap, pitch), "|u1"), device=device)
+        self.ret = torch.as_tensor(_DeviceBuffer(self.region + ret_off, (world * cap, hidden), "<f4"), device=device)
+        self.out = torch.zeros((world * cap, hidden), dtype=torch.float32, device=device)
+
+    def close(self, group=None):
+        """Unmap the peers' regions and free this rank's (all ranks, after the
+        last step; before the process group is destroyed)."""
+        torch.cuda.synchronize()
+        if self.world > 1 and dist.is_initialized():
+            dist.barrier(group=group)
+        for p in self.mapped:
+            self.lib.sb_ep_peer_unmap(C.c_void_p(p))
+        self.mapped = []
+        if self.world > 1 and dist.is_initialized():
+            dist.barrier(group=group)
+        if self.region:
+            self.recv = self.ret = None
+            self.lib.sb_ep_peer_destroy(C.c_void_p(self.region))
+            self.region = 0
+
+
+def ep_loop_peer(dense: BlockEngine, local: BlockEngine | None, xch: PeerExchange, h, x0, loop_idx: int,
+                 expected_pairs: int, stream=None):
+    """One loop of the token-sharded block over the peer-memory transport:
+    route -> dispatch into the owners' regions -> wait -> local experts on the
+    received rows -> return into the sources' regions -> wait -> epilogue."""
+    lib = xch.lib
+    W, cap, pitch, H = xch.world, xch.cap, xch.pitch, xch.hidden
+    sp = torch.cuda.current_stream().cuda_stream if stream is None else stream.cuda_stream
+    msgs, top_idx, top_w = dense.route(h, loop_idx)
+    ret_pos = dense.ep_dispatch(top_idx, top_w, msgs, W, xch.rank, cap, xch.regions)
+    L.check(lib.sb_ep_wait(C.c_void_p(xch.region), W, cap, pitch, H, 0, C.c_void_p(dense.status_ptr()),
+                           C.c_void_p(sp)), "sb_ep_wait")
+    if local is not None:
+        local.expert_rows(xch.recv.view(W * cap, pitch), out=xch.out, expected_pairs=expected_pairs)
+    L.check(lib.sb_ep_return(C.c_void_p(xch.out.data_ptr()), W, xch.rank, cap, pitch, H,
+                             C.c_void_p(xch.regions.data_ptr()), C.c_void_p(sp)), "sb_ep_return")
+    L.check(lib.sb_ep_wait(C.c_void_p(xch.region), W, cap, pitch, H, 1, C.c_void_p(dense.status_ptr()),
+                           C.c_void_p(sp)), "sb_ep_wait")
+    return dense.epilogue(xch.ret, ret_pos, h, x0)
+
+
 class ExpertParallelBlock:
     """The block on one rank of a token-sharded expert-parallel group."""
 
     def __init__(self, cfg, state: dict, device, group=None, act_dtype=torch.bfloat16, max_tokens: int = 64,
-                 weight_format: str | None = None, engine: str = "auto"):
+                 weight_format: str | None = None, engine: str = "auto", transport: str = "nccl"):
         self.cfg = from_any(cfg)
         self.group = group
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -118,6 +200,15 @@ class ExpertParallelBlock:
                                      act_dtype=act_dtype, max_tokens=1, weight_format=weight_format, engine=engine)
         self.ops = CudaOps(self.dense, self.local, self.world)
         self.max_tokens = max_tokens
+        if transport not in ("nccl", "peer"):
+            raise ValueError(f"transport {transport!r}: 'nccl' or 'peer'")
+        self.transport = transport
+        self.xch = None
+        if transport == "peer":
+            # every rank's own dense engine workspace exists before the first step
+            self.dense._ensure_workspace(max_tokens)
+            pitch = self.dense.lib.sb_ep_row_pitch(self.cfg.hidden_size, self.dense.dims.act_dtype, self.cfg.top_k)
+            self.xch = PeerExchange(self.world, self.rank, max_tokens, pitch, self.cfg.hidden_size, device, group)
 
     def loop(self, h, x0, loop_idx: int):
         """One loop; every rank must call it (the exchange is collective).  The
@@ -126,6 +217,9 @@ class ExpertParallelBlock:
         n = h.numel() // self.cfg.hidden_size
         if n > self.max_tokens:
             raise ValueError(f"{n} tokens exceed max_tokens={self.max_tokens} of the expert-parallel block")
+        if self.transport == "peer":
+            return ep_loop_peer(self.dense, self.local, self.xch, h.reshape(n, -1), x0.reshape(n, -1), loop_idx,
+                                self.max_tokens * self.cfg.top_k).view(h.shape)
         return ep_loop(self.ops, h.reshape(n, -1), x0.reshape(n, -1), loop_idx, self.world, self.max_tokens,
                        self.group).view(h.shape)
 
@@ -170,4 +264,12 @@ class ExpertParallelBlock:
 
     def release_graph(self):
         self.graph = None
+
+    def close(self):
+        """Release the peer-memory exchange (all ranks; before the process group
+        is destroyed)."""
+        self.release_graph()
+        if self.xch is not None:
+            self.xch.close(self.group)
+            self.xch = None
 

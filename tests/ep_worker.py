@@ -3,7 +3,9 @@
 Each rank holds its own slice of the tokens; experts are owned by e % world.
 Loop by loop (same input to both), the rank's EP output must match a full
 single-GPU block on the same tokens: routing identical, h_out within the bf16
-tolerance.  Exits non-zero on a mismatch.
+tolerance.  The peer-memory transport must give bit-identical outputs to the
+NCCL one, eagerly and replayed from a CUDA graph.  Exits non-zero on a
+mismatch.
 """
 import datetime
 import os
@@ -31,16 +33,23 @@ def main():
     n = 48
     sd = synth.synthetic_state_dict(cfg, seed=31, device=dev, zipf=1.1 if spec["zipf"] else None, round_bf16=True)
     ep = ExpertParallelBlock(cfg, sd, dev, act_dtype=torch.bfloat16, max_tokens=n, weight_format=spec["wfmt"])
+    # the same step over the peer-memory transport (stores into the owners'
+    # regions over NVLink instead of NCCL all-to-all): bit-identical rows
+    peer = ExpertParallelBlock(cfg, sd, dev, act_dtype=torch.bfloat16, max_tokens=n, weight_format=spec["wfmt"],
+                               transport="peer")
     full = BlockEngine(cfg, sd, dev, act_dtype=torch.bfloat16, max_tokens=n, weight_format=spec["wfmt"])
     h, _ = synth.block_inputs(n * world, cfg.hidden_size, seed=32, device=dev, dtype=torch.bfloat16)
     h = h.view(-1, cfg.hidden_size)[rank * n:(rank + 1) * n].contiguous()
     x0 = h.clone()
     worst = 0.0
     ok = True
+    same = True
     for l in range(cfg.num_loops):
         out_ep = ep.loop(h, x0, l)
+        out_peer = peer.loop(h, x0, l)
         out_full = full.forward(h, x0, l, l + 1)
         torch.cuda.synchronize()
+        same &= torch.equal(out_ep, out_peer)
         num = (out_ep.float() - out_full.float()).abs().amax(-1)
         den = out_full.float().abs().amax(-1).clamp_min(1e-30)
         err = float((num / den).max())
@@ -48,7 +57,21 @@ def main():
         ok &= err < 2e-2
         h = out_full
     full.check_status()
-    print(f"rank {rank}/{world} {name}: worst relative error {worst:.3e} {'ok' if ok else 'MISMATCH'}", flush=True)
+    peer.dense.check_status()
+    # all loops in one CUDA graph over the peer transport, replayed twice
+    peer.capture(n)
+    h0, _ = synth.block_inputs(n * world, cfg.hidden_size, seed=33, device=dev, dtype=torch.bfloat16)
+    h0 = h0.view(-1, cfg.hidden_size)[rank * n:(rank + 1) * n].contiguous()
+    want = ep.forward(h0, h0)
+    for _ in range(2):
+        got = peer.replay(h0, h0)
+        torch.cuda.synchronize()
+        same &= torch.equal(got, want)
+    peer.dense.check_status()
+    peer.close()
+    ok &= same
+    print(f"rank {rank}/{world} {name}: worst relative error {worst:.3e}, peer transport "
+          f"{'identical' if same else 'DIFFERS'} {'ok' if ok else 'MISMATCH'}", flush=True)
     flag = torch.tensor([0 if ok else 1], device=dev)
     dist.all_reduce(flag)
     dist.barrier()

@@ -43,6 +43,37 @@ def test_ep_path_single_gpu_matches_block(name, cuda_device):
         h = b
 
 
+@pytest.mark.parametrize("name", ["cfg2", "cfg5"])
+def test_peer_transport_single_gpu_matches_nccl_path(name, cuda_device):
+    """World of one over the peer-memory transport (the rank's own region as its
+    only peer): the dispatch, flag waits and return run, and the outputs are
+    bit-identical to the NCCL-transport path, eagerly and from a CUDA graph
+    replayed twice (the flags keep counting across loops and replays)."""
+    spec = benchmark_configs()[name]
+    cfg = ModelConfig(**spec["model"]).validate()
+    n = 40
+    sd = synth.synthetic_state_dict(cfg, seed=45, device=cuda_device, zipf=1.1 if spec["zipf"] else None,
+                                    round_bf16=True)
+    ref = ExpertParallelBlock(cfg, sd, cuda_device, act_dtype=torch.bfloat16, max_tokens=n, weight_format=spec["wfmt"])
+    peer = ExpertParallelBlock(cfg, sd, cuda_device, act_dtype=torch.bfloat16, max_tokens=n,
+                               weight_format=spec["wfmt"], transport="peer")
+    h, _ = synth.block_inputs(n, cfg.hidden_size, seed=46, device=cuda_device, dtype=torch.bfloat16)
+    h = h.view(n, -1)
+    try:
+        want = ref.forward(h, h)
+        got = peer.forward(h, h)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+        peer.capture(n)
+        for _ in range(2):
+            out = peer.replay(h, h)
+            torch.cuda.synchronize()
+            assert torch.equal(out, want)
+        peer.dense.check_status()
+    finally:
+        peer.close()
+
+
 def test_ep_owner_hot_expert_loops_row_tiles(cuda_device):
     """200 tokens with two experts taking every token: the owner plans 64-row tiles
     per expert (32 expected pairs per expert on average), so each hot expert's
@@ -71,7 +102,7 @@ def free_port():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_ep_two_gpus_nccl():
+def test_ep_two_gpus_nccl_and_peer():
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr=127.0.0.1", f"--master-port={free_port()}", os.path.join(HERE, "ep_worker.py")]
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=600,
