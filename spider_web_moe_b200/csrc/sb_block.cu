@@ -684,10 +684,18 @@ extern "C" SB_API int sb_expert_rows(const sb_block_dims* dims, const sb_block_w
   const int hint = expected_pairs > 0 ? expected_pairs : N * K;
   const int row_plan = hint <= 32 * G ? (N < 64 ? N : 64) : N;
 #define SB_TRY(x) do { rc = (x); if (rc) return rc; } while (0)
-  SB_TRY(launch(unpack_meta_kernel, dim3((N * K + 255) / 256), dim3(256), 0, st, static_cast<const uint8_t*>(rows),
-                row_pitch, meta_off, N, K, G, b.top_idx, top_w));
-  SB_TRY(sb_group(b.top_idx, top_w, N, K, G, SB_GROUP_POSITIVE_ONLY, b.ffn_off, b.ffn_row, b.ffn_slot, b.ffn_w,
-                  b.ffn_inv, b.group_ws, b.group_ws_bytes, st));
+  // dispatch plan over the rows' local expert ids: one kernel reading the row
+  // metadata, or (many rows) unpack, then sb_group
+  rc = derived_group_launch(0, rows, row_pitch, meta_off, nullptr, G, N, K, G, SB_GROUP_POSITIVE_ONLY, b.ffn_off,
+                            b.ffn_row, b.ffn_slot, b.ffn_w, b.ffn_inv, b.group_ws, b.group_ws_bytes, st);
+  if (rc == SB_ERR_UNSUPPORTED) {
+    SB_TRY(launch(unpack_meta_kernel, dim3((N * K + 255) / 256), dim3(256), 0, st, static_cast<const uint8_t*>(rows),
+                  row_pitch, meta_off, N, K, G, b.top_idx, top_w));
+    SB_TRY(sb_group(b.top_idx, top_w, N, K, G, SB_GROUP_POSITIVE_ONLY, b.ffn_off, b.ffn_row, b.ffn_slot, b.ffn_w,
+                    b.ffn_inv, b.group_ws, b.group_ws_bytes, st));
+  } else if (rc) {
+    return rc;
+  }
   {
     sb_grouped_gemm_args a;
     fill_expert_gemm(a, d, true, w->w_up, w->s_up, w->b_up, w->w_gate, w->s_gate, w->b_gate);

@@ -116,7 +116,8 @@ ep_pack_kernel(const T* __restrict__ msgs, const int32_t* __restrict__ top_idx, 
   // return positions, one thread per (token, slot)
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_tokens * K; i += gridDim.x * blockDim.x) {
     const int p = inv[i];
-    const int q = owner[i];
+    const int e = top_idx[i];
+    const int q = (e >= 0 && e < E) ? e % world : -1;
     ret_pos[i] = (p >= 0 && q >= 0) ? q * cap + (p - off[q]) : -1;
   }
   if (regions) ep_signal_peers(regions, regions[me], ctrl_off, world, me, 0);
@@ -227,11 +228,17 @@ extern "C" SB_API int sb_ep_pack(const int32_t* top_idx, const float* top_w, con
   const int entries = n_tokens * top_k;
   int rc = SB_OK;
   if (n_tokens > 0) {
-    rc = launch(ep_owner_kernel, dim3((entries + 255) / 256), dim3(256), 0, st, top_idx, entries, num_experts, world,
-                b.owner);
-    if (rc) return rc;
-    rc = sb_group(b.owner, nullptr, n_tokens, top_k, world, 0, b.off, b.prow, b.pslot, b.pw, b.inv, b.group_ws,
-                  b.group_ws_bytes, st);
+    // owners of the tokens' experts grouped in one kernel; larger batches:
+    // owner ids, then sb_group
+    rc = derived_group_launch(1, nullptr, 0, 0, top_idx, num_experts, n_tokens, top_k, world, 0, b.off, b.prow,
+                              b.pslot, b.pw, b.inv, b.group_ws, b.group_ws_bytes, st);
+    if (rc == SB_ERR_UNSUPPORTED) {
+      rc = launch(ep_owner_kernel, dim3((entries + 255) / 256), dim3(256), 0, st, top_idx, entries, num_experts,
+                  world, b.owner);
+      if (rc) return rc;
+      rc = sb_group(b.owner, nullptr, n_tokens, top_k, world, 0, b.off, b.prow, b.pslot, b.pw, b.inv, b.group_ws,
+                    b.group_ws_bytes, st);
+    }
   } else {
     rc = cuda_status(cudaMemsetAsync(b.off, 0, sizeof(int32_t) * (world + 1), st));
   }
@@ -316,11 +323,17 @@ extern "C" SB_API int sb_ep_dispatch(const int32_t* top_idx, const float* top_w,
   const int entries = n_tokens * top_k;
   int rc = SB_OK;
   if (n_tokens > 0) {
-    rc = launch(ep_owner_kernel, dim3((entries + 255) / 256), dim3(256), 0, st, top_idx, entries, num_experts, world,
-                b.owner);
-    if (rc) return rc;
-    rc = sb_group(b.owner, nullptr, n_tokens, top_k, world, 0, b.off, b.prow, b.pslot, b.pw, b.inv, b.group_ws,
-                  b.group_ws_bytes, st);
+    // owners of the tokens' experts grouped in one kernel; larger batches:
+    // owner ids, then sb_group
+    rc = derived_group_launch(1, nullptr, 0, 0, top_idx, num_experts, n_tokens, top_k, world, 0, b.off, b.prow,
+                              b.pslot, b.pw, b.inv, b.group_ws, b.group_ws_bytes, st);
+    if (rc == SB_ERR_UNSUPPORTED) {
+      rc = launch(ep_owner_kernel, dim3((entries + 255) / 256), dim3(256), 0, st, top_idx, entries, num_experts,
+                  world, b.owner);
+      if (rc) return rc;
+      rc = sb_group(b.owner, nullptr, n_tokens, top_k, world, 0, b.off, b.prow, b.pslot, b.pw, b.inv, b.group_ws,
+                    b.group_ws_bytes, st);
+    }
   } else {
     rc = cuda_status(cudaMemsetAsync(b.off, 0, sizeof(int32_t) * (world + 1), st));
   }

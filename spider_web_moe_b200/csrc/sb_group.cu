@@ -212,6 +212,64 @@ extern "C" SB_API int sb_group(const int32_t* idx, const float* w, int n_rows, i
 }
 
 namespace sb {
+// ---------------------------------------------------------------------------
+// Groupings whose ids are derived in the same kernel (one CTA, <= kDerivedMax
+// entries): the ids and weights are staged in shared memory, then grouped as
+// sb_group groups them.
+//   mode 0 (expert-parallel owner side): ids / weights from the metadata of
+//     packed rows (K int32 local ids, then K fp32 weights, at meta_off of each
+//     row of `pitch` bytes); ids outside [0, G) are skipped.
+//   mode 1 (expert-parallel sender side): id = top_idx % G (the owning rank of
+//     the expert, G = world), no weights; negative experts are skipped.
+constexpr int kDerivedMax = 1024;  // staging + group_one_cta fit the 48 KB of static shared memory
+
+__global__ void __launch_bounds__(kGroupThreads, 1)
+derived_group_kernel(int mode, const uint8_t* __restrict__ rows, int64_t pitch, int64_t meta_off,
+                     const int32_t* __restrict__ top_idx, int num_experts, int n, int K, int G, int flags,
+                     int32_t* __restrict__ offsets, int32_t* __restrict__ perm_row, int32_t* __restrict__ perm_slot,
+                     float* __restrict__ perm_w, int32_t* __restrict__ inv, int32_t* __restrict__ rank_scratch,
+                     float* __restrict__ w_scratch) {
+  __shared__ int32_t s_ids[kDerivedMax];
+  __shared__ float s_w[kDerivedMax];
+  pdl_wait();
+  pdl_trigger();
+  const int total = n * K;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    if (mode == 0) {
+      const int r = i / K, k = i - r * K;
+      const uint8_t* m = rows + static_cast<int64_t>(r) * pitch + meta_off;
+      const int e = reinterpret_cast<const int32_t*>(m)[k];
+      s_ids[i] = (e >= 0 && e < G) ? e : -1;
+      s_w[i] = reinterpret_cast<const float*>(m + static_cast<int64_t>(K) * 4)[k];
+    } else {
+      const int e = top_idx[i];
+      s_ids[i] = (e >= 0 && e < num_experts) ? e % G : -1;
+      s_w[i] = 1.f;
+    }
+  }
+  __syncthreads();
+  group_one_cta(s_ids, mode == 0 ? s_w : nullptr, n, K, G, flags, offsets, perm_row, perm_slot, perm_w, inv,
+                rank_scratch, w_scratch);
+}
+
+int derived_group_launch(int mode, const void* rows, int64_t pitch, int64_t meta_off, const int32_t* top_idx,
+                         int num_experts, int n, int K, int G, int flags, int32_t* offsets, int32_t* perm_row,
+                         int32_t* perm_slot, float* perm_w, int32_t* inv, void* workspace, size_t workspace_bytes,
+                         cudaStream_t st) {
+  const int64_t total = static_cast<int64_t>(n) * K;
+  if (total > kDerivedMax || G > kGroupMaxG || n <= 0) return SB_ERR_UNSUPPORTED;
+  if (workspace_bytes < sb_group_workspace_bytes(n, K, G)) return SB_ERR_WORKSPACE;
+  Carver c(workspace, workspace_bytes);  // the scratch layout of sb_group
+  c.take<char>(kStatusBytes);
+  int32_t* rank_scratch = c.take<int32_t>(total);
+  float* w_scratch = c.take<float>(total);
+  int threads = static_cast<int>(((total + 31) / 32) * 32);
+  threads = threads < 64 ? 64 : (threads > kGroupThreads ? kGroupThreads : threads);
+  return launch(derived_group_kernel, dim3(1), dim3(threads), 0, st, mode, static_cast<const uint8_t*>(rows), pitch,
+                meta_off, top_idx, num_experts, n, K, G, flags, offsets, perm_row, perm_slot, perm_w, inv, rank_scratch,
+                w_scratch);
+}
+
 int group_pair_launch(const GroupJob& j0, const GroupJob& j1, cudaStream_t st) {
   const int64_t t0 = static_cast<int64_t>(j0.n_rows) * j0.slots, t1 = static_cast<int64_t>(j1.n_rows) * j1.slots;
   const int64_t tmax = t0 > t1 ? t0 : t1;

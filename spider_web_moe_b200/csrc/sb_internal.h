@@ -118,6 +118,14 @@ int combine_ln_route(const float* y, int64_t ldy, int splits, int64_t split_stri
                      const float* ln_b, float alpha, float beta, float eps, void* out, const RouteArgs& r,
                      cudaStream_t st);
 
+// sb_group over ids derived in the grouping kernel itself (sb_group.cu): mode 0
+// ids / weights from packed expert-parallel rows, mode 1 owner = top_idx % G.
+// SB_ERR_UNSUPPORTED above 1024 entries; `workspace` as sb_group's.
+int derived_group_launch(int mode, const void* rows, int64_t pitch, int64_t meta_off, const int32_t* top_idx,
+                         int num_experts, int n, int K, int G, int flags, int32_t* offsets, int32_t* perm_row,
+                         int32_t* perm_slot, float* perm_w, int32_t* inv, void* workspace, size_t workspace_bytes,
+                         cudaStream_t st);
+
 // Top-K routing of router logits that a grouped GEMM computed (sb_router.cu).
 int router_from_logits(const float* logits, int ld, int splits, int64_t split_stride, int n_tokens, int E, int K,
                        int32_t* top_idx, float* top_w, cudaStream_t st);
