@@ -60,9 +60,9 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--engine", default="auto", choices=["auto", "tcgen05", "simt"])
     ap.add_argument("--activation", default="gelu", choices=["gelu", "swiglu"])
-    ap.add_argument("--transport", default="nccl", choices=["nccl", "peer"],
-                    help="N > 1 expert-parallel exchange: NCCL all-to-all, or stores into the peers' memory over "
-                         "NVLink (peer; measured at parity on 2 GPUs)")
+    ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
+                    help="N > 1 expert-parallel exchange: stores into the peers' memory over NVLink (peer) or NCCL "
+                         "all-to-all")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-only", action="store_true",
