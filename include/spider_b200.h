@@ -324,6 +324,19 @@ SB_API int sb_ep_wait(void* region, int world, int cap, int64_t row_pitch, int h
                       void* stream);
 SB_API int sb_ep_return(const float* rows_out, int world, int rank, int cap, int64_t row_pitch, int hidden,
                         void* const* regions, void* stream);
+/* The same step with the waits and the return inside the neighbouring kernels:
+ *   sb_expert_rows_peer = sb_ep_wait(kind 0) + sb_expert_rows on the region's
+ *     receive rows (world * cap rows) + sb_ep_return of the results;
+ *   sb_ep_epilogue_peer = sb_ep_wait(kind 1) + sb_combine_ln of the region's
+ *     returned rows with ret_pos (slots = top_k). */
+SB_API int sb_expert_rows_peer(const sb_block_dims* dims, const sb_block_weights* w, void* region,
+                               void* const* regions, int world, int rank, int cap, int64_t row_pitch,
+                               int expected_pairs, int* status, void* workspace, size_t workspace_bytes,
+                               void* stream);
+SB_API int sb_ep_epilogue_peer(void* region, int world, int cap, int64_t row_pitch, const int32_t* ret_pos,
+                               int top_k, const void* h, const void* x0, int act_dtype, int n_tokens, int hidden,
+                               const float* ln_w, const float* ln_b, float alpha, float beta, float eps, void* out,
+                               int* status, void* stream);
 
 /* Owner side: rows in the packed layout above (n_rows of row_pitch bytes, ids
  * are local expert ids in [0, dims->num_experts)); out[r] = sum over the row's

@@ -117,6 +117,10 @@ SIGNATURES = {
     "sb_ep_dispatch": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, sz, vp]),
     "sb_ep_wait": (i32, [vp, i32, i32, i64, i32, i32, vp, vp]),
     "sb_ep_return": (i32, [vp, i32, i32, i32, i64, i32, vp, vp]),
+    "sb_expert_rows_peer": (i32, [C.POINTER(BlockDims), C.POINTER(BlockWeights), vp, vp, i32, i32, i32, i64, i32, vp,
+                                  vp, sz, vp]),
+    "sb_ep_epilogue_peer": (i32, [vp, i32, i32, i64, vp, i32, vp, vp, i32, i32, i32, vp, vp, f32, f32, f32, vp, vp,
+                                  vp]),
 }
 
 

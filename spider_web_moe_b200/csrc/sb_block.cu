@@ -657,9 +657,13 @@ extern "C" SB_API size_t sb_expert_rows_workspace_bytes(const sb_block_dims* dim
          align_up(static_cast<size_t>(n_rows > 0 ? n_rows : 1) * dims->top_k * 4, 256);
 }
 
-extern "C" SB_API int sb_expert_rows(const sb_block_dims* dims, const sb_block_weights* w, const void* rows,
-                                     int64_t row_pitch, int n_rows, int expected_pairs, float* out, void* workspace,
-                                     size_t workspace_bytes, void* stream) {
+// The owner's experts on received rows.  With `peer` (peer transport) the rows
+// are this rank's region's receive rows, the first kernel waits for every
+// rank's dispatch flag and the last writes the results into the sources'
+// regions and raises the return flags (instead of writing `out`).
+static int expert_rows_impl(const sb_block_dims* dims, const sb_block_weights* w, const void* rows, int64_t row_pitch,
+                            int n_rows, int expected_pairs, float* out, void* workspace, size_t workspace_bytes,
+                            cudaStream_t st, const EpPeerArgs* peer) {
   int rc = check_dims(dims);
   if (rc) return rc;
   const sb_block_dims& d = *dims;
@@ -669,13 +673,12 @@ extern "C" SB_API int sb_expert_rows(const sb_block_dims* dims, const sb_block_w
       row_pitch < meta_off + 8LL * d.top_k)
     return SB_ERR_ARG;
   if (n_rows == 0) return SB_OK;
-  if (!rows || !out) return SB_ERR_ARG;
+  if (!rows || (!out && !peer)) return SB_ERR_ARG;
   BlockBuffers b;
   const size_t need = carve_delta(d, n_rows, workspace, workspace_bytes, &b);
   const size_t wbytes = align_up(static_cast<size_t>(n_rows) * d.top_k * 4, 256);
   if (!workspace || need == static_cast<size_t>(-1) || workspace_bytes < need + wbytes) return SB_ERR_WORKSPACE;
   float* top_w = reinterpret_cast<float*>(static_cast<char*>(workspace) + need);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int N = n_rows, H = d.hidden, K = d.top_k, U = d.ffn, G = d.num_experts;
   const int ldx = static_cast<int>(row_pitch / es);
   // Most received rows are padding: tile choices follow the expected real pairs.
@@ -687,8 +690,11 @@ extern "C" SB_API int sb_expert_rows(const sb_block_dims* dims, const sb_block_w
   // dispatch plan over the rows' local expert ids: one kernel reading the row
   // metadata, or (many rows) unpack, then sb_group
   rc = derived_group_launch(0, rows, row_pitch, meta_off, nullptr, G, N, K, G, SB_GROUP_POSITIVE_ONLY, b.ffn_off,
-                            b.ffn_row, b.ffn_slot, b.ffn_w, b.ffn_inv, b.group_ws, b.group_ws_bytes, st);
+                            b.ffn_row, b.ffn_slot, b.ffn_w, b.ffn_inv, b.group_ws, b.group_ws_bytes, st,
+                            peer ? peer->own : nullptr, peer ? peer->ctrl_off : 0, peer ? peer->world : 0,
+                            peer ? peer->status : nullptr);
   if (rc == SB_ERR_UNSUPPORTED) {
+    if (peer) SB_TRY(sb_ep_wait(peer->own, peer->world, peer->cap, row_pitch, H, 0, peer->status, st));
     SB_TRY(launch(unpack_meta_kernel, dim3((N * K + 255) / 256), dim3(256), 0, st, static_cast<const uint8_t*>(rows),
                   row_pitch, meta_off, N, K, G, b.top_idx, top_w));
     SB_TRY(sb_group(b.top_idx, top_w, N, K, G, SB_GROUP_POSITIVE_ONLY, b.ffn_off, b.ffn_row, b.ffn_slot, b.ffn_w,
@@ -726,10 +732,39 @@ extern "C" SB_API int sb_expert_rows(const sb_block_dims* dims, const sb_block_w
     a.out = b.y_ffn; a.ldo = H; a.status = b.status;
     SB_TRY(run_gemm(a, d.engine, st));
   }
-  SB_TRY(sb_combine_rows(b.y_ffn, H, splits, static_cast<int64_t>(N) * K * H, b.ffn_inv, K, N, H, out, nullptr, 0,
-                         nullptr, d.act_dtype, st));
+  if (peer)
+    SB_TRY(combine_rows_peer(b.y_ffn, H, splits, static_cast<int64_t>(N) * K * H, b.ffn_inv, K, N, H, *peer, st));
+  else
+    SB_TRY(sb_combine_rows(b.y_ffn, H, splits, static_cast<int64_t>(N) * K * H, b.ffn_inv, K, N, H, out, nullptr, 0,
+                           nullptr, d.act_dtype, st));
 #undef SB_TRY
   return SB_OK;
+}
+
+extern "C" SB_API int sb_expert_rows(const sb_block_dims* dims, const sb_block_weights* w, const void* rows,
+                                     int64_t row_pitch, int n_rows, int expected_pairs, float* out, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  return expert_rows_impl(dims, w, rows, row_pitch, n_rows, expected_pairs, out, workspace, workspace_bytes,
+                          static_cast<cudaStream_t>(stream), nullptr);
+}
+
+extern "C" SB_API int sb_expert_rows_peer(const sb_block_dims* dims, const sb_block_weights* w, void* region,
+                                          void* const* regions, int world, int rank, int cap, int64_t row_pitch,
+                                          int expected_pairs, int* status, void* workspace, size_t workspace_bytes,
+                                          void* stream) {
+  if (!dims || !region || !regions || world <= 0 || rank < 0 || rank >= world || cap <= 0 ||
+      !sb_ep_peer_region_bytes(world, cap, row_pitch, dims->hidden))
+    return SB_ERR_ARG;
+  EpPeerArgs pa;
+  pa.regions = regions;
+  pa.own = region;
+  pa.world = world;
+  pa.rank = rank;
+  pa.cap = cap;
+  pa.status = status;
+  ep_region_offsets(world, cap, row_pitch, dims->hidden, &pa.ret_off, &pa.ctrl_off);
+  return expert_rows_impl(dims, w, region, row_pitch, world * cap, expected_pairs, nullptr, workspace,
+                          workspace_bytes, static_cast<cudaStream_t>(stream), &pa);
 }
 
 extern "C" SB_API size_t sb_expert_delta_workspace_bytes(const sb_block_dims* dims, int n_tokens) {

@@ -7,6 +7,7 @@
 // epilogue (model.py:317).
 #include "sb_common.cuh"
 #include "sb_internal.h"
+#include "sb_ep_dev.cuh"
 #include "sb_route_dev.cuh"
 
 namespace sb {
@@ -76,12 +77,15 @@ SB_DEVINL void sum_terms(const float* __restrict__ y, const int64_t* terms, int 
   }
 }
 
+// With peer.regions (expert-parallel owner, peer transport) the fp32 row t goes
+// to rank q = t / cap's returned row [peer.me][t % cap] instead of out_f32, and
+// the last CTA raises the return flags.
 template <typename T>
 __global__ void __launch_bounds__(kCombineThreads)
 combine_rows_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t split_stride,
                     const int32_t* __restrict__ inv, int slots, int cols,
                     float* __restrict__ out_f32, const int32_t* __restrict__ scatter_inv,
-                    int scatter_slots, T* __restrict__ scatter_out) {
+                    int scatter_slots, T* __restrict__ scatter_out, const EpPeer peer) {
   __shared__ int64_t s_terms[kMaxTerms];
   __shared__ int s_dst[kMaxSlots];
   __shared__ int s_n;
@@ -96,10 +100,15 @@ combine_rows_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_
     s_dst[threadIdx.x] = scatter_inv[static_cast<int64_t>(t) * scatter_slots + threadIdx.x];
   __syncthreads();
   const int n = s_n;
+  float* orow = out_f32 ? out_f32 + static_cast<int64_t>(t) * cols : nullptr;
+  if (peer.regions) {
+    const int q = t / peer.cap, j = t - q * peer.cap;
+    orow = reinterpret_cast<float*>(peer.regions[q] + peer.ret_off) + (static_cast<int64_t>(peer.me) * peer.cap + j) * cols;
+  }
   for (int c = threadIdx.x * 4; c < cols; c += kCombineThreads * 4) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     sum_terms(y, s_terms, n, c, acc);
-    if (out_f32) *reinterpret_cast<float4*>(out_f32 + static_cast<int64_t>(t) * cols + c) = acc;
+    if (orow) *reinterpret_cast<float4*>(orow + c) = acc;
     if (scatter_inv) {
       for (int k = 0; k < scatter_slots; ++k) {
         const int q = s_dst[k];
@@ -110,6 +119,7 @@ combine_rows_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_
       Vec4<T>::store(scatter_out + static_cast<int64_t>(t) * cols + c, acc);
     }
   }
+  if (peer.regions) ep_signal_peers(peer.regions, peer.regions[peer.me], peer.ctrl_off, peer.world, peer.me, 1);
 }
 
 constexpr int kLnThreads = 256;
@@ -208,17 +218,27 @@ SB_DEVINL void ln_token(const float* __restrict__ y, int64_t ldy, int splits, in
   }
 }
 
+// With wait_region (expert-parallel source, peer transport) every CTA first
+// waits for all ranks' return flags (the rows y points at are being written by
+// them), and the last CTA counts the wait.
 template <typename T>
 __global__ void __launch_bounds__(kLnThreads)
 combine_ln_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t split_stride,
                   const int32_t* __restrict__ inv, int slots, const float* __restrict__ delta_in,
                   const T* __restrict__ h, const T* __restrict__ x0, int cols,
                   const float* __restrict__ ln_w, const float* __restrict__ ln_b, float alpha,
-                  float beta, float eps, T* __restrict__ out, float* __restrict__ delta_out) {
+                  float beta, float eps, T* __restrict__ out, float* __restrict__ delta_out, uint8_t* wait_region,
+                  int64_t ctrl_off, int wait_world, int* wait_status) {
   pdl_wait();
   pdl_trigger();
+  uint32_t target = 0;
+  if (wait_region) {
+    target = ep_wait_target(wait_region, ctrl_off, wait_world, 1);
+    ep_wait_cta(wait_region, ctrl_off, wait_world, 1, target, wait_status);
+  }
   ln_token<T>(y, ldy, splits, split_stride, inv, slots, delta_in, h, x0, cols, ln_w, ln_b, alpha, beta, eps, out,
               delta_out, nullptr);
+  if (wait_region) ep_count_wait_multi(wait_region, ctrl_off, wait_world, 1, target);
 }
 
 // Decode: the loop's LayerNorm epilogue and the next loop's routing of the
@@ -428,11 +448,12 @@ extern "C" SB_API int sb_combine_rows(const float* y, int64_t ldy, int splits, i
   }
   if (act_dtype == SB_F32)
     return launch(combine_rows_kernel<float>, dim3(n_tokens), dim3(kCombineThreads), 0, st, y, ldy, splits,
-                  split_stride, inv, slots, cols, out_f32, scatter_inv, scatter_slots, static_cast<float*>(scatter_out));
+                  split_stride, inv, slots, cols, out_f32, scatter_inv, scatter_slots, static_cast<float*>(scatter_out),
+                  EpPeer{});
   if (act_dtype == SB_BF16)
     return launch(combine_rows_kernel<__nv_bfloat16>, dim3(n_tokens), dim3(kCombineThreads), 0, st, y, ldy, splits,
                   split_stride, inv, slots, cols, out_f32, scatter_inv, scatter_slots,
-                  static_cast<__nv_bfloat16*>(scatter_out));
+                  static_cast<__nv_bfloat16*>(scatter_out), EpPeer{});
   return SB_ERR_ARG;
 }
 
@@ -461,12 +482,14 @@ extern "C" SB_API int sb_combine_ln(const float* y, int64_t ldy, int splits, int
   if (act_dtype == SB_F32)
     return launch(combine_ln_kernel<float>, dim3(n_tokens), dim3(kLnThreads), 0, st, y, ldy, splits, split_stride,
                   inv, slots, delta_in, static_cast<const float*>(h), static_cast<const float*>(x0), cols, ln_w,
-                  ln_b, alpha, beta, eps, static_cast<float*>(out), delta_out);
+                  ln_b, alpha, beta, eps, static_cast<float*>(out), delta_out, static_cast<uint8_t*>(nullptr),
+                  int64_t(0), 0, static_cast<int*>(nullptr));
   if (act_dtype == SB_BF16)
     return launch(combine_ln_kernel<__nv_bfloat16>, dim3(n_tokens), dim3(kLnThreads), 0, st, y, ldy, splits,
                   split_stride, inv, slots, delta_in, static_cast<const __nv_bfloat16*>(h),
                   static_cast<const __nv_bfloat16*>(x0), cols, ln_w, ln_b, alpha, beta, eps,
-                  static_cast<__nv_bfloat16*>(out), delta_out);
+                  static_cast<__nv_bfloat16*>(out), delta_out, static_cast<uint8_t*>(nullptr), int64_t(0), 0,
+                  static_cast<int*>(nullptr));
   return SB_ERR_ARG;
 }
 
@@ -506,3 +529,50 @@ int combine_ln_route(const float* y, int64_t ldy, int splits, int64_t split_stri
                 static_cast<__nv_bfloat16*>(out), r);
 }
 }  // namespace sb
+
+namespace sb {
+int combine_rows_peer(const float* y, int64_t ldy, int splits, int64_t split_stride, const int32_t* inv, int slots,
+                      int n_tokens, int cols, const EpPeerArgs& pa, cudaStream_t st) {
+  if (n_tokens <= 0 || cols % 4 || slots <= 0 || slots > kMaxSlots || splits <= 0 || splits > kMaxSplits ||
+      !pa.regions || n_tokens != pa.world * pa.cap)
+    return SB_ERR_ARG;
+  EpPeer peer;
+  peer.regions = reinterpret_cast<uint8_t* const*>(pa.regions);
+  peer.world = pa.world;
+  peer.me = pa.rank;
+  peer.cap = pa.cap;
+  peer.ret_off = pa.ret_off;
+  peer.ctrl_off = pa.ctrl_off;
+  return launch(combine_rows_kernel<float>, dim3(n_tokens), dim3(kCombineThreads), 0, st, y, ldy, splits, split_stride,
+                inv, slots, cols, static_cast<float*>(nullptr), static_cast<const int32_t*>(nullptr), 0,
+                static_cast<float*>(nullptr), peer);
+}
+}  // namespace sb
+
+extern "C" SB_API int sb_ep_epilogue_peer(void* region, int world, int cap, int64_t row_pitch,
+                                          const int32_t* ret_pos, int top_k, const void* h, const void* x0,
+                                          int act_dtype, int n_tokens, int hidden, const float* ln_w,
+                                          const float* ln_b, float alpha, float beta, float eps, void* out,
+                                          int* status, void* stream) {
+  if (!region || !ret_pos || top_k <= 0 || top_k > kMaxSlots || n_tokens < 0 || hidden <= 0 || hidden % 4 ||
+      hidden > kLnThreads * kLnMaxVec * 4 || !ln_w || !ln_b || (n_tokens > 0 && (!h || !x0 || !out)) ||
+      !sb_ep_peer_region_bytes(world, cap, row_pitch, hidden) || n_tokens > cap)
+    return SB_ERR_ARG;
+  int64_t ret_off, ctrl_off;
+  ep_region_offsets(world, cap, row_pitch, hidden, &ret_off, &ctrl_off);
+  const float* y = reinterpret_cast<const float*>(static_cast<uint8_t*>(region) + ret_off);
+  uint8_t* reg = static_cast<uint8_t*>(region);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n_tokens == 0) return sb_ep_wait(region, world, cap, row_pitch, hidden, 1, status, stream);
+  if (act_dtype == SB_F32)
+    return launch(combine_ln_kernel<float>, dim3(n_tokens), dim3(kLnThreads), 0, st, y, int64_t(hidden), 1,
+                  int64_t(0), ret_pos, top_k, static_cast<const float*>(nullptr), static_cast<const float*>(h),
+                  static_cast<const float*>(x0), hidden, ln_w, ln_b, alpha, beta, eps, static_cast<float*>(out),
+                  static_cast<float*>(nullptr), reg, ctrl_off, world, status);
+  if (act_dtype != SB_BF16) return SB_ERR_ARG;
+  return launch(combine_ln_kernel<__nv_bfloat16>, dim3(n_tokens), dim3(kLnThreads), 0, st, y, int64_t(hidden), 1,
+                int64_t(0), ret_pos, top_k, static_cast<const float*>(nullptr),
+                static_cast<const __nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(x0), hidden, ln_w, ln_b,
+                alpha, beta, eps, static_cast<__nv_bfloat16*>(out), static_cast<float*>(nullptr), reg, ctrl_off,
+                world, status);
+}

@@ -13,54 +13,10 @@
 #include <cstring>
 
 #include "sb_common.cuh"
+#include "sb_ep_dev.cuh"
 #include "sb_internal.h"
 
 namespace sb {
-
-// ------------------------------------------------------------------ peer exchange region
-// One region per rank (cudaMalloc at set-up, mapped by the peers with CUDA
-// IPC):  recv [world][cap][pitch] packed rows the peers send to this rank |
-// ret [world][cap][hidden] fp32 rows the owners return to it | control:
-// uint32 flag[2][world] (kind 0 dispatch, 1 return; raised by the peer q),
-// uint32 seen[2] (this rank's completed waits), uint32 ticket[2] (last-CTA
-// counters of its own dispatch / return kernels).
-struct EpRegion {
-  int64_t ret_off, ctrl_off, bytes;
-};
-__host__ __device__ inline EpRegion ep_region(int world, int cap, int64_t pitch, int hidden) {
-  EpRegion r;
-  const int64_t recv = static_cast<int64_t>(world) * cap * pitch;
-  r.ret_off = (recv + 255) / 256 * 256;
-  const int64_t ret = static_cast<int64_t>(world) * cap * hidden * 4;
-  r.ctrl_off = (r.ret_off + ret + 255) / 256 * 256;
-  r.bytes = r.ctrl_off + (static_cast<int64_t>(2 * world + 4) * 4 + 255) / 256 * 256;
-  return r;
-}
-SB_DEVINL uint32_t* ep_flags(uint8_t* region, int64_t ctrl_off, int world, int kind) {
-  return reinterpret_cast<uint32_t*>(region + ctrl_off) + kind * world;
-}
-SB_DEVINL uint32_t* ep_seen(uint8_t* region, int64_t ctrl_off, int world) {
-  return reinterpret_cast<uint32_t*>(region + ctrl_off) + 2 * world;
-}
-SB_DEVINL uint32_t* ep_ticket(uint8_t* region, int64_t ctrl_off, int world) {
-  return reinterpret_cast<uint32_t*>(region + ctrl_off) + 2 * world + 2;
-}
-// Raise the `kind` flag of rank `me` in every peer's region, once all CTAs of
-// the calling kernel finished their stores (last-CTA ticket in the own region).
-SB_DEVINL void ep_signal_peers(uint8_t* const* regions, uint8_t* own, int64_t ctrl_off, int world, int me, int kind) {
-  __shared__ bool s_last;
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(ep_ticket(own, ctrl_off, world) + kind, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence_system();
-  for (int q = threadIdx.x; q < world; q += blockDim.x) {
-    uint32_t* f = ep_flags(regions[q], ctrl_off, world, kind) + me;
-    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(f), "r"(1u) : "memory");
-  }
-  if (threadIdx.x == 0) ep_ticket(own, ctrl_off, world)[kind] = 0u;  // ready for the next launch
-}
 
 __global__ void __launch_bounds__(256)
 ep_owner_kernel(const int32_t* __restrict__ top_idx, int n, int E, int world, int32_t* __restrict__ owner) {
@@ -150,28 +106,10 @@ __global__ void __launch_bounds__(256)
 ep_wait_kernel(uint8_t* __restrict__ region, int64_t ctrl_off, int world, int kind, int* status) {
   pdl_wait();
   pdl_trigger();
-  const uint32_t target = ep_seen(region, ctrl_off, world)[kind] + 1u;
-  bool ok = true;
-  for (int q = threadIdx.x; q < world; q += blockDim.x) {
-    const uint32_t* f = ep_flags(region, ctrl_off, world, kind) + q;
-    const uint64_t t0 = global_ns();
-    uint32_t spins = 0;
-    while (true) {
-      uint32_t v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-      if (static_cast<int32_t>(v - target) >= 0) break;
-      if (++spins > 16) __nanosleep(128);
-      if ((spins & 255u) == 0 && global_ns() - t0 > kWaitLimitNs) {
-        record_error(status, SB_DEVERR_PEER_WAIT);
-        ok = false;
-        break;
-      }
-    }
-  }
-  __syncthreads();
+  const uint32_t target = ep_wait_target(region, ctrl_off, world, kind);
+  ep_wait_cta(region, ctrl_off, world, kind, target, status);
   if (threadIdx.x == 0) ep_seen(region, ctrl_off, world)[kind] = target;
   __threadfence_system();
-  (void)ok;
 }
 
 struct EpBuffers {
@@ -378,3 +316,11 @@ extern "C" SB_API int sb_ep_return(const float* rows_out, int world, int rank, i
                 reinterpret_cast<const float4*>(rows_out), world, rank, cap, hidden, r.ret_off, r.ctrl_off,
                 reinterpret_cast<uint8_t* const*>(regions));
 }
+
+namespace sb {
+void ep_region_offsets(int world, int cap, int64_t row_pitch, int hidden, int64_t* ret_off, int64_t* ctrl_off) {
+  const EpRegion r = ep_region(world, cap, row_pitch, hidden);
+  *ret_off = r.ret_off;
+  *ctrl_off = r.ctrl_off;
+}
+}  // namespace sb

@@ -8,6 +8,7 @@
 // <= 0 dropped.  The result is deterministic: ranks come from warp match masks
 // and a fixed-order scan, never from atomics.
 #include "sb_common.cuh"
+#include "sb_ep_dev.cuh"
 #include "sb_group_dev.cuh"
 #include "sb_internal.h"
 
@@ -228,11 +229,18 @@ derived_group_kernel(int mode, const uint8_t* __restrict__ rows, int64_t pitch, 
                      const int32_t* __restrict__ top_idx, int num_experts, int n, int K, int G, int flags,
                      int32_t* __restrict__ offsets, int32_t* __restrict__ perm_row, int32_t* __restrict__ perm_slot,
                      float* __restrict__ perm_w, int32_t* __restrict__ inv, int32_t* __restrict__ rank_scratch,
-                     float* __restrict__ w_scratch) {
+                     float* __restrict__ w_scratch, uint8_t* wait_region, int64_t ctrl_off, int wait_world,
+                     int* status) {
   __shared__ int32_t s_ids[kDerivedMax];
   __shared__ float s_w[kDerivedMax];
   pdl_wait();
   pdl_trigger();
+  if (wait_region) {
+    // peer transport: the rows are there once every rank raised its dispatch flag
+    const uint32_t target = ep_wait_target(wait_region, ctrl_off, wait_world, 0);
+    ep_wait_cta(wait_region, ctrl_off, wait_world, 0, target, status);
+    if (threadIdx.x == 0) ep_seen(wait_region, ctrl_off, wait_world)[0] = target;
+  }
   const int total = n * K;
   for (int i = threadIdx.x; i < total; i += blockDim.x) {
     if (mode == 0) {
@@ -255,7 +263,7 @@ derived_group_kernel(int mode, const uint8_t* __restrict__ rows, int64_t pitch, 
 int derived_group_launch(int mode, const void* rows, int64_t pitch, int64_t meta_off, const int32_t* top_idx,
                          int num_experts, int n, int K, int G, int flags, int32_t* offsets, int32_t* perm_row,
                          int32_t* perm_slot, float* perm_w, int32_t* inv, void* workspace, size_t workspace_bytes,
-                         cudaStream_t st) {
+                         cudaStream_t st, void* wait_region, int64_t ctrl_off, int wait_world, int* status) {
   const int64_t total = static_cast<int64_t>(n) * K;
   if (total > kDerivedMax || G > kGroupMaxG || n <= 0) return SB_ERR_UNSUPPORTED;
   if (workspace_bytes < sb_group_workspace_bytes(n, K, G)) return SB_ERR_WORKSPACE;
@@ -267,7 +275,7 @@ int derived_group_launch(int mode, const void* rows, int64_t pitch, int64_t meta
   threads = threads < 64 ? 64 : (threads > kGroupThreads ? kGroupThreads : threads);
   return launch(derived_group_kernel, dim3(1), dim3(threads), 0, st, mode, static_cast<const uint8_t*>(rows), pitch,
                 meta_off, top_idx, num_experts, n, K, G, flags, offsets, perm_row, perm_slot, perm_w, inv, rank_scratch,
-                w_scratch);
+                w_scratch, static_cast<uint8_t*>(wait_region), ctrl_off, wait_world, status);
 }
 
 int group_pair_launch(const GroupJob& j0, const GroupJob& j1, cudaStream_t st) {

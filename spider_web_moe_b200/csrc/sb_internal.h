@@ -98,6 +98,22 @@ int route_edges(const void* h, int act_dtype, int n_tokens, int hidden, const vo
                 int E, int K, const void* gen_w, const float* gen_bias, int M, int32_t* top_idx, float* top_w,
                 int32_t* edge_idx, float* edge_w, cudaStream_t st);
 
+// Peer-transport operands (region layout in sb_ep_dev.cuh): where the owner's
+// combined rows go and which flags the kernels raise or wait for.
+struct EpPeerArgs {
+  void* const* regions;  // device array of the world regions as mapped here (null: not peer mode)
+  void* own;             // this rank's region
+  int world, rank, cap;
+  int64_t ret_off, ctrl_off;
+  int* status;
+};
+// EP region layout (sb_ep.cu): returns ret_off / ctrl_off for the region.
+void ep_region_offsets(int world, int cap, int64_t row_pitch, int hidden, int64_t* ret_off, int64_t* ctrl_off);
+// Row combine whose results go to the sources' regions (row t = q * cap + j
+// to rank q's returned row [rank][j]) and then raise the return flags (sb_combine.cu).
+int combine_rows_peer(const float* y, int64_t ldy, int splits, int64_t split_stride, const int32_t* inv, int slots,
+                      int n_tokens, int cols, const EpPeerArgs& peer, cudaStream_t st);
+
 // Routing operands of one loop (fused route kernels).
 struct RouteArgs {
   const void* router_w;
@@ -121,10 +137,13 @@ int combine_ln_route(const float* y, int64_t ldy, int splits, int64_t split_stri
 // sb_group over ids derived in the grouping kernel itself (sb_group.cu): mode 0
 // ids / weights from packed expert-parallel rows, mode 1 owner = top_idx % G.
 // SB_ERR_UNSUPPORTED above 1024 entries; `workspace` as sb_group's.
+// With wait_region (peer transport, mode 0) the kernel first waits for every
+// rank's dispatch flag in that region.
 int derived_group_launch(int mode, const void* rows, int64_t pitch, int64_t meta_off, const int32_t* top_idx,
                          int num_experts, int n, int K, int G, int flags, int32_t* offsets, int32_t* perm_row,
                          int32_t* perm_slot, float* perm_w, int32_t* inv, void* workspace, size_t workspace_bytes,
-                         cudaStream_t st);
+                         cudaStream_t st, void* wait_region = nullptr, int64_t ctrl_off = 0, int wait_world = 0,
+                         int* status = nullptr);
 
 // Top-K routing of router logits that a grouped GEMM computed (sb_router.cu).
 int router_from_logits(const float* logits, int ld, int splits, int64_t split_stride, int n_tokens, int E, int K,

@@ -250,6 +250,33 @@ class BlockEngine:
         L.check(rc, "sb_ep_dispatch")
         return ret_pos
 
+    def expert_rows_peer(self, xch, expected_pairs: int, status_ptr: int, stream=None):
+        """Owner side of the peer transport (sb_expert_rows_peer): waits for the
+        ranks' rows in this rank's region, runs the local experts on them and
+        writes the results into the sources' regions."""
+        r = xch.world * xch.cap
+        ws = self._delta_ws(self.lib.sb_expert_rows_workspace_bytes(C.byref(self.dims), r))
+        rc = self.lib.sb_expert_rows_peer(C.byref(self.dims), C.byref(self.weights), xch.region, xch.regions.data_ptr(),
+                                          xch.world, xch.rank, xch.cap, xch.pitch, int(expected_pairs), status_ptr,
+                                          ws.data_ptr(), ws.numel(), _stream_ptr(stream))
+        L.check(rc, "sb_expert_rows_peer")
+
+    def ep_epilogue_peer(self, xch, ret_pos: torch.Tensor, h: torch.Tensor, x0: torch.Tensor, stream=None):
+        """Source side of the peer transport (sb_ep_epilogue_peer): waits for the
+        owners' returned rows, then the delta + LayerNorm epilogue."""
+        H = self.cfg.hidden_size
+        n = h.numel() // H
+        h2 = h.reshape(n, H).to(self.act_dtype).contiguous()
+        x2 = x0.reshape(n, H).to(self.act_dtype).contiguous()
+        out = torch.empty((n, H), dtype=self.act_dtype, device=self.device)
+        rc = self.lib.sb_ep_epilogue_peer(xch.region, xch.world, xch.cap, xch.pitch, ret_pos.data_ptr(),
+                                          ret_pos.shape[-1], h2.data_ptr(), x2.data_ptr(), self.dims.act_dtype, n, H,
+                                          self.t["ln_w"].data_ptr(), self.t["ln_b"].data_ptr(), self.dims.residual_scale,
+                                          self.dims.reinject, self.dims.ln_eps, out.data_ptr(), self.status_ptr(),
+                                          _stream_ptr(stream))
+        L.check(rc, "sb_ep_epilogue_peer")
+        return out.view(h.shape)
+
     def status_ptr(self) -> int:
         """Device address of the status word (kernels outside the block record there)."""
         return self.workspace.data_ptr() + self.lib.sb_status_offset()

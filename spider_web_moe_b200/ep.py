@@ -161,22 +161,23 @@ class PeerExchange:
 def ep_loop_peer(dense: BlockEngine, local: BlockEngine | None, xch: PeerExchange, h, x0, loop_idx: int,
                  expected_pairs: int, stream=None):
     """One loop of the token-sharded block over the peer-memory transport:
-    route -> dispatch into the owners' regions -> wait -> local experts on the
-    received rows -> return into the sources' regions -> wait -> epilogue."""
+    route -> dispatch into the owners' regions -> (owner) wait, local experts
+    on the received rows, results into the sources' regions -> (source) wait,
+    epilogue.  The waits run inside the owner's first and the epilogue kernel."""
     lib = xch.lib
     W, cap, pitch, H = xch.world, xch.cap, xch.pitch, xch.hidden
     sp = torch.cuda.current_stream().cuda_stream if stream is None else stream.cuda_stream
     msgs, top_idx, top_w = dense.route(h, loop_idx)
     ret_pos = dense.ep_dispatch(top_idx, top_w, msgs, W, xch.rank, cap, xch.regions)
-    L.check(lib.sb_ep_wait(C.c_void_p(xch.region), W, cap, pitch, H, 0, C.c_void_p(dense.status_ptr()),
-                           C.c_void_p(sp)), "sb_ep_wait")
     if local is not None:
-        local.expert_rows(xch.recv.view(W * cap, pitch), out=xch.out, expected_pairs=expected_pairs)
-    L.check(lib.sb_ep_return(C.c_void_p(xch.out.data_ptr()), W, xch.rank, cap, pitch, H,
-                             C.c_void_p(xch.regions.data_ptr()), C.c_void_p(sp)), "sb_ep_return")
-    L.check(lib.sb_ep_wait(C.c_void_p(xch.region), W, cap, pitch, H, 1, C.c_void_p(dense.status_ptr()),
-                           C.c_void_p(sp)), "sb_ep_wait")
-    return dense.epilogue(xch.ret, ret_pos, h, x0)
+        local.expert_rows_peer(xch, expected_pairs, dense.status_ptr())
+    else:
+        # no local experts: still take part in the exchange (zero rows back)
+        L.check(lib.sb_ep_wait(C.c_void_p(xch.region), W, cap, pitch, H, 0, C.c_void_p(dense.status_ptr()),
+                               C.c_void_p(sp)), "sb_ep_wait")
+        L.check(lib.sb_ep_return(C.c_void_p(xch.out.data_ptr()), W, xch.rank, cap, pitch, H,
+                                 C.c_void_p(xch.regions.data_ptr()), C.c_void_p(sp)), "sb_ep_return")
+    return dense.ep_epilogue_peer(xch, ret_pos, h, x0)
 
 
 class ExpertParallelBlock:
