@@ -395,7 +395,7 @@ def run_b200_ep(args, rank, world, local, device):
                      "frac": achieved / peaks["hbm_gbs"], "peak_kind": f"{peak_kind} (STREAM copy)",
                      "traffic": None, "kernel": "whole expert-parallel step per rank (dense + local expert weights)"},
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, spec, args.cpu_seconds)
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -518,7 +518,7 @@ def run_b200(args):
         "roofline": roofline,
         "stages_ms_per_step": {k: round(v["ms_per_step"], 5) for k, v in stages.items()},
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, spec, args.cpu_seconds)
     if rank == 0:
         print(json.dumps(line), flush=True)
