@@ -252,6 +252,23 @@ SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block_weights* w
                             int loop_end, void* workspace, size_t workspace_bytes,
                             const sb_block_taps* taps, void* stream);
 
+/* ------------------------------------------------------------------ loop statistics
+ * Replaces the return_stats=True tail of SpiderMoELayer.forward
+ * (spider_moe/model.py:327-343) for loop loop_idx: h_in [n, H] is the loop's
+ * input, h_out [n, H] its output (both dims->act_dtype), top_idx [n, K] the
+ * loop's routing (NULL: recomputed here).  Writes router_probs [n, E] fp32,
+ * confidence [n] = sigmoid(h_out . exit_w + exit_b[0]) (exit_w fp32 [H], exit_b
+ * fp32 [1], both device memory; pass
+ * h_out and confidence both NULL to skip it) and
+ * stats [3E + 2] fp32 = expert_load[E] | edge_load[E] | edge_importance[E] |
+ * aux_loss | edge_loss, the edge histograms taken over the top-M destinations
+ * of ALL E sources as the reference does.  Workspace status word at offset 0. */
+SB_API size_t sb_loop_stats_workspace_bytes(const sb_block_dims* dims, int n_tokens);
+SB_API int sb_loop_stats(const sb_block_dims* dims, const sb_block_weights* w, int loop_idx,
+                         const void* h_in, const void* h_out, const int32_t* top_idx, int n_tokens,
+                         const float* exit_w, const float* exit_b, float* router_probs, float* confidence,
+                         float* stats, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------ sparse expert delta
  * Replaces sparse_expert_delta (spider_moe/sparse_experts.py:11-68) for one
  * rank: delta[t] = sum over the token's experts e in [0, E) with e % world ==

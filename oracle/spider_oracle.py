@@ -269,6 +269,28 @@ def block_forward(p: BlockParams, h: torch.Tensor, x0: torch.Tensor, loop_idx: i
                 h_out=out.view(shape))
 
 
+def loop_stats(r: dict, exit_w: torch.Tensor, exit_b: torch.Tensor, num_experts: int) -> dict:
+    """Statistics of SpiderMoELayer.forward(..., return_stats=True)
+    (model.py:327-343) from one block_forward result ``r``: router / edge load
+    histograms over ALL E sources' top-M destinations (model.py:329-330), the
+    importance-weighted edge load, both auxiliary losses and the exit-head
+    confidence of the loop's output."""
+    e = num_experts
+    load = torch.bincount(r["top_idx"].reshape(-1), minlength=e).float()
+    load = load / load.sum().clamp_min(1.0)
+    edge_load = torch.bincount(r["edge_idx"].reshape(-1), minlength=e).float()
+    edge_load = edge_load / edge_load.sum().clamp_min(1.0)
+    importance = r["edge_w"].new_zeros(e).scatter_add(0, r["edge_idx"].reshape(-1), r["edge_w"].reshape(-1))
+    importance = importance / importance.sum().clamp_min(1e-9)
+    probs = r["probs"].reshape(-1, e)
+    aux = e * torch.sum(load * probs.mean(dim=0))
+    edge_aux = e * torch.sum(edge_load * importance)
+    out = r["h_out"].reshape(-1, r["h_out"].shape[-1]).float()
+    confidence = torch.sigmoid(F.linear(out, exit_w.float().view(1, -1), exit_b.float().view(1))).squeeze(-1)
+    return dict(router_probs=probs, expert_load=load, edge_load=edge_load, edge_importance=importance,
+                aux_loss=aux, edge_loss=edge_aux, confidence=confidence)
+
+
 def run_loops(p: BlockParams, h, x0, cfg, activation=None, dense: bool = False):
     """SpiderWebLM._run_recurrent_full (model.py:445-448): L applications."""
     outs = []

@@ -93,6 +93,9 @@ SIGNATURES = {
     "sb_block_workspace_bytes": (sz, [C.POINTER(BlockDims)]),
     "sb_block_forward": (i32, [C.POINTER(BlockDims), C.POINTER(BlockWeights), vp, vp, vp, i32, i32,
                                i32, vp, sz, C.POINTER(BlockTaps), vp]),
+    "sb_loop_stats_workspace_bytes": (sz, [C.POINTER(BlockDims), i32]),
+    "sb_loop_stats": (i32, [C.POINTER(BlockDims), C.POINTER(BlockWeights), i32, vp, vp, vp, i32, vp, vp, vp, vp,
+                            vp, vp, sz, vp]),
     "sb_expert_delta_workspace_bytes": (sz, [C.POINTER(BlockDims), i32]),
     "sb_expert_delta": (i32, [C.POINTER(BlockDims), C.POINTER(BlockWeights), vp, vp, vp, i32, i32,
                               i32, vp, vp, sz, vp]),

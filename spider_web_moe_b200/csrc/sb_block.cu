@@ -871,3 +871,76 @@ extern "C" SB_API const char* sb_stage_name(int stage) {
 extern "C" SB_API unsigned long long sb_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 extern "C" SB_API int sb_num_stages(void) { return kNumStages; }
+
+// ---------------------------------------------------------------------------
+// Loop statistics (model.py:327-343): router probabilities, the routed and
+// edge load histograms over all E sources, both losses, exit confidence.
+// ---------------------------------------------------------------------------
+struct StatsBuffers {
+  int* status;
+  LoopStatsAcc acc;
+  int32_t* top_idx;
+  float* top_w;
+  float* elog;
+};
+
+static size_t carve_stats(const sb_block_dims& d, int n, void* base, size_t size, StatsBuffers* b) {
+  Carver c(base, size);
+  const int64_t N = n, E = d.num_experts, K = d.top_k;
+  b->status = c.take<int>(kStatusBytes / sizeof(int));
+  b->acc.expert_count = c.take<uint32_t>(E);
+  b->acc.edge_count = c.take<uint32_t>(E);
+  b->acc.prob_sum = c.take<float>(kLoopStatsMaxParts * E);
+  b->acc.importance = c.take<float>(kLoopStatsMaxParts * E);
+  b->top_idx = c.take<int32_t>(N * K);
+  b->top_w = c.take<float>(N * K);
+  b->elog = c.take<float>(N * E * E);
+  return c.overflow ? static_cast<size_t>(-1) : align_up(c.used, 256);
+}
+
+extern "C" SB_API size_t sb_loop_stats_workspace_bytes(const sb_block_dims* dims, int n_tokens) {
+  if (check_dims(dims) != SB_OK || n_tokens < 0) return 0;
+  StatsBuffers b;
+  return carve_stats(*dims, n_tokens > 0 ? n_tokens : 1, nullptr, ~size_t(0) >> 1, &b);
+}
+
+extern "C" SB_API int sb_loop_stats(const sb_block_dims* dims, const sb_block_weights* w, int loop_idx,
+                                    const void* h_in, const void* h_out, const int32_t* top_idx, int n_tokens,
+                                    const float* exit_w, const float* exit_b, float* router_probs, float* confidence,
+                                    float* stats, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_dims(dims);
+  if (rc) return rc;
+  const sb_block_dims& d = *dims;
+  if (!w || !w->router_w || !w->loop_bias || !w->gen_w || !w->gen_bias || loop_idx < 0 || loop_idx >= d.num_loops ||
+      n_tokens < 0 || !stats || !workspace || (n_tokens > 0 && (!h_in || !router_probs)) ||
+      ((confidence != nullptr) != (h_out != nullptr)) || (confidence && (!exit_w || !exit_b)))
+    return SB_ERR_ARG;
+  StatsBuffers b;
+  const size_t need = carve_stats(d, n_tokens > 0 ? n_tokens : 1, workspace, workspace_bytes, &b);
+  if (need > workspace_bytes) return SB_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int H = d.hidden, E = d.num_experts, K = d.top_k, M = d.edges_per_expert;
+  // status word and the two [E] counters are contiguous at the front
+  rc = cuda_status(cudaMemsetAsync(b.status, 0,
+                                   reinterpret_cast<char*>(b.acc.prob_sum) - reinterpret_cast<char*>(b.status), st));
+  if (rc) return rc;
+  if (n_tokens > 0) {
+    rc = sb_router(h_in, d.act_dtype, n_tokens, H, w->router_w, w->loop_bias + static_cast<int64_t>(loop_idx) * E, E,
+                   K, b.top_idx, b.top_w, router_probs, st);
+    if (rc) return rc;
+    // edge logits of every (token, source): one dense group of E*E generator rows
+    sb_grouped_gemm_args a;
+    std::memset(&a, 0, sizeof(a));
+    a.engine = d.engine; a.wfmt = d.act_dtype == SB_F32 ? SB_W_F32 : SB_W_BF16; a.act_dtype = d.act_dtype;
+    a.epilogue = SB_EPI_LINEAR;
+    a.num_groups = 1; a.m_rows = E * E; a.k = H; a.a_group_rows = E * E; a.lda = H;
+    a.a_rows_total = static_cast<int64_t>(E) * E; a.a = w->gen_w;
+    a.bias = w->gen_bias + static_cast<int64_t>(loop_idx) * E * E; a.bias_group_stride = E * E;
+    a.x = h_in; a.ldx = H; a.max_rows = n_tokens; a.rows_hint = n_tokens; a.offsets = nullptr;
+    a.out = b.elog; a.ldo = E * E; a.splits = 1; a.status = b.status;
+    rc = run_gemm(a, d.engine, st);
+    if (rc) return rc;
+  }
+  return loop_stats_launch(b.elog, router_probs, top_idx ? top_idx : b.top_idx, h_out, d.act_dtype, exit_w, exit_b,
+                           n_tokens, H, E, K, M, confidence, b.acc, stats, st);
+}

@@ -153,4 +153,20 @@ int router_from_logits(const float* logits, int ld, int splits, int64_t split_st
 int current_sm_count();
 int current_cc_major();
 
+// Accumulators of the loop statistics (sb_stats.cu): integer counts [E],
+// zeroed by the caller, and per-CTA float partials [kLoopStatsMaxParts, E].
+constexpr int kLoopStatsMaxParts = 1024;
+struct LoopStatsAcc {
+  float* prob_sum;
+  uint32_t* expert_count;
+  uint32_t* edge_count;
+  float* importance;
+};
+// Histograms of the full edge logits elog [N, E*E], the router probabilities
+// probs [N, E] and the routing top_idx [N, K]; exit-head confidence of h_out
+// into `confidence` (may be null); then the normalised statistics into stats [3E + 2].
+int loop_stats_launch(const float* elog, const float* probs, const int32_t* top_idx, const void* h_out,
+                      int act_dtype, const float* exit_w, const float* exit_b, int N, int H, int E, int K, int M,
+                      float* confidence, LoopStatsAcc acc, float* stats, cudaStream_t st);
+
 }  // namespace sb

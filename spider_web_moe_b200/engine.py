@@ -332,6 +332,45 @@ class BlockEngine:
         L.check(rc, "sb_expert_delta")
         return delta
 
+    def loop_stats(self, h: torch.Tensor, h_out: torch.Tensor | None, loop_idx: int,
+                   top_idx: torch.Tensor | None = None, exit_w: torch.Tensor | None = None,
+                   exit_b: torch.Tensor | None = None, stream=None) -> dict:
+        """return_stats=True statistics of loop loop_idx (sb_loop_stats,
+        model.py:327-343): h is the loop's input, h_out its output, top_idx
+        [n, K] int32 its routing (None: recomputed).  Returns the reference's
+        keys; confidence is None without exit-head weights."""
+        cfg = self.cfg
+        H, E = cfg.hidden_size, cfg.num_experts
+        n = h.numel() // H
+        act = lambda t: t.reshape(n, H).to(self.act_dtype).contiguous()  # noqa: E731
+        h2 = act(h)
+        conf = None
+        hp = ew = eb = None
+        if exit_w is not None and h_out is not None:
+            ho = act(h_out)
+            ew = exit_w.detach().reshape(H).to(self.device, torch.float32).contiguous()
+            eb = exit_b.detach().reshape(1).to(self.device, torch.float32).contiguous()
+            conf = torch.empty(n, dtype=torch.float32, device=self.device)
+            hp = ho.data_ptr()
+        ti = None
+        if top_idx is not None:
+            ti = top_idx.reshape(n, cfg.top_k).to(self.device, torch.int32).contiguous()
+        probs = torch.empty(n, E, dtype=torch.float32, device=self.device)
+        stats = torch.empty(3 * E + 2, dtype=torch.float32, device=self.device)
+        nbytes = self.lib.sb_loop_stats_workspace_bytes(C.byref(self.dims), n)
+        if nbytes == 0:
+            raise L.SpiderB200Error(L.SB_ERR_ARG, "sb_loop_stats_workspace_bytes")
+        ws = self._delta_ws(nbytes)
+        rc = self.lib.sb_loop_stats(C.byref(self.dims), C.byref(self.weights), int(loop_idx), h2.data_ptr(), hp,
+                                    ti.data_ptr() if ti is not None else None, n,
+                                    ew.data_ptr() if ew is not None else None, eb.data_ptr() if eb is not None else None,
+                                    probs.data_ptr(), conf.data_ptr() if conf is not None else None, stats.data_ptr(),
+                                    ws.data_ptr(), ws.numel(), _stream_ptr(stream))
+        L.check(rc, "sb_loop_stats")
+        return {"router_probs": probs, "expert_load": stats[:E], "edge_load": stats[E:2 * E],
+                "edge_importance": stats[2 * E:3 * E], "aux_loss": stats[3 * E], "edge_loss": stats[3 * E + 1],
+                "confidence": conf}
+
     def _delta_ws(self, nbytes: int) -> torch.Tensor:
         ws = getattr(self, "_dws", None)
         if ws is None or ws.numel() < nbytes:

@@ -131,7 +131,7 @@ class SpiderMoELayer(nn.Module):
             out = self._forward_ep(eng, h, x0, loop_idx, taps)
         if not return_stats:
             return out
-        return out, self._stats(taps, out)
+        return out, self._stats(eng, h, out, loop_idx, taps)
 
     def _forward_ep(self, eng, h, x0, loop_idx, taps):
         """Reference expert-parallel semantics: local experts, SUM all-reduce of delta."""
@@ -151,16 +151,14 @@ class SpiderMoELayer(nn.Module):
         eng = self.engine(h.device, h.dtype, n)
         return eng.forward(h, x0, loop_begin, loop_end)
 
-    def _stats(self, taps, out):
-        """Router / edge load statistics of model.py:327-349 from the loop's taps."""
-        e = self.num_experts
-        ti = taps["top_idx"].long().reshape(-1)
-        load = torch.bincount(ti, minlength=e).float()
-        load = load / load.sum().clamp_min(1.0)
-        ei = taps["edge_idx"].long().reshape(-1)
-        edge_load = torch.bincount(ei, minlength=e).float()
-        edge_load = edge_load / edge_load.sum().clamp_min(1.0)
-        confidence = torch.sigmoid(self.exit_head(out.float() if out.dtype != self.exit_head.weight.dtype
-                                                  else out).float()).squeeze(-1)
-        return {"expert_load": load, "edge_load": edge_load, "confidence": confidence,
-                "top_indices": taps["top_idx"], "top_weights": taps["top_w"]}
+    def _stats(self, eng, h, out, loop_idx, taps):
+        """The stats dict of model.py:327-343 (sb_loop_stats): router
+        probabilities [B, T, E], expert / edge load, both auxiliary losses and
+        the exit-head confidence [B, T] of the loop's output."""
+        st = eng.loop_stats(h, out, loop_idx, top_idx=taps["top_idx"], exit_w=self.exit_head.weight,
+                            exit_b=self.exit_head.bias)
+        lead = h.shape[:-1]
+        return {"router_probs": st["router_probs"].view(*lead, self.num_experts),
+                "expert_load": st["expert_load"], "edge_load": st["edge_load"],
+                "aux_loss": st["aux_loss"], "edge_loss": st["edge_loss"],
+                "confidence": st["confidence"].view(lead)}

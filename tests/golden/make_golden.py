@@ -227,6 +227,37 @@ def cfg1_full_model(synth):
     print("cfg1_model loops", len(records))
 
 
+def stats_case(synth):
+    """SpiderMoELayer.forward(..., return_stats=True) (model.py:324-349) of the
+    reference on seeded parameters: each loop's input, output and stats dict."""
+    from spider_moe.config import ModelConfig
+    import spider_moe.model as model_mod
+
+    kw = dict(num_heads=4, loop_embed_size=32, hidden_size=64, num_experts=8, top_k=2, edges_per_expert=3,
+              num_loops=3, expert_ffn_size=96)
+    cfg = ModelConfig(**dict(dict(vocab_size=512), **kw)).validate()
+    cfg.expert_parallel = False
+    layer = model_mod.SpiderMoELayer(cfg).eval()
+    synth.init_block_params_(layer, seed=7)
+    with torch.no_grad():
+        layer.exit_head.weight.normal_(0.0, 0.3, generator=torch.Generator().manual_seed(8))
+        layer.exit_head.bias.fill_(0.25)
+    h, x0 = synth.block_inputs(24, cfg.hidden_size, seed=9)
+    records = []
+    with torch.no_grad():
+        hh = h
+        for l in range(cfg.num_loops):
+            out, st = layer(hh, x0, l, return_stats=True)
+            records.append(dict(loop_idx=l, h_in=hh.clone(), h_out=out.clone(),
+                                stats={k: v.detach().clone() for k, v in st.items()}))
+            hh = out
+    res = dict(name="e8_stats", cfg=kw, tokens=24, seed=7, zipf=None, bf16=False,
+               exit_head={k: v.detach().clone() for k, v in layer.exit_head.state_dict().items()},
+               x0=x0, records=records)
+    torch.save(res, os.path.join(HERE, "e8_stats.pt"))
+    print("e8_stats loops", len(records))
+
+
 def quant_vectors():
     from spider_moe.quant import quantize_int4, quantize_fp8_with_scale_tensor, dequantize_int4
     g = torch.Generator().manual_seed(5)
@@ -269,6 +300,7 @@ def main():
                edges_per_expert=4, num_loops=2, expert_ffn_size=256), 12, bf16=True, zipf=1.1,
                int4_group=128)
     quant_vectors()
+    stats_case(synth)
 
 
 if __name__ == "__main__":

@@ -133,3 +133,25 @@ def test_quantized_expert_fixtures():
             q = Q.quantize_fp8_per_channel(sd[f"experts.{i}.{j}.weight"])
             assert tensor_digest(q.q.view(torch.uint8)) == fx["fp8_digest"][f"experts.{i}.{j}.q"]
             assert tensor_digest(q.scale) == fx["fp8_digest"][f"experts.{i}.{j}.s"]
+
+
+def test_oracle_stats_match_reference():
+    """return_stats=True (model.py:324-349): the oracle's loop statistics equal
+    what the reference layer returned, loop by loop."""
+    fx = load_golden("e8_stats")
+    cfg = golden_cfg(fx)
+    p = oracle_params(fx, cfg)
+    ew, eb = fx["exit_head"]["weight"], fx["exit_head"]["bias"]
+    h = fx["records"][0]["h_in"]
+    for rec in fx["records"]:
+        r = O.block_forward(p, h, fx["x0"], rec["loop_idx"], cfg)
+        assert rel_err(r["h_out"], rec["h_out"]) < 1e-5
+        st = O.loop_stats(r, ew, eb, cfg.num_experts)
+        want = rec["stats"]
+        assert torch.equal(st["expert_load"], want["expert_load"])
+        assert torch.equal(st["edge_load"], want["edge_load"])
+        assert rel_err(st["router_probs"], want["router_probs"].reshape(-1, cfg.num_experts)) < 1e-6
+        for k in ("aux_loss", "edge_loss"):
+            assert abs(float(st[k]) - float(want[k])) <= 1e-6 * abs(float(want[k])), k
+        assert rel_err(st["confidence"].view(1, -1), want["confidence"].reshape(1, -1)) < 1e-6
+        h = rec["h_out"]
