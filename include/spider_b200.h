@@ -269,6 +269,25 @@ SB_API int sb_loop_stats(const sb_block_dims* dims, const sb_block_weights* w, i
                          const float* exit_w, const float* exit_b, float* router_probs, float* confidence,
                          float* stats, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------ early-exit active set
+ * One step of the early-exit decode loop SpiderWebLM._run_recurrent_decode
+ * (spider_moe/model.py:462-472) with the ActiveSet primitives
+ * (spider_moe/active_set.py: drop, compact_active, scatter_active).  h_new
+ * [n_active, positions, hidden] is loop l's output for the active batch rows
+ * act_idx [n_active] (ascending), x0c [n_active, positions, hidden] their block
+ * inputs.  confidence[r] = sigmoid(h_new[r, 0, :] . exit_w + exit_b[0])
+ * (exit_w fp32 [hidden], exit_b fp32 [1]); row r leaves when confidence >
+ * threshold.  Writes h_full[act_idx[r]] = h_new[r] for every r, and for the
+ * rows that stay, in order: act_next, h_next and x0_next (the next loop's
+ * compact inputs) and *n_next (device int32).  flags: scratch of n_active
+ * int32; confidence [n_active] optional.  h_next / x0_next / h_full must not
+ * overlap h_new / x0c.  Row pointers 16-byte aligned. */
+SB_API int sb_active_set_step(int act_dtype, int n_active, int positions, int hidden, const void* h_new,
+                              const void* x0c, const int32_t* act_idx, const float* exit_w,
+                              const float* exit_b, float threshold, void* h_full, int32_t* act_next,
+                              void* h_next, void* x0_next, int32_t* n_next, int32_t* flags,
+                              float* confidence, void* stream);
+
 /* ------------------------------------------------------------------ sparse expert delta
  * Replaces sparse_expert_delta (spider_moe/sparse_experts.py:11-68) for one
  * rank: delta[t] = sum over the token's experts e in [0, E) with e % world ==

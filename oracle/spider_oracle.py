@@ -291,6 +291,36 @@ def loop_stats(r: dict, exit_w: torch.Tensor, exit_b: torch.Tensor, num_experts:
                 aux_loss=aux, edge_loss=edge_aux, confidence=confidence)
 
 
+def run_recurrent_decode(p: BlockParams, h, x0, cfg, exit_w, exit_b, threshold: float, confidences=None):
+    """SpiderWebLM._run_recurrent_decode with early_exit=True (model.py:450-473)
+    and the ActiveSet primitives (active_set.py: all_active, drop,
+    compact_active, scatter_active): each loop runs the block on the batch rows
+    still active, writes their outputs back, and drops the rows whose
+    exit-head confidence at position 0 exceeds the threshold.
+
+    h, x0: [B, T, H].  Returns (h [B, T, H], the active row lists per loop);
+    ``confidences`` (a list) collects each loop's confidences."""
+    h = h.float().clone()
+    x0 = x0.float()
+    indices = torch.arange(h.shape[0])
+    trace = []
+    for loop_idx in range(cfg.num_loops):
+        if indices.numel() == 0:
+            break
+        trace.append(indices.clone())
+        h_act = h.index_select(0, indices)
+        x0_act = x0.index_select(0, indices)
+        h_new = block_forward(p, h_act, x0_act, loop_idx, cfg)["h_out"]
+        h.index_copy_(0, indices, h_new)
+        conf = torch.sigmoid(F.linear(h_new, exit_w.float().view(1, -1), exit_b.float().view(1))).squeeze(-1)
+        if conf.ndim > 1:
+            conf = conf[:, 0]
+        if confidences is not None:
+            confidences.append(conf)
+        indices = indices[~(conf > threshold)]
+    return h, trace
+
+
 def run_loops(p: BlockParams, h, x0, cfg, activation=None, dense: bool = False):
     """SpiderWebLM._run_recurrent_full (model.py:445-448): L applications."""
     outs = []

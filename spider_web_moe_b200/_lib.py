@@ -96,6 +96,7 @@ SIGNATURES = {
     "sb_loop_stats_workspace_bytes": (sz, [C.POINTER(BlockDims), i32]),
     "sb_loop_stats": (i32, [C.POINTER(BlockDims), C.POINTER(BlockWeights), i32, vp, vp, vp, i32, vp, vp, vp, vp,
                             vp, vp, sz, vp]),
+    "sb_active_set_step": (i32, [i32, i32, i32, i32, vp, vp, vp, vp, vp, f32, vp, vp, vp, vp, vp, vp, vp, vp]),
     "sb_expert_delta_workspace_bytes": (sz, [C.POINTER(BlockDims), i32]),
     "sb_expert_delta": (i32, [C.POINTER(BlockDims), C.POINTER(BlockWeights), vp, vp, vp, i32, i32,
                               i32, vp, vp, sz, vp]),

@@ -34,18 +34,24 @@ loop_stats_kernel(const float* __restrict__ elog, const float* __restrict__ prob
                   const int32_t* __restrict__ top_idx, const T* __restrict__ h_out,
                   const float* __restrict__ exit_w, const float* __restrict__ exit_b, int N, int H, int E, int K, int M,
                   float* __restrict__ confidence, LoopStatsAcc acc) {
-  __shared__ float s_psum[kRouterMaxE], s_imp[kRouterMaxE];
-  __shared__ uint32_t s_cnt[kRouterMaxE], s_ecnt[kRouterMaxE];
+  // per-warp histograms: a warp's M selected destinations are distinct, so its
+  // lanes never update one bin at once and each bin sees a fixed order
+  __shared__ float s_imp[kStatsWarps][kRouterMaxE];
+  __shared__ uint32_t s_ecnt[kStatsWarps][kRouterMaxE];
+  __shared__ float s_psum[kRouterMaxE];
+  __shared__ uint32_t s_cnt[kRouterMaxE];
   pdl_wait();
   pdl_trigger();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int e = lane; e < E; e += 32) {
+    s_imp[warp][e] = 0.f;
+    s_ecnt[warp][e] = 0u;
+  }
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     s_psum[e] = 0.f;
-    s_imp[e] = 0.f;
     s_cnt[e] = 0u;
-    s_ecnt[e] = 0u;
   }
   __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int t = blockIdx.x; t < N; t += gridDim.x) {
     const float* row0 = elog + static_cast<int64_t>(t) * E * E;
     for (int s = warp; s < E; s += kStatsWarps) {
@@ -53,12 +59,13 @@ loop_stats_kernel(const float* __restrict__ elog, const float* __restrict__ prob
       float sel_w;
       topm_select(row0 + static_cast<int64_t>(s) * E, E, M, lane, sel_i, sel_w);
       if (lane < M) {
-        atomicAdd(&s_ecnt[sel_i], 1u);
-        atomicAdd(&s_imp[sel_i], sel_w);
+        s_ecnt[warp][sel_i] += 1u;
+        s_imp[warp][sel_i] += sel_w;
       }
+      __syncwarp();
     }
     if (warp == 0) {
-      for (int e = lane; e < E; e += 32) atomicAdd(&s_psum[e], probs[static_cast<int64_t>(t) * E + e]);
+      for (int e = lane; e < E; e += 32) s_psum[e] += probs[static_cast<int64_t>(t) * E + e];
       if (lane < K) atomicAdd(&s_cnt[top_idx[static_cast<int64_t>(t) * K + lane]], 1u);
     } else if (warp == kStatsWarps - 1 && confidence) {
       const T* hr = h_out + static_cast<int64_t>(t) * H;
@@ -70,10 +77,17 @@ loop_stats_kernel(const float* __restrict__ elog, const float* __restrict__ prob
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    float imp = 0.f;
+    uint32_t ecnt = 0u;
+#pragma unroll
+    for (int w = 0; w < kStatsWarps; ++w) {
+      imp += s_imp[w][e];
+      ecnt += s_ecnt[w][e];
+    }
     acc.prob_sum[static_cast<int64_t>(blockIdx.x) * E + e] = s_psum[e];
-    acc.importance[static_cast<int64_t>(blockIdx.x) * E + e] = s_imp[e];
+    acc.importance[static_cast<int64_t>(blockIdx.x) * E + e] = imp;
     if (s_cnt[e]) atomicAdd(&acc.expert_count[e], s_cnt[e]);
-    if (s_ecnt[e]) atomicAdd(&acc.edge_count[e], s_ecnt[e]);
+    if (ecnt) atomicAdd(&acc.edge_count[e], ecnt);
   }
 }
 

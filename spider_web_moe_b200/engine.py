@@ -332,6 +332,62 @@ class BlockEngine:
         L.check(rc, "sb_expert_delta")
         return delta
 
+    def run_recurrent_decode(self, h: torch.Tensor, x0: torch.Tensor, threshold: float, exit_w: torch.Tensor,
+                             exit_b: torch.Tensor, stream=None, loop_fn=None, trace: list | None = None):
+        """Early-exit decode over all loops (SpiderWebLM._run_recurrent_decode,
+        model.py:450-473): h, x0 [B, T, H].  Each loop runs the block on the
+        compact rows still active, then sb_active_set_step scatters them back,
+        computes the exit confidence and compacts the next loop's inputs on the
+        device; the host reads only the new count (as ActiveSet.n_active does).
+        ``loop_fn(h, x0, loop_idx, out)`` replaces the block call (the module's
+        expert-parallel forward uses it); ``trace`` collects, per loop, host
+        copies of the active batch rows, their inputs, outputs and exit
+        confidences (dict keys rows, h_in, h_new, conf).  Returns (h [B, T, H],
+        loops run)."""
+        H = self.cfg.hidden_size
+        B = h.shape[0]
+        P = h[0].numel() // H if B else 1
+        dt = self.act_dtype
+        h_full = h.detach().to(self.device, dt).contiguous().clone()
+        if B == 0:
+            return h_full.to(h.dtype), 0
+        self._ensure_workspace(B * P)
+        hc = [h_full.clone(), torch.empty_like(h_full)]
+        xc = [x0.detach().to(self.device, dt).contiguous().clone(), torch.empty_like(h_full)]
+        idx = [torch.arange(B, dtype=torch.int32, device=self.device),
+               torch.empty(B, dtype=torch.int32, device=self.device)]
+        h_new = torch.empty(B * P, H, dtype=dt, device=self.device)
+        flags = torch.empty(B, dtype=torch.int32, device=self.device)
+        n_next = torch.zeros(1, dtype=torch.int32, device=self.device)
+        conf = torch.empty(B, dtype=torch.float32, device=self.device) if trace is not None else None
+        ew = exit_w.detach().reshape(H).to(self.device, torch.float32).contiguous()
+        eb = exit_b.detach().reshape(1).to(self.device, torch.float32).contiguous()
+        n, cur, loops = B, 0, 0
+        for l in range(self.cfg.num_loops):
+            if n == 0:
+                break
+            out = h_new[: n * P]
+            if loop_fn is None:
+                self.forward(hc[cur][:n], xc[cur][:n], l, l + 1, out=out, stream=stream)
+            else:
+                loop_fn(hc[cur][:n], xc[cur][:n], l, out)
+            nxt = cur ^ 1
+            rc = self.lib.sb_active_set_step(self.dims.act_dtype, n, P, H, out.data_ptr(), xc[cur].data_ptr(),
+                                             idx[cur].data_ptr(), ew.data_ptr(), eb.data_ptr(), float(threshold),
+                                             h_full.data_ptr(), idx[nxt].data_ptr(), hc[nxt].data_ptr(),
+                                             xc[nxt].data_ptr(), n_next.data_ptr(), flags.data_ptr(),
+                                             conf.data_ptr() if conf is not None else None, _stream_ptr(stream))
+            L.check(rc, "sb_active_set_step")
+            if trace is not None:
+                trace.append(dict(rows=idx[cur][:n].cpu(), h_in=hc[cur][:n].cpu(), h_new=out.view(n, *h.shape[1:]).cpu(),
+                                  conf=conf[:n].cpu()))
+            if stream is not None:
+                stream.synchronize()
+            n = int(n_next.item())
+            cur = nxt
+            loops += 1
+        return h_full.to(h.dtype), loops
+
     def loop_stats(self, h: torch.Tensor, h_out: torch.Tensor | None, loop_idx: int,
                    top_idx: torch.Tensor | None = None, exit_w: torch.Tensor | None = None,
                    exit_b: torch.Tensor | None = None, stream=None) -> dict:

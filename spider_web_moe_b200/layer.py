@@ -151,6 +151,34 @@ class SpiderMoELayer(nn.Module):
         eng = self.engine(h.device, h.dtype, n)
         return eng.forward(h, x0, loop_begin, loop_end)
 
+    def run_recurrent_decode(self, h, x0, early_exit: bool = True, threshold: float | None = None):
+        """SpiderWebLM._run_recurrent_decode (model.py:450-473) on this block:
+        with early_exit, batch rows whose exit confidence passes the threshold
+        (cfg.early_exit_threshold by default) stop looping; the active set is
+        kept and compacted on the device (sb_active_set_step)."""
+        if not early_exit:
+            return self.run_recurrent_full(h, x0)
+        thr = self.cfg.early_exit_threshold if threshold is None else float(threshold)
+        n = h.numel() // h.shape[-1]
+        eng = self.engine(h.device, h.dtype if h.dtype in (torch.float32, torch.bfloat16) else torch.float32, n)
+        loop_fn = None
+        if self.expert_parallel and ep_helpers.ep_enabled():
+            # every rank holds the same rows (replicated tokens), so the active
+            # sets agree and each loop's all-reduce has the same shape everywhere
+            def loop_fn(hc, xc, loop_idx, out):
+                out.copy_(self(hc, xc, loop_idx).reshape(out.shape))
+        out, _ = eng.run_recurrent_decode(h, x0, thr, self.exit_head.weight, self.exit_head.bias, loop_fn=loop_fn)
+        return out.view(h.shape).to(h.dtype)
+
+    def run_recurrent_full(self, h, x0):
+        """SpiderWebLM._run_recurrent_full (model.py:445-448): all loops in one
+        library call, or loop by loop under the reference's expert parallelism."""
+        if self.expert_parallel and ep_helpers.ep_enabled():
+            for loop_idx in range(self.cfg.num_loops):
+                h = self(h, x0, loop_idx)
+            return h
+        return self.run_loops(h, x0).to(h.dtype)
+
     def _stats(self, eng, h, out, loop_idx, taps):
         """The stats dict of model.py:327-343 (sb_loop_stats): router
         probabilities [B, T, E], expert / edge load, both auxiliary losses and

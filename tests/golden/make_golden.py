@@ -258,6 +258,40 @@ def stats_case(synth):
     print("e8_stats loops", len(records))
 
 
+def early_exit_case(synth):
+    """SpiderWebLM._run_recurrent_decode(h, x0, early_exit=True) (model.py:450-473)
+    of the reference on seeded recurrent-block parameters: the returned h and
+    the active batch rows each loop ran on."""
+    from spider_moe.config import ModelConfig
+    import spider_moe.model as model_mod
+
+    kw = dict(num_heads=4, loop_embed_size=32, hidden_size=64, num_experts=8, top_k=2, edges_per_expert=2,
+              num_loops=5, expert_ffn_size=96)
+    cfg = ModelConfig(**dict(dict(vocab_size=512), **kw)).validate()
+    cfg.expert_parallel = False
+    model = model_mod.SpiderWebLM(cfg).eval()
+    layer = model.recurrent
+    # weights of std 0.3 make each loop move h, so rows leave at different loops
+    synth.init_block_params_(layer, seed=11, std=0.3)
+    with torch.no_grad():
+        layer.exit_head.weight.normal_(0.0, 0.05, generator=torch.Generator().manual_seed(12))
+        layer.exit_head.bias.fill_(1.7)
+    h, _ = synth.block_inputs(32, cfg.hidden_size, seed=13)
+    h = h.view(32, 1, cfg.hidden_size)
+    x0 = h.clone()
+    active_rows = []
+    hook = layer.register_forward_pre_hook(lambda mod, args: active_rows.append(args[0].shape[0]))
+    with torch.no_grad():
+        out = model._run_recurrent_decode(h.clone(), x0, True)
+    hook.remove()
+    res = dict(name="e8_early_exit", cfg=kw, seed=11, std=0.3, zipf=None, bf16=False,
+               threshold=float(cfg.early_exit_threshold),
+               exit_head={k: v.detach().clone() for k, v in layer.exit_head.state_dict().items()},
+               h=h, x0=x0, out=out.clone(), active_rows=active_rows)
+    torch.save(res, os.path.join(HERE, "e8_early_exit.pt"))
+    print("e8_early_exit active rows per loop", active_rows)
+
+
 def quant_vectors():
     from spider_moe.quant import quantize_int4, quantize_fp8_with_scale_tensor, dequantize_int4
     g = torch.Generator().manual_seed(5)
@@ -301,6 +335,7 @@ def main():
                int4_group=128)
     quant_vectors()
     stats_case(synth)
+    early_exit_case(synth)
 
 
 if __name__ == "__main__":

@@ -155,3 +155,17 @@ def test_oracle_stats_match_reference():
             assert abs(float(st[k]) - float(want[k])) <= 1e-6 * abs(float(want[k])), k
         assert rel_err(st["confidence"].view(1, -1), want["confidence"].reshape(1, -1)) < 1e-6
         h = rec["h_out"]
+
+
+def test_oracle_early_exit_decode_matches_reference():
+    """_run_recurrent_decode(h, x0, early_exit=True) (model.py:450-473): the
+    oracle's active rows per loop and returned h equal the reference's."""
+    fx = load_golden("e8_early_exit")
+    cfg = golden_cfg(fx)
+    sd = synth.synthetic_state_dict(cfg, seed=fx["seed"], std=fx["std"])
+    p = O.params_from_state_dict(sd, cfg.num_experts)
+    ew, eb = fx["exit_head"]["weight"], fx["exit_head"]["bias"]
+    out, trace = O.run_recurrent_decode(p, fx["h"], fx["x0"], cfg, ew, eb, fx["threshold"])
+    assert [t.numel() for t in trace] == fx["active_rows"]
+    assert len(set(fx["active_rows"])) >= 4  # rows leave at several different loops
+    assert rel_err(out, fx["out"]) < 1e-5
