@@ -288,6 +288,34 @@ SB_API int sb_active_set_step(int act_dtype, int n_active, int positions, int hi
                               void* h_next, void* x0_next, int32_t* n_next, int32_t* flags,
                               float* confidence, void* stream);
 
+/* ------------------------------------------------------------------ Lumen workspace
+ * Replaces LumenWorkspace.forward (spider_moe/lumen.py:81-123), applied by
+ * SpiderMoELayer.forward after its LayerNorm (model.py:318-323) when
+ * cfg.use_lumen: scores = W_q h + slot_bias, w = softmax(scores), values =
+ * W_v h, raw = W_o ((sum_s w_s^2) values), gate = sigmoid(gate . [h ; raw] +
+ * gate_bias), out = LayerNorm(h + gate raw).  wqv stacks write_q.weight [S, H]
+ * over write_v.weight [D, H] (act dtype), qv_bias = slot_bias then D zeros
+ * (fp32), w_o = slot_to_h.weight [H, D] (act dtype), gate_w = gate.weight
+ * [2H] fp32, gate_b [1] fp32, ln_w / ln_b = norm [H] fp32.  Optional outputs
+ * (NULL to skip): slot_weights [n, S], values [n, D], broadcast = gate raw
+ * [n, H] and its L2 norm [n], all fp32.  1 <= S <= 32. */
+typedef struct sb_lumen_weights {
+  const void* wqv;
+  const float* qv_bias;
+  const void* w_o;
+  const float* gate_w;
+  const float* gate_b;
+  const float* ln_w;
+  const float* ln_b;
+  float ln_eps;
+} sb_lumen_weights;
+
+SB_API size_t sb_lumen_workspace_bytes(int n_tokens, int hidden, int slots, int slot_dim);
+SB_API int sb_lumen_forward(int act_dtype, int engine, int n_tokens, int hidden, int slots, int slot_dim,
+                            const sb_lumen_weights* w, const void* h, void* out, float* slot_weights,
+                            float* values, float* broadcast, float* broadcast_norm, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------ sparse expert delta
  * Replaces sparse_expert_delta (spider_moe/sparse_experts.py:11-68) for one
  * rank: delta[t] = sum over the token's experts e in [0, E) with e % world ==

@@ -58,6 +58,7 @@ class BlockParams:
     ln_b: torch.Tensor          # [H]               norm.bias
     w_gate: torch.Tensor | None = None  # [E, U, H]  SwiGLU gate (B200 extra mode)
     b_gate: torch.Tensor | None = None  # [E, U]
+    lumen: dict | None = None           # lumen.* parameters (model.py:202-210) when use_lumen
 
     @property
     def num_experts(self):
@@ -83,6 +84,7 @@ def params_from_state_dict(sd: dict, num_experts: int) -> BlockParams:
         ln_b=f(sd["norm.bias"]),
         w_gate=torch.stack([f(sd[f"expert_gates.{i}.weight"]) for i in range(e)]) if gates else None,
         b_gate=torch.stack([f(sd[f"expert_gates.{i}.bias"]) for i in range(e)]) if gates else None,
+        lumen={k[len("lumen."):]: f(v) for k, v in sd.items() if k.startswith("lumen.")} or None,
     )
 
 
@@ -243,6 +245,28 @@ def block_epilogue(h, delta, x0, ln_w, ln_b, residual_scale=0.5, reinject=0.1, e
     return F.layer_norm(u, (u.shape[-1],), ln_w, ln_b, eps)
 
 
+def lumen_forward(h: torch.Tensor, lp: dict, eps: float = 1e-5, j_lens: bool = False):
+    """LumenWorkspace.forward (spider_moe/lumen.py:81-123) in fp32, dropout off.
+
+    lp holds the module's parameters by their names under ``lumen.``
+    (slot_bias, write_q.weight, write_v.weight, slot_to_h.weight, gate.weight,
+    gate.bias, norm.weight, norm.bias, optional j_lens.weight).  Returns
+    (out, state dict with slots, slot_weights, broadcast, j_logits)."""
+    h = h.float()
+    w = (F.linear(h, lp["write_q.weight"]) + lp["slot_bias"]).softmax(dim=-1)   # competition over slots
+    values = F.linear(h, lp["write_v.weight"])
+    slots = torch.einsum("...s,...d->...sd", w, values)                        # every token writes every slot
+    mixed = torch.einsum("...s,...sd->...d", w, slots)                         # read back with the same weights
+    raw = F.linear(mixed, lp["slot_to_h.weight"])
+    gate = torch.sigmoid(F.linear(torch.cat([h, raw], dim=-1), lp["gate.weight"], lp["gate.bias"]))
+    broadcast = gate * raw
+    out = F.layer_norm(h + broadcast, (h.shape[-1],), lp["norm.weight"], lp["norm.bias"], eps)
+    j_logits = None
+    if j_lens and "j_lens.weight" in lp:
+        j_logits = F.linear(slots.mean(dim=-2), lp["j_lens.weight"])
+    return out, dict(slots=slots, slot_weights=w, broadcast=broadcast, j_logits=j_logits)
+
+
 def block_forward(p: BlockParams, h: torch.Tensor, x0: torch.Tensor, loop_idx: int, cfg,
                   activation: str | None = None, local_experts=None, dense: bool = False) -> dict:
     """One SpiderMoELayer.forward (model.py:240-317) on fp32 CPU tensors.
@@ -264,9 +288,12 @@ def block_forward(p: BlockParams, h: torch.Tensor, x0: torch.Tensor, loop_idx: i
     delta = expert_delta(msgs, top_idx, top_w, p.w_up, p.b_up, p.w_down, p.b_down, e,
                          local_experts, act, p.w_gate, p.b_gate)
     out = block_epilogue(hid, delta, x0f, p.ln_w, p.ln_b, cfg.residual_scale, cfg.re_inject_weight)
+    lumen = None
+    if p.lumen is not None:  # model.py:318-323
+        out, lumen = lumen_forward(out, p.lumen)
     return dict(top_idx=top_idx, top_w=top_w, probs=probs, edge_idx=edge_idx, edge_w=edge_w,
                 edge_logits=edge_logits, coef=coef, messages=msgs, delta=delta,
-                h_out=out.view(shape))
+                h_out=out.view(shape), lumen=lumen)
 
 
 def loop_stats(r: dict, exit_w: torch.Tensor, exit_b: torch.Tensor, num_experts: int) -> dict:
@@ -287,8 +314,12 @@ def loop_stats(r: dict, exit_w: torch.Tensor, exit_b: torch.Tensor, num_experts:
     edge_aux = e * torch.sum(edge_load * importance)
     out = r["h_out"].reshape(-1, r["h_out"].shape[-1]).float()
     confidence = torch.sigmoid(F.linear(out, exit_w.float().view(1, -1), exit_b.float().view(1))).squeeze(-1)
-    return dict(router_probs=probs, expert_load=load, edge_load=edge_load, edge_importance=importance,
-                aux_loss=aux, edge_loss=edge_aux, confidence=confidence)
+    st = dict(router_probs=probs, expert_load=load, edge_load=edge_load, edge_importance=importance,
+              aux_loss=aux, edge_loss=edge_aux, confidence=confidence)
+    if r.get("lumen") is not None:  # model.py:346-348
+        st["lumen_slot_weights"] = r["lumen"]["slot_weights"]
+        st["lumen_broadcast_norm"] = r["lumen"]["broadcast"].norm(dim=-1)
+    return st
 
 
 def run_recurrent_decode(p: BlockParams, h, x0, cfg, exit_w, exit_b, threshold: float, confidences=None):

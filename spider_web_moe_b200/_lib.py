@@ -68,6 +68,13 @@ class BlockWeights(C.Structure):
     ]
 
 
+class LumenWeights(C.Structure):
+    _fields_ = [
+        ("wqv", vp), ("qv_bias", vp), ("w_o", vp), ("gate_w", vp), ("gate_b", vp), ("ln_w", vp), ("ln_b", vp),
+        ("ln_eps", C.c_float),
+    ]
+
+
 class BlockTaps(C.Structure):
     _fields_ = [
         ("top_idx", vp), ("top_w", vp), ("edge_idx", vp), ("edge_w", vp), ("messages", vp),
@@ -97,6 +104,9 @@ SIGNATURES = {
     "sb_loop_stats": (i32, [C.POINTER(BlockDims), C.POINTER(BlockWeights), i32, vp, vp, vp, i32, vp, vp, vp, vp,
                             vp, vp, sz, vp]),
     "sb_active_set_step": (i32, [i32, i32, i32, i32, vp, vp, vp, vp, vp, f32, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "sb_lumen_workspace_bytes": (sz, [i32, i32, i32, i32]),
+    "sb_lumen_forward": (i32, [i32, i32, i32, i32, i32, i32, C.POINTER(LumenWeights), vp, vp, vp, vp, vp, vp, vp,
+                               sz, vp]),
     "sb_expert_delta_workspace_bytes": (sz, [C.POINTER(BlockDims), i32]),
     "sb_expert_delta": (i32, [C.POINTER(BlockDims), C.POINTER(BlockWeights), vp, vp, vp, i32, i32,
                               i32, vp, vp, sz, vp]),

@@ -36,6 +36,8 @@ def build_spider_b200(model_config, device="cuda", model=None, engine="auto", **
         layer = SpiderMoELayer(model_config)
         layer.load_state_dict(rec.state_dict(), strict=False)
         layer.engine_name = engine
+        if getattr(rec, "lumen", None) is not None and layer.lumen is not None:
+            layer.lumen.j_lens = rec.lumen.j_lens  # the model's J-lens head (model.py:365-371)
         model.recurrent = layer.to(device)
         _attach_recurrent_drivers(model)
         return model.to(device).eval()

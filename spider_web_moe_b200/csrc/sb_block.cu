@@ -944,3 +944,76 @@ extern "C" SB_API int sb_loop_stats(const sb_block_dims* dims, const sb_block_we
   return loop_stats_launch(b.elog, router_probs, top_idx ? top_idx : b.top_idx, h_out, d.act_dtype, exit_w, exit_b,
                            n_tokens, H, E, K, M, confidence, b.acc, stats, st);
 }
+
+// ---------------------------------------------------------------------------
+// Lumen workspace (lumen.py:81-123): two one-group GEMMs and two warp-per-token
+// kernels (sb_lumen.cu).
+// ---------------------------------------------------------------------------
+struct LumenBuffers {
+  int* status;
+  float* qv;
+  void* values;
+  float* c;
+  float* raw;
+};
+
+static size_t carve_lumen(int n, int H, int S, int D, void* base, size_t size, LumenBuffers* b) {
+  Carver c(base, size);
+  b->status = c.take<int>(kStatusBytes / sizeof(int));
+  b->qv = c.take<float>(static_cast<int64_t>(n) * (S + D));
+  b->values = c.take<char>(static_cast<int64_t>(n) * D * 4);
+  b->c = c.take<float>(n);
+  b->raw = c.take<float>(static_cast<int64_t>(n) * H);
+  return c.overflow ? static_cast<size_t>(-1) : align_up(c.used, 256);
+}
+
+extern "C" SB_API size_t sb_lumen_workspace_bytes(int n_tokens, int hidden, int slots, int slot_dim) {
+  if (n_tokens < 0 || hidden <= 0 || slots <= 0 || slot_dim <= 0) return 0;
+  LumenBuffers b;
+  return carve_lumen(n_tokens > 0 ? n_tokens : 1, hidden, slots, slot_dim, nullptr, ~size_t(0) >> 1, &b);
+}
+
+extern "C" SB_API int sb_lumen_forward(int act_dtype, int engine, int n_tokens, int hidden, int slots, int slot_dim,
+                                       const sb_lumen_weights* w, const void* h, void* out, float* slot_weights,
+                                       float* values, float* broadcast, float* broadcast_norm, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  if ((act_dtype != SB_F32 && act_dtype != SB_BF16) || n_tokens < 0 || hidden <= 0 || hidden % 8 || slots <= 0 ||
+      slots > 32 || slot_dim <= 0 || !w || !w->wqv || !w->qv_bias || !w->w_o || !w->gate_w || !w->gate_b ||
+      !w->ln_w || !w->ln_b || !workspace || engine < SB_ENGINE_AUTO || engine > SB_ENGINE_TCGEN05)
+    return SB_ERR_ARG;
+  if (n_tokens == 0) return SB_OK;
+  if (!h || !out) return SB_ERR_ARG;
+  LumenBuffers b;
+  const size_t need = carve_lumen(n_tokens, hidden, slots, slot_dim, workspace, workspace_bytes, &b);
+  if (need == static_cast<size_t>(-1) || workspace_bytes < need) return SB_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int H = hidden, S = slots, D = slot_dim;
+  const int wfmt = act_dtype == SB_F32 ? SB_W_F32 : SB_W_BF16;
+  int rc = cuda_status(cudaMemsetAsync(b.status, 0, kStatusBytes, st));
+  if (rc) return rc;
+  {  // scores and values
+    sb_grouped_gemm_args a;
+    std::memset(&a, 0, sizeof(a));
+    a.engine = engine; a.wfmt = wfmt; a.act_dtype = act_dtype; a.epilogue = SB_EPI_LINEAR;
+    a.num_groups = 1; a.m_rows = S + D; a.k = H; a.a_group_rows = S + D; a.lda = H; a.a_rows_total = S + D;
+    a.a = w->wqv; a.bias = w->qv_bias; a.bias_group_stride = S + D;
+    a.x = h; a.ldx = H; a.max_rows = n_tokens; a.rows_hint = n_tokens; a.offsets = nullptr;
+    a.out = b.qv; a.ldo = S + D; a.splits = 1; a.status = b.status;
+    rc = run_gemm(a, engine, st);
+    if (rc) return rc;
+  }
+  rc = lumen_mix_launch(b.qv, n_tokens, S, D, act_dtype, b.values, b.c, slot_weights, values, st);
+  if (rc) return rc;
+  {  // raw = c * (W_o values)
+    sb_grouped_gemm_args a;
+    std::memset(&a, 0, sizeof(a));
+    a.engine = engine; a.wfmt = wfmt; a.act_dtype = act_dtype; a.epilogue = SB_EPI_LINEAR;
+    a.num_groups = 1; a.m_rows = H; a.k = D; a.a_group_rows = H; a.lda = D; a.a_rows_total = H;
+    a.a = w->w_o; a.x = b.values; a.ldx = D; a.max_rows = n_tokens; a.rows_hint = n_tokens; a.offsets = nullptr;
+    a.row_scale = b.c; a.out = b.raw; a.ldo = H; a.splits = 1; a.status = b.status;
+    rc = run_gemm(a, engine, st);
+    if (rc) return rc;
+  }
+  return lumen_gate_ln_launch(h, b.raw, n_tokens, H, act_dtype, w->gate_w, w->gate_b, w->ln_w, w->ln_b, w->ln_eps, out,
+                              broadcast, broadcast_norm, st);
+}

@@ -169,4 +169,12 @@ int loop_stats_launch(const float* elog, const float* probs, const int32_t* top_
                       int act_dtype, const float* exit_w, const float* exit_b, int N, int H, int E, int K, int M,
                       float* confidence, LoopStatsAcc acc, float* stats, cudaStream_t st);
 
+// Lumen kernels (sb_lumen.cu): softmax / slot mix after GEMM 1, gate +
+// LayerNorm after GEMM 2.
+int lumen_mix_launch(const float* qv, int n, int S, int D, int act_dtype, void* values, float* c, float* slot_w,
+                     float* values_f32, cudaStream_t st);
+int lumen_gate_ln_launch(const void* h, const float* raw, int n, int H, int act_dtype, const float* gate_w,
+                         const float* gate_b, const float* ln_w, const float* ln_b, float eps, void* out,
+                         float* broadcast, float* bnorm, cudaStream_t st);
+
 }  // namespace sb

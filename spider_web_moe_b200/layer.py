@@ -21,6 +21,7 @@ from torch import nn
 from . import expert_parallel as ep_helpers
 from .config import from_any
 from .engine import BlockEngine
+from .lumen import LumenWorkspace
 from .quant import Int4Tensor, quantize_fp8_per_channel, quantize_int4
 
 
@@ -46,6 +47,11 @@ class SpiderMoELayer(nn.Module):
         ])
         self.norm = nn.LayerNorm(h)
         self.exit_head = nn.Linear(h, 1)
+        # Lumen global workspace after the LayerNorm (model.py:202-210)
+        self.lumen: LumenWorkspace | None = None
+        if bool(getattr(cfg, "use_lumen", False)):
+            self.lumen = LumenWorkspace(h, num_slots=int(getattr(cfg, "lumen_slots", 8)),
+                                        slot_dim=(int(getattr(cfg, "lumen_slot_dim", 0)) or None), vocab_size=None)
         if cfg.expert_activation == "swiglu":
             self.expert_gates = nn.ModuleList([nn.Linear(h, cfg.expert_ffn_size) for _ in range(e)])
         self.residual_scale = cfg.residual_scale
@@ -123,15 +129,26 @@ class SpiderMoELayer(nn.Module):
         eng = self.engine(h.device, h.dtype if h.dtype in (torch.float32, torch.bfloat16) else torch.float32, n)
         use_ep = self.expert_parallel and ep_helpers.ep_enabled()
         if not use_ep and not return_stats:
-            return eng.forward(h, x0, loop_idx, loop_idx + 1).to(h.dtype)
+            out = eng.forward(h, x0, loop_idx, loop_idx + 1).to(h.dtype)
+            return self.lumen(out) if self.lumen is not None else out
         taps = eng.make_taps(n)
         if not use_ep:
             out = eng.forward(h, x0, loop_idx, loop_idx + 1, taps=taps).to(h.dtype)
         else:
             out = self._forward_ep(eng, h, x0, loop_idx, taps)
+        lumen_state = None
+        if self.lumen is not None:
+            if return_stats:
+                out, lumen_state = self.lumen(out, return_state=True)
+            else:
+                out = self.lumen(out)
         if not return_stats:
             return out
-        return out, self._stats(eng, h, out, loop_idx, taps)
+        stats = self._stats(eng, h, out, loop_idx, taps)
+        if lumen_state is not None:  # model.py:346-348
+            stats["lumen_slot_weights"] = lumen_state.slot_weights
+            stats["lumen_broadcast_norm"] = lumen_state.broadcast.float().norm(dim=-1).to(lumen_state.broadcast.dtype)
+        return out, stats
 
     def _forward_ep(self, eng, h, x0, loop_idx, taps):
         """Reference expert-parallel semantics: local experts, SUM all-reduce of delta."""
@@ -149,7 +166,12 @@ class SpiderMoELayer(nn.Module):
         """All loops [loop_begin, loop_end) in one library call (model.py:445-448)."""
         n = h.numel() // h.shape[-1]
         eng = self.engine(h.device, h.dtype, n)
-        return eng.forward(h, x0, loop_begin, loop_end)
+        if self.lumen is None:
+            return eng.forward(h, x0, loop_begin, loop_end)
+        loop_end = self.cfg.num_loops if loop_end is None else loop_end
+        for loop_idx in range(loop_begin, loop_end):  # Lumen after every loop's LayerNorm
+            h = self.lumen(eng.forward(h, x0, loop_idx, loop_idx + 1))
+        return h
 
     def run_recurrent_decode(self, h, x0, early_exit: bool = True, threshold: float | None = None):
         """SpiderWebLM._run_recurrent_decode (model.py:450-473) on this block:
@@ -162,6 +184,9 @@ class SpiderMoELayer(nn.Module):
         n = h.numel() // h.shape[-1]
         eng = self.engine(h.device, h.dtype if h.dtype in (torch.float32, torch.bfloat16) else torch.float32, n)
         loop_fn = None
+        if self.lumen is not None:
+            def loop_fn(hc, xc, loop_idx, out):
+                out.copy_(self.lumen(eng.forward(hc, xc, loop_idx, loop_idx + 1)).reshape(out.shape))
         if self.expert_parallel and ep_helpers.ep_enabled():
             # every rank holds the same rows (replicated tokens), so the active
             # sets agree and each loop's all-reduce has the same shape everywhere

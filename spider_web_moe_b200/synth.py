@@ -5,7 +5,8 @@ measurement and parity case uses seeded synthetic data:
 
 * every weight and bias ~ N(0, 0.02) drawn from one ``torch.Generator`` in
   ``named_parameters()`` order (the order of spider_moe/model.py:165-216, which
-  this package's module reproduces), LayerNorm weight 1 and bias 0;
+  this package's module reproduces), LayerNorm weights 1 and biases 0 (the
+  block's and Lumen's);
 * ``loop_bias`` zero, or a Zipf(s) bias per expert (the reference has no Zipf
   option; its own ``loop_bias[num_loops, E]`` parameter, added to the router
   logits at spider_moe/model.py:255, is the hook);
@@ -16,6 +17,11 @@ from __future__ import annotations
 import math
 
 import torch
+
+
+def _is_layer_norm(name: str) -> bool:
+    """The block's LayerNorm and Lumen's (weight 1, bias 0)."""
+    return name.startswith("norm.") or name.startswith("lumen.norm.")
 
 
 def block_param_shapes(cfg) -> list:
@@ -30,6 +36,12 @@ def block_param_shapes(cfg) -> list:
         out += [(f"experts.{i}.0.weight", (u, h)), (f"experts.{i}.0.bias", (u,)),
                 (f"experts.{i}.2.weight", (h, u)), (f"experts.{i}.2.bias", (h,))]
     out += [("norm.weight", (h,)), ("norm.bias", (h,)), ("exit_head.weight", (1, h)), ("exit_head.bias", (1,))]
+    if getattr(cfg, "use_lumen", False):  # LumenWorkspace (lumen.py:62-79): own parameter first
+        s = int(getattr(cfg, "lumen_slots", 8))
+        d = int(getattr(cfg, "lumen_slot_dim", 0) or max(32, h // 4))
+        out += [("lumen.slot_bias", (s,)), ("lumen.write_q.weight", (s, h)), ("lumen.write_v.weight", (d, h)),
+                ("lumen.slot_to_h.weight", (h, d)), ("lumen.gate.weight", (1, 2 * h)), ("lumen.gate.bias", (1,)),
+                ("lumen.norm.weight", (h,)), ("lumen.norm.bias", (h,))]
     if getattr(cfg, "expert_activation", "gelu") == "swiglu":
         for i in range(e):
             out += [(f"expert_gates.{i}.weight", (u, h)), (f"expert_gates.{i}.bias", (u,))]
@@ -47,7 +59,7 @@ def synthetic_state_dict(cfg, seed: int = 0, device="cpu", std: float = 0.02, zi
     g = torch.Generator(device=dev).manual_seed(int(seed))
     sd = {}
     for name, shape in block_param_shapes(cfg):
-        if name.startswith("norm."):
+        if _is_layer_norm(name):
             t = torch.full(shape, 1.0 if name.endswith("weight") else 0.0, device=dev)
         elif name == "loop_bias":
             t = torch.zeros(shape, device=dev)
@@ -67,7 +79,7 @@ def init_block_params_(module: torch.nn.Module, seed: int = 0, std: float = 0.02
     g = torch.Generator(device="cpu").manual_seed(int(seed))
     with torch.no_grad():
         for name, p in module.named_parameters():
-            if name.startswith("norm."):
+            if _is_layer_norm(name):
                 p.fill_(1.0 if name.endswith("weight") else 0.0)
                 continue
             if name == "loop_bias":

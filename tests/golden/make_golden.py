@@ -292,6 +292,45 @@ def early_exit_case(synth):
     print("e8_early_exit active rows per loop", active_rows)
 
 
+def lumen_case(synth):
+    """The reference's LumenWorkspace on its own (return_state, J-lens) and a
+    SpiderMoELayer with use_lumen over two loops with return_stats
+    (lumen.py:81-123, model.py:318-348)."""
+    from spider_moe.config import ModelConfig
+    from spider_moe.lumen import LumenWorkspace
+    import spider_moe.model as model_mod
+
+    torch.manual_seed(3)
+    ws = LumenWorkspace(hidden_size=64, num_slots=4, slot_dim=16, vocab_size=50).eval()
+    with torch.no_grad():
+        ws.slot_bias.normal_(0.0, 0.5)
+    h = torch.randn(2, 5, 64, generator=torch.Generator().manual_seed(4))
+    with torch.no_grad():
+        out, st = ws(h, return_state=True, j_lens=True)
+    module = dict(state_dict={k: v.clone() for k, v in ws.state_dict().items()}, h=h, out=out,
+                  slots=st.slots, slot_weights=st.slot_weights, broadcast=st.broadcast, j_logits=st.j_logits,
+                  j_space=ws.read_j_space(st, top_k=3))
+    kw = dict(num_heads=4, loop_embed_size=32, hidden_size=64, num_experts=4, top_k=2, edges_per_expert=2,
+              num_loops=2, expert_ffn_size=96, use_lumen=True, lumen_slots=4)
+    cfg = ModelConfig(**dict(dict(vocab_size=512), **kw)).validate()
+    cfg.expert_parallel = False
+    layer = model_mod.SpiderMoELayer(cfg).eval()
+    synth.init_block_params_(layer, seed=5, std=0.1)
+    hb, x0 = synth.block_inputs(24, 64, seed=6)
+    records = []
+    with torch.no_grad():
+        hh = hb
+        for l in range(cfg.num_loops):
+            o, stats = layer(hh, x0, l, return_stats=True)
+            records.append(dict(loop_idx=l, h_in=hh.clone(), h_out=o.clone(),
+                                stats={k: v.detach().clone() for k, v in stats.items()}))
+            hh = o
+    res = dict(name="lumen", module=module, cfg=kw, seed=5, std=0.1, zipf=None, bf16=False, x0=x0,
+               records=records)
+    torch.save(res, os.path.join(HERE, "lumen.pt"))
+    print("lumen loops", len(records), "stats keys", sorted(records[0]["stats"]))
+
+
 def quant_vectors():
     from spider_moe.quant import quantize_int4, quantize_fp8_with_scale_tensor, dequantize_int4
     g = torch.Generator().manual_seed(5)
@@ -336,6 +375,7 @@ def main():
     quant_vectors()
     stats_case(synth)
     early_exit_case(synth)
+    lumen_case(synth)
 
 
 if __name__ == "__main__":

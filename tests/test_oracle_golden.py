@@ -169,3 +169,25 @@ def test_oracle_early_exit_decode_matches_reference():
     assert [t.numel() for t in trace] == fx["active_rows"]
     assert len(set(fx["active_rows"])) >= 4  # rows leave at several different loops
     assert rel_err(out, fx["out"]) < 1e-5
+
+
+def test_oracle_lumen_matches_reference():
+    """LumenWorkspace.forward (lumen.py:81-123) on its own and inside the layer
+    with return_stats (model.py:318-348): the oracle reproduces the reference."""
+    fx = load_golden("lumen")
+    m = fx["module"]
+    out, st = O.lumen_forward(m["h"], m["state_dict"], j_lens=True)
+    assert rel_err(out, m["out"]) < 1e-5
+    for k in ("slots", "slot_weights", "broadcast", "j_logits"):
+        assert rel_err(st[k], m[k]) < 1e-5, k
+    cfg = golden_cfg(fx)
+    sd = synth.synthetic_state_dict(cfg, seed=fx["seed"], std=fx["std"])
+    p = O.params_from_state_dict(sd, cfg.num_experts)
+    for rec in fx["records"]:
+        r = O.block_forward(p, rec["h_in"], fx["x0"], rec["loop_idx"], cfg)
+        assert rel_err(r["h_out"], rec["h_out"]) < 1e-5
+        want = rec["stats"]
+        got = O.loop_stats(r, sd["exit_head.weight"], sd["exit_head.bias"], cfg.num_experts)
+        assert rel_err(got["lumen_slot_weights"], want["lumen_slot_weights"].reshape(-1, 4)) < 1e-5
+        assert rel_err(got["lumen_broadcast_norm"].view(1, -1), want["lumen_broadcast_norm"].reshape(1, -1)) < 1e-5
+        assert torch.equal(got["expert_load"], want["expert_load"])
