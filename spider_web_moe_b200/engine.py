@@ -133,6 +133,17 @@ class BlockEngine:
         self.workspace = None
         self._ensure_workspace(int(max_tokens))
 
+    @classmethod
+    def from_spiderw(cls, path, device, act_dtype=torch.bfloat16, max_tokens: int = 64, **kwargs) -> "BlockEngine":
+        """Engine for the block of a .spiderw bundle: sections go to the device
+        once and are packed there (spiderw.block_state_dict)."""
+        from .spiderw import block_state_dict, load_spiderw, model_config
+
+        bundle = load_spiderw(path)
+        cfg = model_config(bundle.meta)
+        return cls(cfg, block_state_dict(bundle, device), device, act_dtype=act_dtype, max_tokens=max_tokens,
+                   **kwargs)
+
     # ------------------------------------------------------------------ workspace
     def _ensure_workspace(self, n_tokens: int):
         if self.workspace is not None and n_tokens <= self.dims.max_tokens:

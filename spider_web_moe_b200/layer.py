@@ -65,6 +65,17 @@ class SpiderMoELayer(nn.Module):
         self._engine: BlockEngine | None = None
         self._engine_key = None
 
+    @classmethod
+    def from_spiderw(cls, path, device="cuda", **cfg_overrides) -> "SpiderMoELayer":
+        """The block stored in a .spiderw bundle (docs/NATIVE_WEIGHT_FORMAT.md of
+        the reference); the format keeps no biases, so they load as zeros."""
+        from .spiderw import block_state_dict, load_spiderw, model_config
+
+        bundle = load_spiderw(path)
+        layer = cls(model_config(bundle.meta, **cfg_overrides)).to(device)
+        layer.load_state_dict(block_state_dict(bundle, device), strict=False)
+        return layer.eval()
+
     # ------------------------------------------------------------------ weight formats
     @torch.no_grad()
     def quantize_experts(self, group_size: int = 64) -> None:

@@ -331,6 +331,48 @@ def lumen_case(synth):
     print("lumen loops", len(records), "stats keys", sorted(records[0]["stats"]))
 
 
+def spiderw_case(synth, ref_root):
+    """.spiderw bundles (docs/NATIVE_WEIGHT_FORMAT.md): a block exported by the
+    reference's own exporter (scripts/export_native_weights.py) from seeded
+    parameters, what the reference's loader (spider_infer/orbit/weight_loader.py)
+    reads back from it, and a bundle of mixed section kinds written by the
+    reference's writer."""
+    import importlib.util
+    import numpy as np
+    from spider_moe.config import ModelConfig
+    from spider_infer.orbit.weight_loader import SpiderWMeta, load_spiderw, write_spiderw
+
+    spec = importlib.util.spec_from_file_location(
+        "export_native_weights", os.path.join(ref_root, "scripts", "export_native_weights.py"))
+    exporter = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(exporter)
+    kw = dict(vocab_size=64, num_heads=4, loop_embed_size=32, hidden_size=32, num_experts=4, top_k=2,
+              edges_per_expert=2, num_loops=2, expert_ffn_size=64)
+    cfg = ModelConfig(**kw).validate()
+    sd = synth.synthetic_state_dict(cfg, seed=21, std=0.1)
+    state = {"recurrent." + k: v for k, v in sd.items()}
+    state["token_embedding.weight"] = torch.randn(64, 32, generator=torch.Generator().manual_seed(22))
+    block_path = os.path.join(HERE, "e4_block.spiderw")
+    exporter.export_from_state_dict(state, cfg, block_path)
+    ref = load_spiderw(block_path)
+    mixed = {"router": np.arange(12, dtype=np.float32).reshape(3, 4), "loop_bias": np.ones((2, 3), np.float16),
+             "csr_row_ptr": np.array([0, 2, 4], np.int32), "prelude.0.W_qkv": np.full((2, 5), 0.5, np.float32),
+             "extra_f64": np.linspace(0, 1, 7)}
+    meta = SpiderWMeta(version=1, flags=2, vocab_size=10, hidden_size=4, num_heads=2, num_experts=3, top_k=2,
+                       edges_per_expert=1, num_loops=2, expert_ffn_size=8, num_prelude_layers=1,
+                       num_coda_layers=0)
+    mixed_path = os.path.join(HERE, "mixed_sections.spiderw")
+    write_spiderw(mixed_path, meta, mixed)
+    ref_mixed = load_spiderw(mixed_path)
+    res = dict(cfg=kw, seed=21, std=0.1, block_meta=vars(ref.meta), block_sections={k: torch.from_numpy(v.copy())
+                                                                                     for k, v in ref.tensors.items()},
+               mixed_meta=vars(meta), mixed_in={k: torch.from_numpy(np.asarray(v).copy()) for k, v in mixed.items()},
+               mixed_sections={k: torch.from_numpy(v.copy()) for k, v in ref_mixed.tensors.items()},
+               mixed_csr=sorted(ref_mixed.csr) if ref_mixed.csr else None)
+    torch.save(res, os.path.join(HERE, "spiderw.pt"))
+    print("spiderw sections", sorted(ref.tensors), "mixed", sorted(ref_mixed.tensors))
+
+
 def quant_vectors():
     from spider_moe.quant import quantize_int4, quantize_fp8_with_scale_tensor, dequantize_int4
     g = torch.Generator().manual_seed(5)
@@ -376,6 +418,7 @@ def main():
     stats_case(synth)
     early_exit_case(synth)
     lumen_case(synth)
+    spiderw_case(synth, ref_root)
 
 
 if __name__ == "__main__":
