@@ -316,6 +316,21 @@ SB_API int sb_lumen_forward(int act_dtype, int engine, int n_tokens, int hidden,
                             float* values, float* broadcast, float* broadcast_norm, void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------ Dobu expert offload
+ * Helpers of the offload store (spider_moe/expert_store.py:120-166), whose
+ * experts live in host memory with a few resident in device slots.
+ * sb_active_experts: active[e] = 1 when some token's summed routing weight for
+ * e is positive (the experts the reference materialises), else 0.
+ * sb_remap_routes: routing rewritten onto device slots: idx_out = slot_of[e],
+ * w_out = w where slot_of[e] >= 0, else slot 0 with weight 0 (dropped by the
+ * positive-only grouping), so sb_expert_delta over the slots computes the
+ * experts of one wave. */
+SB_API int sb_active_experts(const int32_t* top_idx, const float* top_w, int n_tokens, int top_k,
+                             int num_experts, int32_t* active, void* stream);
+SB_API int sb_remap_routes(const int32_t* top_idx, const float* top_w, int n_tokens, int top_k,
+                           const int32_t* slot_of, int num_experts, int32_t* idx_out, float* w_out,
+                           void* stream);
+
 /* ------------------------------------------------------------------ sparse expert delta
  * Replaces sparse_expert_delta (spider_moe/sparse_experts.py:11-68) for one
  * rank: delta[t] = sum over the token's experts e in [0, E) with e % world ==

@@ -107,6 +107,8 @@ SIGNATURES = {
     "sb_lumen_workspace_bytes": (sz, [i32, i32, i32, i32]),
     "sb_lumen_forward": (i32, [i32, i32, i32, i32, i32, i32, C.POINTER(LumenWeights), vp, vp, vp, vp, vp, vp, vp,
                                sz, vp]),
+    "sb_active_experts": (i32, [vp, vp, i32, i32, i32, vp, vp]),
+    "sb_remap_routes": (i32, [vp, vp, i32, i32, vp, i32, vp, vp, vp]),
     "sb_expert_delta_workspace_bytes": (sz, [C.POINTER(BlockDims), i32]),
     "sb_expert_delta": (i32, [C.POINTER(BlockDims), C.POINTER(BlockWeights), vp, vp, vp, i32, i32,
                               i32, vp, vp, sz, vp]),

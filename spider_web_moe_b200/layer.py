@@ -21,6 +21,7 @@ from torch import nn
 from . import expert_parallel as ep_helpers
 from .config import from_any
 from .engine import BlockEngine
+from .dobu import ExpertChunkStore
 from .lumen import LumenWorkspace
 from .quant import Int4Tensor, quantize_fp8_per_channel, quantize_int4
 
@@ -57,6 +58,10 @@ class SpiderMoELayer(nn.Module):
         self.residual_scale = cfg.residual_scale
         self.reinject_weight = cfg.re_inject_weight
         self.expert_parallel = bool(getattr(cfg, "expert_parallel", True))
+        # Dobu offload (model.py:185-199): experts stay in host memory, a few
+        # in device slots; the store is built at the first forward
+        self.offload_experts = bool(getattr(cfg, "offload_experts", False))
+        self._expert_store: ExpertChunkStore | None = None
         self.engine_name = "auto"
         self._int4_w_up: Int4Tensor | None = None
         self._int4_w_down: Int4Tensor | None = None
@@ -125,7 +130,11 @@ class SpiderMoELayer(nn.Module):
                 int4 = {"up": self._int4_w_up, "down": self._int4_w_down}
                 if self._int4_w_gate is not None:
                     int4["gate"] = self._int4_w_gate
-            self._engine = BlockEngine(self.cfg, self.state_dict(), device, act_dtype=act_dtype,
+            state = self.state_dict()
+            if self.offload_experts:  # dense parts only: the experts come from the store
+                state = {k: v for k, v in state.items() if not k.startswith(("experts.", "expert_gates."))}
+                int4 = None
+            self._engine = BlockEngine(self.cfg, state, device, act_dtype=act_dtype,
                                        max_tokens=max(n_tokens, 1), engine=self.engine_name,
                                        int4=int4, fp8=self._fp8)
             self._engine_key = key
@@ -139,13 +148,16 @@ class SpiderMoELayer(nn.Module):
         n = h.numel() // h.shape[-1]
         eng = self.engine(h.device, h.dtype if h.dtype in (torch.float32, torch.bfloat16) else torch.float32, n)
         use_ep = self.expert_parallel and ep_helpers.ep_enabled()
-        if not use_ep and not return_stats:
+        if self.offload_experts:
+            out, taps = self._forward_offload(eng, h, x0, loop_idx)
+        elif not use_ep and not return_stats:
             out = eng.forward(h, x0, loop_idx, loop_idx + 1).to(h.dtype)
             return self.lumen(out) if self.lumen is not None else out
-        taps = eng.make_taps(n)
-        if not use_ep:
+        elif not use_ep:
+            taps = eng.make_taps(n)
             out = eng.forward(h, x0, loop_idx, loop_idx + 1, taps=taps).to(h.dtype)
         else:
+            taps = eng.make_taps(n)
             out = self._forward_ep(eng, h, x0, loop_idx, taps)
         lumen_state = None
         if self.lumen is not None:
@@ -160,6 +172,25 @@ class SpiderMoELayer(nn.Module):
             stats["lumen_slot_weights"] = lumen_state.slot_weights
             stats["lumen_broadcast_norm"] = lumen_state.broadcast.float().norm(dim=-1).to(lumen_state.broadcast.dtype)
         return out, stats
+
+    def expert_store(self, device) -> ExpertChunkStore:
+        if self._expert_store is None:
+            self._expert_store = ExpertChunkStore(self.experts, storage_device="cpu", compute_device=device,
+                                                  max_gpu_experts=self.top_dobu)
+        return self._expert_store
+
+    def _forward_offload(self, eng, h, x0, loop_idx):
+        """The block with offloaded experts (model.py:294-297): routing and
+        messages on the device (sb_block_route), the delta from the Dobu store,
+        the LayerNorm epilogue (sb_combine_ln).  Returns (out, routing taps)."""
+        if self.expert_parallel and ep_helpers.ep_enabled():
+            raise NotImplementedError("expert offload with reference expert parallelism")
+        n, H = h.numel() // h.shape[-1], h.shape[-1]
+        msgs, top_idx, top_w = eng.route(h, loop_idx)
+        delta = self.expert_store(h.device).sparse_delta_f32(msgs, top_idx, top_w, self.top_k)
+        inv = torch.arange(n, dtype=torch.int32, device=h.device).view(n, 1)
+        out = eng.epilogue(delta, inv, h, x0).to(h.dtype)
+        return out, {"top_idx": top_idx, "top_w": top_w}
 
     def _forward_ep(self, eng, h, x0, loop_idx, taps):
         """Reference expert-parallel semantics: local experts, SUM all-reduce of delta."""
@@ -177,6 +208,10 @@ class SpiderMoELayer(nn.Module):
         """All loops [loop_begin, loop_end) in one library call (model.py:445-448)."""
         n = h.numel() // h.shape[-1]
         eng = self.engine(h.device, h.dtype, n)
+        if self.offload_experts:  # the store's residency decisions run per loop on the host
+            for loop_idx in range(loop_begin, self.cfg.num_loops if loop_end is None else loop_end):
+                h = self(h, x0, loop_idx)
+            return h
         if self.lumen is None:
             return eng.forward(h, x0, loop_begin, loop_end)
         loop_end = self.cfg.num_loops if loop_end is None else loop_end
@@ -198,9 +233,10 @@ class SpiderMoELayer(nn.Module):
         if self.lumen is not None:
             def loop_fn(hc, xc, loop_idx, out):
                 out.copy_(self.lumen(eng.forward(hc, xc, loop_idx, loop_idx + 1)).reshape(out.shape))
-        if self.expert_parallel and ep_helpers.ep_enabled():
-            # every rank holds the same rows (replicated tokens), so the active
-            # sets agree and each loop's all-reduce has the same shape everywhere
+        if (self.expert_parallel and ep_helpers.ep_enabled()) or self.offload_experts:
+            # the module's own loop (Lumen included); under expert parallelism
+            # every rank holds the same rows, so the active sets agree and each
+            # loop's all-reduce has the same shape everywhere
             def loop_fn(hc, xc, loop_idx, out):
                 out.copy_(self(hc, xc, loop_idx).reshape(out.shape))
         out, _ = eng.run_recurrent_decode(h, x0, thr, self.exit_head.weight, self.exit_head.bias, loop_fn=loop_fn)

@@ -373,6 +373,58 @@ def spiderw_case(synth, ref_root):
     print("spiderw sections", sorted(ref.tensors), "mixed", sorted(ref_mixed.tensors))
 
 
+def dobu_case(synth):
+    """The reference's Dobu store (expert_store.py:40-205): a sequence of
+    sparse_delta calls with its LRU statistics after each, and a layer with
+    offload_experts over two loops (model.py:185-199, 294-297)."""
+    from torch import nn
+    from spider_moe.config import ModelConfig
+    from spider_moe.expert_store import ExpertChunkStore
+    import spider_moe.model as model_mod
+
+    torch.manual_seed(7)
+    experts = nn.ModuleList([nn.Sequential(nn.Linear(16, 32), nn.GELU(), nn.Linear(32, 16)) for _ in range(6)])
+    store = ExpertChunkStore(experts, storage_device="cpu", compute_device="cpu", max_gpu_experts=2)
+    g = torch.Generator().manual_seed(8)
+    routes = [[[0, 1], [1, 2], [0, 2], [1, 0], [2, 1]],       # experts 0,1,2: misses, 2 evicts 0
+              [[3, 4], [4, 3], [3, 3], [4, 5], [3, 4]],       # 3,4,5
+              [[5, 4], [5, 5], [4, 5], [4, 4], [5, 4]],       # hits on 4,5
+              [[0, 5], [1, 5], [0, 1], [5, 0], [1, 1]]]       # 0,1 misses, 5 hit
+    calls = []
+    for r in routes:
+        msgs = torch.randn(1, 5, 16, generator=g)
+        idx = torch.tensor([r])
+        w = torch.rand(1, 5, 2, generator=g)
+        w[0, 2, 1] = -0.5                                        # a non-positive slot weight
+        d = store.sparse_delta(msgs, idx, w, top_k=2)
+        st = store.stats()
+        calls.append(dict(msgs=msgs, idx=idx, w=w, delta=d, hits=st["hits"], misses=st["misses"],
+                          loads=st["loads"], hot=st["gpu_hot_experts"], storage_bytes=st["storage_bytes"],
+                          gpu_bytes=st["gpu_working_set_bytes"]))
+    kw = dict(num_heads=4, loop_embed_size=32, hidden_size=64, num_experts=8, top_k=2, edges_per_expert=2,
+              num_loops=2, expert_ffn_size=96, offload_experts=True, offload_max_gpu_experts=3)
+    cfg = ModelConfig(**dict(dict(vocab_size=512), **kw)).validate()
+    cfg.expert_parallel = False
+    layer = model_mod.SpiderMoELayer(cfg).eval()
+    synth.init_block_params_(layer, seed=9, std=0.1)
+    # the store copied the experts at construction: rebuild it from the seeded weights
+    layer._expert_store = ExpertChunkStore(layer.experts, storage_device="cpu", compute_device="cpu",
+                                           max_gpu_experts=3)
+    h, x0 = synth.block_inputs(16, 64, seed=10)
+    outs = []
+    with torch.no_grad():
+        hh = h
+        for l in range(cfg.num_loops):
+            hh = layer(hh, x0, l)
+            outs.append(hh.clone())
+    st = layer._expert_store.stats()
+    res = dict(name="dobu", experts={k: v.clone() for k, v in experts.state_dict().items()}, calls=calls,
+               cfg=kw, seed=9, std=0.1, zipf=None, bf16=False, h=h, x0=x0, outs=outs,
+               layer_stats={k: st[k] for k in ("hits", "misses", "loads", "gpu_hot_experts")})
+    torch.save(res, os.path.join(HERE, "dobu.pt"))
+    print("dobu calls", [(c["hits"], c["misses"], c["loads"], c["hot"]) for c in calls], res["layer_stats"])
+
+
 def quant_vectors():
     from spider_moe.quant import quantize_int4, quantize_fp8_with_scale_tensor, dequantize_int4
     g = torch.Generator().manual_seed(5)
@@ -419,6 +471,7 @@ def main():
     early_exit_case(synth)
     lumen_case(synth)
     spiderw_case(synth, ref_root)
+    dobu_case(synth)
 
 
 if __name__ == "__main__":
