@@ -414,7 +414,7 @@ def run_b200(args):
     if world > 1 and not args.profile_only:
         return run_b200_ep(args, rank, world, local, device)
     from spider_web_moe_b200 import synth
-    from spider_web_moe_b200.engine import CapturedBlock
+    from spider_web_moe_b200.engine import CapturedBlock, HostPipeline
 
     cfg, spec = workload(args)
     n = spec["tokens"]
@@ -456,27 +456,23 @@ def run_b200(args):
     value = n * world / (ms_step / 1e3)
     gpu_launches = g.kernels_per_replay * args.steps  # libspider_b200 kernels counted at capture
 
-    # e2e: host (pinned) input -> device, all loops, device -> host output, every step
-    h_host = h.cpu().pin_memory()
-    out_host = torch.empty(n, cfg.hidden_size, dtype=torch.bfloat16).pin_memory()
-    for _ in range(3):
-        g.h.copy_(h_host, non_blocking=True)
-        g.x0.copy_(h_host, non_blocking=True)
-        g.graph.replay()
-        out_host.copy_(g.out, non_blocking=True)
+    # e2e through the public API (HostPipeline): every step copies its input in
+    # from pinned host memory and its output back; step s + 1's input and step
+    # s - 1's output move while step s runs.  x0 = h, the block input.
+    pipe = HostPipeline(eng, n, x0_is_h=True)
+    h_hosts = [h.cpu().pin_memory() for _ in range(2)]
+    out_hosts = [torch.empty(n, cfg.hidden_size, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    pipe.run([h_hosts[s & 1] for s in range(3)], [out_hosts[s & 1] for s in range(3)])
     torch.cuda.synchronize(device)
     barrier(world)
     start.record(stream)
-    for _ in range(args.steps):
-        g.h.copy_(h_host, non_blocking=True)
-        g.x0.copy_(h_host, non_blocking=True)
-        g.graph.replay()
-        out_host.copy_(g.out, non_blocking=True)
+    pipe.run([h_hosts[s & 1] for s in range(args.steps)], [out_hosts[s & 1] for s in range(args.steps)])
     end.record(stream)
     torch.cuda.synchronize(device)
     barrier(world)
     e2e_ms = max_over_ranks(start.elapsed_time(end), world, device) / args.steps
-    h2d = 2 * n * cfg.hidden_size * 2
+    assert torch.equal(out_hosts[(args.steps - 1) & 1], g.out.cpu()), "e2e output differs from the device run"
+    h2d = n * cfg.hidden_size * 2
     d2h = n * cfg.hidden_size * 2
 
     # per-stage timing pass (eager, events around every launch) for the roofline

@@ -449,13 +449,16 @@ class BlockEngine:
 class CapturedBlock:
     """All loops of a block for a fixed token count, captured in one CUDA graph."""
 
-    def __init__(self, engine: BlockEngine, n_tokens: int, loop_begin: int = 0, loop_end: int | None = None):
+    def __init__(self, engine: BlockEngine, n_tokens: int, loop_begin: int = 0, loop_end: int | None = None,
+                 x0_is_h: bool = False):
+        """x0_is_h: the block input is also x0 (the whole recurrent stack from
+        its input), so one buffer serves both and a step copies one tensor in."""
         self.engine = engine
         H = engine.cfg.hidden_size
         dev, dt = engine.device, engine.act_dtype
         engine._ensure_workspace(n_tokens)
         self.h = torch.zeros(n_tokens, H, dtype=dt, device=dev)
-        self.x0 = torch.zeros(n_tokens, H, dtype=dt, device=dev)
+        self.x0 = self.h if x0_is_h else torch.zeros(n_tokens, H, dtype=dt, device=dev)
         self.out = torch.zeros(n_tokens, H, dtype=dt, device=dev)
         s = torch.cuda.Stream(device=dev)
         s.wait_stream(torch.cuda.current_stream(dev))
@@ -473,7 +476,56 @@ class CapturedBlock:
     def __call__(self, h=None, x0=None):
         if h is not None:
             self.h.copy_(h.reshape(self.h.shape))
-        if x0 is not None:
+        if x0 is not None and self.x0 is not self.h:
             self.x0.copy_(x0.reshape(self.x0.shape))
         self.graph.replay()
         return self.out
+
+
+class HostPipeline:
+    """Block steps from and to pinned host memory with the copies off the
+    critical path: two captured graphs on two buffer sets, the input of step
+    s + 1 copied in (one stream) and the output of step s - 1 copied out
+    (another stream) while step s runs, events ordering each buffer's reuse.
+    Every step still moves its own input in and its output out."""
+
+    def __init__(self, engine: BlockEngine, n_tokens: int, loop_begin: int = 0, loop_end: int | None = None,
+                 x0_is_h: bool = False):
+        dev = engine.device
+        self.x0_is_h = x0_is_h
+        self.blocks = [CapturedBlock(engine, n_tokens, loop_begin, loop_end, x0_is_h=x0_is_h) for _ in range(2)]
+        self.kernels_per_replay = self.blocks[0].kernels_per_replay
+        self.h2d = torch.cuda.Stream(device=dev)
+        self.d2h = torch.cuda.Stream(device=dev)
+        ev = lambda: [torch.cuda.Event(), torch.cuda.Event()]  # noqa: E731
+        self.ev_in, self.ev_done, self.ev_out = ev(), ev(), ev()
+        self.device = dev
+
+    def run(self, h_hosts, out_hosts, x0_hosts=None) -> None:
+        """Steps s = 0.. : out_hosts[s] <- block(h_hosts[s], x0_hosts[s]) (x0 = h
+        when the pipeline was built with x0_is_h).  Host tensors should be
+        pinned; returns once every step is enqueued (synchronise to read)."""
+        compute = torch.cuda.current_stream(self.device)
+        self.h2d.wait_stream(compute)
+        self.d2h.wait_stream(compute)
+        for s, h_host in enumerate(h_hosts):
+            b = s & 1
+            blk = self.blocks[b]
+            with torch.cuda.stream(self.h2d):
+                if s >= 2:
+                    self.h2d.wait_event(self.ev_done[b])  # step s - 2 no longer reads this input
+                blk.h.copy_(h_host.reshape(blk.h.shape), non_blocking=True)
+                if not self.x0_is_h:
+                    blk.x0.copy_(x0_hosts[s].reshape(blk.x0.shape), non_blocking=True)
+                self.ev_in[b].record(self.h2d)
+            compute.wait_event(self.ev_in[b])
+            if s >= 2:
+                compute.wait_event(self.ev_out[b])  # step s - 2's output has left this buffer
+            blk.graph.replay()
+            self.ev_done[b].record(compute)
+            with torch.cuda.stream(self.d2h):
+                self.d2h.wait_event(self.ev_done[b])
+                out_hosts[s].copy_(blk.out.reshape(out_hosts[s].shape), non_blocking=True)
+                self.ev_out[b].record(self.d2h)
+        compute.wait_stream(self.h2d)
+        compute.wait_stream(self.d2h)
