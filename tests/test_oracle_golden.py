@@ -2,7 +2,7 @@
 
 tests/golden/*.pt hold what the reference's own SpiderMoELayer computed
 (captured by tests/golden/make_golden.py); the oracle must reproduce them
-before it may judge the CUDA path.
+before it may check the CUDA path.
 """
 import pytest
 import torch
