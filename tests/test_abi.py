@@ -88,3 +88,37 @@ def test_product_path_refuses_cpu_tensors():
         forge_ep.ForgeEP().run_dispatched_ffn(h, torch.zeros(1, 4, 2, dtype=torch.long), torch.ones(1, 4, 2),
                                               w_up=torch.zeros(4, 8, 64), b_up=torch.zeros(4, 8),
                                               w_down=torch.zeros(4, 64, 8), b_down=torch.zeros(4, 64), num_experts=4)
+
+
+def test_header_is_plain_c():
+    """The header compiles as C99 on its own: a cgo / C caller can include it."""
+    import shutil
+    import subprocess
+
+    if shutil.which("gcc") is None:
+        pytest.skip("no gcc")
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-fsyntax-only", "-x", "c", HEADER],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+
+
+def test_new_entry_points_validate_without_device():
+    lib = L.load()
+    d = L.BlockDims(hidden=64, num_experts=8, top_k=2, edges_per_expert=2, ffn=64, num_loops=2,
+                    act_dtype=L.SB_F32, wfmt=L.SB_W_F32, max_tokens=16)
+    wts = L.BlockWeights()
+    assert lib.sb_loop_stats_workspace_bytes(C.byref(d), 16) > 0
+    assert lib.sb_loop_stats(C.byref(d), C.byref(wts), 0, None, None, None, 4, None, None, None, None, None, None,
+                             0, None) == L.SB_ERR_ARG
+    # confidence without h_out is rejected
+    assert lib.sb_active_set_step(L.SB_F32, 4, 1, 63, None, None, None, None, None, 0.5, None, None, None, None,
+                                  None, None, None, None) == L.SB_ERR_ARG
+    assert lib.sb_active_set_step(L.SB_F32, 4, 1, 64, None, None, None, None, None, 0.5, None, None, None, None,
+                                  None, None, None, None) == L.SB_ERR_ARG
+    assert lib.sb_lumen_workspace_bytes(16, 64, 4, 16) > 0
+    assert lib.sb_lumen_workspace_bytes(16, 64, 0, 16) == 0
+    lw = L.LumenWeights()
+    assert lib.sb_lumen_forward(L.SB_F32, 0, 4, 64, 33, 16, C.byref(lw), None, None, None, None, None, None, None,
+                                0, None) == L.SB_ERR_ARG   # more than 32 slots
+    assert lib.sb_active_experts(None, None, 4, 2, 8, None, None) == L.SB_ERR_ARG
+    assert lib.sb_remap_routes(None, None, 4, 2, None, 8, None, None, None) == L.SB_ERR_ARG
