@@ -790,9 +790,13 @@ struct PairCfg {
   static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
   static constexpr int kAccCols = BN * (kGate ? 2 : 1);
   static constexpr int kTmemCols = 2 * kAccCols;
-  static constexpr int kEpiWarps = 8;
+  // epilogue warps: 0-3 and 6-9, and for bf16 weights also 10-17 (four per
+  // TMEM lane quarter, each a quarter of the tile's columns: the GELU
+  // epilogue of short-K tiles would otherwise outlast the next tile's MMAs);
+  // with fp8 / int4 weights warps 10-13 convert instead
+  static constexpr int kEpiWarps = kConvert ? 8 : 16;
   static constexpr int kConvWarps = 4;
-  static constexpr int kThreads = kConvert ? 448 : 320;
+  static constexpr int kThreads = kConvert ? 448 : 576;
   // B stages first: every operand read stays inside the allocation
   static constexpr int kOffB = 0;
   static constexpr int kOffA = kOffB + kStages * kBBytes;
@@ -969,9 +973,9 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       }
     }
     __syncwarp();
-  } else if (warp >= 10) {
+  } else if (C::kConvert && warp >= 10) {
     // ---------------------------------------------------------------- dequant (fp8 / int4, both CTAs)
-    if (C::kConvert) {
+    {
       const int ctid = tid - 320;
       int it = 0;
       for (int j = 0; j < my_tiles; ++j) {
@@ -999,10 +1003,12 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       }
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 0-3, 6-9; both CTAs)
-    constexpr int HB = BN / 2;
+    // ---------------------------------------------------------------- epilogue (both CTAs)
+    // warp w reads TMEM lane quarter w % 4; its ordinal / 4 picks the column part
+    constexpr int kParts = C::kEpiWarps / 4;
+    constexpr int HB = BN / kParts;
     const int quarter = warp & 3;
-    const int half = warp < 4 ? 0 : 1;
+    const int half = (warp < 4 ? warp : warp - 2) >> 2;  // column part
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + half * HB;
     for (int j = 0; j < my_tiles; ++j) {
       int g, nt, mt;
