@@ -150,6 +150,9 @@ group_place_kernel(const int32_t* __restrict__ idx, int n_rows, int slots, int G
   inv[e] = pos;
 }
 
+// One warp per permuted row: the source row index is read once, then every
+// lane moves 16-byte vectors c, c+32, ... with four loads in flight before
+// their stores.
 template <typename V>
 __global__ void gather_rows_kernel(const V* __restrict__ src, int vec_per_row,
                                    const int32_t* __restrict__ perm_row,
@@ -158,12 +161,20 @@ __global__ void gather_rows_kernel(const V* __restrict__ src, int vec_per_row,
   pdl_wait();
   pdl_trigger();
   const int rows = min(offsets[G], max_rows);
-  const int64_t n = static_cast<int64_t>(rows) * vec_per_row;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t r = i / vec_per_row;
-    const int c = static_cast<int>(i - r * vec_per_row);
-    dst[i] = src[static_cast<int64_t>(perm_row[r]) * vec_per_row + c];
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  for (int r = blockIdx.x * wpb + (threadIdx.x >> 5); r < rows; r += gridDim.x * wpb) {
+    const V* s = src + static_cast<int64_t>(perm_row[r]) * vec_per_row;
+    V* d = dst + static_cast<int64_t>(r) * vec_per_row;
+    int c = lane;
+    for (; c + 96 < vec_per_row; c += 128) {
+      const V v0 = s[c], v1 = s[c + 32], v2 = s[c + 64], v3 = s[c + 96];
+      d[c] = v0;
+      d[c + 32] = v1;
+      d[c + 64] = v2;
+      d[c + 96] = v3;
+    }
+    for (; c < vec_per_row; c += 32) d[c] = s[c];
   }
 }
 
@@ -310,8 +321,7 @@ extern "C" SB_API int sb_gather_rows(const void* src, int act_dtype, int cols,
   if (!esize || (static_cast<int64_t>(cols) * esize) % 16) return SB_ERR_ARG;
   if (max_rows == 0) return SB_OK;
   const int vpr = cols * esize / 16;
-  int64_t n = static_cast<int64_t>(max_rows) * vpr;
-  int blocks = static_cast<int>((n + 255) / 256);
+  int blocks = (max_rows + 7) / 8;  // 8 rows (warps) per CTA
   const int cap = 8 * current_sm_count();
   blocks = blocks > cap ? cap : blocks;
   return launch(gather_rows_kernel<uint4>, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream),
