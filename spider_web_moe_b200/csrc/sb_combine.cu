@@ -12,7 +12,7 @@
 
 namespace sb {
 
-constexpr int kCombineThreads = 128;
+constexpr int kCombineThreads = 256;
 
 template <typename T> struct Vec4;
 template <> struct Vec4<float> {
