@@ -9,14 +9,24 @@ the synthetic-data helpers load without the CUDA library.
 """
 from .config import ModelConfig, load_config  # noqa: F401
 
-__all__ = ["ModelConfig", "load_config", "SpiderMoELayer", "sparse_expert_delta"]
+__all__ = ["ModelConfig", "load_config", "SpiderMoELayer", "sparse_expert_delta", "LumenWorkspace",
+           "ExpertChunkStore", "CudaGraphDecodeRunner", "load_spiderw", "write_spiderw"]
+
+_LAZY = {
+    "SpiderMoELayer": ("layer", "SpiderMoELayer"),
+    "sparse_expert_delta": ("sparse_experts", "sparse_expert_delta"),
+    "LumenWorkspace": ("lumen", "LumenWorkspace"),
+    "ExpertChunkStore": ("dobu", "ExpertChunkStore"),
+    "CudaGraphDecodeRunner": ("cuda_graph", "CudaGraphDecodeRunner"),
+    "load_spiderw": ("spiderw", "load_spiderw"),
+    "write_spiderw": ("spiderw", "write_spiderw"),
+}
 
 
 def __getattr__(name):
-    if name == "SpiderMoELayer":
-        from .layer import SpiderMoELayer
-        return SpiderMoELayer
-    if name == "sparse_expert_delta":
-        from .sparse_experts import sparse_expert_delta
-        return sparse_expert_delta
+    if name in _LAZY:
+        import importlib
+
+        mod, attr = _LAZY[name]
+        return getattr(importlib.import_module(f".{mod}", __name__), attr)
     raise AttributeError(name)
