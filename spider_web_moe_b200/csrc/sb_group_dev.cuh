@@ -43,8 +43,53 @@ SB_DEVINL void group_one_cta(const int32_t* __restrict__ idx, const float* __res
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nthreads = blockDim.x, nwarps = nthreads >> 5;
   const int64_t total = static_cast<int64_t>(n_rows) * slots;
-  for (int g = tid; g < G; g += nthreads) run_total[g] = 0;
   const unsigned lt_mask = (1u << lane) - 1u;
+  if (total <= nthreads) {
+    // one entry per thread (decode sizes): group, rank and weight stay in
+    // registers instead of a round trip through the scratch arrays
+    for (int i = tid; i < nwarps * kGroupMaxG; i += nthreads) (&wcnt[0][0])[i] = 0;
+    __syncthreads();
+    const int64_t e = tid;
+    float wsum = 0.f;
+    const int g = e < total ? entry_group(idx, w, slots, G, flags, e, wsum) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, g);
+    const int rank_w = __popc(peers & lt_mask);
+    if (g >= 0 && rank_w == 0) wcnt[warp][g] = __popc(peers);
+    __syncthreads();
+    for (int gg = tid; gg < G; gg += nthreads) {  // warp-order scan per group, then the group totals
+      int acc = 0;
+      for (int ww = 0; ww < nwarps; ++ww) {
+        const int c = wcnt[ww][gg];
+        wcnt[ww][gg] = acc;
+        acc += c;
+      }
+      run_total[gg] = acc;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0;
+      for (int gg = 0; gg < G; ++gg) {
+        s_off[gg] = acc;
+        acc += run_total[gg];
+      }
+      s_off[G] = acc;
+    }
+    __syncthreads();
+    for (int gg = tid; gg <= G; gg += nthreads) offsets[gg] = s_off[gg];
+    if (e < total) {
+      if (g < 0) {
+        inv[e] = -1;
+      } else {
+        const int pos = s_off[g] + wcnt[warp][g] + rank_w;
+        perm_row[pos] = static_cast<int32_t>(e / slots);
+        perm_slot[pos] = static_cast<int32_t>(e);
+        perm_w[pos] = wsum;
+        inv[e] = pos;
+      }
+    }
+    return;
+  }
+  for (int g = tid; g < G; g += nthreads) run_total[g] = 0;
 
   for (int64_t base = 0; base < total; base += nthreads) {
     for (int i = tid; i < nwarps * kGroupMaxG; i += nthreads) (&wcnt[0][0])[i] = 0;
