@@ -198,6 +198,43 @@ def algorithmic_bytes(cfg, spec, taps, n):
     return {"gemm_expert_up": up, "gemm_expert_down": down, "gemm_edge_values": edge}
 
 
+def algorithmic_flops(cfg, taps, n):
+    """Multiply-add FLOPs (2 per MAC) of the grouped-GEMM launches of one loop,
+    from the loop's routing: edge values per (token, destination) pair, expert
+    up (and gate) and down per (token, expert) pair."""
+    H, U = cfg.hidden_size, cfg.expert_ffn_size
+    pairs = int(taps["ffn_offsets"][-1].item())
+    eidx = taps["edge_idx"].long().cpu().reshape(n, -1)
+    dst_pairs = sum(int(torch.unique(eidx[i]).numel()) for i in range(n))
+    gates = 2 if cfg.expert_activation == "swiglu" else 1
+    return {"gemm_edge_values": 2.0 * dst_pairs * H * H, "gemm_expert_up": 2.0 * pairs * H * U * gates,
+            "gemm_expert_down": 2.0 * pairs * U * H}
+
+
+def gemm_roofline(gemm_bytes, gemm_flops, gemm_ms, launches, peaks, peak_kind, traffic):
+    """Roofline of the grouped-GEMM family: HBM-bound (GB/s against the measured
+    copy peak) when its arithmetic intensity is below the ridge point of the
+    measured peaks, tensor-bound (TFLOP/s against the measured bf16 GEMM peak)
+    above it."""
+    sec = gemm_ms / 1e3
+    gbs = gemm_bytes / sec / 1e9
+    tflops = gemm_flops / sec / 1e12
+    ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    tensor = gemm_flops / max(gemm_bytes, 1.0) > ridge
+    r = {"bound": "tensor" if tensor else "hbm",
+         "achieved": tflops if tensor else gbs,
+         "peak": peaks["bf16_tflops"] if tensor else peaks["hbm_gbs"],
+         "unit": "TFLOP/s" if tensor else "GB/s",
+         "peak_kind": f"{peak_kind} ({'cuBLAS bf16 GEMM, burst' if tensor else 'STREAM copy'})",
+         "traffic": (traffic / launches if traffic else None),
+         "kernel": "tc_gemm_kernel (grouped GEMM, tcgen05) edge-value + expert up/down launches",
+         "algorithmic_bytes_per_launch": gemm_bytes / launches, "algorithmic_flops_per_launch": gemm_flops / launches,
+         "arithmetic_intensity": gemm_flops / max(gemm_bytes, 1.0), "ridge": ridge,
+         "achieved_gbs": gbs, "achieved_tflops": tflops, "launch_ms": gemm_ms / launches}
+    r["frac"] = r["achieved"] / r["peak"]
+    return r
+
+
 def build_engine(cfg, spec, args, device, n):
     from spider_web_moe_b200 import synth
     from spider_web_moe_b200.engine import BlockEngine
@@ -481,19 +518,15 @@ def run_b200(args):
     torch.cuda.synchronize(device)
     stages = stage_timing(eng, h, steps=20)
     bytes_loop = algorithmic_bytes(cfg, spec, taps, n)
+    flops_loop = algorithmic_flops(cfg, taps, n)
     gemm_names = ["gemm_edge_values", "gemm_expert_up", "gemm_expert_down"]
     gemm_ms = sum(stages[k]["ms_per_step"] for k in gemm_names)
     gemm_bytes = sum(bytes_loop[k] for k in gemm_names) * cfg.num_loops
+    gemm_flops = sum(flops_loop[k] for k in gemm_names) * cfg.num_loops
     launches = sum(stages[k]["launches_per_step"] for k in gemm_names)
     peaks, peak_kind = load_peaks()
-    achieved = gemm_bytes / (gemm_ms / 1e3) / 1e9
-    traffic = NCU_TRAFFIC_PER_STEP.get(args.config)
-    roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "peak_kind": f"{peak_kind} (STREAM copy)",
-                "traffic": (traffic / launches if traffic else None),
-                "kernel": "tc_gemm_kernel (grouped GEMM, tcgen05) edge-value + expert up/down launches",
-                "algorithmic_bytes_per_launch": gemm_bytes / launches,
-                "launch_ms": gemm_ms / launches}
+    roofline = gemm_roofline(gemm_bytes, gemm_flops, gemm_ms, launches, peaks, peak_kind,
+                             NCU_TRAFFIC_PER_STEP.get(args.config))
 
     line = {
         "metric": "spider_moe_block_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
