@@ -505,6 +505,8 @@ class HostPipeline:
         """Steps s = 0.. : out_hosts[s] <- block(h_hosts[s], x0_hosts[s]) (x0 = h
         when the pipeline was built with x0_is_h).  Host tensors should be
         pinned; returns once every step is enqueued (synchronise to read)."""
+        if len(out_hosts) < len(h_hosts) or (not self.x0_is_h and (x0_hosts is None or len(x0_hosts) < len(h_hosts))):
+            raise ValueError("HostPipeline.run needs an output (and, without x0_is_h, an x0) per input step")
         compute = torch.cuda.current_stream(self.device)
         self.h2d.wait_stream(compute)
         self.d2h.wait_stream(compute)
