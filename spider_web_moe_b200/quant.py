@@ -10,6 +10,12 @@
 * fp8: e4m3 with one fp32 scale per output row, ``s = amax(|w|)/448`` with a
   1e-12 floor, quantised by ``quantize_fp8_with_scale_tensor(w, s[:, None])``
   (quant.py:146-158) and dequantised as ``fp32(q) * s`` (quant.py:161-169).
+* the reference's general fp8 helpers (quant.py:16-69, 146-169):
+  ``quantize_fp8`` / ``dequantize_fp8`` with one per-tensor scale (computed as
+  amax/448 with a 1e-12 floor when not given), the broadcastable-scale pair
+  ``quantize_fp8_with_scale_tensor`` / ``dequantize_fp8_with_scale_tensor``,
+  and ``fp8_available`` / ``fp8_dtype`` / ``is_fp8_dtype`` /
+  ``compute_fp8_scale``.
 
 The packing is a format that must match the reference byte for byte, so the
 steps are the reference's steps (the golden vectors in tests/golden pin it).
@@ -85,3 +91,69 @@ def quantize_fp8_per_channel(w: torch.Tensor) -> Fp8Tensor:
     s = (w.detach().float().abs().amax(dim=-1) / FP8_E4M3_MAX).clamp_min(1e-12)
     q = (w.detach().float() / s.unsqueeze(-1).clamp_min(1e-12)).to(torch.float8_e4m3fn)
     return Fp8Tensor(q, s)
+
+
+# ---------------------------------------------------------------------------
+# general fp8 helpers of the reference (quant.py:16-69, 146-169)
+# ---------------------------------------------------------------------------
+_E4M3 = getattr(torch, "float8_e4m3fn", None)
+
+
+def fp8_available() -> bool:
+    return _E4M3 is not None
+
+
+def fp8_dtype() -> torch.dtype:
+    if _E4M3 is None:
+        raise RuntimeError("torch.float8_e4m3fn is not available in this PyTorch build")
+    return _E4M3
+
+
+def is_fp8_dtype(dtype: torch.dtype) -> bool:
+    return _E4M3 is not None and dtype == _E4M3
+
+
+def compute_fp8_scale(x: torch.Tensor, eps: float = 1e-12) -> torch.Tensor:
+    """One scale for the whole tensor: amax(|x|) / 448, at least eps (0-dim fp32)."""
+    return (x.detach().float().abs().amax() / FP8_E4M3_MAX).clamp_min(eps)
+
+
+def _scalar_scale(scale, device) -> torch.Tensor:
+    if isinstance(scale, torch.Tensor):
+        return scale.detach().float().reshape(()).to(device)
+    return torch.tensor(float(scale), dtype=torch.float32, device=device)
+
+
+def quantize_fp8(x: torch.Tensor, scale=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """(e4m3 tensor, 0-dim fp32 scale): x / scale cast to e4m3, the scale
+    computed from x when not given."""
+    s = compute_fp8_scale(x) if scale is None else _scalar_scale(scale, x.device)
+    return (x.float() / s).to(fp8_dtype()), s
+
+
+def dequantize_fp8(x: torch.Tensor, scale=None, compute_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+    """fp32(x) * scale in compute_dtype (a plain cast without a scale)."""
+    y = x.to(torch.float32)
+    if scale is None:
+        return y.to(compute_dtype)
+    s = scale.to(device=y.device, dtype=torch.float32) if isinstance(scale, torch.Tensor) else \
+        torch.tensor(float(scale), dtype=torch.float32, device=y.device)
+    return (y * s).to(compute_dtype)
+
+
+def _broadcast_scale(scale: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    s = scale.to(device=x.device, dtype=torch.float32)
+    while s.ndim < x.ndim:  # trailing singleton dims, so [H] scales rows of [H, D]
+        s = s.unsqueeze(-1)
+    return s
+
+
+def quantize_fp8_with_scale_tensor(x: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """x / scale (broadcast over trailing dims, floored at 1e-12) cast to e4m3."""
+    return (x.float() / _broadcast_scale(scale, x).clamp_min(1e-12)).to(fp8_dtype())
+
+
+def dequantize_fp8_with_scale_tensor(x: torch.Tensor, scale: torch.Tensor,
+                                     compute_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+    """fp32(x) * scale (broadcast over trailing dims) in compute_dtype."""
+    return (x.float() * _broadcast_scale(scale, x)).to(compute_dtype)

@@ -425,6 +425,28 @@ def dobu_case(synth):
     print("dobu calls", [(c["hits"], c["misses"], c["loads"], c["hot"]) for c in calls], res["layer_stats"])
 
 
+def fp8_helper_vectors():
+    """The reference's general fp8 helpers (spider_moe/quant.py:16-69, 146-169)
+    on seeded tensors: per-tensor quantize with a computed, a float and a tensor
+    scale, dequantize in the default and an explicit dtype, and the
+    broadcastable-scale pair."""
+    from spider_moe import quant as RQ
+
+    g = torch.Generator().manual_seed(6)
+    x = torch.randn(5, 24, generator=g) * 3.0
+    q, s = RQ.quantize_fp8(x)
+    q2, s2 = RQ.quantize_fp8(x, 0.05)
+    q3, s3 = RQ.quantize_fp8(x, torch.tensor([0.02]))
+    rows = torch.rand(5, generator=g) * 0.1 + 1e-3
+    q4 = RQ.quantize_fp8_with_scale_tensor(x, rows)
+    res = dict(x=x, rows=rows, q=q.view(torch.uint8), s=s, q2=q2.view(torch.uint8), s2=s2, q3=q3.view(torch.uint8),
+               s3=s3, deq=RQ.dequantize_fp8(q, s), deq_bf16=RQ.dequantize_fp8(q, s, torch.bfloat16),
+               deq_plain=RQ.dequantize_fp8(q), q4=q4.view(torch.uint8),
+               deq4=RQ.dequantize_fp8_with_scale_tensor(q4, rows), scale=RQ.compute_fp8_scale(x))
+    torch.save(res, os.path.join(HERE, "fp8_helpers.pt"))
+    print("fp8 helper vectors")
+
+
 def quant_vectors():
     from spider_moe.quant import quantize_int4, quantize_fp8_with_scale_tensor, dequantize_int4
     g = torch.Generator().manual_seed(5)
@@ -472,6 +494,7 @@ def main():
     lumen_case(synth)
     spiderw_case(synth, ref_root)
     dobu_case(synth)
+    fp8_helper_vectors()
 
 
 if __name__ == "__main__":

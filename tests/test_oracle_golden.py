@@ -191,3 +191,23 @@ def test_oracle_lumen_matches_reference():
         assert rel_err(got["lumen_slot_weights"], want["lumen_slot_weights"].reshape(-1, 4)) < 1e-5
         assert rel_err(got["lumen_broadcast_norm"].view(1, -1), want["lumen_broadcast_norm"].reshape(1, -1)) < 1e-5
         assert torch.equal(got["expert_load"], want["expert_load"])
+
+
+def test_fp8_helpers_match_reference_vectors():
+    """quant.py's general fp8 helpers reproduce the reference's bytes and values."""
+    v = load_golden("fp8_helpers")
+    x = v["x"]
+    q, s = Q.quantize_fp8(x)
+    assert torch.equal(q.view(torch.uint8), v["q"]) and torch.equal(s, v["s"])
+    assert torch.equal(Q.compute_fp8_scale(x), v["scale"])
+    q2, s2 = Q.quantize_fp8(x, 0.05)
+    assert torch.equal(q2.view(torch.uint8), v["q2"]) and torch.equal(s2, v["s2"])
+    q3, s3 = Q.quantize_fp8(x, torch.tensor([0.02]))
+    assert torch.equal(q3.view(torch.uint8), v["q3"]) and torch.equal(s3, v["s3"])
+    assert torch.equal(Q.dequantize_fp8(q, s), v["deq"])
+    assert torch.equal(Q.dequantize_fp8(q, s, torch.bfloat16), v["deq_bf16"])
+    assert torch.equal(Q.dequantize_fp8(q), v["deq_plain"])
+    q4 = Q.quantize_fp8_with_scale_tensor(x, v["rows"])
+    assert torch.equal(q4.view(torch.uint8), v["q4"])
+    assert torch.equal(Q.dequantize_fp8_with_scale_tensor(q4, v["rows"]), v["deq4"])
+    assert Q.fp8_available() and Q.is_fp8_dtype(Q.fp8_dtype()) and not Q.is_fp8_dtype(torch.float16)
