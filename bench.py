@@ -1,11 +1,12 @@
 """Benchmark: recurrent Spider-MoE block tokens/s on B200 (BASELINE.json metric).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg3] [--impl b200|reference]
 
 A step is one forward of the block -- all ``num_loops`` loops -- over one batch
-of synthetic tokens of the named config (default cfg2: bf16 decode, 64 tokens,
-H 1024, 16 experts, top-2, 2 edges, 6 loops, FFN 2048).  Weights N(0,0.02)
-(seeded), inputs N(0,1), no network data.
+of synthetic tokens of the named config.  The default is cfg3, the largest
+single-GPU configuration: bf16 prefill, 8192 tokens (8 x 1024), H 1024, 16
+experts with a Zipf(1.1) router bias, top-2, 2 edges, 6 loops, SwiGLU FFN
+2048.  Weights N(0,0.02) (seeded), inputs N(0,1), no network data.
 
 Arms:
 * ``--impl b200`` (default): the CUDA path.  ``value`` = tokens/s of CUDA-graph
@@ -42,24 +43,23 @@ import torch.distributed as dist  # noqa: E402
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum, one ncu capture) of the
-# grouped-GEMM launches of one step, per config; None where no capture of all of
-# them exists yet.
-# DRAM bytes (read + write) of the edge-value, expert-up and expert-down GEMM
-# launches of one step, from ncu (dram__bytes_read.sum + dram__bytes_write.sum
-# over the 18 launches of one cfg2 replay; profiles/gemm_tcgen05_cfg2.txt).
-NCU_TRAFFIC_PER_STEP = {"cfg2": 1013465344}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum, one ncu capture) of
+# the edge-value, expert-up and expert-down GEMM launches of one step, keyed by
+# "config:activation"; a workload without a capture reports traffic null.
+#   cfg2:gelu  -- the 18 launches of one cfg2 replay (profiles/gemm_tcgen05_cfg2.txt)
+NCU_TRAFFIC_PER_STEP = {"cfg2:gelu": 1013465344}
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--config", default="cfg2")
+    ap.add_argument("--config", default="cfg3")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--engine", default="auto", choices=["auto", "tcgen05", "simt"])
-    ap.add_argument("--activation", default="gelu", choices=["gelu", "swiglu"])
+    ap.add_argument("--activation", default=None, choices=["gelu", "swiglu"],
+                    help="expert FFN; default: the one the workload names (SwiGLU for cfg2-cfg5)")
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="N > 1 expert-parallel exchange: stores into the peers' memory over NVLink (peer) or NCCL "
                          "all-to-all")
@@ -169,9 +169,25 @@ def workload(args):
 
     spec = benchmark_configs()[args.config]
     model = dict(spec["model"])
-    model["expert_activation"] = args.activation
+    model["expert_activation"] = args.activation or spec["activation"]
     cfg = ModelConfig(**model).validate()
     return cfg, spec
+
+
+def workload_config(args, cfg, spec, world: int) -> dict:
+    """The ``config`` object of the JSON line.  Both arms print this same dict
+    for the same arguments: it names the workload, not the implementation (the
+    reference arm's bounded sample is described in its ``cpu_baseline``)."""
+    par = "single GPU" if world <= 1 else (
+        f"ep{world}: tokens sharded by rank, experts e % {world}, "
+        + ("dispatch/combine stored into peer memory over NVLink" if args.transport == "peer"
+           else "NCCL all-to-all"))
+    return {"workload": args.config, "tokens_per_step_per_gpu": spec["tokens"], "num_loops": cfg.num_loops,
+            "hidden": cfg.hidden_size, "experts": cfg.num_experts, "top_k": cfg.top_k,
+            "edges_per_expert": cfg.edges_per_expert, "ffn": cfg.expert_ffn_size,
+            "expert_activation": cfg.expert_activation, "expert_weights": spec["wfmt"],
+            "router_bias": "zipf(1.1)" if spec["zipf"] else "none", "parallelism": par,
+            "l2": "not flushed: every step re-reads the block's weights, a working set larger than the 126 MB L2"}
 
 
 def algorithmic_bytes(cfg, spec, taps, n):
@@ -270,25 +286,45 @@ def stage_timing(eng, h, steps):
             for i in range(ns)}
 
 
+PORT_NOTE = ("the reference block's algorithm restated in fp32 PyTorch (oracle/spider_oracle.py: the dense "
+             "edge transform of all E destinations as spider_moe/model.py:271-288 computes it); the restatement "
+             "packs the expert and edge weights once, where the reference module re-stacks them on every loop "
+             "(model.py:271,305-308), so it runs faster than the module itself")
+
+
+def port_params(cfg, spec):
+    """Oracle parameters of the workload (bf16-valued fp32 weights, seeded as the GPU arm)."""
+    from oracle import spider_oracle as O
+    from spider_web_moe_b200 import synth
+
+    zipf = 1.1 if spec["zipf"] else None
+    sd = synth.synthetic_state_dict(cfg, seed=0, device="cpu", zipf=zipf, round_bf16=True)
+    return O.params_from_state_dict(sd, cfg.num_experts)
+
+
+def port_seconds_per_token(p, cfg) -> float:
+    """Calibration: one token through all loops (after one untimed call)."""
+    from oracle import spider_oracle as O
+    from spider_web_moe_b200 import synth
+
+    h, _ = synth.block_inputs(1, cfg.hidden_size, seed=1)
+    O.run_loops(p, h.view(1, -1), h.view(1, -1), cfg, dense=True)
+    t0 = time.perf_counter()
+    O.run_loops(p, h.view(1, -1), h.view(1, -1), cfg, dense=True)
+    return time.perf_counter() - t0
+
+
 def cpu_baseline(cfg, spec, seconds, threads=None):
-    """The reference block's algorithm on the host cores: dense edge transform as
-    spider_moe/model.py:271-288 computes it, fp32 (bf16-valued weights)."""
+    """The reference block's algorithm on the host cores (the oracle port, fp32,
+    bf16-valued weights) on a bounded sample of the workload's tokens."""
     from oracle import spider_oracle as O
     from spider_web_moe_b200 import synth
 
     if threads:
         torch.set_num_threads(threads)
-    zipf = 1.1 if spec["zipf"] else None
-    sd = synth.synthetic_state_dict(cfg, seed=0, device="cpu", zipf=zipf, round_bf16=True)
-    p = O.params_from_state_dict(sd, cfg.num_experts)
-    del sd
-    tokens_total = spec["tokens"]
-    # calibrate: one token through all loops
-    h, _ = synth.block_inputs(1, cfg.hidden_size, seed=1)
-    t0 = time.perf_counter()
-    O.run_loops(p, h.view(1, -1), h.view(1, -1), cfg, dense=True)
-    per_tok = time.perf_counter() - t0
-    chunk = int(max(1, min(tokens_total, seconds / 4 / max(per_tok, 1e-6))))
+    p = port_params(cfg, spec)
+    per_tok = port_seconds_per_token(p, cfg)
+    chunk = int(max(1, min(spec["tokens"], seconds / 4 / max(per_tok, 1e-6))))
     h, _ = synth.block_inputs(chunk, cfg.hidden_size, seed=1)
     h = h.view(chunk, -1)
     done = 0
@@ -300,8 +336,14 @@ def cpu_baseline(cfg, spec, seconds, threads=None):
             break
     dt = time.perf_counter() - t0
     return {"value": done / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{done} tokens ({chunk}-token chunks) x {cfg.num_loops} loops of {spec_name(spec)} "
-                      f"in {dt:.1f} s, fp32 oracle (dense edge transform as the reference)"}
+            "sample": f"{done} of the workload's tokens ({chunk}-token chunks; the block is token-independent) x "
+                      f"{cfg.num_loops} loops of {spec_name(spec)} {cfg.expert_activation} in {dt:.1f} s; "
+                      + PORT_NOTE}
+
+
+def step_median(marks) -> float:
+    """Median device time of one step from the events recorded between replays."""
+    return statistics.median(marks[i].elapsed_time(marks[i + 1]) for i in range(len(marks) - 1))
 
 
 def spec_name(spec):
@@ -321,14 +363,8 @@ def run_reference(args):
     from oracle import spider_oracle as O
     from spider_web_moe_b200 import synth
 
-    zipf = 1.1 if spec["zipf"] else None
-    sd = synth.synthetic_state_dict(cfg, seed=0, device="cpu", zipf=zipf, round_bf16=True)
-    p = O.params_from_state_dict(sd, cfg.num_experts)
-    del sd
-    h1, _ = synth.block_inputs(1, cfg.hidden_size, seed=1)
-    t0 = time.perf_counter()
-    O.run_loops(p, h1.view(1, -1), h1.view(1, -1), cfg, dense=True)
-    per_tok = time.perf_counter() - t0
+    p = port_params(cfg, spec)
+    per_tok = port_seconds_per_token(p, cfg)
     budget = 150.0  # seconds for the whole --steps/--warmup run
     chunk = int(max(1, min(spec["tokens"], budget / max(1, args.steps + args.warmup) / max(per_tok, 1e-6))))
     h, _ = synth.block_inputs(chunk, cfg.hidden_size, seed=1)
@@ -344,13 +380,10 @@ def run_reference(args):
         "impl": "reference", "metric": "spider_moe_block_tokens_per_s", "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.config, "tokens_per_step": chunk, "num_loops": cfg.num_loops,
-                   "hidden": cfg.hidden_size, "experts": cfg.num_experts, "top_k": cfg.top_k,
-                   "edges_per_expert": cfg.edges_per_expert, "ffn": cfg.expert_ffn_size,
-                   "expert_weights": spec["wfmt"]},
+        "config": workload_config(args, cfg, spec, world),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{chunk} tokens x {cfg.num_loops} loops per step (fp32 oracle, dense edge "
-                                   f"transform as spider_moe/model.py:271-288)"},
+                         "sample": f"each step: {chunk} of the workload's {spec['tokens']} tokens (the block is "
+                                   f"token-independent) x {cfg.num_loops} loops; " + PORT_NOTE},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -383,16 +416,20 @@ def run_b200_ep(args, rank, world, local, device):
     torch.cuda.synchronize(device)
     ep.dense.check_status()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     barrier(world)
     torch.cuda.synchronize(device)
     with ClockSampler(local) as clk:
         start.record(stream)
-        for _ in range(args.steps):
+        for i in range(args.steps):
+            marks[i].record(stream)
             ep.graph.replay()
+        marks[-1].record(stream)
         end.record(stream)
         torch.cuda.synchronize(device)
     barrier(world)
     ms_step = max_over_ranks(start.elapsed_time(end), world, device) / args.steps
+    med_step = max_over_ranks(step_median(marks), world, device)
     # e2e through the public API: pinned host input in, output back, every step
     h_host = h.cpu().pin_memory()
     out_host = torch.empty(n, cfg.hidden_size, dtype=torch.bfloat16).pin_memory()
@@ -416,14 +453,8 @@ def run_b200_ep(args, rank, world, local, device):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) hidden states)",
-        "config": {"workload": args.config, "tokens_per_step_per_gpu": n, "num_loops": cfg.num_loops,
-                   "hidden": cfg.hidden_size, "experts": cfg.num_experts, "top_k": cfg.top_k,
-                   "edges_per_expert": cfg.edges_per_expert, "ffn": cfg.expert_ffn_size,
-                   "expert_activation": cfg.expert_activation, "expert_weights": spec["wfmt"],
-                   "parallelism": f"ep{world}: tokens sharded by rank, experts e % {world}, "
-                                  + ("dispatch/combine stored into peer memory over NVLink" if args.transport == "peer"
-                                     else "NCCL all-to-all"),
-                   "l2": "not flushed: dense + local expert weights re-read every loop", "engine": args.engine},
+        "config": workload_config(args, cfg, spec, world), "engine": args.engine,
+        "ms_per_step_median": med_step,
         "clocks": clk.summary(),
         "e2e": {"value": n * world / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 2 * n * cfg.hidden_size * 2,
                 "d2h_bytes_per_step": n * cfg.hidden_size * 2, "ms_per_step": e2e_ms},
@@ -478,18 +509,22 @@ def run_b200(args):
         return
 
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     barrier(world)
     torch.cuda.synchronize(device)
     with ClockSampler(local) as clk:
         start.record(stream)
-        for _ in range(args.steps):
+        for i in range(args.steps):
+            marks[i].record(stream)
             g.graph.replay()
+        marks[-1].record(stream)
         end.record(stream)
         torch.cuda.synchronize(device)
     barrier(world)
     ms = start.elapsed_time(end)
     ms = max_over_ranks(ms, world, device)
     ms_step = ms / args.steps
+    med_step = max_over_ranks(step_median(marks), world, device)
     value = n * world / (ms_step / 1e3)
     gpu_launches = g.kernels_per_replay * args.steps  # libspider_b200 kernels counted at capture
 
@@ -526,20 +561,15 @@ def run_b200(args):
     launches = sum(stages[k]["launches_per_step"] for k in gemm_names)
     peaks, peak_kind = load_peaks()
     roofline = gemm_roofline(gemm_bytes, gemm_flops, gemm_ms, launches, peaks, peak_kind,
-                             NCU_TRAFFIC_PER_STEP.get(args.config))
+                             NCU_TRAFFIC_PER_STEP.get(f"{args.config}:{cfg.expert_activation}"))
 
     line = {
         "metric": "spider_moe_block_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) hidden states)",
-        "config": {"workload": args.config, "tokens_per_step_per_gpu": n, "num_loops": cfg.num_loops,
-                   "hidden": cfg.hidden_size, "experts": cfg.num_experts, "top_k": cfg.top_k,
-                   "edges_per_expert": cfg.edges_per_expert, "ffn": cfg.expert_ffn_size,
-                   "expert_activation": cfg.expert_activation, "expert_weights": spec["wfmt"],
-                   "parallelism": "replicas" if world > 1 else "single",
-                   "l2": f"not flushed: per-step weight working set {eng.weight_bytes() / 1e6:.0f} MB > 126 MB L2",
-                   "engine": args.engine},
+        "config": workload_config(args, cfg, spec, world), "engine": args.engine,
+        "weight_bytes": eng.weight_bytes(), "ms_per_step_median": med_step,
         "clocks": clk.summary(),
         "e2e": {"value": n * world / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},

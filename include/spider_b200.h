@@ -103,16 +103,20 @@ SB_API int sb_group(const int32_t* idx, const float* w, int n_rows, int slots, i
                     void* stream);
 
 /* No reference counterpart: the grouping of sb_group for callers that cannot
- * allocate device memory (a binding that only forwards pointers it was given,
- * or code running during stream capture, where cudaMalloc is not allowed).
+ * allocate device memory -- a thin C / ctypes / cgo binding that only forwards
+ * pointers it was given and owns no GPU allocator, or a host process whose
+ * device memory is all reserved up front by another allocator's pool.
  * Same arguments and results as sb_group, without the workspace: its scratch
  * is a fixed device array of SB_GROUP_NOALLOC_MAX_ENTRIES entries (n_rows *
  * slots) inside the library, held on every device that loads the library until
  * the process exits.  Larger inputs return SB_ERR_WORKSPACE.  All calls on a
  * device share the array (it keeps the last call's contents; nothing in it has
  * to start at zero), so calls whose kernels can overlap on the GPU race.  The
- * first call on a device looks up the array's address and should come before
- * any stream capture.  Nothing is allocated. */
+ * first call on a device looks up the array's address (cudaGetSymbolAddress,
+ * with that device current) and should come before any stream capture.  The
+ * address is cached per device ordinal for the life of the process: it assumes
+ * the CUDA runtime's primary context and no cudaDeviceReset afterwards.
+ * Nothing is allocated. */
 #define SB_GROUP_NOALLOC_MAX_ENTRIES 65536
 SB_API int sb_group_noalloc(const int32_t* idx, const float* w, int n_rows, int slots, int num_groups,
                             int flags, int32_t* offsets, int32_t* perm_row, int32_t* perm_slot,
@@ -430,6 +434,21 @@ SB_API int sb_expert_rows(const sb_block_dims* dims, const sb_block_weights* w, 
 
 /* Byte offset of the device status word inside every workspace above. */
 SB_API size_t sb_status_offset(void);
+
+/* Bits kernels OR into a device status word.  Every wait on the device (an
+ * mbarrier of the TMA / MMA pipeline, a peer rank's exchange flag) gives up
+ * after about 2 s of %globaltimer time, records its bit, lets its own copies
+ * in flight land and returns, so a lost arrival or a dead peer leaves an error
+ * the host reads (SB_ERR_DEVICE_STATUS) instead of a hung GPU. */
+enum {
+  SB_DEVERR_TMA_WAIT = 1 << 0,  /* producer / consumer gave up on a TMA barrier */
+  SB_DEVERR_MMA_WAIT = 1 << 1,  /* gave up on an MMA-completion barrier */
+  SB_DEVERR_CONV_WAIT = 1 << 2, /* gave up on the weight-dequant barrier */
+  SB_DEVERR_EPI_WAIT = 1 << 3,  /* epilogue gave up on the accumulator barrier */
+  SB_DEVERR_BAD_INDEX = 1 << 4, /* an index outside its range was met and skipped */
+  SB_DEVERR_DRAIN = 1 << 5,     /* in-flight copies not drained before exit */
+  SB_DEVERR_PEER_WAIT = 1 << 6  /* gave up waiting for a peer rank's exchange flag */
+};
 
 /* ------------------------------------------------------------------ profiling aid
  * Per-stage CUDA-event timing of sb_block_forward (no reference counterpart;

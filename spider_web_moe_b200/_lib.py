@@ -19,6 +19,10 @@ SB_ERR_NO_DEVICE = 4
 SB_ERR_WORKSPACE = 5
 SB_ERR_DEVICE_STATUS = 6
 
+# device status word bits (SB_DEVERR_* in include/spider_b200.h)
+SB_DEVERR_TMA_WAIT, SB_DEVERR_MMA_WAIT, SB_DEVERR_CONV_WAIT, SB_DEVERR_EPI_WAIT = 1, 2, 4, 8
+SB_DEVERR_BAD_INDEX, SB_DEVERR_DRAIN, SB_DEVERR_PEER_WAIT = 16, 32, 64
+
 SB_F32, SB_BF16 = 0, 1
 SB_W_F32, SB_W_BF16, SB_W_FP8, SB_W_INT4 = 0, 1, 2, 3
 SB_ACT_GELU, SB_ACT_SWIGLU = 0, 1

@@ -102,22 +102,28 @@ def benchmark_configs() -> dict:
     cfg2: bf16 decode, 64 tokens.  cfg3: bf16 prefill, 8192 tokens, Zipf bias.
     cfg4: fp8 experts, 64 experts, 4096 tokens.  cfg5: int4 experts, 128
     experts, 256 tokens, Zipf bias.
+
+    ``activation`` is the expert FFN the workload names: cfg1 is the
+    reference's own model (erf-GELU, spider_moe/model.py:177-183); cfg2 and
+    cfg3 are stated as SwiGLU blocks, and the quantised cfg4 / cfg5 experts
+    are SwiGLU FFNs in the fp8 / int4 formats.  ``model`` holds only reference
+    ``ModelConfig`` fields, so a test can run any workload in either mode.
     """
     return {
         "cfg1": dict(model=dict(vocab_size=512, hidden_size=64, num_heads=4, num_experts=4,
                                 top_k=2, edges_per_expert=2, num_loops=2, expert_ffn_size=128),
-                     tokens=64, dtype="fp32", wfmt="native", zipf=False),
+                     tokens=64, dtype="fp32", wfmt="native", zipf=False, activation="gelu"),
         "cfg2": dict(model=dict(hidden_size=1024, num_heads=8, num_experts=16, top_k=2,
                                 edges_per_expert=2, num_loops=6, expert_ffn_size=2048),
-                     tokens=64, dtype="bf16", wfmt="bf16", zipf=False),
+                     tokens=64, dtype="bf16", wfmt="bf16", zipf=False, activation="swiglu"),
         "cfg3": dict(model=dict(hidden_size=1024, num_heads=8, num_experts=16, top_k=2,
                                 edges_per_expert=2, num_loops=6, expert_ffn_size=2048),
-                     tokens=8192, dtype="bf16", wfmt="bf16", zipf=True),
+                     tokens=8192, dtype="bf16", wfmt="bf16", zipf=True, activation="swiglu"),
         "cfg4": dict(model=dict(hidden_size=2048, num_heads=8, num_experts=64, top_k=4,
                                 edges_per_expert=3, num_loops=6, expert_ffn_size=1024),
-                     tokens=4096, dtype="bf16", wfmt="fp8", zipf=False),
+                     tokens=4096, dtype="bf16", wfmt="fp8", zipf=False, activation="swiglu"),
         "cfg5": dict(model=dict(hidden_size=2048, num_heads=8, num_experts=128, top_k=8,
                                 edges_per_expert=4, num_loops=4, expert_ffn_size=768,
                                 moe_int4_group_size=128),
-                     tokens=256, dtype="bf16", wfmt="int4", zipf=True),
+                     tokens=256, dtype="bf16", wfmt="int4", zipf=True, activation="swiglu"),
     }

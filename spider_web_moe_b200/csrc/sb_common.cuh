@@ -17,16 +17,7 @@
 
 #define SB_DEVINL __device__ __forceinline__
 
-// Status word bits written by kernels (first int of the workspace status area).
-enum {
-  SB_DEVERR_TMA_WAIT = 1 << 0,     // producer / consumer gave up on a TMA barrier
-  SB_DEVERR_MMA_WAIT = 1 << 1,     // gave up on an MMA-completion barrier
-  SB_DEVERR_CONV_WAIT = 1 << 2,    // gave up on the weight-dequant barrier
-  SB_DEVERR_EPI_WAIT = 1 << 3,     // epilogue gave up on the accumulator barrier
-  SB_DEVERR_BAD_INDEX = 1 << 4,    // an index outside its range was met and skipped
-  SB_DEVERR_DRAIN = 1 << 5,        // in-flight copies not drained before exit
-  SB_DEVERR_PEER_WAIT = 1 << 6,    // gave up waiting for a peer rank's exchange flag
-};
+// Status word bits written by kernels: SB_DEVERR_* in spider_b200.h.
 
 namespace sb {
 

@@ -3,10 +3,10 @@
 //
 // Some callers have no way to allocate device memory: a thin C / ctypes / cgo
 // binding that only forwards pointers it was given and owns no GPU allocator,
-// or code that runs while a CUDA stream is being captured, where a cudaMalloc
-// is not allowed.  For them this entry point keeps its scratch (one int32 rank
-// and one float weight per entry) in a fixed array that lives in the library's
-// device image, so nothing is allocated per call.
+// or a host process whose device memory is all reserved up front by another
+// allocator's pool.  For them this entry point keeps its scratch (one int32
+// rank and one float weight per entry) in a fixed array that lives in the
+// library's device image, so nothing is allocated per call.
 //
 // Limits and sharing:
 // * at most SB_GROUP_NOALLOC_MAX_ENTRIES (n_rows * slots) entries; larger
@@ -20,7 +20,10 @@
 //   ordering between them) race on the array, so order such calls;
 // * the first call on each device looks up the array's device address (with
 //   that device current) and caches it; make that first call before capturing
-//   a stream.
+//   a stream.  The cache is keyed by device ordinal for the life of the
+//   process, so it assumes the CUDA runtime's primary context (the one the
+//   runtime API uses) and no cudaDeviceReset afterwards: either would leave a
+//   stale address behind.
 #include <mutex>
 
 #include "sb_common.cuh"

@@ -157,8 +157,7 @@ class SpiderMoELayer(nn.Module):
             taps = eng.make_taps(n)
             out = eng.forward(h, x0, loop_idx, loop_idx + 1, taps=taps).to(h.dtype)
         else:
-            taps = eng.make_taps(n)
-            out = self._forward_ep(eng, h, x0, loop_idx, taps)
+            out, taps = self._forward_ep(eng, h, x0, loop_idx)
         lumen_state = None
         if self.lumen is not None:
             if return_stats:
@@ -192,17 +191,20 @@ class SpiderMoELayer(nn.Module):
         out = eng.epilogue(delta, inv, h, x0).to(h.dtype)
         return out, {"top_idx": top_idx, "top_w": top_w}
 
-    def _forward_ep(self, eng, h, x0, loop_idx, taps):
-        """Reference expert-parallel semantics: local experts, SUM all-reduce of delta."""
+    def _forward_ep(self, eng, h, x0, loop_idx):
+        """Reference expert-parallel semantics (sparse_experts.py:38-43,66-67):
+        every rank routes all tokens and computes their messages
+        (sb_block_route), runs only its own experts (sb_expert_delta with
+        e % world == rank), SUM-all-reduces the delta, and applies the LayerNorm
+        epilogue (sb_combine_ln).  Returns (out, routing taps for the stats)."""
         rank, world = ep_helpers.get_rank_world()
-        eng.forward(h, x0, loop_idx, loop_idx + 1, taps=taps)  # routing + messages for all tokens
-        delta = eng.expert_delta(taps["messages"], taps["top_idx"], taps["top_w"], rank, world)
+        n = h.numel() // h.shape[-1]
+        msgs, top_idx, top_w = eng.route(h, loop_idx)
+        delta = eng.expert_delta(msgs, top_idx, top_w, rank, world)
         ep_helpers.all_reduce_sum_(delta)
-        n, H = delta.shape
-        hh = h.reshape(n, H).float()
-        u = hh + self.residual_scale * delta + self.reinject_weight * x0.reshape(n, H).float()
-        out = torch.nn.functional.layer_norm(u, (H,), eng.t["ln_w"], eng.t["ln_b"], 1e-5)
-        return out.to(h.dtype).view(h.shape)
+        inv = torch.arange(n, dtype=torch.int32, device=h.device).view(n, 1)
+        out = eng.epilogue(delta, inv, h, x0).to(h.dtype)
+        return out, {"top_idx": top_idx, "top_w": top_w}
 
     def run_loops(self, h, x0, loop_begin: int = 0, loop_end: int | None = None):
         """All loops [loop_begin, loop_end) in one library call (model.py:445-448)."""

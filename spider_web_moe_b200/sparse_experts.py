@@ -16,15 +16,26 @@ from .config import ModelConfig
 from .engine import BlockEngine
 from .expert_parallel import all_reduce_sum_, ep_enabled, get_rank_world
 
+# Packed engines of recently used weight sets.  An entry keeps the weight
+# tensors themselves and is reused only for those same tensor objects at the
+# same in-place version: a freed and reallocated tensor can come back at the
+# same address with version 0, so addresses alone would hand out an engine
+# packed from the old weights.
 _CACHE: dict = {}
+_CACHE_MAX = 8
 
 
 def _engine_for(w_up, b_up, w_down, b_down, num_experts, top_k, act_dtype, device) -> BlockEngine:
-    key = (w_up.data_ptr(), w_down.data_ptr(), b_up.data_ptr(), b_down.data_ptr(), tuple(w_up.shape),
-           act_dtype, str(device), int(w_up._version), int(w_down._version))
-    eng = _CACHE.get(key)
-    if eng is not None:
-        return eng
+    tensors = (w_up, b_up, w_down, b_down)
+    key = (tuple(t.data_ptr() for t in tensors), tuple(w_up.shape), int(num_experts), int(top_k), act_dtype,
+           str(device))
+    versions = tuple(int(t._version) for t in tensors)
+    hit = _CACHE.get(key)
+    if hit is not None:
+        held, held_versions, eng = hit
+        if all(a is b for a, b in zip(held, tensors)) and held_versions == versions:
+            return eng
+        del _CACHE[key]
     e, u, h = w_up.shape
     cfg = ModelConfig(hidden_size=h, num_heads=1, num_experts=num_experts, top_k=top_k, edges_per_expert=1,
                       num_loops=1, expert_ffn_size=u, loop_embed_size=8)
@@ -35,9 +46,9 @@ def _engine_for(w_up, b_up, w_down, b_down, num_experts, top_k, act_dtype, devic
         state[f"experts.{i}.2.weight"] = w_down[i]
         state[f"experts.{i}.2.bias"] = b_down[i]
     eng = BlockEngine(cfg, state, device, act_dtype=act_dtype, max_tokens=1)
-    if len(_CACHE) > 8:
-        _CACHE.clear()
-    _CACHE[key] = eng
+    if len(_CACHE) >= _CACHE_MAX:
+        _CACHE.pop(next(iter(_CACHE)))  # oldest entry
+    _CACHE[key] = (tensors, versions, eng)
     return eng
 
 

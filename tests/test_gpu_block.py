@@ -94,18 +94,23 @@ def test_block_matches_reference_fixture(name, kind, engine, cuda_device):
             assert rel_err(out, rec["h_out"].reshape(n, -1)) < tol
 
 
-def full_config(name, tokens=None):
+def full_config(name, tokens=None, activation="gelu"):
     spec = benchmark_configs()[name]
-    cfg = ModelConfig(**spec["model"]).validate()
+    cfg = ModelConfig(**spec["model"], expert_activation=activation).validate()
     return cfg, spec, tokens or spec["tokens"]
 
 
-@pytest.mark.parametrize("name,tokens,engine", [
-    ("cfg2", None, "tcgen05"), ("cfg2", None, "simt"), ("cfg3", 512, "tcgen05"),
-    ("cfg4", 128, "tcgen05"), ("cfg5", 64, "tcgen05"), ("cfg5", 64, "simt")])
-def test_full_size_config_one_loop(name, tokens, engine, cuda_device):
-    """Full-width configs (bounded token counts for the CPU oracle), loop 1, teacher forced."""
-    cfg, spec, n = full_config(name, tokens)
+@pytest.mark.parametrize("name,tokens,engine,activation", [
+    ("cfg2", None, "tcgen05", "gelu"), ("cfg2", None, "simt", "gelu"), ("cfg3", 512, "tcgen05", "gelu"),
+    ("cfg4", 128, "tcgen05", "gelu"), ("cfg5", 64, "tcgen05", "gelu"), ("cfg5", 64, "simt", "gelu"),
+    ("cfg2", None, "tcgen05", "swiglu"), ("cfg2", None, "simt", "swiglu"), ("cfg3", 512, "tcgen05", "swiglu"),
+    ("cfg4", 128, "tcgen05", "swiglu"), ("cfg4", 128, "simt", "swiglu"), ("cfg5", 64, "tcgen05", "swiglu"),
+    ("cfg5", 64, "simt", "swiglu")])
+def test_full_size_config_one_loop(name, tokens, engine, activation, cuda_device):
+    """Full-width configs (bounded token counts for the CPU oracle), loop 1, teacher forced;
+    the reference's GELU FFN and the SwiGLU mode (gate weights expert_gates.*) in bf16, fp8
+    and int4 on both engines."""
+    cfg, spec, n = full_config(name, tokens, activation)
     zipf = 1.1 if spec["zipf"] else None
     sd = synth.synthetic_state_dict(cfg, seed=0, device=cuda_device, zipf=zipf, round_bf16=True)
     wf = spec["wfmt"]
@@ -115,12 +120,13 @@ def test_full_size_config_one_loop(name, tokens, engine, cuda_device):
                       engine=engine)
     sd_cpu = {k: v.cpu() for k, v in sd.items()}
     p = O.params_from_state_dict(sd_cpu, cfg.num_experts)
-    if wf == "fp8":
-        p.w_up = (eng.t["w_up"].view(torch.float8_e4m3fn).float() * eng.t["s_up"].unsqueeze(-1)).cpu()
-        p.w_down = (eng.t["w_down"].view(torch.float8_e4m3fn).float() * eng.t["s_down"].unsqueeze(-1)).cpu()
-    if wf == "int4":
-        p.w_up = O.dequantize_int4(eng.t["w_up"].cpu(), eng.t["s_up"].float().cpu(), 128)
-        p.w_down = O.dequantize_int4(eng.t["w_down"].cpu(), eng.t["s_down"].float().cpu(), 128)
+    for short in ["up", "down"] + (["gate"] if activation == "swiglu" else []):
+        if wf == "fp8":
+            setattr(p, "w_" + short, (eng.t["w_" + short].view(torch.float8_e4m3fn).float()
+                                      * eng.t["s_" + short].unsqueeze(-1)).cpu())
+        if wf == "int4":
+            setattr(p, "w_" + short, O.dequantize_int4(eng.t["w_" + short].cpu(), eng.t["s_" + short].float().cpu(),
+                                                       128))
     h, x0 = synth.block_inputs(n, cfg.hidden_size, seed=1)
     h = h.to(torch.bfloat16).float()
     want = O.block_forward(p, h, h, 1, cfg)

@@ -95,6 +95,37 @@ def test_ep_owner_hot_expert_loops_row_tiles(cuda_device):
     assert rel_err(a, b) < 2e-2
 
 
+def test_reference_semantics_path_matches_block(cuda_device, monkeypatch):
+    """The drop-in layer's expert-parallel forward (route, this rank's experts,
+    SUM all-reduce, LayerNorm epilogue: all library calls) at a world of one
+    with expert parallelism forced on computes what the block computes."""
+    from spider_web_moe_b200 import expert_parallel as EPH
+    from spider_web_moe_b200.layer import SpiderMoELayer
+
+    spec = benchmark_configs()["cfg2"]
+    cfg = ModelConfig(**spec["model"]).validate()
+    n = 24
+    sd = synth.synthetic_state_dict(cfg, seed=47, device="cpu", round_bf16=True)
+    layer = SpiderMoELayer(cfg)
+    layer.load_state_dict(sd, strict=False)
+    layer = layer.to(cuda_device).eval()
+    full = BlockEngine(cfg, {k: v.to(cuda_device) for k, v in sd.items()}, cuda_device, act_dtype=torch.bfloat16,
+                       max_tokens=n)
+    calls = []
+    monkeypatch.setattr(EPH, "ep_enabled", lambda: True)
+    monkeypatch.setattr(EPH, "get_rank_world", lambda: (0, 1))
+    monkeypatch.setattr(EPH, "all_reduce_sum_", lambda t: calls.append(t.shape) or t)
+    h, _ = synth.block_inputs(n, cfg.hidden_size, seed=48, device=cuda_device, dtype=torch.bfloat16)
+    h = h.view(1, n, -1)
+    for l in range(2):
+        got = layer(h, h, l)
+        want = full.forward(h, h, l, l + 1)
+        torch.cuda.synchronize()
+        assert rel_err(got, want) < 2e-2, f"loop {l}"
+        h = want
+    assert len(calls) == 2 and calls[0] == (n, cfg.hidden_size)
+
+
 def free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

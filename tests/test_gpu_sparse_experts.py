@@ -60,3 +60,32 @@ def test_bf16_tcgen05(cuda_device):
     assert got.dtype == torch.bfloat16
     want = O.expert_delta(msgs.float(), ti, tw, *[x.float() for x in w], e)
     assert rel_err(got, want) < 2e-2
+
+
+def test_new_weights_are_never_served_from_a_stale_engine(cuda_device):
+    """The engine cache must not reuse packed weights for different tensors:
+    weights freed and reallocated (the caching allocator tends to hand back the
+    same addresses, at version 0), weights changed in place, and the same
+    weights called with another top_k each give the oracle's result."""
+    n, h, e, u = 12, 32, 4, 64
+    g = torch.Generator().manual_seed(9)
+    msgs = torch.randn(1, n, h, generator=g)
+    tw, ti = torch.randn(1, n, e, generator=g).softmax(-1).topk(2, -1)
+    tw = tw / tw.sum(-1, keepdim=True)
+    md, tid, twd = msgs.to(cuda_device), ti.to(cuda_device), tw.to(cuda_device)
+    for seed in (10, 11, 12):  # a fresh set of device weights each time, the old set freed
+        w = weights(e, u, h, seed)
+        dev = [x.to(cuda_device) for x in w]
+        got = sparse_expert_delta(md, tid, twd, *dev, num_experts=e, top_k=2)
+        assert rel_err(got, O.expert_delta(msgs, ti, tw, *w, e)) < 1e-5, f"weights of seed {seed}"
+        del dev, got
+    w = weights(e, u, h, 13)
+    dev = [x.to(cuda_device) for x in w]
+    sparse_expert_delta(md, tid, twd, *dev, num_experts=e, top_k=2)
+    dev[0].mul_(2.0)  # in place: same address, new version
+    w[0] = w[0] * 2.0
+    got = sparse_expert_delta(md, tid, twd, *dev, num_experts=e, top_k=2)
+    assert rel_err(got, O.expert_delta(msgs, ti, tw, *w, e)) < 1e-5, "in-place update"
+    t1w, t1i = tw[..., :1] / tw[..., :1], ti[..., :1].contiguous()
+    got = sparse_expert_delta(md, t1i.to(cuda_device), t1w.contiguous().to(cuda_device), *dev, num_experts=e, top_k=1)
+    assert rel_err(got, O.expert_delta(msgs, t1i, t1w, *w, e)) < 1e-5, "another top_k"

@@ -1,13 +1,16 @@
 """sb_group_noalloc: the grouping entry point that allocates nothing.
 
 Some callers cannot allocate device memory -- a thin binding that only passes
-on pointers it was given, or code running while a stream is being captured --
-so they cannot supply the workspace sb_group needs.  sb_group_noalloc keeps
-its scratch in a fixed device array inside the library instead.  This test
-calls it through the C ABI twice in a row (different inputs, so the second
-call runs over the first call's leftovers in the shared array) and checks each
-result against sb_group with a caller workspace: the permutation is integer
-work and must match exactly, the summed weights too (same kernel, same order).
+on pointers it was given, or a process whose device memory another allocator's
+pool has reserved -- so they cannot supply the workspace sb_group needs.
+sb_group_noalloc keeps its scratch in a fixed device array inside the library
+instead.  This test calls it through the C ABI twice in a row (different
+inputs, so the second call runs over the first call's leftovers in the shared
+array) and checks each result against sb_group with a caller workspace.  At
+these sizes the two are different kernels (sb_group takes its multi-CTA
+two-pass path, sb_group_noalloc the single-CTA one), but both sum a token's
+weights in slot order in the same helper, so the permutation (integer work)
+and the summed weights must both match exactly.
 
 The file name sorts last so that a run stopping at the first failure has run
 every other test before this one; it also passes alone in a fresh process.
