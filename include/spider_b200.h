@@ -235,6 +235,12 @@ typedef struct sb_block_weights {
   const void* w_gate; const void* s_gate; const float* b_gate; /* SwiGLU only */
   const void* w_down; const void* s_down; const float* b_down; /* [E, H, U] */
   const float* ln_w;  const float* ln_b;                       /* norm.{weight,bias} */
+  /* Optional [E + E*E, H] act dtype: the router rows followed by gen_w's rows
+   * in one buffer (router_w == route_w and gen_w == route_w + E*H then).  Given
+   * it, large batches compute every router and edge logit in one GEMM (the
+   * dense edge-generator product model.py:261-263 forms) instead of grouping
+   * tokens by selected source; NULL keeps the grouped route. */
+  const void* route_w;
 } sb_block_weights;
 
 /* Optional copies of the last executed loop's intermediates (any may be NULL). */

@@ -68,7 +68,7 @@ class BlockWeights(C.Structure):
         ("w_up", vp), ("s_up", vp), ("b_up", vp),
         ("w_gate", vp), ("s_gate", vp), ("b_gate", vp),
         ("w_down", vp), ("s_down", vp), ("b_down", vp),
-        ("ln_w", vp), ("ln_b", vp),
+        ("ln_w", vp), ("ln_b", vp), ("route_w", vp),
     ]
 
 

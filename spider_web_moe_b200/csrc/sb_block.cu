@@ -146,6 +146,14 @@ struct BlockBuffers {
 
 static int max_splits_for(int n_tokens) { return n_tokens <= 512 ? 4 : 1; }
 
+// Columns of the dense routing logits (router + every source's edge logits),
+// or 0 for expert counts whose E*E logits are too wide to compute densely.
+constexpr int kDenseRouteMaxE = 32;
+static int64_t dense_route_cols(const sb_block_dims& d) {
+  const int64_t E = d.num_experts;
+  return E <= kDenseRouteMaxE ? E + E * E : 0;
+}
+
 static size_t carve_block(const sb_block_dims& d, int n_cap, void* base, size_t size, BlockBuffers* b) {
   Carver c(base, size);
   const int64_t N = n_cap, H = d.hidden, E = d.num_experts, K = d.top_k, M = d.edges_per_expert, U = d.ffn;
@@ -164,7 +172,7 @@ static size_t carve_block(const sb_block_dims& d, int n_cap, void* base, size_t 
   b->src_w = c.take<float>(N * K);
   b->src_inv = c.take<int32_t>(N * K);
   b->x_src = c.take<char>(N * K * H * as);
-  b->elog = c.take<float>(N * K * E);
+  b->elog = c.take<float>(N * (dense_route_cols(d) > K * E ? dense_route_cols(d) : K * E));
   b->edge_idx = c.take<int32_t>(N * K * M);
   b->edge_w = c.take<float>(N * K * M);
   b->dst_off = c.take<int32_t>(E + 1);
@@ -372,6 +380,24 @@ static bool use_fused_route(const sb_block_dims& d, int N) {
          route_edges_smem(d.act_dtype, d.hidden, d.num_experts, d.top_k) <= kRouteEdgesMaxSmem;
 }
 
+// Whether a batch of N tokens computes all router and edge logits with one
+// dense GEMM over the packed routing rows (then one selection kernel) instead
+// of the router, the source grouping and gather, the edge-logit GEMM over the
+// selected sources and the top-M kernel.  The dense product computes E / K
+// times the edge-logit FLOPs the selected sources need, so it is taken while
+// those FLOPs stay small next to the loop (here: at most 8 GFLOP, a few
+// microseconds of tensor time) and the batch is large enough for a GEMM.
+constexpr double kDenseRouteMaxFlops = 8e9;
+static bool use_dense_route(const sb_block_dims& d, const sb_block_weights* w, int N) {
+  const int64_t cols = dense_route_cols(d);
+  if (!w->route_w || !cols || d.engine == SB_ENGINE_SIMT || N < kRouterGemmMinTokens) return false;
+  if (w->router_w != w->route_w ||
+      static_cast<const char*>(w->gen_w) !=
+          static_cast<const char*>(w->route_w) + static_cast<int64_t>(d.num_experts) * d.hidden * act_size(d.act_dtype))
+    return false;
+  return 2.0 * N * cols * d.hidden <= kDenseRouteMaxFlops;
+}
+
 // `routed`: the fused route of this loop already ran (inside the previous
 // loop's LayerNorm kernel); steps 1-5 are skipped.
 static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBuffers& b, const void* cur, int N,
@@ -392,6 +418,21 @@ static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBu
     SB_TRY(route_edges(cur, d.act_dtype, N, H, w->router_w, w->loop_bias + static_cast<int64_t>(l) * E, E, K, w->gen_w,
                        w->gen_bias + static_cast<int64_t>(l) * E * E, M, b.top_idx, b.top_w, b.edge_idx, b.edge_w,
                        st));
+  } else if (use_dense_route(d, w, N)) {
+    // 1-5 as one GEMM of every router and edge logit ([N, E + E*E], biases
+    // added by the selection) and one selection kernel
+    StageScope sc_(0, st);
+    const int64_t cols = dense_route_cols(d);
+    sb_grouped_gemm_args a;
+    std::memset(&a, 0, sizeof(a));
+    a.engine = d.engine; a.wfmt = dense_fmt; a.act_dtype = d.act_dtype; a.epilogue = SB_EPI_LINEAR;
+    a.num_groups = 1; a.m_rows = static_cast<int>(cols); a.k = H; a.a_group_rows = cols; a.lda = H;
+    a.a_rows_total = cols; a.a = w->route_w; a.bias = nullptr; a.bias_group_stride = cols;
+    a.x = cur; a.ldx = H; a.max_rows = N; a.rows_hint = N; a.offsets = nullptr;
+    a.out = b.elog; a.ldo = cols; a.splits = 1; a.split_stride = 0; a.status = b.status;
+    SB_TRY(run_gemm(a, d.engine, st));
+    SB_TRY(select_dense(b.elog, cols, N, E, K, M, w->loop_bias + static_cast<int64_t>(l) * E,
+                        w->gen_bias + static_cast<int64_t>(l) * E * E, b.top_idx, b.top_w, b.edge_idx, b.edge_w, st));
   } else {
     // 1. router: large batches as a one-group GEMM (logits into the edge-logit
     // buffer, free until step 4) and a top-K kernel; small ones in one kernel

@@ -124,6 +124,14 @@ SB_DEVINL uint64_t global_ns() {
   return t;
 }
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far above any legitimate wait
+// A waiting thread spins this many polls before it starts to back off with
+// __nanosleep(SB_MBAR_SLEEP_NS) between polls (0: never sleeps).
+#ifndef SB_MBAR_SPINS_BEFORE_SLEEP
+#define SB_MBAR_SPINS_BEFORE_SLEEP 16
+#endif
+#ifndef SB_MBAR_SLEEP_NS
+#define SB_MBAR_SLEEP_NS 64
+#endif
 
 SB_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int err_bit,
                          uint64_t limit_ns = kWaitLimitNs) {
@@ -132,7 +140,7 @@ SB_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int err_bi
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (++spins > 16) __nanosleep(64);
+    if (++spins > SB_MBAR_SPINS_BEFORE_SLEEP && SB_MBAR_SLEEP_NS > 0) __nanosleep(SB_MBAR_SLEEP_NS);
     if ((spins & 255u) == 0 && global_ns() - t0 > limit_ns) {
       record_error(status, err_bit);
       return false;
@@ -246,7 +254,7 @@ SB_DEVINL bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* status, in
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
-    if (++spins > 16) __nanosleep(64);
+    if (++spins > SB_MBAR_SPINS_BEFORE_SLEEP && SB_MBAR_SLEEP_NS > 0) __nanosleep(SB_MBAR_SLEEP_NS);
     if ((spins & 255u) == 0 && global_ns() - t0 > limit_ns) {
       record_error(status, err_bit);
       return false;

@@ -777,6 +777,11 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
 // barrier.  fp8 / int4: loads count on the CTA's own barrier, its dequant warps
 // convert and then arrive on the leader's conversion barrier.
 // Warps as in the one-CTA kernel: 0-3, 6-9 epilogue, 4 TMA, 5 MMA, 10-13 dequant.
+// Shared memory for the pair kernel's pipeline stages.
+#ifndef SB_PAIR_STAGE_BUDGET
+#define SB_PAIR_STAGE_BUDGET (200 * 1024)
+#endif
+
 template <int BN, int WFMT, int EPI>
 struct PairCfg {
   static constexpr bool kGate = EPI == SB_EPI_SWIGLU;
@@ -786,7 +791,7 @@ struct PairCfg {
   static constexpr int kBBytes = kBH * kTcBK * 2;
   static constexpr int kRawBytes = WFMT == SB_W_FP8 ? kTcBM * kTcBK : (WFMT == SB_W_INT4 ? kTcBM * kTcBK / 2 : 0);
   static constexpr int kStageBytes = kABytes * (kGate ? 2 : 1) + kBBytes + kRawBytes * (kGate ? 2 : 1);
-  static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
+  static constexpr int kStagesRaw = (SB_PAIR_STAGE_BUDGET) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
   static constexpr int kAccCols = BN * (kGate ? 2 : 1);
   static constexpr int kTmemCols = 2 * kAccCols;

@@ -149,6 +149,14 @@ int derived_group_launch(int mode, const void* rows, int64_t pitch, int64_t meta
 int router_from_logits(const float* logits, int ld, int splits, int64_t split_stride, int n_tokens, int E, int K,
                        int32_t* top_idx, float* top_w, cudaStream_t st);
 
+// Router + edge top-M of one token per warp from one row of dense logits
+// [n_tokens, ld] (sb_router.cu): columns [0, E) the router logits, then the
+// E x E edge logits of every source (s*E + d), all before their biases
+// (rbias [E], gbias [E*E], added here in fp32).
+int select_dense(const float* logits, int64_t ld, int n_tokens, int E, int K, int M, const float* rbias,
+                 const float* gbias, int32_t* top_idx, float* top_w, int32_t* edge_idx, float* edge_w,
+                 cudaStream_t st);
+
 // Device properties cached per device.
 int current_sm_count();
 int current_cc_major();

@@ -207,6 +207,63 @@ int router_from_logits(const float* logits, int ld, int splits, int64_t split_st
                 st, logits, ld, splits, split_stride, n_tokens, E, K, top_idx, top_w);
 }
 
+// Router and edge graph of one token per warp from its dense logits row: the
+// E router logits (+ loop_bias[l]: softmax, top-K, renormalisation,
+// spider_moe/model.py:254-258), then for each selected source s in router
+// slot order its E edge logits (columns E + s*E .., + the folded generator
+// bias: top-M and softmax, model.py:260-266).  The biases are added in fp32
+// after the GEMM's product sum, as F.linear adds them.
+__global__ void __launch_bounds__(kRouterWarps * 32)
+select_dense_kernel(const float* __restrict__ logits, int64_t ld, int n_tokens, int E, int K, int M,
+                    const float* __restrict__ rbias, const float* __restrict__ gbias, int32_t* __restrict__ top_idx,
+                    float* __restrict__ top_w, int32_t* __restrict__ edge_idx, float* __restrict__ edge_w) {
+  __shared__ float srow[kRouterWarps][kRouterMaxE];
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * kRouterWarps + warp; t < n_tokens;
+       t += static_cast<int64_t>(gridDim.x) * kRouterWarps) {
+    const float* row = logits + t * ld;
+    for (int e = lane; e < E; e += 32) srow[warp][e] = row[e] + rbias[e];
+    __syncwarp();
+    int sel_i;
+    float sel_w;
+    router_select(srow[warp], E, K, lane, nullptr, sel_i, sel_w);
+    if (lane < K) {
+      top_idx[t * K + lane] = sel_i;
+      top_w[t * K + lane] = sel_w;
+    }
+    for (int k = 0; k < K; ++k) {
+      const int s = __shfl_sync(0xffffffffu, sel_i, k);
+      __syncwarp();  // every lane is done reading the previous row of srow
+      const float* src = row + E + static_cast<int64_t>(s) * E;
+      const float* bias = gbias + static_cast<int64_t>(s) * E;
+      for (int e = lane; e < E; e += 32) srow[warp][e] = src[e] + bias[e];
+      __syncwarp();
+      int m_i;
+      float m_w;
+      topm_select(srow[warp], E, M, lane, m_i, m_w);
+      if (lane < M) {
+        edge_idx[(t * K + k) * M + lane] = m_i;
+        edge_w[(t * K + k) * M + lane] = m_w;
+      }
+    }
+    __syncwarp();
+  }
+}
+
+int select_dense(const float* logits, int64_t ld, int n_tokens, int E, int K, int M, const float* rbias,
+                 const float* gbias, int32_t* top_idx, float* top_w, int32_t* edge_idx, float* edge_w,
+                 cudaStream_t st) {
+  if (n_tokens <= 0) return SB_OK;
+  if (E > kRouterMaxE || K > 32 || K > E || M > 32 || M > E || ld < E + static_cast<int64_t>(E) * E) return SB_ERR_ARG;
+  int blocks = (n_tokens + kRouterWarps - 1) / kRouterWarps;
+  const int cap = 8 * current_sm_count();
+  blocks = blocks > cap ? cap : blocks;
+  return launch(select_dense_kernel, dim3(blocks), dim3(kRouterWarps * 32), 0, st, logits, ld, n_tokens, E, K, M,
+                rbias, gbias, top_idx, top_w, edge_idx, edge_w);
+}
+
 // One warp per permuted (token, source) row: top-M over E destination logits.
 __global__ void __launch_bounds__(256)
 edge_topm_kernel(const float* __restrict__ logits, int64_t ld, int E, int M,

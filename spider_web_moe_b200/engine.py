@@ -5,9 +5,11 @@ spider_moe/model.py:165-216) into the layouts the kernels read, owns the
 workspace, and runs loops of the block through ``sb_block_forward``.  Packed
 layouts in HBM:
 
-* router ``[E, H]``, edge-generator hidden part ``[E*E, H]``, edge values
-  ``[E, H, H]`` -- all in the activation dtype, row-major, i.e. each weight
-  row is one K-major MMA operand row;
+* routing weights ``[E + E*E, H]``: the router rows followed by the hidden
+  part of the edge generator's rows (one tensor, so a large batch computes
+  every router and edge logit in one GEMM), and edge values ``[E, H, H]`` --
+  all in the activation dtype, row-major, i.e. each weight row is one K-major
+  MMA operand row;
 * per-loop edge-generator bias ``[L, E*E]`` fp32: the generator bias plus the
   loop-embedding columns applied to ``loop_embedding[l]``, folded once at
   packing time (the loop embedding is constant per loop, model.py:260-263);
@@ -74,10 +76,9 @@ class BlockEngine:
         self.t = {}
         t = self.t
         if "router.weight" in state:  # experts-only engines (sparse_expert_delta) skip the dense parts
-            t["router_w"] = g("router.weight").to(dt).contiguous()
             t["loop_bias"] = g("loop_bias").to(f32).contiguous()
             gen_full = g("edge_generator.weight").to(f32)
-            t["gen_w"] = gen_full[:, :H].to(dt).contiguous()
+            t["route_w"] = torch.cat([g("router.weight").to(dt), gen_full[:, :H].to(dt)]).contiguous()
             emb = g("loop_embedding.weight").to(f32)                  # [L, Le]
             t["gen_bias"] = (g("edge_generator.bias").to(f32).unsqueeze(0)
                              + emb @ gen_full[:, H:].t()).contiguous()  # [L, E*E]
@@ -125,8 +126,11 @@ class BlockEngine:
             engine=L.ENGINES[engine], max_tokens=int(max_tokens),
             residual_scale=float(cfg.residual_scale), reinject=float(cfg.re_inject_weight), ln_eps=1e-5)
         p = lambda k: t[k].data_ptr() if k in t else None  # noqa: E731
+        rw = t.get("route_w")
+        gen_ptr = rw[E:].data_ptr() if rw is not None else None
         self.weights = L.BlockWeights(
-            router_w=p("router_w"), loop_bias=p("loop_bias"), gen_w=p("gen_w"), gen_bias=p("gen_bias"),
+            router_w=p("route_w"), loop_bias=p("loop_bias"), gen_w=gen_ptr, gen_bias=p("gen_bias"),
+            route_w=p("route_w"),
             edge_w=p("edge_w"), w_up=p("w_up"), s_up=p("s_up"), b_up=p("b_up"), w_gate=p("w_gate"),
             s_gate=p("s_gate"), b_gate=p("b_gate"), w_down=p("w_down"), s_down=p("s_down"),
             b_down=p("b_down"), ln_w=p("ln_w"), ln_b=p("ln_b"))

@@ -115,7 +115,8 @@ def test_benchmark_workload_all_loops_at_full_size(name, activation, cuda_device
     for loop in range(cfg.num_loops):
         cur, nt = check_workload_loop(eng, cfg, p, cur, h, loop, rows, tol, f"{name}/{activation}")
         ties += nt
-    assert ties <= rows.numel() // 50, f"{ties} tie rows: the tie rule would hide real mismatches"
+    checked = rows.numel() * cfg.num_loops
+    assert ties <= checked // 50, f"{ties} of {checked} rows are ties: the tie rule would hide real mismatches"
 
 
 def test_full_size_graph_replay_matches_eager(cuda_device):
