@@ -59,7 +59,16 @@ enum { SB_ACT_GELU = 0, SB_ACT_SWIGLU = 1 };
 enum {
   SB_EPI_LINEAR = 0, /* out_f32[row, m] = (acc + bias[m]) * row_scale[row]  (bias, scale optional) */
   SB_EPI_GELU = 1,   /* out_act[row, m] = gelu_erf(acc + bias[m])                             */
-  SB_EPI_SWIGLU = 2  /* out_act[row, m] = silu(acc_gate + bias_gate[m]) * (acc + bias[m])      */
+  SB_EPI_SWIGLU = 2, /* out_act[row, m] = silu(acc_gate + bias_gate[m]) * (acc + bias[m])      */
+  /* SwiGLU with the gate and up rows of one weight tensor a, interleaved in
+   * blocks of 64: rows [128 b, 128 b + 64) are the gate rows of output
+   * features [64 b, 64 b + 64) and rows [128 b + 64, 128 b + 128) their up
+   * rows (scales and biases interleaved the same way).  m_rows counts the
+   * interleaved rows (a multiple of 128); the output has m_rows / 2 features:
+   * out_act[row, f] = silu(acc[gate row of f] + bias) * (acc[up row of f] + bias).
+   * One MMA operand covers both halves, so the tensor core runs its widest
+   * tiles on SwiGLU as on the other epilogues.  a_gate is not used. */
+  SB_EPI_SWIGLU_IL = 3
 };
 /* GEMM engines */
 enum { SB_ENGINE_AUTO = 0, SB_ENGINE_SIMT = 1, SB_ENGINE_TCGEN05 = 2 };
@@ -232,7 +241,10 @@ typedef struct sb_block_weights {
   const float* gen_bias;  /* [L, E*E] edge_generator.bias + weight[:, H:] . loop_embedding[l] */
   const void* edge_w;     /* [E, H, H] act dtype            edge_value.{d}.weight   */
   const void* w_up;   const void* s_up;   const float* b_up;   /* [E, U, H] */
-  const void* w_gate; const void* s_gate; const float* b_gate; /* SwiGLU only */
+  /* SB_ACT_SWIGLU: w_up / s_up / b_up hold the gate and up projections
+   * interleaved as SB_EPI_SWIGLU_IL describes ([E, 2U, H]); the w_gate fields
+   * are not used and may be NULL. */
+  const void* w_gate; const void* s_gate; const float* b_gate;
   const void* w_down; const void* s_down; const float* b_down; /* [E, H, U] */
   const float* ln_w;  const float* ln_b;                       /* norm.{weight,bias} */
   /* Optional [E + E*E, H] act dtype: the router rows followed by gen_w's rows

@@ -26,7 +26,7 @@ SB_DEVERR_BAD_INDEX, SB_DEVERR_DRAIN, SB_DEVERR_PEER_WAIT = 16, 32, 64
 SB_F32, SB_BF16 = 0, 1
 SB_W_F32, SB_W_BF16, SB_W_FP8, SB_W_INT4 = 0, 1, 2, 3
 SB_ACT_GELU, SB_ACT_SWIGLU = 0, 1
-SB_EPI_LINEAR, SB_EPI_GELU, SB_EPI_SWIGLU = 0, 1, 2
+SB_EPI_LINEAR, SB_EPI_GELU, SB_EPI_SWIGLU, SB_EPI_SWIGLU_IL = 0, 1, 2, 3
 SB_ENGINE_AUTO, SB_ENGINE_SIMT, SB_ENGINE_TCGEN05 = 0, 1, 2
 SB_GROUP_POSITIVE_ONLY = 1
 

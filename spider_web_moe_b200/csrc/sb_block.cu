@@ -250,13 +250,16 @@ static int pick_splits(int m_rows, int k, int rows_hint, int groups, int max_spl
   return s;
 }
 
+// The up projection of a SwiGLU block reads the gate and up rows interleaved
+// in one tensor (SB_EPI_SWIGLU_IL: 2 * ffn rows per expert); the w_gate
+// fields of the block weights are not used.
 static void fill_expert_gemm(sb_grouped_gemm_args& a, const sb_block_dims& d, bool up, const void* w,
-                             const void* sc, const float* bias, const void* wg, const void* sg, const float* bg) {
+                             const void* sc, const float* bias, const void*, const void*, const float*) {
   std::memset(&a, 0, sizeof(a));
   a.engine = d.engine;
   a.wfmt = d.wfmt;
   a.act_dtype = d.act_dtype;
-  a.m_rows = up ? d.ffn : d.hidden;
+  a.m_rows = up ? (d.activation == SB_ACT_SWIGLU ? 2 * d.ffn : d.ffn) : d.hidden;
   a.k = up ? d.hidden : d.ffn;
   a.group_size = d.group_size;
   a.lda = a.k;
@@ -264,10 +267,7 @@ static void fill_expert_gemm(sb_grouped_gemm_args& a, const sb_block_dims& d, bo
   a.a_rows_total = static_cast<int64_t>(d.num_experts) * a.m_rows;
   a.a = w;
   a.a_scale = sc;
-  a.a_gate = wg;
-  a.a_gate_scale = sg;
   a.bias = bias;
-  a.bias_gate = bg;
   a.bias_group_stride = a.m_rows;
 }
 
@@ -331,7 +331,7 @@ extern "C" SB_API int sb_grouped_gemm(const sb_grouped_gemm_args* args, void* st
       a.k <= 0 || a.lda < a.k ||
       a.ldx < a.k || a.max_rows < 0 || a.splits <= 0 || a.a_rows_total <= 0 ||
       (a.epilogue != SB_EPI_LINEAR && a.splits != 1) || (a.epilogue == SB_EPI_SWIGLU && !a.a_gate) ||
-      (a.wfmt != SB_W_BF16 && a.wfmt != SB_W_F32 && !a.a_scale) || a.epilogue < 0 || a.epilogue > 2)
+      (a.wfmt != SB_W_BF16 && a.wfmt != SB_W_F32 && !a.a_scale) || a.epilogue < 0 || a.epilogue > 3)
     return SB_ERR_ARG;
   if (a.max_rows == 0) return SB_OK;
   sb_grouped_gemm_args c = a;
@@ -531,7 +531,7 @@ static int check_block_args(const sb_block_dims& d, const sb_block_weights* w, b
   if (need_dense && (!w->router_w || !w->loop_bias || !w->gen_w || !w->gen_bias || !w->edge_w || !w->ln_w || !w->ln_b))
     return SB_ERR_ARG;
   if (need_experts && (!w->w_up || !w->b_up || !w->w_down || !w->b_down ||
-                       (d.activation == SB_ACT_SWIGLU && (!w->w_gate || !w->b_gate)) ||
+                       (d.activation == SB_ACT_SWIGLU && d.ffn % 64) ||
                        ((d.wfmt == SB_W_FP8 || d.wfmt == SB_W_INT4) && (!w->s_up || !w->s_down))))
     return SB_ERR_ARG;
   return SB_OK;
@@ -578,7 +578,7 @@ extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block
     {
       sb_grouped_gemm_args a;
       fill_expert_gemm(a, d, true, w->w_up, w->s_up, w->b_up, w->w_gate, w->s_gate, w->b_gate);
-      a.epilogue = d.activation == SB_ACT_SWIGLU ? SB_EPI_SWIGLU : SB_EPI_GELU;
+      a.epilogue = d.activation == SB_ACT_SWIGLU ? SB_EPI_SWIGLU_IL : SB_EPI_GELU;
       a.num_groups = E; a.x = b.x_ffn; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N;
       a.offsets = b.ffn_off; a.out = b.act; a.ldo = U; a.splits = 1; a.status = b.status;
       const bool gather = gemm_gathers(a, d.engine);
@@ -746,7 +746,7 @@ static int expert_rows_impl(const sb_block_dims* dims, const sb_block_weights* w
   {
     sb_grouped_gemm_args a;
     fill_expert_gemm(a, d, true, w->w_up, w->s_up, w->b_up, w->w_gate, w->s_gate, w->b_gate);
-    a.epilogue = d.activation == SB_ACT_SWIGLU ? SB_EPI_SWIGLU : SB_EPI_GELU;
+    a.epilogue = d.activation == SB_ACT_SWIGLU ? SB_EPI_SWIGLU_IL : SB_EPI_GELU;
     a.num_groups = G; a.x = b.x_ffn; a.ldx = H; a.max_rows = N * K; a.rows_hint = hint; a.group_rows_bound = row_plan;
     a.offsets = b.ffn_off; a.out = b.act; a.ldo = U; a.splits = 1; a.status = b.status;
     sb_grouped_gemm_args g = a;
@@ -844,7 +844,7 @@ extern "C" SB_API int sb_expert_delta(const sb_block_dims* dims, const sb_block_
     sb_grouped_gemm_args a;
     fill_expert_gemm(a, d, true, w->w_up, w->s_up, w->b_up, w->w_gate, w->s_gate, w->b_gate);
     shard_expert_gemm(a, d, rank, world);
-    a.epilogue = d.activation == SB_ACT_SWIGLU ? SB_EPI_SWIGLU : SB_EPI_GELU;
+    a.epilogue = d.activation == SB_ACT_SWIGLU ? SB_EPI_SWIGLU_IL : SB_EPI_GELU;
     a.num_groups = G; a.x = b.x_ffn; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N;
     a.offsets = b.ffn_off; a.out = b.act; a.ldo = U; a.splits = 1; a.status = b.status;
     if (gemm_gathers(a, d.engine)) {

@@ -168,6 +168,40 @@ SB_DEVINL void tma_load_2d(void* smem_dst, const void* desc, uint64_t* bar, int 
       : "memory");
 }
 
+// Named barrier over `threads` threads (whole warps) of the CTA; id 0 is __syncthreads.
+SB_DEVINL void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Named barrier that also ANDs a predicate over its threads (all of them get the result).
+SB_DEVINL bool named_bar_and(int id, int threads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(threads)
+      : "memory");
+  return r != 0;
+}
+
+// 2-D tiled bulk tensor store of a shared-memory box to global memory (the
+// box's rows are the tensor's rows, no swizzle), committed as one bulk group.
+SB_DEVINL void tma_store_2d(const void* desc, const void* smem_src, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(desc)),
+      "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+      : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until this thread's committed bulk stores finished reading shared memory.
+SB_DEVINL void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until this thread's committed bulk stores are complete.
+SB_DEVINL void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // ---------------------------------------------------------------- tcgen05
 SB_DEVINL void tmem_alloc(uint32_t* smem_slot, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),

@@ -37,7 +37,10 @@ SB_DEVINL float row_scale_of(const sb_grouped_gemm_args& p, const void* scale, i
   return p.wfmt == SB_W_FP8 ? static_cast<const float*>(scale)[row] : 1.f;
 }
 
-template <bool kGate>
+// kIL: interleaved SwiGLU (SB_EPI_SWIGLU_IL) -- a CTA's 64 output features
+// have their gate rows at 128 * (m0 / 64) .. + 63 of the group and their up
+// rows 64 further; both come from `a`.
+template <bool kGate, bool kIL = false>
 __global__ void __launch_bounds__(kSimtThreads)
 simt_gemm_kernel(const sb_grouped_gemm_args p) {
   __shared__ float As[kSimtBK][kSimtBM + 4];
@@ -63,7 +66,12 @@ simt_gemm_kernel(const sb_grouped_gemm_args p) {
   const int m0 = blockIdx.x * kSimtBM;
   const int ks = p.k / p.splits;
   const int kb = blockIdx.z * ks, ke = (blockIdx.z == p.splits - 1) ? p.k : kb + ks;
-  const int64_t arow0 = static_cast<int64_t>(g) * p.a_group_rows + m0;
+  const int m_out = kIL ? p.m_rows / 2 : p.m_rows;   // output features
+  const int lrow0 = kIL ? 2 * m0 + 64 : m0;          // group-local row of feature m0 (the up row)
+  const int64_t arow0 = static_cast<int64_t>(g) * p.a_group_rows + lrow0;
+  const int64_t grow0 = kIL ? arow0 - 64 : arow0;    // its gate row (interleaved layout)
+  const void* gate_w = kIL ? p.a : p.a_gate;
+  const void* gate_s = kIL ? p.a_scale : p.a_gate_scale;
 
   const int tx = tid % 16, ty = tid / 16;  // rows n = 2*tx + j, features m = 4*ty + i
   float acc[4][2] = {}, accg[4][2] = {};
@@ -71,9 +79,9 @@ simt_gemm_kernel(const sb_grouped_gemm_args p) {
     for (int i = tid; i < kSimtBM * kSimtBK; i += kSimtThreads) {
       const int mm = i / kSimtBK, kk = i % kSimtBK;
       const int64_t row = arow0 + mm;
-      const bool ok = (m0 + mm) < p.m_rows && row < p.a_rows_total && (k0 + kk) < ke;
+      const bool ok = (m0 + mm) < m_out && row < p.a_rows_total && (k0 + kk) < ke;
       As[kk][mm] = ok ? load_weight(p, p.a, p.a_scale, row, k0 + kk) : 0.f;
-      if (kGate) Gs[kk][mm] = ok ? load_weight(p, p.a_gate, p.a_gate_scale, row, k0 + kk) : 0.f;
+      if (kGate) Gs[kk][mm] = ok ? load_weight(p, gate_w, gate_s, grow0 + mm, k0 + kk) : 0.f;
     }
     for (int i = tid; i < kSimtBN * kSimtBK; i += kSimtThreads) {
       const int nn = i / kSimtBK, kk = i % kSimtBK;
@@ -109,10 +117,11 @@ simt_gemm_kernel(const sb_grouped_gemm_args p) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int m = m0 + 4 * ty + i;
-    if (m >= p.m_rows) continue;
+    if (m >= m_out) continue;
     const int64_t row = arow0 + 4 * ty + i;
+    const int lrow = lrow0 + 4 * ty + i;  // group-local weight row (bias index)
     const float sa = row_scale_of(p, p.a_scale, row);
-    const float bias = (p.bias && blockIdx.z == 0) ? p.bias[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
+    const float bias = (p.bias && blockIdx.z == 0) ? p.bias[static_cast<int64_t>(g) * p.bias_group_stride + lrow] : 0.f;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const int r = n0 + 2 * tx + j;
@@ -126,8 +135,9 @@ simt_gemm_kernel(const sb_grouped_gemm_args p) {
         if (p.epilogue == SB_EPI_GELU) {
           o = gelu_erf(v);
         } else {
-          const float sg = row_scale_of(p, p.a_gate_scale, row);
-          const float bg = p.bias_gate ? p.bias_gate[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
+          const float sg = row_scale_of(p, gate_s, grow0 + 4 * ty + i);
+          const float* gb = kIL ? p.bias : p.bias_gate;
+          const float bg = gb ? gb[static_cast<int64_t>(g) * p.bias_group_stride + (kIL ? lrow - 64 : m)] : 0.f;
           o = silu(accg[i][j] * sg + bg) * v;
         }
         if (p.act_dtype == SB_F32)
@@ -140,9 +150,12 @@ simt_gemm_kernel(const sb_grouped_gemm_args p) {
 }
 
 int gemm_simt(const sb_grouped_gemm_args& a, cudaStream_t st) {
-  const int m_tiles = (a.m_rows + kSimtBM - 1) / kSimtBM;
+  const bool il = a.epilogue == SB_EPI_SWIGLU_IL;
+  if (il && a.m_rows % 128) return SB_ERR_UNSUPPORTED;
+  const int m_tiles = ((il ? a.m_rows / 2 : a.m_rows) + kSimtBM - 1) / kSimtBM;
   const int n_slots = (a.max_rows + kSimtBN - 1) / kSimtBN + a.num_groups;
   const dim3 grid(m_tiles, n_slots, a.splits);
+  if (il) return launch(simt_gemm_kernel<true, true>, grid, dim3(kSimtThreads), 0, st, a);
   if (a.epilogue == SB_EPI_SWIGLU) return launch(simt_gemm_kernel<true>, grid, dim3(kSimtThreads), 0, st, a);
   return launch(simt_gemm_kernel<false>, grid, dim3(kSimtThreads), 0, st, a);
 }

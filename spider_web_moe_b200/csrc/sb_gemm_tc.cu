@@ -47,6 +47,10 @@ constexpr int kTcSmemBudgetLargeN = 200 * 1024;
 template <int BN, int WFMT, int EPI, bool kFixed>
 struct TcCfg {
   static constexpr bool kGate = EPI == SB_EPI_SWIGLU;
+  // interleaved SwiGLU: warps 0-1 (gate rows) hand silu(gate) to warps 2-3
+  // (up rows of the same features) through a 2 KB buffer per warp pair
+  static constexpr bool kIL = EPI == SB_EPI_SWIGLU_IL;
+  static constexpr int kXBytes = kIL ? 2 * 2048 : 0;
   static constexpr bool kConvert = WFMT != SB_W_BF16;
   static constexpr int kABytes = kTcBM * kTcBK * 2;                       // bf16 tile
   static constexpr int kBBytes = BN * kTcBK * 2;
@@ -69,7 +73,8 @@ struct TcCfg {
   // int4: the CTA's group scales (128 rows x up to 32 groups of its K range)
   static constexpr int kScaleBytes = WFMT == SB_W_INT4 ? 8192 : 0;
   static constexpr int kOffScale = kOffMisc + 64;
-  static constexpr int kSmemBytes = kOffScale + kScaleBytes + 1024;  // + alignment slack
+  static constexpr int kOffX = kOffScale + kScaleBytes;
+  static constexpr int kSmemBytes = kOffX + kXBytes + 1024;  // + alignment slack
   static_assert(kTmemCols <= 512, "TMEM holds 512 columns");
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "M=128 MMA needs N in [16, 256], N % 16 == 0");
 };
@@ -428,6 +433,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
       // tcgen05.ld is warp-collective: every lane must take the same branch.
       live = __all_sync(0xffffffffu, live && mbar_wait(acc_full, t & 1, p.status, SB_DEVERR_EPI_WAIT));
+      // interleaved SwiGLU: both warps of a (gate, up) pair take the same path
+      if (C::kIL) live = named_bar_and(1 + (warp & 1), 64, live);
       tc_fence_after();
       if (!live) break;
 #pragma unroll
@@ -436,6 +443,33 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         float v[16], vg[16], o[16];
         tmem_ld16(lane_addr + c0, v);
         if (C::kGate) tmem_ld16(lane_addr + BN + c0, vg);
+        if constexpr (C::kIL) {
+          // warps 0-1 hold the gate rows of the tile's 64 features, warps 2-3
+          // their up rows: silu(gate) goes across through shared memory
+          float* xb = reinterpret_cast<float*>(smem + C::kOffX) + (warp & 1) * 512;
+          if (warp < 2) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) xb[j * 32 + lane] = silu_bf16out(v[j] * sa + bias);
+            named_bar_sync(1 + (warp & 1), 64);  // values ready
+            named_bar_sync(1 + (warp & 1), 64);  // values taken
+            continue;
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = v[j] * sa + bias;
+          named_bar_sync(1 + (warp & 1), 64);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] *= xb[j * 32 + lane];
+          named_bar_sync(1 + (warp & 1), 64);
+          if (!mvalid) continue;
+          const int nvalid = tend - (tn0 + c0);
+          const int64_t base = static_cast<int64_t>(tn0 + c0) * p.ldo + m0 / 2 + (warp - 2) * 32 + lane;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            if (nvalid < 16 && j >= nvalid) break;
+            static_cast<__nv_bfloat16*>(p.out)[base + static_cast<int64_t>(j) * p.ldo] = __float2bfloat16_rn(o[j]);
+          }
+          continue;
+        }
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const float x = v[j] * sa + bias;
@@ -483,12 +517,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 template <int BN, int WFMT, int EPI>
 struct PCfg {
   static constexpr bool kGate = EPI == SB_EPI_SWIGLU;
+  static constexpr bool kIL = EPI == SB_EPI_SWIGLU_IL;  // four gate/up warp pairs, 2 KB each
+  static constexpr int kXBytes = kIL ? 4 * 2048 : 0;
   static constexpr bool kConvert = WFMT != SB_W_BF16;
   static constexpr int kABytes = kTcBM * kTcBK * 2;
   static constexpr int kBBytes = BN * kTcBK * 2;
   static constexpr int kRawBytes = WFMT == SB_W_FP8 ? kTcBM * kTcBK : (WFMT == SB_W_INT4 ? kTcBM * kTcBK / 2 : 0);
   static constexpr int kStageBytes = kABytes * (kGate ? 2 : 1) + kBBytes + kRawBytes * (kGate ? 2 : 1);
-  static constexpr int kStagesRaw = (212 * 1024) / kStageBytes;
+  static constexpr int kStagesRaw = (212 * 1024 - kXBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 6 ? 6 : (kStagesRaw < 2 ? 2 : kStagesRaw);
   static constexpr int kAccCols = BN * (kGate ? 2 : 1);
   static constexpr int kTmemCols = 2 * kAccCols;
@@ -504,7 +540,8 @@ struct PCfg {
   static constexpr int kOffPrefix = kOffMisc + 64;                  // int[kMaxG + 1]
   static constexpr int kMaxG = 256;
   static constexpr int kOffOffsets = kOffPrefix + (kMaxG + 1) * 4;  // int[kMaxG + 1]: group row offsets
-  static constexpr int kSmemBytes = kOffOffsets + (kMaxG + 1) * 4 + 1024;
+  static constexpr int kOffX = kOffOffsets + (kMaxG + 1) * 4;
+  static constexpr int kSmemBytes = kOffX + kXBytes + 1024;
   static_assert(kTmemCols <= 512, "two accumulators must fit the 512 TMEM columns");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 };
@@ -722,7 +759,11 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
         const int r = tn0 + i * 32 + lane;
         rsv[i] = (EPI == SB_EPI_LINEAR && p.row_scale && r < tend) ? p.row_scale[r] : 1.f;
       }
-      const bool ready = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (j >> 1) & 1, p.status, SB_DEVERR_EPI_WAIT));
+      bool ready = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (j >> 1) & 1, p.status, SB_DEVERR_EPI_WAIT));
+      // interleaved SwiGLU: quarters 0-1 hold gate rows, 2-3 the up rows of the
+      // same features; warp pair (quarter q, q + 2) of each column half
+      const int xpair = half * 2 + (quarter & 1);
+      if (C::kIL) ready = named_bar_and(1 + xpair, 64, ready);
       tc_fence_after();
       if (!ready) break;
       const uint32_t acc_addr = lane_addr + buf * C::kAccCols;
@@ -732,6 +773,31 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
         float v[16], vg[16], o[16];
         tmem_ld16(acc_addr + c0, v);
         if (C::kGate) tmem_ld16(acc_addr + BN + c0, vg);
+        if constexpr (C::kIL) {
+          float* xb = reinterpret_cast<float*>(smem + C::kOffX) + xpair * 512;
+          if (quarter < 2) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) xb[q * 32 + lane] = silu_bf16out(v[q] * sa + bias);
+            named_bar_sync(1 + xpair, 64);
+            named_bar_sync(1 + xpair, 64);
+            continue;
+          }
+#pragma unroll
+          for (int q = 0; q < 16; ++q) o[q] = v[q] * sa + bias;
+          named_bar_sync(1 + xpair, 64);
+#pragma unroll
+          for (int q = 0; q < 16; ++q) o[q] *= xb[q * 32 + lane];
+          named_bar_sync(1 + xpair, 64);
+          if (!mvalid) continue;
+          const int nvalid = tend - (tn0 + c0);
+          const int64_t base = static_cast<int64_t>(tn0 + c0) * p.ldo + mt * (kTcBM / 2) + (quarter - 2) * 32 + lane;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            if (nvalid < 16 && q >= nvalid) break;
+            static_cast<__nv_bfloat16*>(p.out)[base + static_cast<int64_t>(q) * p.ldo] = __float2bfloat16_rn(o[q]);
+          }
+          continue;
+        }
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
           const float x = v[q] * sa + bias;
@@ -785,16 +851,13 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
 template <int BN, int WFMT, int EPI>
 struct PairCfg {
   static constexpr bool kGate = EPI == SB_EPI_SWIGLU;
+  static constexpr bool kIL = EPI == SB_EPI_SWIGLU_IL;
   static constexpr bool kConvert = WFMT != SB_W_BF16;
   static constexpr int kBH = BN / 2;  // token rows of B per CTA
   static constexpr int kABytes = kTcBM * kTcBK * 2;
   static constexpr int kBBytes = kBH * kTcBK * 2;
   static constexpr int kRawBytes = WFMT == SB_W_FP8 ? kTcBM * kTcBK : (WFMT == SB_W_INT4 ? kTcBM * kTcBK / 2 : 0);
   static constexpr int kStageBytes = kABytes * (kGate ? 2 : 1) + kBBytes + kRawBytes * (kGate ? 2 : 1);
-  static constexpr int kStagesRaw = (SB_PAIR_STAGE_BUDGET) / kStageBytes;
-  static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
-  static constexpr int kAccCols = BN * (kGate ? 2 : 1);
-  static constexpr int kTmemCols = 2 * kAccCols;
   // epilogue warps: 0-3 and 6-9, and for bf16 weights also 10-17 (four per
   // TMEM lane quarter, each a quarter of the tile's columns: the GELU
   // epilogue of short-K tiles would otherwise outlast the next tile's MMAs);
@@ -802,28 +865,50 @@ struct PairCfg {
   static constexpr int kEpiWarps = kConvert ? 8 : 16;
   static constexpr int kConvWarps = 4;
   static constexpr int kThreads = kConvert ? 448 : 576;
+  // Output staging for the bulk (TMA) stores of the epilogue: 1 KB per
+  // epilogue warp, a box of 32 features x kStoreRows tokens (fp32: 8, bf16: 16).
+  // Interleaved SwiGLU: the gate warp of each (gate, up) warp pair hands
+  // silu(gate) to the up warp through a 2 KB buffer; only up warps store.
+  static constexpr int kOutBytes = EPI == SB_EPI_LINEAR ? 4 : 2;
+  static constexpr int kStoreRows = 1024 / (32 * kOutBytes);
+  static constexpr int kXBytes = kIL ? (kEpiWarps / 2) * 2048 : 0;
+  static constexpr int kStagingBytes = (kIL ? kEpiWarps / 2 : kEpiWarps) * 1024 + kXBytes;
+  static constexpr int kMaxG = 256;
+  static constexpr int kFixedBytes = (3 * 8 + 4) * 8 + 64 + 2 * (kMaxG + 1) * 4 + 1024;
+  static constexpr int kSmemMax = 227 * 1024;
+  static constexpr int kBudget = (SB_PAIR_STAGE_BUDGET) < kSmemMax - kStagingBytes - kFixedBytes
+                                     ? (SB_PAIR_STAGE_BUDGET) : kSmemMax - kStagingBytes - kFixedBytes;
+  static constexpr int kStagesRaw = kBudget / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
+  static constexpr int kAccCols = BN * (kGate ? 2 : 1);
+  static constexpr int kTmemCols = 2 * kAccCols;
   // B stages first: every operand read stays inside the allocation
   static constexpr int kOffB = 0;
   static constexpr int kOffA = kOffB + kStages * kBBytes;
   static constexpr int kOffG = kOffA + kStages * kABytes;
   static constexpr int kOffRaw = kOffG + (kGate ? kStages * kABytes : 0);
   static constexpr int kOffRawG = kOffRaw + kStages * kRawBytes;
-  static constexpr int kOffBar = kOffRawG + (kGate ? kStages * kRawBytes : 0);
+  static constexpr int kOffOut = kOffRawG + (kGate ? kStages * kRawBytes : 0);
+  static constexpr int kOffX = kOffOut + (kIL ? kEpiWarps / 2 : kEpiWarps) * 1024;
+  static constexpr int kOffBar = kOffOut + kStagingBytes;
   static constexpr int kOffMisc = kOffBar + (3 * kStages + 4) * 8;
   static constexpr int kOffPrefix = kOffMisc + 64;
-  static constexpr int kMaxG = 256;
   static constexpr int kOffOffsets = kOffPrefix + (kMaxG + 1) * 4;
   static constexpr int kSmemBytes = kOffOffsets + (kMaxG + 1) * 4 + 1024;
   static_assert(kTmemCols <= 512, "two accumulators must fit the 512 TMEM columns");
-  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+  static_assert(kSmemBytes <= kSmemMax, "shared memory per CTA");
   static_assert(kBBytes % 1024 == 0 && kABytes % 1024 == 0, "1024-byte aligned swizzled stages");
+  static_assert(kOffOut % 1024 == 0, "aligned output staging");
   static_assert(BN == 128 || BN == 256, "pair tiles are 128 or 256 tokens wide");
 };
 
+// tmO (when tma_out): the output [max_rows, m_rows] with a box of 32 features x
+// kStoreRows tokens; full 16-token chunks of 32 valid features leave through it.
 template <int BN, int WFMT, int EPI>
 __global__ void __launch_bounds__(PairCfg<BN, WFMT, EPI>::kThreads, 1)
 tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmG,
-                    const __grid_constant__ CUtensorMap tmB, const sb_grouped_gemm_args p) {
+                    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmO,
+                    const sb_grouped_gemm_args p, const int tma_out) {
   using C = PairCfg<BN, WFMT, EPI>;
   constexpr int S = C::kStages;
   constexpr int kPairM = 2 * kTcBM;
@@ -1013,8 +1098,10 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     constexpr int kParts = C::kEpiWarps / 4;
     constexpr int HB = BN / kParts;
     const int quarter = warp & 3;
-    const int half = (warp < 4 ? warp : warp - 2) >> 2;  // column part
+    const int ord = warp < 4 ? warp : warp - 2;  // 0 .. kEpiWarps - 1
+    const int half = ord >> 2;                   // column part
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + half * HB;
+    uint8_t* stage_out = smem + C::kOffOut + ord * 1024;
     for (int j = 0; j < my_tiles; ++j) {
       int g, nt, mt;
       decode_tile(prefix, G, m_tiles, pair + j * npairs, g, nt, mt);
@@ -1034,16 +1121,59 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         const int r = tn0 + i * 32 + lane;
         rsv[i] = (EPI == SB_EPI_LINEAR && p.row_scale && r < tend) ? p.row_scale[r] : 1.f;
       }
-      const bool ready = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (j >> 1) & 1, p.status, SB_DEVERR_EPI_WAIT));
+      bool ready = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (j >> 1) & 1, p.status, SB_DEVERR_EPI_WAIT));
+      // interleaved SwiGLU: quarters 0-1 hold gate rows, 2-3 the up rows of the
+      // same features; warp pair (quarter q, q + 2) of each column part
+      const int xpair = half * 2 + (quarter & 1);
+      if (C::kIL) ready = named_bar_and(1 + xpair, 64, ready);
       tc_fence_after();
       if (!ready) break;
       const uint32_t acc_addr = lane_addr + buf * C::kAccCols;
+      // bulk stores need all 32 features of the warp in range
+      const bool bulk = tma_out && __all_sync(0xffffffffu, mvalid);
 #pragma unroll
       for (int c0 = 0; c0 < HB; c0 += 16) {
         if (tn0 + c0 >= tend) break;  // warp-uniform
         float v[16], vg[16], o[16];
         tmem_ld16(acc_addr + c0, v);
         if (C::kGate) tmem_ld16(acc_addr + BN + c0, vg);
+        if constexpr (C::kIL) {
+          float* xb = reinterpret_cast<float*>(smem + C::kOffX) + xpair * 512;
+          if (quarter < 2) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) xb[q * 32 + lane] = silu_bf16out(v[q] * sa + bias);
+            named_bar_sync(1 + xpair, 64);
+            named_bar_sync(1 + xpair, 64);
+            continue;
+          }
+#pragma unroll
+          for (int q = 0; q < 16; ++q) o[q] = v[q] * sa + bias;
+          named_bar_sync(1 + xpair, 64);
+#pragma unroll
+          for (int q = 0; q < 16; ++q) o[q] *= xb[q * 32 + lane];
+          named_bar_sync(1 + xpair, 64);
+          const int fo0 = (mt * kPairM + static_cast<int>(rank) * kTcBM) / 2 + (quarter - 2) * 32;  // lane 0's feature
+          const int nvalid = tend - (tn0 + c0);
+          if (bulk && nvalid >= 16) {
+            uint8_t* so = smem + C::kOffOut + xpair * 1024;
+            if (lane == 0) tma_store_wait_read();
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 16; ++q) reinterpret_cast<__nv_bfloat16*>(so)[q * 32 + lane] = __float2bfloat16_rn(o[q]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) tma_store_2d(&tmO, so, fo0, tn0 + c0);
+            continue;
+          }
+          if (!mvalid) continue;
+          const int64_t base = static_cast<int64_t>(tn0 + c0) * p.ldo + fo0 + lane;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            if (nvalid < 16 && q >= nvalid) break;
+            static_cast<__nv_bfloat16*>(p.out)[base + static_cast<int64_t>(q) * p.ldo] = __float2bfloat16_rn(o[q]);
+          }
+          continue;
+        }
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
           const float x = v[q] * sa + bias;
@@ -1054,8 +1184,29 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           else
             o[q] = silu_bf16out(vg[q] * sg + bgate) * x;
         }
-        if (!mvalid) continue;
         const int nvalid = tend - (tn0 + c0);
+        if (bulk && nvalid >= 16) {
+          // a whole chunk: 32 features x 16 tokens through the staging box
+          // (token-major, as the output rows), then one bulk store per box
+#pragma unroll
+          for (int h = 0; h < 16 / C::kStoreRows; ++h) {
+            if (lane == 0) tma_store_wait_read();  // the previous box has left the buffer
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < C::kStoreRows; ++q) {
+              if (EPI == SB_EPI_LINEAR)
+                reinterpret_cast<float*>(stage_out)[q * 32 + lane] = o[h * C::kStoreRows + q];
+              else
+                reinterpret_cast<__nv_bfloat16*>(stage_out)[q * 32 + lane] =
+                    __float2bfloat16_rn(o[h * C::kStoreRows + q]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) tma_store_2d(&tmO, stage_out, m - lane, tn0 + c0 + h * C::kStoreRows);
+          }
+          continue;
+        }
+        if (!mvalid) continue;
         const int64_t base = static_cast<int64_t>(tn0 + c0) * p.ldo + m;
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
@@ -1070,6 +1221,8 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc_empty_lead + 8u * buf);
     }
+    if (lane == 0) tma_store_wait_all();  // every bulk store complete before the CTA leaves
+    __syncwarp();
   }
   __syncwarp();
   tc_fence_before();
@@ -1131,6 +1284,7 @@ bool tcgen05_supported(const sb_grouped_gemm_args& a) {
   if (a.ldx % 8 || (a.wfmt == SB_W_BF16 && a.lda % 8) || (a.wfmt != SB_W_BF16 && a.lda % 32)) return false;
   if (reinterpret_cast<uintptr_t>(a.a) % 16 || reinterpret_cast<uintptr_t>(a.x) % 16) return false;
   if (a.epilogue == SB_EPI_SWIGLU && (!a.a_gate || reinterpret_cast<uintptr_t>(a.a_gate) % 16)) return false;
+  if (a.epilogue == SB_EPI_SWIGLU_IL && a.m_rows % kTcBM) return false;  // whole 64-feature blocks
   if (a.a_rows_total > 0x7fffffffLL || a.max_rows <= 0) return false;
   if (a.x_row_index && (tc_tile_n(a) > 64 || a.x_rows <= 0)) return false;
   return current_cc_major() == 10;
@@ -1207,6 +1361,16 @@ static int launch_persistent(const sb_grouped_gemm_args& a, cudaStream_t st) {
   return launch(kern, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, ma, mg, mb, a);
 }
 
+// SPIDER_B200_TMA_STORE=0 makes the large-tile epilogues store element by
+// element instead of through shared memory and bulk tensor stores (for comparisons).
+static bool use_tma_out() {
+  static const bool enabled = [] {
+    const char* e = std::getenv("SPIDER_B200_TMA_STORE");
+    return !(e && e[0] == '0');
+  }();
+  return enabled;
+}
+
 // SPIDER_B200_PAIR=0 keeps large tiles on one-CTA tiles (for comparisons).
 static bool use_pair(const sb_grouped_gemm_args& a) {
   static const bool enabled = [] {
@@ -1261,13 +1425,23 @@ static int launch_pair(const sb_grouped_gemm_args& a, cudaStream_t st) {
   if (!make_map(&mb, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.k, a.max_rows, a.ldx * 2, kTcBK, C::kBH,
                 CU_TENSOR_MAP_SWIZZLE_128B))
     return SB_ERR_UNSUPPORTED;
+  // The output as a tensor for the epilogue's bulk stores: [max_rows, m_rows]
+  // with row pitch ldo (fp32 for LINEAR, else bf16); without one (an
+  // unaligned output) every element is stored by the epilogue threads.
+  CUtensorMap mo = mb;
+  const int out_cols = C::kIL ? a.m_rows / 2 : a.m_rows;  // interleaved SwiGLU: two rows per feature
+  const int tma_out = use_tma_out() && out_cols >= 32 &&
+                      make_map(&mo, a.out, EPI == SB_EPI_LINEAR ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                                : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                               out_cols, a.max_rows, a.ldo * C::kOutBytes, 32, C::kStoreRows,
+                               CU_TENSOR_MAP_SWIZZLE_NONE);
   const int m_tiles = (a.m_rows + 2 * kTcBM - 1) / (2 * kTcBM);
   const int64_t bound = static_cast<int64_t>(m_tiles) * ((a.max_rows + BN - 1) / BN + a.num_groups);
   const int pairs = static_cast<int>(bound < max_pairs ? bound : max_pairs);
   cfg.gridDim = dim3(2 * pairs);
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   note_launch();
-  return cuda_status(cudaLaunchKernelEx(&cfg, kern, ma, mg, mb, a));
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, ma, mg, mb, mo, a, tma_out));
 }
 
 template <int BN, int WFMT, int EPI>
@@ -1311,6 +1485,7 @@ static int launch_epi(const sb_grouped_gemm_args& a, cudaStream_t st, int bn) {
   switch (a.epilogue) {
     case SB_EPI_LINEAR: return launch_bn<WFMT, SB_EPI_LINEAR>(a, st, bn);
     case SB_EPI_GELU: return launch_bn<WFMT, SB_EPI_GELU>(a, st, bn);
+    case SB_EPI_SWIGLU_IL: return launch_bn<WFMT, SB_EPI_SWIGLU_IL>(a, st, bn);
     default: return launch_bn<WFMT, SB_EPI_SWIGLU>(a, st, bn);
   }
 }

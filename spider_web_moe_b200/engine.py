@@ -46,6 +46,25 @@ def stacked(sd: dict, fmt: str, e: int) -> torch.Tensor:
     return torch.stack([sd[fmt.format(i)] for i in range(e)])
 
 
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """[E, U, ...] gate and up rows (weights, their per-row scales or biases) ->
+    [E, 2U, ...] with, for every block b of 64 features, the 64 gate rows then
+    the 64 up rows: the layout SB_EPI_SWIGLU_IL reads."""
+    e, u = up.shape[:2]
+    rest = up.shape[2:]
+    g = gate.reshape(e, u // 64, 1, 64, *rest)
+    v = up.reshape(e, u // 64, 1, 64, *rest)
+    return torch.cat([g, v], dim=2).reshape(e, 2 * u, *rest).contiguous()
+
+
+def split_gate_up(packed: torch.Tensor, which: str) -> torch.Tensor:
+    """Inverse of interleave_gate_up for one half: "gate" or "up" rows [E, U, ...]."""
+    e, u2 = packed.shape[:2]
+    rest = packed.shape[2:]
+    half = packed.reshape(e, u2 // 128, 2, 64, *rest)[:, :, 0 if which == "gate" else 1]
+    return half.reshape(e, u2 // 2, *rest)
+
+
 class BlockEngine:
     """Packed weights + workspace for one block on one device."""
 
@@ -118,6 +137,15 @@ class BlockEngine:
                 t["s_" + short] = qt.device_scales().to(dev).contiguous()
             else:
                 raise ValueError(f"unknown weight format {fmt}")
+        self.swiglu = swiglu and has_experts
+        if self.swiglu:
+            # SwiGLU: gate and up rows interleaved in blocks of 64 in one tensor
+            # ([E, 2U, ...]; SB_EPI_SWIGLU_IL), so one MMA operand covers both
+            if U % 64:
+                raise ValueError("SwiGLU experts need expert_ffn_size divisible by 64")
+            for k in ("w", "s", "b"):
+                if k + "_gate" in t:
+                    t[k + "_up"] = interleave_gate_up(t.pop(k + "_gate"), t[k + "_up"])
         wcode = {"f32": L.SB_W_F32, "bf16": L.SB_W_BF16, "fp8": L.SB_W_FP8, "int4": L.SB_W_INT4}[fmt]
         self.dims = L.BlockDims(
             hidden=H, num_experts=E, top_k=cfg.top_k, edges_per_expert=cfg.edges_per_expert, ffn=U,
@@ -160,6 +188,18 @@ class BlockEngine:
 
     def weight_bytes(self) -> int:
         return sum(v.numel() * v.element_size() for v in self.t.values())
+
+    def expert_tensors(self, short: str):
+        """(weights, scales or None, biases) of one expert projection ("up",
+        "gate" or "down") in the [E, rows, ...] layout of the reference's
+        stacked Linear weights, as stored on the device (views; SwiGLU's
+        interleaved gate/up tensor is split back into its halves)."""
+        t = self.t
+        if self.swiglu and short in ("up", "gate"):
+            s = t.get("s_up")
+            return (split_gate_up(t["w_up"], short), None if s is None else split_gate_up(s, short),
+                    split_gate_up(t["b_up"], short))
+        return t["w_" + short], t.get("s_" + short), t["b_" + short]
 
     def status(self) -> int:
         """Device status word (non-zero: a bounded wait ran out); synchronises."""

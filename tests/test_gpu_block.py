@@ -121,12 +121,11 @@ def test_full_size_config_one_loop(name, tokens, engine, activation, cuda_device
     sd_cpu = {k: v.cpu() for k, v in sd.items()}
     p = O.params_from_state_dict(sd_cpu, cfg.num_experts)
     for short in ["up", "down"] + (["gate"] if activation == "swiglu" else []):
+        q, s, _ = eng.expert_tensors(short)
         if wf == "fp8":
-            setattr(p, "w_" + short, (eng.t["w_" + short].view(torch.float8_e4m3fn).float()
-                                      * eng.t["s_" + short].unsqueeze(-1)).cpu())
+            setattr(p, "w_" + short, (q.view(torch.float8_e4m3fn).float() * s.unsqueeze(-1)).cpu())
         if wf == "int4":
-            setattr(p, "w_" + short, O.dequantize_int4(eng.t["w_" + short].cpu(), eng.t["s_" + short].float().cpu(),
-                                                       128))
+            setattr(p, "w_" + short, O.dequantize_int4(q.cpu(), s.float().cpu(), 128))
     h, x0 = synth.block_inputs(n, cfg.hidden_size, seed=1)
     h = h.to(torch.bfloat16).float()
     want = O.block_forward(p, h, h, 1, cfg)

@@ -50,7 +50,7 @@ def workload_engine(name, activation, device):
     del sd
     names = ["up", "down"] + (["gate"] if activation == "swiglu" else [])
     for short in names:
-        q, s = eng.t["w_" + short], eng.t.get("s_" + short)
+        q, s, _ = eng.expert_tensors(short)
         if wf == "fp8":
             w = O.dequantize_fp8_per_channel(q.view(torch.float8_e4m3fn).cpu(), s.cpu())
         elif wf == "int4":

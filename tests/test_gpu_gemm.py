@@ -17,11 +17,13 @@ import pytest
 import torch
 
 from spider_web_moe_b200 import _lib as L
+from spider_web_moe_b200.engine import interleave_gate_up, split_gate_up
 from spider_web_moe_b200.quant import quantize_fp8_per_channel, quantize_int4
 
 pytestmark = pytest.mark.gpu
 
-EPI = {"linear": L.SB_EPI_LINEAR, "gelu": L.SB_EPI_GELU, "swiglu": L.SB_EPI_SWIGLU}
+EPI = {"linear": L.SB_EPI_LINEAR, "gelu": L.SB_EPI_GELU, "swiglu": L.SB_EPI_SWIGLU,
+       "swiglu_il": L.SB_EPI_SWIGLU_IL}
 WFMT = {"bf16": L.SB_W_BF16, "fp8": L.SB_W_FP8, "int4": L.SB_W_INT4}
 ENGINE = {"tcgen05": L.SB_ENGINE_TCGEN05, "simt": L.SB_ENGINE_SIMT}
 
@@ -59,8 +61,18 @@ def run_case(rows, m, k, wfmt, epi, engine, dev, bound=0, splits=1, gather=False
     bias_g = torch.randn(G, m, generator=g) * 0.1
     x = torch.randn(total, k, generator=g).to(torch.bfloat16)
     row_scale = torch.rand(total, generator=g) + 0.5
-    a, a_s, deq, s_row = device_weight(w, wfmt, group_size, dev)
-    ag, ag_s, deq_g, s_row_g = device_weight(wg, wfmt, group_size, dev) if epi == "swiglu" else (None, None, None, None)
+    il = epi == "swiglu_il"
+    if il:
+        # one operand: gate and up rows interleaved in blocks of 64 (per-row scales
+        # and biases likewise); the reference reads the two halves back
+        a, a_s, deq_il, s_il = device_weight(interleave_gate_up(wg, w), wfmt, group_size, dev)
+        deq, deq_g = split_gate_up(deq_il, "up"), split_gate_up(deq_il, "gate")
+        s_row, s_row_g = (None, None) if s_il is None else (split_gate_up(s_il, "up"), split_gate_up(s_il, "gate"))
+        ag = ag_s = None
+    else:
+        a, a_s, deq, s_row = device_weight(w, wfmt, group_size, dev)
+        ag, ag_s, deq_g, s_row_g = (device_weight(wg, wfmt, group_size, dev) if epi == "swiglu"
+                                    else (None, None, None, None))
 
     # torch fp32 statement
     want = torch.zeros(total, m)
@@ -95,6 +107,8 @@ def run_case(rows, m, k, wfmt, epi, engine, dev, bound=0, splits=1, gather=False
     status = torch.zeros(64, dtype=torch.int32, device=dev)
     keep = [a, a_s, ag, ag_s, d_x, d_idx, d_off, out, status]
     d_bias, d_bias_g, d_rs = bias.to(dev), bias_g.to(dev), row_scale.to(dev)
+    if il:
+        d_bias = interleave_gate_up(bias_g, bias).to(dev)
     keep += [d_bias, d_bias_g, d_rs]
 
     args = L.GemmArgs()
@@ -103,12 +117,13 @@ def run_case(rows, m, k, wfmt, epi, engine, dev, bound=0, splits=1, gather=False
     args.act_dtype = L.SB_BF16
     args.epilogue = EPI[epi]
     args.num_groups = G
-    args.m_rows = m
+    rows_a = 2 * m if il else m  # weight rows per group
+    args.m_rows = rows_a
     args.k = k
     args.group_size = group_size
-    args.a_group_rows = m
+    args.a_group_rows = rows_a
     args.lda = k
-    args.a_rows_total = G * m
+    args.a_rows_total = G * rows_a
     args.a = a.data_ptr()
     args.a_scale = a_s.data_ptr() if a_s is not None else None
     if epi == "swiglu":
@@ -116,7 +131,7 @@ def run_case(rows, m, k, wfmt, epi, engine, dev, bound=0, splits=1, gather=False
         args.a_gate_scale = ag_s.data_ptr() if ag_s is not None else None
         args.bias_gate = d_bias_g.data_ptr()
     args.bias = d_bias.data_ptr()
-    args.bias_group_stride = m
+    args.bias_group_stride = rows_a
     args.x = d_x.data_ptr()
     args.ldx = k
     if gather:
@@ -143,6 +158,7 @@ def run_case(rows, m, k, wfmt, epi, engine, dev, bound=0, splits=1, gather=False
 
 
 def check(got, want, epi):
+    epi = "swiglu" if epi == "swiglu_il" else epi
     err = (got - want).abs()
     # fp32 accumulation order (LINEAR), plus bf16 rounding of the output (GELU / SwiGLU)
     tol = (1e-4 if epi == "linear" else 8e-3) * want.abs() + 2e-4 * want.abs().max()
@@ -182,6 +198,20 @@ def test_tcgen05_swiglu(sched, wfmt, cuda_device):
     check(got, want, "swiglu")
 
 
+@pytest.mark.parametrize("sched", ["fixed16_gather", "fixed64", "fixed_multi_tile", "slot64", "persistent128",
+                                   "persistent256"])
+@pytest.mark.parametrize("wfmt", ["bf16", "fp8", "int4"])
+def test_tcgen05_swiglu_interleaved(sched, wfmt, cuda_device):
+    """SB_EPI_SWIGLU_IL, the layout the block's SwiGLU experts use: gate and up
+    rows of one operand, the two halves of each 128-row tile handed across
+    between epilogue warps; every schedule (fixed groups, slot grid, the
+    persistent and CTA-pair kernels)."""
+    rows, bound, splits, gather = SCHEDULES[sched]
+    got, want = run_case(rows, 256, 384, wfmt, "swiglu_il", "tcgen05", cuda_device, bound=bound, splits=splits,
+                         gather=gather, seed=9)
+    check(got, want, "swiglu_il")
+
+
 def test_persistent_many_tiles_and_groups(cuda_device):
     """More tiles than SMs (each CTA loops, both TMEM accumulators turn over many
     times) and 200 groups of ragged sizes, zeros included."""
@@ -192,10 +222,11 @@ def test_persistent_many_tiles_and_groups(cuda_device):
     check(got, want, "gelu")
 
 
-@pytest.mark.parametrize("epi", ["linear", "gelu", "swiglu"])
+@pytest.mark.parametrize("epi", ["linear", "gelu", "swiglu", "swiglu_il"])
 @pytest.mark.parametrize("wfmt", ["bf16", "fp8", "int4"])
 def test_simt_engine(epi, wfmt, cuda_device):
-    got, want = run_case([33, 0, 70, 5], 160, 256, wfmt, epi, "simt", cuda_device, seed=3)
+    m = 192 if epi == "swiglu_il" else 160  # the interleaved layout comes in 64-feature blocks
+    got, want = run_case([33, 0, 70, 5], m, 256, wfmt, epi, "simt", cuda_device, seed=3)
     check(got, want, epi)
 
 
