@@ -20,9 +20,12 @@ Arms:
   restatement, dense as the reference computes it) on all host threads, rank 0.
 
 With N > 1 (torchrun) every rank holds its own batch of the config's token
-count (weak scaling) and the experts are sharded e % N: the token-sharded
-expert-parallel block (spider_web_moe_b200.ep: NCCL all-to-all of message rows
-to expert owners and back every loop).
+count (weak scaling).  The block is token-independent, so by default
+(``--parallel dp``) every rank runs it on its own tokens with the weights
+replicated and no collective on the data path.  ``--parallel ep`` runs the
+token-sharded expert-parallel block instead (spider_web_moe_b200.ep: experts
+e % N, message rows to the expert owners and back every loop, over peer memory
+or NCCL all-to-all).
 """
 from __future__ import annotations
 
@@ -60,6 +63,10 @@ def parse():
     ap.add_argument("--engine", default="auto", choices=["auto", "tcgen05", "simt"])
     ap.add_argument("--activation", default=None, choices=["gelu", "swiglu"],
                     help="expert FFN; default: the one the workload names (SwiGLU for cfg2-cfg5)")
+    ap.add_argument("--parallel", default="dp", choices=["dp", "ep"],
+                    help="N > 1: dp = every rank runs the whole block on its own tokens (weights replicated, no "
+                         "collective on the data path); ep = token-sharded expert parallelism (experts e % N, "
+                         "message rows exchanged with the expert owners every loop)")
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="N > 1 expert-parallel exchange: stores into the peers' memory over NVLink (peer) or NCCL "
                          "all-to-all")
@@ -178,10 +185,14 @@ def workload_config(args, cfg, spec, world: int) -> dict:
     """The ``config`` object of the JSON line.  Both arms print this same dict
     for the same arguments: it names the workload, not the implementation (the
     reference arm's bounded sample is described in its ``cpu_baseline``)."""
-    par = "single GPU" if world <= 1 else (
-        f"ep{world}: tokens sharded by rank, experts e % {world}, "
-        + ("dispatch/combine stored into peer memory over NVLink" if args.transport == "peer"
-           else "NCCL all-to-all"))
+    if world <= 1:
+        par = "single GPU"
+    elif args.parallel == "dp":
+        par = f"dp{world}: tokens sharded by rank, block weights replicated, no collective on the data path"
+    else:
+        par = (f"ep{world}: tokens sharded by rank, experts e % {world}, "
+               + ("dispatch/combine stored into peer memory over NVLink" if args.transport == "peer"
+                  else "NCCL all-to-all"))
     return {"workload": args.config, "tokens_per_step_per_gpu": spec["tokens"], "num_loops": cfg.num_loops,
             "hidden": cfg.hidden_size, "experts": cfg.num_experts, "top_k": cfg.top_k,
             "edges_per_expert": cfg.edges_per_expert, "ffn": cfg.expert_ffn_size,
@@ -479,7 +490,7 @@ def run_b200(args):
         raise SystemExit("bench.py --impl b200 needs a CUDA device")
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    if world > 1 and not args.profile_only:
+    if world > 1 and args.parallel == "ep" and not args.profile_only:
         return run_b200_ep(args, rank, world, local, device)
     from spider_web_moe_b200 import synth
     from spider_web_moe_b200.engine import CapturedBlock, HostPipeline

@@ -751,7 +751,9 @@ static int expert_rows_impl(const sb_block_dims* dims, const sb_block_weights* w
     a.offsets = b.ffn_off; a.out = b.act; a.ldo = U; a.splits = 1; a.status = b.status;
     sb_grouped_gemm_args g = a;
     g.x = rows; g.ldx = ldx; g.x_row_index = b.ffn_row; g.x_rows = N;
-    if (gemm_gathers(g, d.engine)) {
+    // decided on the plain operand: large tiles read materialised rows on the
+    // tensor cores rather than gathering on the CUDA-core engine
+    if (gemm_gathers(a, d.engine)) {
       a = g;
     } else {
       // materialise the message rows (first hidden columns of each packed row), then in expert order
