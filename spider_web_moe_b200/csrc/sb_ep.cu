@@ -69,12 +69,22 @@ ep_pack_kernel(const T* __restrict__ msgs, const int32_t* __restrict__ top_idx, 
       for (int v = lane; v < vec; v += 32) dst[v] = src[v];
     }
   }
-  // return positions, one thread per (token, slot)
+  // return positions, one thread per (token, slot): the owner's row of the
+  // token's first slot it owns -- unless none of the token's slots it owns has
+  // a positive weight (the owner's plan drops those, and returns no row)
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_tokens * K; i += gridDim.x * blockDim.x) {
     const int p = inv[i];
     const int e = top_idx[i];
     const int q = (e >= 0 && e < E) ? e % world : -1;
-    ret_pos[i] = (p >= 0 && q >= 0) ? q * cap + (p - off[q]) : -1;
+    bool any_pos = false;
+    if (p >= 0 && q >= 0) {
+      const int64_t t0 = static_cast<int64_t>(i / K) * K;
+      for (int k2 = 0; k2 < K; ++k2) {
+        const int e2 = top_idx[t0 + k2];
+        if (e2 >= 0 && e2 < E && e2 % world == q && top_w[t0 + k2] > 0.f) any_pos = true;
+      }
+    }
+    ret_pos[i] = any_pos ? q * cap + (p - off[q]) : -1;
   }
   if (regions) ep_signal_peers(regions, regions[me], ctrl_off, world, me, 0);
 }

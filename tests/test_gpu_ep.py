@@ -24,11 +24,14 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-@pytest.mark.parametrize("name", ["cfg2", "cfg5"])
-def test_ep_path_single_gpu_matches_block(name, cuda_device):
+@pytest.mark.parametrize("name,n,activation", [("cfg2", 40, "gelu"), ("cfg5", 40, "gelu"), ("cfg3", 1024, "swiglu"),
+                                               ("cfg4", 700, "swiglu")])
+def test_ep_path_single_gpu_matches_block(name, n, activation, cuda_device):
+    """The token-sharded EP loop at a world of one (route, pack, owner-side
+    experts on the packed rows, combine, epilogue) against the block; the
+    prefill-size cases take the tensor-core schedules on materialised rows."""
     spec = benchmark_configs()[name]
-    cfg = ModelConfig(**spec["model"]).validate()
-    n = 40
+    cfg = ModelConfig(**spec["model"], expert_activation=activation).validate()
     sd = synth.synthetic_state_dict(cfg, seed=41, device=cuda_device, zipf=1.1 if spec["zipf"] else None,
                                     round_bf16=True)
     ep = ExpertParallelBlock(cfg, sd, cuda_device, act_dtype=torch.bfloat16, max_tokens=n, weight_format=spec["wfmt"])
@@ -43,15 +46,15 @@ def test_ep_path_single_gpu_matches_block(name, cuda_device):
         h = b
 
 
-@pytest.mark.parametrize("name", ["cfg2", "cfg5"])
-def test_peer_transport_single_gpu_matches_nccl_path(name, cuda_device):
+@pytest.mark.parametrize("name,n", [("cfg2", 40), ("cfg5", 40), ("cfg2", 600), ("cfg4", 700)])
+def test_peer_transport_single_gpu_matches_nccl_path(name, n, cuda_device):
     """World of one over the peer-memory transport (the rank's own region as its
     only peer): the dispatch, flag waits and return run, and the outputs are
     bit-identical to the NCCL-transport path, eagerly and from a CUDA graph
-    replayed twice (the flags keep counting across loops and replays)."""
+    replayed twice (the flags keep counting across loops and replays).  From
+    512 rows the owner's return and the source's epilogue run warp per row."""
     spec = benchmark_configs()[name]
-    cfg = ModelConfig(**spec["model"]).validate()
-    n = 40
+    cfg = ModelConfig(**spec["model"], expert_activation=spec["activation"]).validate()
     sd = synth.synthetic_state_dict(cfg, seed=45, device=cuda_device, zipf=1.1 if spec["zipf"] else None,
                                     round_bf16=True)
     ref = ExpertParallelBlock(cfg, sd, cuda_device, act_dtype=torch.bfloat16, max_tokens=n, weight_format=spec["wfmt"])
