@@ -158,7 +158,9 @@ typedef struct sb_grouped_gemm_args {
   int64_t lda;            /* elements per row of a (bytes per row = lda/2 for int4) */
   int64_t a_rows_total;   /* rows of a (bounds of the weight tensor) */
   const void* a;
-  const void* a_scale;    /* fp8: float[a_rows_total]; int4: bf16[a_rows_total, lda/group_size] */
+  const void* a_scale;    /* fp8: float[a_rows_total]; int4: bf16[a_rows_total, lda/group_size];
+                             bf16: NULL, or float[a_rows_total] row scales applied to the accumulator
+                             (fp8 weights converted to bf16 exactly keep their per-channel scale) */
   const void* a_gate;     /* SwiGLU gate weights, same layout as a */
   const void* a_gate_scale;
   const float* bias;      /* bias[g*bias_group_stride + m], may be NULL */

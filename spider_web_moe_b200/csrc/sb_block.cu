@@ -80,11 +80,11 @@ __global__ void remap_local_kernel(const int32_t* __restrict__ idx, int n, int E
 // ------------------------------------------------------------------ stage timing
 // Optional per-stage CUDA-event timing of sb_block_forward (a profiling aid;
 // off by default, never used during graph capture).
-constexpr int kNumStages = 13;
+constexpr int kNumStages = 14;
 static const char* kStageNames[kNumStages] = {
     "router", "group_sources", "gather_sources", "gemm_edge_logits", "edge_topm", "group_destinations",
     "gather_destinations", "gemm_edge_values", "group_experts", "combine_messages", "gemm_expert_up",
-    "gemm_expert_down", "combine_layernorm"};
+    "gemm_expert_down", "combine_layernorm", "dequant_experts"};
 struct StageTiming {
   bool on = false;
   std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> marks;
@@ -138,13 +138,40 @@ struct BlockBuffers {
   void* msg_act;
   int32_t *ffn_off, *ffn_row, *ffn_slot, *ffn_inv; float* ffn_w;
   int32_t *dst_rank, *ffn_rank; float *dst_wsc, *ffn_wsc;  // scratch of the two-plan grouping launch
+  int32_t *cc_dst, *cc_ffn;                                  // its chunk counts (multi-CTA schedule)
   void* x_ffn; void* act; float* y_ffn;
+  void *w_up_bf, *w_down_bf;  // bf16 copies of fp8 / int4 expert weights (prefill batches), or NULL
   void* hbuf[2];
   void* group_ws; size_t group_ws_bytes;
   int64_t cap_dst, y_msg_stride, y_ffn_stride;
 };
 
 static int max_splits_for(int n_tokens) { return n_tokens <= 512 ? 4 : 1; }
+
+// Prefill-size batches of fp8 / int4 experts convert the expert weights to
+// bf16 once per sb_block_forward call, into the workspace, and run the
+// expert GEMMs on the bf16 tensor-core schedules (the CTA-pair kernel)
+// instead of dequantising every weight tile in shared memory inside each
+// loop's GEMM -- with many rows per expert the GEMMs are tensor-bound and the
+// in-GEMM conversion is what limits them.  The conversion is the one the
+// GEMM does in shared memory (fp8 e4m3 -> bf16 exactly, the per-row scale
+// still applied to the accumulator; int4 -> bf16(q * group scale)), so the
+// results are the same.  From this many expected rows per expert:
+constexpr int kDequantOnceMinRows = 128;
+// SPIDER_B200_DEQUANT_ONCE=0 keeps fp8 / int4 prefill on the in-GEMM dequant (for comparisons).
+static bool dequant_once_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("SPIDER_B200_DEQUANT_ONCE");
+    return !(e && e[0] == '0');
+  }();
+  return v;
+}
+
+static bool dequant_once_possible(const sb_block_dims& d, int n_tokens) {
+  return (d.wfmt == SB_W_FP8 || d.wfmt == SB_W_INT4) && d.engine != SB_ENGINE_SIMT && d.act_dtype == SB_BF16 &&
+         static_cast<int64_t>(n_tokens) * d.top_k >= static_cast<int64_t>(kDequantOnceMinRows) * d.num_experts &&
+         dequant_once_enabled();
+}
 
 // Columns of the dense routing logits (router + every source's edge logits),
 // or 0 for expert counts whose E*E logits are too wide to compute densely.
@@ -192,12 +219,20 @@ static size_t carve_block(const sb_block_dims& d, int n_cap, void* base, size_t 
   b->x_ffn = c.take<char>(N * K * H * as);
   b->act = c.take<char>(N * K * U * as);
   b->y_ffn = c.take<float>(ffn_rows * H);
+  b->w_up_bf = b->w_down_bf = nullptr;
+  if (dequant_once_possible(d, static_cast<int>(N))) {
+    const int64_t up_rows = (d.activation == SB_ACT_SWIGLU ? 2 : 1) * U;
+    b->w_up_bf = c.take<__nv_bfloat16>(E * up_rows * H);
+    b->w_down_bf = c.take<__nv_bfloat16>(E * H * U);
+  }
   b->hbuf[0] = c.take<char>(N * H * as);
   b->hbuf[1] = c.take<char>(N * H * as);
   b->dst_rank = c.take<int32_t>(N * K * M);
   b->dst_wsc = c.take<float>(N * K * M);
   b->ffn_rank = c.take<int32_t>(N * K);
   b->ffn_wsc = c.take<float>(N * K);
+  b->cc_dst = c.take<int32_t>((N * K * M + kGroupChunk - 1) / kGroupChunk * E);
+  b->cc_ffn = c.take<int32_t>((N * K + kGroupChunk - 1) / kGroupChunk * E);
   b->group_ws_bytes = sb_group_workspace_bytes(static_cast<int>(N), static_cast<int>(K * M), static_cast<int>(E));
   b->group_ws = c.take<char>(b->group_ws_bytes);
   b->cap_dst = cap_dst;
@@ -398,6 +433,16 @@ static bool use_dense_route(const sb_block_dims& d, const sb_block_weights* w, i
   return 2.0 * N * cols * d.hidden <= kDenseRouteMaxFlops;
 }
 
+// SPIDER_B200_MULTI_PLAN=0 keeps large batches on separate sb_group launches
+// for the two plans and a separate row gather (for comparisons).
+static bool multi_plan_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("SPIDER_B200_MULTI_PLAN");
+    return !(e && e[0] == '0');
+  }();
+  return v;
+}
+
 // `routed`: the fused route of this loop already ran (inside the previous
 // loop's LayerNorm kernel); steps 1-5 are skipped.
 static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBuffers& b, const void* cur, int N,
@@ -480,9 +525,24 @@ static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBu
     // 5. top-M destinations per (token, source)
     { StageScope sc_(4, st); SB_TRY(sb_edge_topm(b.elog, E, E, M, b.src_slot, b.src_off, E, N * K, b.edge_idx, b.edge_w, st)); }
   }
+  // 8's operands (sizes only): whether the edge-value GEMM gathers its token
+  // rows itself or reads them from x_dst
+  sb_grouped_gemm_args a;
+  std::memset(&a, 0, sizeof(a));
+  a.engine = d.engine; a.wfmt = dense_fmt; a.act_dtype = d.act_dtype; a.epilogue = SB_EPI_LINEAR;
+  a.num_groups = E; a.m_rows = H; a.k = H; a.a_group_rows = H; a.lda = H;
+  a.a_rows_total = static_cast<int64_t>(E) * H; a.a = w->edge_w;
+  a.x = b.x_dst; a.ldx = H; a.max_rows = static_cast<int>(cap_dst);
+  a.rows_hint = static_cast<int>(cap_dst * 7 / 8); a.group_rows_bound = N; a.offsets = b.dst_off; a.row_scale = b.dst_w;
+  const int msg_splits = pick_splits(H, H, a.rows_hint, E, max_splits_for(N), tc_pref, N);
+  a.splits = msg_splits; a.split_stride = cap_dst * H;
+  a.out = b.y_msg; a.ldo = H; a.status = b.status;
+  const bool edge_gathers = gemm_gathers(a, d.engine);
   // 6-7. (token, destination) pairs with summed coefficients (and, when asked,
-  // the expert dispatch plan of step 9 in the same launch)
-  bool both = false;
+  // the expert dispatch plan of step 9 in the same launches): one CTA per plan
+  // for small batches, else both plans' two passes in two launches, the place
+  // pass also copying the destination-ordered rows the edge-value GEMM reads
+  bool both = false, gathered = false;
   if (ffn_planned) {
     const GroupJob jd{b.edge_idx, b.edge_w, N, KM, E, 0, b.dst_off, b.dst_row, b.dst_slot, b.dst_w, b.dst_inv,
                       b.dst_rank, b.dst_wsc};
@@ -490,6 +550,12 @@ static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBu
                       b.ffn_inv, b.ffn_rank, b.ffn_wsc};
     StageScope sc_(5, st);
     rc = group_pair_launch(jd, jf, st);
+    if (rc == SB_ERR_UNSUPPORTED && multi_plan_enabled()) {
+      rc = group_pair_multi_launch(jd, jf, b.cc_dst, b.cc_ffn, edge_gathers ? nullptr : cur,
+                                   static_cast<int64_t>(H) * act_size(d.act_dtype), edge_gathers ? nullptr : b.x_dst,
+                                   st);
+      gathered = rc == SB_OK && !edge_gathers;
+    }
     if (rc != SB_OK && rc != SB_ERR_UNSUPPORTED) return rc;
     both = rc == SB_OK;
     *ffn_planned = both;
@@ -501,19 +567,9 @@ static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBu
   }
   // 8. c[t,d] * W_edge[d] h[t]
   {
-    sb_grouped_gemm_args a;
-    std::memset(&a, 0, sizeof(a));
-    a.engine = d.engine; a.wfmt = dense_fmt; a.act_dtype = d.act_dtype; a.epilogue = SB_EPI_LINEAR;
-    a.num_groups = E; a.m_rows = H; a.k = H; a.a_group_rows = H; a.lda = H;
-    a.a_rows_total = static_cast<int64_t>(E) * H; a.a = w->edge_w;
-    a.x = b.x_dst; a.ldx = H; a.max_rows = static_cast<int>(cap_dst);
-    a.rows_hint = static_cast<int>(cap_dst * 7 / 8); a.group_rows_bound = N; a.offsets = b.dst_off; a.row_scale = b.dst_w;
-    const int msg_splits = pick_splits(H, H, a.rows_hint, E, max_splits_for(N), tc_pref, N);
-    a.splits = msg_splits; a.split_stride = cap_dst * H;
-    a.out = b.y_msg; a.ldo = H; a.status = b.status;
-    if (gemm_gathers(a, d.engine)) {
+    if (edge_gathers) {
       a.x = cur; a.x_row_index = b.dst_row; a.x_rows = N;
-    } else {
+    } else if (!gathered) {
       StageScope sc_(6, st);
       SB_TRY(sb_gather_rows(cur, d.act_dtype, H, b.dst_row, b.dst_off, E, static_cast<int>(cap_dst), b.x_dst, st));
     }
@@ -562,6 +618,23 @@ extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block
   // decode: loop l's LayerNorm kernel also routes loop l+1 (SPIDER_B200_FUSE_LN_ROUTE=0 disables)
   const bool fuse_next = use_fused_route(d, N) && fuse_ln_route_enabled();
   bool routed = false;
+  // prefill with fp8 / int4 experts: the expert weights in bf16 once for all loops of this call
+  const bool deq = b.w_up_bf && dequant_once_possible(d, N);
+  if (deq) {
+    StageScope sc_(13, st);
+    const int64_t up_rows = static_cast<int64_t>(d.activation == SB_ACT_SWIGLU ? 2 : 1) * U;
+    SB_TRY(dequant_to_bf16(d.wfmt, w->w_up, w->s_up, d.group_size, static_cast<int64_t>(E) * up_rows, H, b.w_up_bf,
+                           st));
+    SB_TRY(dequant_to_bf16(d.wfmt, w->w_down, w->s_down, d.group_size, static_cast<int64_t>(E) * H, U, b.w_down_bf,
+                           st));
+  }
+  // the expert GEMMs on the bf16 copies: fp8 keeps its per-row scale in the epilogue
+  auto use_copy = [&](sb_grouped_gemm_args& a, void* copy) {
+    if (!deq) return;
+    a.wfmt = SB_W_BF16;
+    a.a = copy;
+    if (d.wfmt != SB_W_FP8) a.a_scale = nullptr;
+  };
   for (int l = loop_begin; l < loop_end; ++l) {
     void* next = (l == loop_end - 1) ? h_out : b.hbuf[(l - loop_begin) & 1];
     int msg_splits = 1;
@@ -578,6 +651,7 @@ extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block
     {
       sb_grouped_gemm_args a;
       fill_expert_gemm(a, d, true, w->w_up, w->s_up, w->b_up, w->w_gate, w->s_gate, w->b_gate);
+      use_copy(a, b.w_up_bf);
       a.epilogue = d.activation == SB_ACT_SWIGLU ? SB_EPI_SWIGLU_IL : SB_EPI_GELU;
       a.num_groups = E; a.x = b.x_ffn; a.ldx = H; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N;
       a.offsets = b.ffn_off; a.out = b.act; a.ldo = U; a.splits = 1; a.status = b.status;
@@ -596,6 +670,7 @@ extern "C" SB_API int sb_block_forward(const sb_block_dims* dims, const sb_block
     {
       sb_grouped_gemm_args a;
       fill_expert_gemm(a, d, false, w->w_down, w->s_down, w->b_down, nullptr, nullptr, nullptr);
+      use_copy(a, b.w_down_bf);
       a.epilogue = SB_EPI_LINEAR;
       a.num_groups = E; a.x = b.act; a.ldx = U; a.max_rows = N * K; a.rows_hint = N * K; a.group_rows_bound = N;
       a.offsets = b.ffn_off; a.row_scale = b.ffn_w;

@@ -33,8 +33,9 @@ SB_DEVINL float load_weight(const sb_grouped_gemm_args& p, const void* base, con
   }
 }
 
+// fp8 weights, or bf16 weights with a per-row scale (fp8 weights converted exactly)
 SB_DEVINL float row_scale_of(const sb_grouped_gemm_args& p, const void* scale, int64_t row) {
-  return p.wfmt == SB_W_FP8 ? static_cast<const float*>(scale)[row] : 1.f;
+  return (p.wfmt == SB_W_FP8 || (p.wfmt == SB_W_BF16 && scale)) ? static_cast<const float*>(scale)[row] : 1.f;
 }
 
 // kIL: interleaved SwiGLU (SB_EPI_SWIGLU_IL) -- a CTA's 64 output features

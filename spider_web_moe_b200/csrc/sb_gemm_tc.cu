@@ -398,8 +398,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int m = m0 + mloc;
     const int64_t arow = arow0 + mloc;
     const bool mvalid = m < p.m_rows && arow < p.a_rows_total;
-    const float sa = (WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_scale)[arow] : 1.f;
-    const float sg = (C::kGate && WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_gate_scale)[arow] : 1.f;
+    const float sa = ((WFMT == SB_W_FP8 || (WFMT == SB_W_BF16 && p.a_scale)) && mvalid) ? static_cast<const float*>(p.a_scale)[arow] : 1.f;
+    const float sg = (C::kGate && (WFMT == SB_W_FP8 || (WFMT == SB_W_BF16 && p.a_gate_scale)) && mvalid) ? static_cast<const float*>(p.a_gate_scale)[arow] : 1.f;
     const float bias = (p.bias && mvalid && blockIdx.z == 0) ? p.bias[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
     const float bgate = (C::kGate && p.bias_gate && mvalid) ? p.bias_gate[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
@@ -746,8 +746,8 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
       const int m = mt * kTcBM + quarter * 32 + lane;
       const int64_t arow = static_cast<int64_t>(g) * p.a_group_rows + m;
       const bool mvalid = m < p.m_rows && arow < p.a_rows_total;
-      const float sa = (WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_scale)[arow] : 1.f;
-      const float sg = (C::kGate && WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_gate_scale)[arow] : 1.f;
+      const float sa = ((WFMT == SB_W_FP8 || (WFMT == SB_W_BF16 && p.a_scale)) && mvalid) ? static_cast<const float*>(p.a_scale)[arow] : 1.f;
+      const float sg = (C::kGate && (WFMT == SB_W_FP8 || (WFMT == SB_W_BF16 && p.a_gate_scale)) && mvalid) ? static_cast<const float*>(p.a_gate_scale)[arow] : 1.f;
       const float bias = (p.bias && mvalid) ? p.bias[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
       const float bgate = (C::kGate && p.bias_gate && mvalid) ? p.bias_gate[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
       const int tn0 = s_off[g] + nt * BN + half * HB;
@@ -1109,8 +1109,8 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       const int m = mt * kPairM + static_cast<int>(rank) * kTcBM + quarter * 32 + lane;
       const int64_t arow = static_cast<int64_t>(g) * p.a_group_rows + m;
       const bool mvalid = m < p.m_rows && arow < p.a_rows_total;
-      const float sa = (WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_scale)[arow] : 1.f;
-      const float sg = (C::kGate && WFMT == SB_W_FP8 && mvalid) ? static_cast<const float*>(p.a_gate_scale)[arow] : 1.f;
+      const float sa = ((WFMT == SB_W_FP8 || (WFMT == SB_W_BF16 && p.a_scale)) && mvalid) ? static_cast<const float*>(p.a_scale)[arow] : 1.f;
+      const float sg = (C::kGate && (WFMT == SB_W_FP8 || (WFMT == SB_W_BF16 && p.a_gate_scale)) && mvalid) ? static_cast<const float*>(p.a_gate_scale)[arow] : 1.f;
       const float bias = (p.bias && mvalid) ? p.bias[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
       const float bgate = (C::kGate && p.bias_gate && mvalid) ? p.bias_gate[static_cast<int64_t>(g) * p.bias_group_stride + m] : 0.f;
       const int tn0 = s_off[g] + nt * BN + half * HB;
@@ -1508,6 +1508,68 @@ int tc_tile_n(const sb_grouped_gemm_args& a) {
   if (per_group <= 64) return 64;
   if (per_group <= 128) return 128;
   return 256;
+}
+
+// fp8 e4m3 / packed int4 weights [rows, k] -> bf16 [rows, k]: e4m3 exactly
+// (its per-row scale stays with the GEMM epilogue), int4 as bf16(q * s) with
+// the bf16 group scale -- the values convert_tile produces in shared memory.
+// One thread per 16 source bytes.
+__global__ void __launch_bounds__(256)
+dequant_bf16_kernel(const uint8_t* __restrict__ q, int wfmt, const __nv_bfloat16* __restrict__ scales, int group_size,
+                    int64_t rows, int64_t k, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t row_bytes = wfmt == SB_W_FP8 ? k : k / 2;
+  const int64_t chunks = rows * (row_bytes / 16);
+  const int64_t groups = wfmt == SB_W_INT4 ? k / group_size : 0;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < chunks;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / (row_bytes / 16), cb = (i - r * (row_bytes / 16)) * 16;  // row, byte offset in the row
+    const uint4 v = *reinterpret_cast<const uint4*>(q + r * row_bytes + cb);
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(&v);
+    if (wfmt == SB_W_FP8) {
+      uint32_t o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(
+            static_cast<__nv_fp8x2_storage_t>(b[2 * j] | (b[2 * j + 1] << 8)), __NV_E4M3);
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+        const __nv_bfloat162 bb = __floats2bfloat162_rn(f.x, f.y);
+        o[j] = *reinterpret_cast<const uint32_t*>(&bb);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(out + r * k + cb);
+      dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+      dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+    } else {
+      const int64_t k0 = cb * 2;  // first weight of the chunk (32 weights)
+      const float s = __bfloat162float(scales[r * groups + k0 / group_size]);  // 32 | group_size: one group
+      uint32_t o[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int lo = ((b[j] & 0xF) ^ 8) - 8, hi = ((b[j] >> 4) ^ 8) - 8;
+        const __nv_bfloat162 bb = __floats2bfloat162_rn(static_cast<float>(lo) * s, static_cast<float>(hi) * s);
+        o[j] = *reinterpret_cast<const uint32_t*>(&bb);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(out + r * k + k0);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dst[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+    }
+  }
+}
+
+int dequant_to_bf16(int wfmt, const void* q, const void* scales, int group_size, int64_t rows, int64_t k, void* out,
+                    cudaStream_t st) {
+  if ((wfmt != SB_W_FP8 && wfmt != SB_W_INT4) || !q || !out || rows <= 0 || k % 64 ||
+      (wfmt == SB_W_INT4 && (!scales || group_size <= 0 || group_size % 32 || k % group_size)) ||
+      reinterpret_cast<uintptr_t>(q) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    return SB_ERR_ARG;
+  const int64_t chunks = rows * ((wfmt == SB_W_FP8 ? k : k / 2) / 16);
+  int64_t blocks = (chunks + 255) / 256;
+  const int64_t cap = 8 * current_sm_count();
+  blocks = blocks > cap ? cap : blocks;
+  return launch(dequant_bf16_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st,
+                static_cast<const uint8_t*>(q), wfmt, static_cast<const __nv_bfloat16*>(scales), group_size, rows, k,
+                static_cast<__nv_bfloat16*>(out));
 }
 
 int gemm_tcgen05(const sb_grouped_gemm_args& a, cudaStream_t st) {

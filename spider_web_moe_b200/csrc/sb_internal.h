@@ -88,6 +88,14 @@ struct GroupJob {
 };
 // SB_ERR_UNSUPPORTED when either grouping is too large for one CTA.
 int group_pair_launch(const GroupJob& j0, const GroupJob& j1, cudaStream_t st);
+// The same two groupings with the multi-CTA two-pass schedule of sb_group
+// (identical positions), both in one count launch and one place launch;
+// cc0 / cc1 hold ceil(entries / 256) * num_groups counts per job.  With
+// gather_src the place pass also copies each of job 0's placed entries' rows
+// (row index = entry / slots, row_bytes a multiple of 16) to gather_dst.
+constexpr int kGroupChunk = 256;
+int group_pair_multi_launch(const GroupJob& j0, const GroupJob& j1, int32_t* cc0, int32_t* cc1,
+                            const void* gather_src, int64_t row_bytes, void* gather_dst, cudaStream_t st);
 
 // Router + edge generator + edge top-M of small batches in one kernel
 // (sb_router.cu); SB_ERR_UNSUPPORTED when its shared memory would exceed
@@ -156,6 +164,11 @@ int router_from_logits(const float* logits, int ld, int splits, int64_t split_st
 int select_dense(const float* logits, int64_t ld, int n_tokens, int E, int K, int M, const float* rbias,
                  const float* gbias, int32_t* top_idx, float* top_w, int32_t* edge_idx, float* edge_w,
                  cudaStream_t st);
+
+// fp8 e4m3 (exact) / int4 (bf16(q * group scale)) weights [rows, k] -> bf16 [rows, k]
+// (sb_gemm_tc.cu): the values the tcgen05 GEMM's shared-memory conversion makes.
+int dequant_to_bf16(int wfmt, const void* q, const void* scales, int group_size, int64_t rows, int64_t k, void* out,
+                    cudaStream_t st);
 
 // Device properties cached per device.
 int current_sm_count();

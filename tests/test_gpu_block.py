@@ -215,3 +215,27 @@ def test_all_tokens_on_one_expert(n, cuda_device):
     h = h.to(torch.bfloat16).float()
     want = O.block_forward(p, h, h, 0, cfg)
     check_loop(eng, cfg, h, h, 0, want, TOL["bf16"], torch.bfloat16, "one-expert")
+
+
+@pytest.mark.parametrize("wf,activation", [("fp8", "swiglu"), ("int4", "swiglu"), ("fp8", "gelu"), ("int4", "gelu")])
+def test_quantised_prefill_through_bf16_copies(wf, activation, cuda_device):
+    """Prefill-size batches (here 256 expected rows per expert) of fp8 / int4
+    experts convert the expert weights to bf16 once per call and run the bf16
+    CTA-pair GEMMs (fp8 keeping its per-row scale in the epilogue): the same
+    weights the in-GEMM dequantisation makes, checked against the oracle."""
+    cfg = ModelConfig(hidden_size=512, num_heads=4, num_experts=8, top_k=2, edges_per_expert=2, num_loops=1,
+                      expert_ffn_size=512, expert_activation=activation, moe_int4_group_size=128).validate()
+    n = 1024
+    sd = synth.synthetic_state_dict(cfg, seed=13, device=cuda_device, round_bf16=True)
+    eng = BlockEngine(cfg, sd, cuda_device, act_dtype=torch.bfloat16, max_tokens=n, weight_format=wf)
+    p = O.params_from_state_dict({k: v.cpu() for k, v in sd.items()}, cfg.num_experts)
+    for short in ["up", "down"] + (["gate"] if activation == "swiglu" else []):
+        q, s, _ = eng.expert_tensors(short)
+        if wf == "fp8":
+            setattr(p, "w_" + short, (q.view(torch.float8_e4m3fn).float() * s.unsqueeze(-1)).cpu())
+        else:
+            setattr(p, "w_" + short, O.dequantize_int4(q.cpu(), s.float().cpu(), 128))
+    h, _ = synth.block_inputs(n, cfg.hidden_size, seed=14)
+    h = h.to(torch.bfloat16).float()
+    want = O.block_forward(p, h, h, 0, cfg)
+    check_loop(eng, cfg, h, h, 0, want, TOL[wf], torch.bfloat16, f"{wf}/{activation}/bf16-copies")
