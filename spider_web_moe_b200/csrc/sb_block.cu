@@ -540,9 +540,8 @@ static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBu
   const bool edge_gathers = gemm_gathers(a, d.engine);
   // 6-7. (token, destination) pairs with summed coefficients (and, when asked,
   // the expert dispatch plan of step 9 in the same launches): one CTA per plan
-  // for small batches, else both plans' two passes in two launches, the place
-  // pass also copying the destination-ordered rows the edge-value GEMM reads
-  bool both = false, gathered = false;
+  // for small batches, else both plans' two passes in two launches
+  bool both = false;
   if (ffn_planned) {
     const GroupJob jd{b.edge_idx, b.edge_w, N, KM, E, 0, b.dst_off, b.dst_row, b.dst_slot, b.dst_w, b.dst_inv,
                       b.dst_rank, b.dst_wsc};
@@ -551,10 +550,7 @@ static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBu
     StageScope sc_(5, st);
     rc = group_pair_launch(jd, jf, st);
     if (rc == SB_ERR_UNSUPPORTED && multi_plan_enabled()) {
-      rc = group_pair_multi_launch(jd, jf, b.cc_dst, b.cc_ffn, edge_gathers ? nullptr : cur,
-                                   static_cast<int64_t>(H) * act_size(d.act_dtype), edge_gathers ? nullptr : b.x_dst,
-                                   st);
-      gathered = rc == SB_OK && !edge_gathers;
+      rc = group_pair_multi_launch(jd, jf, b.cc_dst, b.cc_ffn, st);
     }
     if (rc != SB_OK && rc != SB_ERR_UNSUPPORTED) return rc;
     both = rc == SB_OK;
@@ -569,7 +565,7 @@ static int route_loop(const sb_block_dims& d, const sb_block_weights* w, BlockBu
   {
     if (edge_gathers) {
       a.x = cur; a.x_row_index = b.dst_row; a.x_rows = N;
-    } else if (!gathered) {
+    } else {
       StageScope sc_(6, st);
       SB_TRY(sb_gather_rows(cur, d.act_dtype, H, b.dst_row, b.dst_off, E, static_cast<int>(cap_dst), b.x_dst, st));
     }

@@ -279,7 +279,7 @@ constexpr int kWarpRowsPerCta = 8;
 // rank q = t / cap's returned row [peer.me][t % cap] instead of out_f32 --
 // only rows that summed at least one term: the padding rows of the
 // fixed-capacity exchange carry nothing the source reads.
-template <typename T, int NV>
+template <typename T, int NV, bool kPeer>
 SB_DEVINL void combine_row_warp(const float* __restrict__ y, int64_t ldy, int splits, int64_t split_stride,
                                 const int32_t* __restrict__ inv, int slots, int64_t t, int lane,
                                 float* __restrict__ out_f32, const int32_t* __restrict__ scatter_inv,
@@ -294,7 +294,7 @@ SB_DEVINL void combine_row_warp(const float* __restrict__ y, int64_t ldy, int sp
   for (int j = 0; j < slots; ++j) {
     const int r = __shfl_sync(0xffffffffu, j < 32 ? my_inv0 : my_inv1, j & 31);
     if (r < 0) continue;  // warp-uniform
-    ++terms;
+    if (kPeer) ++terms;
     for (int s = 0; s < splits; ++s) {
       const float* row = y + s * split_stride + static_cast<int64_t>(r) * ldy;
 #pragma unroll
@@ -304,7 +304,7 @@ SB_DEVINL void combine_row_warp(const float* __restrict__ y, int64_t ldy, int sp
       }
     }
   }
-  if (peer.regions) {
+  if constexpr (kPeer) {
     if (terms == 0) return;  // warp-uniform
     const int q = static_cast<int>(t / peer.cap), jj = static_cast<int>(t - static_cast<int64_t>(q) * peer.cap);
     float* orow = reinterpret_cast<float*>(peer.regions[q] + peer.ret_off) +
@@ -331,21 +331,34 @@ SB_DEVINL void combine_row_warp(const float* __restrict__ y, int64_t ldy, int sp
   }
 }
 
-// With peer.regions the last CTA raises the return flags once every row is stored.
 template <typename T, int NV>
 __global__ void __launch_bounds__(kWarpRowsPerCta * 32)
 combine_rows_warp_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t split_stride,
                          const int32_t* __restrict__ inv, int slots, int n_tokens, float* __restrict__ out_f32,
-                         const int32_t* __restrict__ scatter_inv, int scatter_slots, T* __restrict__ scatter_out,
-                         const EpPeer peer) {
+                         const int32_t* __restrict__ scatter_inv, int scatter_slots, T* __restrict__ scatter_out) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * kWarpRowsPerCta + (threadIdx.x >> 5);
+  if (t >= n_tokens) return;
+  combine_row_warp<T, NV, false>(y, ldy, splits, split_stride, inv, slots, t, lane, out_f32, scatter_inv,
+                                 scatter_slots, scatter_out, EpPeer{});
+}
+
+// Expert-parallel owner, peer transport: the rows go to their sources'
+// regions, and the last CTA raises the return flags once every row is stored.
+template <int NV>
+__global__ void __launch_bounds__(kWarpRowsPerCta * 32)
+combine_rows_peer_warp_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t split_stride,
+                              const int32_t* __restrict__ inv, int slots, int n_tokens, const EpPeer peer) {
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * kWarpRowsPerCta + (threadIdx.x >> 5);
   if (t < n_tokens)
-    combine_row_warp<T, NV>(y, ldy, splits, split_stride, inv, slots, t, lane, out_f32, scatter_inv, scatter_slots,
-                            scatter_out, peer);
-  if (peer.regions) ep_signal_peers(peer.regions, peer.regions[peer.me], peer.ctrl_off, peer.world, peer.me, 1);
+    combine_row_warp<float, NV, true>(y, ldy, splits, split_stride, inv, slots, t, lane, nullptr, nullptr, 0, nullptr,
+                                      peer);
+  ep_signal_peers(peer.regions, peer.regions[peer.me], peer.ctrl_off, peer.world, peer.me, 1);
 }
 
 // One token's delta sum and LayerNorm epilogue (one warp).
@@ -414,28 +427,38 @@ SB_DEVINL void ln_token_warp(const float* __restrict__ y, int64_t ldy, int split
 }
 
 
-// With wait_region (expert-parallel source, peer transport) every CTA first
-// waits for all ranks' return flags and the last CTA counts the wait.
 template <typename T, int NV>
 __global__ void __launch_bounds__(kWarpRowsPerCta * 32)
 combine_ln_warp_kernel(const float* __restrict__ y, int64_t ldy, int splits, int64_t split_stride,
                        const int32_t* __restrict__ inv, int slots, const float* __restrict__ delta_in,
                        const T* __restrict__ h, const T* __restrict__ x0, int n_tokens,
                        const float* __restrict__ ln_w, const float* __restrict__ ln_b, float alpha, float beta,
-                       float eps, T* __restrict__ out, float* __restrict__ delta_out, uint8_t* wait_region,
-                       int64_t ctrl_off, int wait_world, int* wait_status) {
+                       float eps, T* __restrict__ out, float* __restrict__ delta_out) {
   pdl_wait();
   pdl_trigger();
-  uint32_t target = 0;
-  if (wait_region) {
-    target = ep_wait_target(wait_region, ctrl_off, wait_world, 1);
-    ep_wait_cta(wait_region, ctrl_off, wait_world, 1, target, wait_status);
-  }
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * kWarpRowsPerCta + (threadIdx.x >> 5);
+  if (t >= n_tokens) return;
+  ln_token_warp<T, NV>(y, ldy, splits, split_stride, inv, slots, delta_in, h, x0, t, ln_w, ln_b, alpha, beta, eps, out,
+                       delta_out);
+}
+
+// Expert-parallel source, peer transport: every CTA first waits for all
+// ranks' return flags, and the last CTA counts the wait.
+template <typename T, int NV>
+__global__ void __launch_bounds__(kWarpRowsPerCta * 32)
+combine_ln_wait_warp_kernel(const float* __restrict__ y, int64_t ldy, const int32_t* __restrict__ inv, int slots,
+                            const T* __restrict__ h, const T* __restrict__ x0, int n_tokens,
+                            const float* __restrict__ ln_w, const float* __restrict__ ln_b, float alpha, float beta,
+                            float eps, T* __restrict__ out, uint8_t* wait_region, int64_t ctrl_off, int wait_world,
+                            int* wait_status) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t target = ep_wait_target(wait_region, ctrl_off, wait_world, 1);
+  ep_wait_cta(wait_region, ctrl_off, wait_world, 1, target, wait_status);
   const int64_t t = static_cast<int64_t>(blockIdx.x) * kWarpRowsPerCta + (threadIdx.x >> 5);
   if (t < n_tokens)
-    ln_token_warp<T, NV>(y, ldy, splits, split_stride, inv, slots, delta_in, h, x0, t, ln_w, ln_b, alpha, beta, eps,
-                         out, delta_out);
-  if (wait_region) ep_count_wait_multi(wait_region, ctrl_off, wait_world, 1, target);
+    ln_token_warp<T, NV>(y, ldy, 1, 0, inv, slots, nullptr, h, x0, t, ln_w, ln_b, alpha, beta, eps, out, nullptr);
+  ep_count_wait_multi(wait_region, ctrl_off, wait_world, 1, target);
 }
 
 }  // namespace sb
@@ -450,11 +473,11 @@ bool use_warp_rows(int n_tokens, int cols) { return n_tokens >= 512 && cols % 12
 template <typename T>
 int launch_combine_rows_warp(const float* y, int64_t ldy, int splits, int64_t split_stride, const int32_t* inv,
                              int slots, int n_tokens, int cols, float* out_f32, const int32_t* scatter_inv,
-                             int scatter_slots, T* scatter_out, cudaStream_t st, const EpPeer& peer = EpPeer{}) {
+                             int scatter_slots, T* scatter_out, cudaStream_t st) {
   const dim3 grid((n_tokens + kWarpRowsPerCta - 1) / kWarpRowsPerCta), block(kWarpRowsPerCta * 32);
 #define SB_ROWS_CASE(NV) \
   case NV: return launch(combine_rows_warp_kernel<T, NV>, grid, block, 0, st, y, ldy, splits, split_stride, inv, \
-                         slots, n_tokens, out_f32, scatter_inv, scatter_slots, scatter_out, peer);
+                         slots, n_tokens, out_f32, scatter_inv, scatter_slots, scatter_out);
   switch (cols / 128) {
     SB_ROWS_CASE(1) SB_ROWS_CASE(2) SB_ROWS_CASE(4) SB_ROWS_CASE(8) SB_ROWS_CASE(16)
     default: return SB_ERR_UNSUPPORTED;
@@ -462,22 +485,49 @@ int launch_combine_rows_warp(const float* y, int64_t ldy, int splits, int64_t sp
 #undef SB_ROWS_CASE
 }
 
+int launch_combine_rows_peer_warp(const float* y, int64_t ldy, int splits, int64_t split_stride, const int32_t* inv,
+                                  int slots, int n_tokens, int cols, const EpPeer& peer, cudaStream_t st) {
+  const dim3 grid((n_tokens + kWarpRowsPerCta - 1) / kWarpRowsPerCta), block(kWarpRowsPerCta * 32);
+#define SB_PEER_CASE(NV) \
+  case NV: return launch(combine_rows_peer_warp_kernel<NV>, grid, block, 0, st, y, ldy, splits, split_stride, inv, \
+                         slots, n_tokens, peer);
+  switch (cols / 128) {
+    SB_PEER_CASE(1) SB_PEER_CASE(2) SB_PEER_CASE(4) SB_PEER_CASE(8) SB_PEER_CASE(16)
+    default: return SB_ERR_UNSUPPORTED;
+  }
+#undef SB_PEER_CASE
+}
+
 template <typename T>
 int launch_combine_ln_warp(const float* y, int64_t ldy, int splits, int64_t split_stride, const int32_t* inv,
                            int slots, const float* delta_in, const T* h, const T* x0, int n_tokens, int cols,
                            const float* ln_w, const float* ln_b, float alpha, float beta, float eps, T* out,
-                           float* delta_out, cudaStream_t st, uint8_t* wait_region = nullptr, int64_t ctrl_off = 0,
-                           int wait_world = 0, int* wait_status = nullptr) {
+                           float* delta_out, cudaStream_t st) {
   const dim3 grid((n_tokens + kWarpRowsPerCta - 1) / kWarpRowsPerCta), block(kWarpRowsPerCta * 32);
 #define SB_LN_CASE(NV) \
   case NV: return launch(combine_ln_warp_kernel<T, NV>, grid, block, 0, st, y, ldy, splits, split_stride, inv, slots, \
-                         delta_in, h, x0, n_tokens, ln_w, ln_b, alpha, beta, eps, out, delta_out, wait_region, \
-                         ctrl_off, wait_world, wait_status);
+                         delta_in, h, x0, n_tokens, ln_w, ln_b, alpha, beta, eps, out, delta_out);
   switch (cols / 128) {
     SB_LN_CASE(1) SB_LN_CASE(2) SB_LN_CASE(4) SB_LN_CASE(8) SB_LN_CASE(16)
     default: return SB_ERR_UNSUPPORTED;
   }
 #undef SB_LN_CASE
+}
+
+template <typename T>
+int launch_combine_ln_wait_warp(const float* y, const int32_t* inv, int slots, const T* h, const T* x0, int n_tokens,
+                                int cols, const float* ln_w, const float* ln_b, float alpha, float beta, float eps,
+                                T* out, uint8_t* wait_region, int64_t ctrl_off, int wait_world, int* wait_status,
+                                cudaStream_t st) {
+  const dim3 grid((n_tokens + kWarpRowsPerCta - 1) / kWarpRowsPerCta), block(kWarpRowsPerCta * 32);
+#define SB_LNW_CASE(NV) \
+  case NV: return launch(combine_ln_wait_warp_kernel<T, NV>, grid, block, 0, st, y, int64_t(cols), inv, slots, h, x0, \
+                         n_tokens, ln_w, ln_b, alpha, beta, eps, out, wait_region, ctrl_off, wait_world, wait_status);
+  switch (cols / 128) {
+    SB_LNW_CASE(1) SB_LNW_CASE(2) SB_LNW_CASE(4) SB_LNW_CASE(8) SB_LNW_CASE(16)
+    default: return SB_ERR_UNSUPPORTED;
+  }
+#undef SB_LNW_CASE
 }
 }  // namespace
 
@@ -598,8 +648,7 @@ int combine_rows_peer(const float* y, int64_t ldy, int splits, int64_t split_str
   peer.ret_off = pa.ret_off;
   peer.ctrl_off = pa.ctrl_off;
   if (use_warp_rows(n_tokens, cols) && ldy % 4 == 0)
-    return launch_combine_rows_warp<float>(y, ldy, splits, split_stride, inv, slots, n_tokens, cols, nullptr, nullptr,
-                                           0, nullptr, st, peer);
+    return launch_combine_rows_peer_warp(y, ldy, splits, split_stride, inv, slots, n_tokens, cols, peer, st);
   return launch(combine_rows_kernel<float>, dim3(n_tokens), dim3(kCombineThreads), 0, st, y, ldy, splits, split_stride,
                 inv, slots, cols, static_cast<float*>(nullptr), static_cast<const int32_t*>(nullptr), 0,
                 static_cast<float*>(nullptr), peer);
@@ -623,14 +672,13 @@ extern "C" SB_API int sb_ep_epilogue_peer(void* region, int world, int cap, int6
   if (n_tokens == 0) return sb_ep_wait(region, world, cap, row_pitch, hidden, 1, status, stream);
   if (use_warp_rows(n_tokens, hidden) && (act_dtype == SB_F32 || act_dtype == SB_BF16)) {
     if (act_dtype == SB_F32)
-      return launch_combine_ln_warp<float>(y, hidden, 1, 0, ret_pos, top_k, nullptr, static_cast<const float*>(h),
-                                           static_cast<const float*>(x0), n_tokens, hidden, ln_w, ln_b, alpha, beta,
-                                           eps, static_cast<float*>(out), nullptr, st, reg, ctrl_off, world, status);
-    return launch_combine_ln_warp<__nv_bfloat16>(y, hidden, 1, 0, ret_pos, top_k, nullptr,
-                                                 static_cast<const __nv_bfloat16*>(h),
-                                                 static_cast<const __nv_bfloat16*>(x0), n_tokens, hidden, ln_w, ln_b,
-                                                 alpha, beta, eps, static_cast<__nv_bfloat16*>(out), nullptr, st, reg,
-                                                 ctrl_off, world, status);
+      return launch_combine_ln_wait_warp<float>(y, ret_pos, top_k, static_cast<const float*>(h),
+                                                static_cast<const float*>(x0), n_tokens, hidden, ln_w, ln_b, alpha,
+                                                beta, eps, static_cast<float*>(out), reg, ctrl_off, world, status, st);
+    return launch_combine_ln_wait_warp<__nv_bfloat16>(y, ret_pos, top_k, static_cast<const __nv_bfloat16*>(h),
+                                                      static_cast<const __nv_bfloat16*>(x0), n_tokens, hidden, ln_w,
+                                                      ln_b, alpha, beta, eps, static_cast<__nv_bfloat16*>(out), reg,
+                                                      ctrl_off, world, status, st);
   }
   if (act_dtype == SB_F32)
     return launch(combine_ln_kernel<float>, dim3(n_tokens), dim3(kLnThreads), 0, st, y, int64_t(hidden), 1,

@@ -172,10 +172,7 @@ group_place_kernel(const int32_t* __restrict__ idx, int n_rows, int slots, int G
 }
 
 // Two groupings' passes in one launch each: CTAs [0, nch0) take job 0's
-// chunks, the rest job 1's.  With gather_src, the place pass of job 0 also
-// copies every placed entry's source row (its row index e / slots of
-// gather_src, row_bytes bytes) to its position in gather_dst -- the rows the
-// grouped GEMM of job 0's groups reads.
+// chunks, the rest job 1's.
 __global__ void __launch_bounds__(kChunk)
 group_count2_kernel(const GroupJob j0, const GroupJob j1, int nch0, int32_t* __restrict__ cc0,
                     int32_t* __restrict__ cc1) {
@@ -189,40 +186,15 @@ group_count2_kernel(const GroupJob j0, const GroupJob j1, int nch0, int32_t* __r
 
 __global__ void __launch_bounds__(kChunk)
 group_place2_kernel(const GroupJob j0, const GroupJob j1, int nch0, int nch1, const int32_t* __restrict__ cc0,
-                    const int32_t* __restrict__ cc1, const uint4* __restrict__ gather_src, int row_vec,
-                    uint4* __restrict__ gather_dst) {
-  __shared__ int s_pos[kChunk];
-  __shared__ int s_row[kChunk];
+                    const int32_t* __restrict__ cc1) {
   pdl_wait();
   pdl_trigger();
   const bool first = static_cast<int>(blockIdx.x) < nch0;
   const GroupJob& j = first ? j0 : j1;
-  const int chunk = first ? blockIdx.x : blockIdx.x - nch0;
   int pos;
-  group_place_chunk(j.idx, j.n_rows, j.slots, j.num_groups, first ? nch0 : nch1, chunk, j.rank_scratch, j.w_scratch,
-                    first ? cc0 : cc1, j.offsets, j.perm_row, j.perm_slot, j.perm_w, j.inv, pos);
-  if (!first || !gather_src) return;  // CTA-uniform
-  const int64_t e = static_cast<int64_t>(chunk) * kChunk + threadIdx.x;
-  s_pos[threadIdx.x] = pos;
-  s_row[threadIdx.x] = pos >= 0 ? static_cast<int>(e / j.slots) : -1;
-  __syncthreads();
-  // the chunk's placed rows, one warp per row, 16-byte vectors
-  const int lane = threadIdx.x & 31;
-  for (int i = threadIdx.x >> 5; i < kChunk; i += kChunk / 32) {
-    const int p = s_pos[i];
-    if (p < 0) continue;  // warp-uniform
-    const uint4* src = gather_src + static_cast<int64_t>(s_row[i]) * row_vec;
-    uint4* dst = gather_dst + static_cast<int64_t>(p) * row_vec;
-    int c = lane;
-    for (; c + 96 < row_vec; c += 128) {
-      const uint4 v0 = src[c], v1 = src[c + 32], v2 = src[c + 64], v3 = src[c + 96];
-      dst[c] = v0;
-      dst[c + 32] = v1;
-      dst[c + 64] = v2;
-      dst[c + 96] = v3;
-    }
-    for (; c < row_vec; c += 32) dst[c] = src[c];
-  }
+  group_place_chunk(j.idx, j.n_rows, j.slots, j.num_groups, first ? nch0 : nch1, first ? blockIdx.x : blockIdx.x - nch0,
+                    j.rank_scratch, j.w_scratch, first ? cc0 : cc1, j.offsets, j.perm_row, j.perm_slot, j.perm_w,
+                    j.inv, pos);
 }
 
 // One warp per permuted row: the source row index is read once, then every
@@ -374,19 +346,15 @@ int group_pair_launch(const GroupJob& j0, const GroupJob& j1, cudaStream_t st) {
   return launch(group_pair_kernel, dim3(2), dim3(threads), 0, st, j0, j1);
 }
 
-int group_pair_multi_launch(const GroupJob& j0, const GroupJob& j1, int32_t* cc0, int32_t* cc1,
-                            const void* gather_src, int64_t row_bytes, void* gather_dst, cudaStream_t st) {
-  if (j0.num_groups > kGroupMaxG || j1.num_groups > kGroupMaxG || j0.n_rows <= 0 || j1.n_rows <= 0 ||
-      (gather_src && (!gather_dst || row_bytes <= 0 || row_bytes % 16)))
+int group_pair_multi_launch(const GroupJob& j0, const GroupJob& j1, int32_t* cc0, int32_t* cc1, cudaStream_t st) {
+  if (j0.num_groups > kGroupMaxG || j1.num_groups > kGroupMaxG || j0.n_rows <= 0 || j1.n_rows <= 0 || !cc0 || !cc1)
     return SB_ERR_ARG;
   const int64_t t0 = static_cast<int64_t>(j0.n_rows) * j0.slots, t1 = static_cast<int64_t>(j1.n_rows) * j1.slots;
   const int nch0 = static_cast<int>((t0 + kChunk - 1) / kChunk), nch1 = static_cast<int>((t1 + kChunk - 1) / kChunk);
   int rc = launch(group_count2_kernel, dim3(nch0 + nch1), dim3(kChunk), 0, st, j0, j1, nch0, cc0, cc1);
   if (rc) return rc;
   return launch(group_place2_kernel, dim3(nch0 + nch1), dim3(kChunk), 0, st, j0, j1, nch0, nch1,
-                static_cast<const int32_t*>(cc0), static_cast<const int32_t*>(cc1),
-                static_cast<const uint4*>(gather_src), static_cast<int>(row_bytes / 16),
-                static_cast<uint4*>(gather_dst));
+                static_cast<const int32_t*>(cc0), static_cast<const int32_t*>(cc1));
 }
 
 // Launch of the grouping kernel with caller-chosen scratch arrays (used by the

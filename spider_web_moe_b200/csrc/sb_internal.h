@@ -90,12 +90,9 @@ struct GroupJob {
 int group_pair_launch(const GroupJob& j0, const GroupJob& j1, cudaStream_t st);
 // The same two groupings with the multi-CTA two-pass schedule of sb_group
 // (identical positions), both in one count launch and one place launch;
-// cc0 / cc1 hold ceil(entries / 256) * num_groups counts per job.  With
-// gather_src the place pass also copies each of job 0's placed entries' rows
-// (row index = entry / slots, row_bytes a multiple of 16) to gather_dst.
+// cc0 / cc1 hold ceil(entries / 256) * num_groups counts per job.
 constexpr int kGroupChunk = 256;
-int group_pair_multi_launch(const GroupJob& j0, const GroupJob& j1, int32_t* cc0, int32_t* cc1,
-                            const void* gather_src, int64_t row_bytes, void* gather_dst, cudaStream_t st);
+int group_pair_multi_launch(const GroupJob& j0, const GroupJob& j1, int32_t* cc0, int32_t* cc1, cudaStream_t st);
 
 // Router + edge generator + edge top-M of small batches in one kernel
 // (sb_router.cu); SB_ERR_UNSUPPORTED when its shared memory would exceed
