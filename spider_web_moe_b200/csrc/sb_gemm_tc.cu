@@ -546,6 +546,15 @@ struct PCfg {
   static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 };
 
+// MMA width for a tile holding `rows` valid token rows (the last tile of a
+// group is usually partial): rows rounded up to 16, at most BN -- the tensor
+// core then spends no cycles on the empty columns of short tiles.
+template <int BN>
+SB_DEVINL int tile_mma_n(int rows) {
+  const int n = (rows + 15) & ~15;
+  return n < 16 ? 16 : (n > BN ? BN : n);
+}
+
 // Tile t -> (group, row tile, feature tile) from the per-group tile prefix.
 SB_DEVINL void decode_tile(const int* prefix, int G, int m_tiles, int t, int& g, int& nt, int& mt) {
   int lo = 0, hi = G - 1;
@@ -674,11 +683,15 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
   } else if (warp == 5) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(kTcBM, BN);
       int it = 0;
       bool ok = true;
       for (int j = 0; j < my_tiles && ok; ++j) {
         const int buf = j & 1;
+        int g, nt, mt;
+        decode_tile(prefix, G, m_tiles, blockIdx.x + j * gridDim.x, g, nt, mt);
+        const int tile_n0 = s_off[g] + nt * BN;
+        const int tile_end = min(min(s_off[g + 1], p.max_rows), tile_n0 + BN);
+        const uint32_t idesc = idesc_bf16_f32(kTcBM, tile_mma_n<BN>(tile_end - tile_n0));
         if (!mbar_wait(&acc_empty[buf], ((j >> 1) & 1) ^ 1, p.status, SB_DEVERR_EPI_WAIT)) break;
         tc_fence_after();
         const uint32_t acc = tmem + buf * C::kAccCols;
@@ -1001,7 +1014,11 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         int g, nt, mt;
         decode_tile(prefix, G, m_tiles, pair + j * npairs, g, nt, mt);
         const int arow = static_cast<int>(static_cast<int64_t>(g) * p.a_group_rows) + mt * kPairM + static_cast<int>(rank) * kTcBM;
-        const int nrow = s_off[g] + nt * BN + static_cast<int>(rank) * C::kBH;
+        // each CTA holds half of the tile's MMA columns: with a short last
+        // tile (tile_mma_n < BN) CTA 1's half starts at the narrower midpoint
+        const int tile_n0 = s_off[g] + nt * BN;
+        const int tile_end = min(min(s_off[g + 1], p.max_rows), tile_n0 + BN);
+        const int nrow = tile_n0 + static_cast<int>(rank) * (tile_mma_n<BN>(tile_end - tile_n0) / 2);
         for (int kk = 0; kk < nk; ++kk, ++it) {
           const int s = it % S;
           if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, p.status, SB_DEVERR_MMA_WAIT)) { ok = false; break; }
@@ -1032,11 +1049,15 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   } else if (warp == 5) {
     // ---------------------------------------------------------------- MMA issuer (leader)
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(kPairM, BN);
       int it = 0;
       bool ok = true;
       for (int j = 0; j < my_tiles && ok; ++j) {
         const int buf = j & 1;
+        int g, nt, mt;
+        decode_tile(prefix, G, m_tiles, pair + j * npairs, g, nt, mt);
+        const int tile_n0 = s_off[g] + nt * BN;
+        const int tile_end = min(min(s_off[g + 1], p.max_rows), tile_n0 + BN);
+        const uint32_t idesc = idesc_bf16_f32(kPairM, tile_mma_n<BN>(tile_end - tile_n0));
         if (!mbar_wait_cluster(&acc_empty[buf], ((j >> 1) & 1) ^ 1, p.status, SB_DEVERR_EPI_WAIT)) break;
         tc_fence_after();
         const uint32_t acc = tmem + buf * C::kAccCols;
