@@ -1399,8 +1399,10 @@ static bool use_pair(const sb_grouped_gemm_args& a) {
     return !(e && e[0] == '0');
   }();
   // fp8 / int4 weights stay on one-CTA tiles: their dequant-then-signal path
-  // measured slower on pairs than the one-CTA kernel.
-  return enabled && a.m_rows > kTcBM && a.wfmt == SB_W_BF16;
+  // measured slower on pairs than the one-CTA kernel.  So do narrow weight
+  // matrices (fewer than two 256-row pair tiles, as the dense routing
+  // logits' 272 rows): the pair's second tile would be mostly empty rows.
+  return enabled && a.m_rows >= 4 * kTcBM && a.wfmt == SB_W_BF16;
 }
 
 template <int BN, int WFMT, int EPI>

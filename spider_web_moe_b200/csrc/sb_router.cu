@@ -213,42 +213,46 @@ int router_from_logits(const float* logits, int ld, int splits, int64_t split_st
 // slot order its E edge logits (columns E + s*E .., + the folded generator
 // bias: top-M and softmax, model.py:260-266).  The biases are added in fp32
 // after the GEMM's product sum, as F.linear adds them.
+// The whole row (E + E*E logits) is loaded into shared memory in one round of
+// independent loads, with the biases staged once per CTA, so a token's
+// selection waits on one memory latency rather than three dependent ones.
+constexpr int kSelectMaxCols = 32 + 32 * 32;  // E <= 32 (the dense route's limit)
 __global__ void __launch_bounds__(kRouterWarps * 32)
 select_dense_kernel(const float* __restrict__ logits, int64_t ld, int n_tokens, int E, int K, int M,
                     const float* __restrict__ rbias, const float* __restrict__ gbias, int32_t* __restrict__ top_idx,
                     float* __restrict__ top_w, int32_t* __restrict__ edge_idx, float* __restrict__ edge_w) {
-  __shared__ float srow[kRouterWarps][kRouterMaxE];
+  __shared__ float s_bias[kSelectMaxCols];
+  __shared__ float s_row[kRouterWarps][kSelectMaxCols];
+  const int cols = E + E * E;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) s_bias[c] = c < E ? rbias[c] : gbias[c - E];
   pdl_wait();
   pdl_trigger();
+  __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* srow = s_row[warp];
   for (int64_t t = static_cast<int64_t>(blockIdx.x) * kRouterWarps + warp; t < n_tokens;
        t += static_cast<int64_t>(gridDim.x) * kRouterWarps) {
     const float* row = logits + t * ld;
-    for (int e = lane; e < E; e += 32) srow[warp][e] = row[e] + rbias[e];
+    for (int c = lane; c < cols; c += 32) srow[c] = row[c] + s_bias[c];
     __syncwarp();
     int sel_i;
     float sel_w;
-    router_select(srow[warp], E, K, lane, nullptr, sel_i, sel_w);
+    router_select(srow, E, K, lane, nullptr, sel_i, sel_w);
     if (lane < K) {
       top_idx[t * K + lane] = sel_i;
       top_w[t * K + lane] = sel_w;
     }
     for (int k = 0; k < K; ++k) {
       const int s = __shfl_sync(0xffffffffu, sel_i, k);
-      __syncwarp();  // every lane is done reading the previous row of srow
-      const float* src = row + E + static_cast<int64_t>(s) * E;
-      const float* bias = gbias + static_cast<int64_t>(s) * E;
-      for (int e = lane; e < E; e += 32) srow[warp][e] = src[e] + bias[e];
-      __syncwarp();
       int m_i;
       float m_w;
-      topm_select(srow[warp], E, M, lane, m_i, m_w);
+      topm_select(srow + E + s * E, E, M, lane, m_i, m_w);
       if (lane < M) {
         edge_idx[(t * K + k) * M + lane] = m_i;
         edge_w[(t * K + k) * M + lane] = m_w;
       }
     }
-    __syncwarp();
+    __syncwarp();  // every lane done with srow before the next token overwrites it
   }
 }
 
@@ -256,7 +260,7 @@ int select_dense(const float* logits, int64_t ld, int n_tokens, int E, int K, in
                  const float* gbias, int32_t* top_idx, float* top_w, int32_t* edge_idx, float* edge_w,
                  cudaStream_t st) {
   if (n_tokens <= 0) return SB_OK;
-  if (E > kRouterMaxE || K > 32 || K > E || M > 32 || M > E || ld < E + static_cast<int64_t>(E) * E) return SB_ERR_ARG;
+  if (E > 32 || K > 32 || K > E || M > 32 || M > E || ld < E + static_cast<int64_t>(E) * E) return SB_ERR_ARG;
   int blocks = (n_tokens + kRouterWarps - 1) / kRouterWarps;
   const int cap = 8 * current_sm_count();
   blocks = blocks > cap ? cap : blocks;

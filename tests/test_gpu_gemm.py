@@ -212,6 +212,16 @@ def test_tcgen05_swiglu_interleaved(sched, wfmt, cuda_device):
     check(got, want, "swiglu_il")
 
 
+@pytest.mark.parametrize("epi", ["linear", "gelu"])
+@pytest.mark.parametrize("rows", [[300, 0, 517, 129], [40, 256, 0, 1000]])
+def test_cta_pair_kernel(epi, rows, cuda_device):
+    """bf16 weights with at least two 256-row pair tiles take the CTA-pair
+    kernel (tcgen05.mma.cta_group::2); ragged groups end in short tiles whose
+    MMA width shrinks to the rows they hold."""
+    got, want = run_case(rows, 512, 384, "bf16", epi, "tcgen05", cuda_device, seed=len(rows) + sum(rows) % 7)
+    check(got, want, epi)
+
+
 def test_persistent_many_tiles_and_groups(cuda_device):
     """More tiles than SMs (each CTA loops, both TMEM accumulators turn over many
     times) and 200 groups of ragged sizes, zeros included."""
