@@ -350,6 +350,16 @@ SB_DEVINL uint64_t smem_desc_k_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Untiled bulk copy of `bytes` contiguous global bytes into this CTA's shared
+// memory, completing on `bar` (both addresses 16-byte aligned, bytes a
+// multiple of 16).
+SB_DEVINL void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // Four rows (row0..row3) x one box of columns starting at c0 gathered into
 // this CTA's shared memory (2-D tensor map with a one-row box).
 SB_DEVINL void tma_gather4(void* smem_dst, const void* desc, uint64_t* bar, int c0, int r0, int r1, int r2,

@@ -90,12 +90,60 @@ SB_DEVINL uint32_t int4x2_biased_bf16x2(uint32_t x) {
   return lo | hi | 0x43004300u;
 }
 
+// One 16-byte chunk of a raw fp8 tile row (16 weights, e4m3) -> two 16-byte
+// bf16 chunks of the swizzled tile: row `row`, 16-byte chunk c16 of its 64 bytes.
+SB_DEVINL void convert_fp8_chunk(const uint4 v, uint8_t* dst, int row, int c16) {
+  const uint8_t* b = reinterpret_cast<const uint8_t*>(&v);
+  uint32_t out[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(
+        static_cast<__nv_fp8x2_storage_t>(b[2 * j] | (b[2 * j + 1] << 8)), __NV_E4M3);
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+    const __nv_bfloat162 bb = __floats2bfloat162_rn(f.x, f.y);
+    out[j] = *reinterpret_cast<const uint32_t*>(&bb);
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int kc = c16 * 2 + h;  // 16-byte chunk (8 bf16) index along k
+    *reinterpret_cast<uint4*>(dst + row * 128 + ((kc ^ (row & 7)) << 4)) =
+        make_uint4(out[4 * h], out[4 * h + 1], out[4 * h + 2], out[4 * h + 3]);
+  }
+}
+
+// One 16-byte chunk of a raw int4 tile row (32 weights) with its group scale
+// -> four 16-byte bf16 chunks of the swizzled tile (row `row`, chunk c16 of
+// its 32 bytes).  Each weight is bf16(q * s) with one rounding, as the
+// CUDA-core engine and the oracle compute it: (128 + u) - 136 is exact in
+// bf16 and the bf16x2 multiply rounds the exact product once.
+SB_DEVINL void convert_int4_chunk(const uint4 v, const __nv_bfloat16 sb, uint8_t* dst, int row, int c16) {
+  const __nv_bfloat162 bias = __float2bfloat162_rn(136.f);
+  const __nv_bfloat162 s2 = __bfloat162bfloat162(sb);
+  const uint32_t w[4] = {v.x ^ 0x88888888u, v.y ^ 0x88888888u, v.z ^ 0x88888888u, v.w ^ 0x88888888u};
+  uint32_t out[16];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t pr[4] = {int4x2_biased_bf16x2<0>(w[i]), int4x2_biased_bf16x2<8>(w[i]),
+                      int4x2_biased_bf16x2<16>(w[i]), int4x2_biased_bf16x2<24>(w[i])};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __nv_bfloat162 qv = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&pr[j]), bias);
+      const __nv_bfloat162 r = __hmul2(qv, s2);
+      out[4 * i + j] = *reinterpret_cast<const uint32_t*>(&r);
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const int kc = c16 * 4 + h;
+    *reinterpret_cast<uint4*>(dst + row * 128 + ((kc ^ (row & 7)) << 4)) =
+        make_uint4(out[4 * h], out[4 * h + 1], out[4 * h + 2], out[4 * h + 3]);
+  }
+}
+
 // Convert the raw fp8 / int4 tile of this stage into the swizzled bf16 tile.
 // int4: the group scale of (row, k0) comes from `s_scale[row * s_ngr + k0 /
 // group_size - s_g0]` in shared memory when s_scale is given, else from global
-// memory.  Each weight is bf16(q * s) with one rounding, as the CUDA-core
-// engine and the oracle compute it: (128 + u) - 136 is exact in bf16 and the
-// bf16x2 multiply rounds the exact product once.
+// memory.
 template <int WFMT>
 SB_DEVINL void convert_tile(const uint8_t* raw, uint8_t* dst, const sb_grouped_gemm_args& p,
                             const void* scales, int64_t arow0, int k0, int tid,
@@ -106,29 +154,12 @@ SB_DEVINL void convert_tile(const uint8_t* raw, uint8_t* dst, const sb_grouped_g
     for (int q = 0; q < 4; ++q) {
       const int item = tid + 128 * q;
       const int row = item >> 2, c16 = item & 3;
-      const uint4 v = *reinterpret_cast<const uint4*>(raw + row * 64 + c16 * 16);
-      const uint8_t* b = reinterpret_cast<const uint8_t*>(&v);
-      uint32_t out[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(
-            static_cast<__nv_fp8x2_storage_t>(b[2 * j] | (b[2 * j + 1] << 8)), __NV_E4M3);
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
-        const __nv_bfloat162 bb = __floats2bfloat162_rn(f.x, f.y);
-        out[j] = *reinterpret_cast<const uint32_t*>(&bb);
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int kc = c16 * 2 + h;  // 16-byte chunk (8 bf16) index along k
-        *reinterpret_cast<uint4*>(dst + row * 128 + ((kc ^ (row & 7)) << 4)) =
-            make_uint4(out[4 * h], out[4 * h + 1], out[4 * h + 2], out[4 * h + 3]);
-      }
+      convert_fp8_chunk(*reinterpret_cast<const uint4*>(raw + row * 64 + c16 * 16), dst, row, c16);
     }
   } else {
     // 128 rows x 32 bytes; item = (row, 16-byte chunk): 256 items over 128 threads.
     const int groups = static_cast<int>(p.lda / p.group_size);
     const int gk = k0 / p.group_size;
-    const __nv_bfloat162 bias = __float2bfloat162_rn(136.f);
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const int item = tid + 128 * q;
@@ -140,27 +171,7 @@ SB_DEVINL void convert_tile(const uint8_t* raw, uint8_t* dst, const sb_grouped_g
       else
         sb = arow < p.a_rows_total ? static_cast<const __nv_bfloat16*>(scales)[arow * groups + gk]
                                    : __float2bfloat16_rn(0.f);
-      const __nv_bfloat162 s2 = __bfloat162bfloat162(sb);
-      const uint4 v = *reinterpret_cast<const uint4*>(raw + row * 32 + c16 * 16);
-      const uint32_t w[4] = {v.x ^ 0x88888888u, v.y ^ 0x88888888u, v.z ^ 0x88888888u, v.w ^ 0x88888888u};
-      uint32_t out[16];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        uint32_t pr[4] = {int4x2_biased_bf16x2<0>(w[i]), int4x2_biased_bf16x2<8>(w[i]),
-                          int4x2_biased_bf16x2<16>(w[i]), int4x2_biased_bf16x2<24>(w[i])};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const __nv_bfloat162 qv = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&pr[j]), bias);
-          const __nv_bfloat162 r = __hmul2(qv, s2);
-          out[4 * i + j] = *reinterpret_cast<const uint32_t*>(&r);
-        }
-      }
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        const int kc = c16 * 4 + h;
-        *reinterpret_cast<uint4*>(dst + row * 128 + ((kc ^ (row & 7)) << 4)) =
-            make_uint4(out[4 * h], out[4 * h + 1], out[4 * h + 2], out[4 * h + 3]);
-      }
+      convert_int4_chunk(*reinterpret_cast<const uint4*>(raw + row * 32 + c16 * 16), sb, dst, row, c16);
     }
   }
 }
@@ -845,6 +856,465 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
   }
 }
 
+// ------------------------------------------------------------------ quantised decode GEMM
+//
+// fp8 / int4 weights with few token rows per group (decode batches; a
+// Zipf-skewed router still sends up to every token to a few experts).  A
+// tcgen05.mma of M=128, K=16 keeps the tensor pipe busy about as long at N=16
+// as at N=256, so here the roles are swapped: the converted weights are the B
+// operand (N = 256 weight rows per MMA) and the token rows the A operand
+// (M = 128; rows past the item's tokens are never stored) -- twice the weights
+// per MMA of a weights-as-A tile.  A persistent CTA per SM walks the
+// (group, 128-token chunk, 256-weight-row tile) items, weight tile fastest.
+// Packed weight tiles have a ring of their own; two groups of converter warps
+// take alternate stages, so one group's conversion overlaps the other's waits.
+// int4 group scales of an item (256 consecutive rows of the scale matrix, one
+// contiguous block) come with one bulk copy into a double-buffered slot.  Two
+// TMEM accumulators of 256 columns: the epilogue of item i overlaps the MMAs
+// of item i+1; an epilogue thread holds one token row of the item.
+// Warps: 0-3 epilogue, 4-19 convert (two groups of eight), 20 weight TMA,
+// 21 MMA (+TMEM), 22 token-row TMA (16-row boxes, or tile::gather4).
+template <int WFMT, int EPI>
+struct QCfg {
+  static constexpr bool kIL = EPI == SB_EPI_SWIGLU_IL;
+  static constexpr int kWRows = 256;                  // weight rows per item (MMA N)
+  static constexpr int kTokM = 128;                   // token rows per item (MMA M)
+  static constexpr int kWBytes = kWRows * kTcBK * 2;  // converted weights of a stage (B operand)
+  static constexpr int kXBytes = kTokM * kTcBK * 2;   // token rows of a stage (A operand)
+  static constexpr int kRawBytes = WFMT == SB_W_FP8 ? kWRows * kTcBK : kWRows * kTcBK / 2;
+  // Ring depths.  The two converter groups take the stages of even / odd
+  // global index: with an even raw ring every raw slot stays with one group,
+  // so a group never polls a slot's barrier two phases ahead of it (a parity
+  // wait cannot tell those apart).  The three converted stages alternate
+  // between the groups, which is safe because a group reaches stage i only
+  // after its stage i - 2, whose wait saw the MMAs of stage i - 5 complete.
+  static constexpr int kStages = 3;
+  static constexpr int kRawStages = 4;
+  static constexpr int kGroupThreads = 256;  // one converter group
+  static constexpr int kConvThreads = 2 * kGroupThreads;
+  static constexpr int kChunks = kRawBytes / 16 / kGroupThreads;  // 16-byte chunks per thread and stage
+  static constexpr int kEpiThreads = 128;
+  static constexpr int kThreads = 736;
+  static constexpr int kTmemCols = 512;
+  static constexpr int kMaxG = 256;
+  static constexpr int kOffW = 0;
+  static constexpr int kOffX = kOffW + kStages * kWBytes;
+  static constexpr int kOffRaw = kOffX + kStages * kXBytes;
+  static constexpr int kOffBar = kOffRaw + kRawStages * kRawBytes;
+  static constexpr int kOffMisc = kOffBar + (2 * kRawStages + 3 * kStages + 8) * 8;
+  static constexpr int kOffPrefix = kOffMisc + 64;                  // int[kMaxG + 1]
+  static constexpr int kOffOffsets = kOffPrefix + (kMaxG + 1) * 4;  // int[kMaxG + 1]
+  // int4: two slots of an item's group scales, 256 rows x up to 32 groups of bf16
+  static constexpr int kScaleMaxGroups = 32;
+  static constexpr int kScaleSlotBytes = WFMT == SB_W_INT4 ? kWRows * kScaleMaxGroups * 2 : 0;
+  static constexpr int kOffScale = (kOffOffsets + (kMaxG + 1) * 4 + 127) / 128 * 128;  // 16-byte aligned copies
+  static constexpr int kSmemBytes = kOffScale + 2 * kScaleSlotBytes + 1024;
+  static_assert(WFMT == SB_W_FP8 || WFMT == SB_W_INT4, "packed weight formats only");
+  static_assert(EPI == SB_EPI_LINEAR || EPI == SB_EPI_GELU || EPI == SB_EPI_SWIGLU_IL, "one weight operand");
+  static_assert(kChunks * 16 * kGroupThreads == kRawBytes, "whole chunks per thread");
+  static_assert(kRawStages % 2 == 0, "raw slots must stay with one converter group");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+};
+
+template <int WFMT, int EPI, bool kGather>
+__global__ void __launch_bounds__(QCfg<WFMT, EPI>::kThreads, 1)
+tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                    const sb_grouped_gemm_args p) {
+  using C = QCfg<WFMT, EPI>;
+  constexpr int S = C::kStages, R = C::kRawStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* rfull = reinterpret_cast<uint64_t*>(smem + C::kOffBar);  // [R] packed weight tile landed
+  uint64_t* rempty = rfull + R;                                      // [R] packed tile read by its converters
+  uint64_t* xfull = rempty + R;                                      // [S] token rows landed
+  uint64_t* conv = xfull + S;                                        // [S] bf16 weight tile written
+  uint64_t* empty = conv + S;                                        // [S] stage's MMAs done
+  uint64_t* acc_full = empty + S;                                    // [2]
+  uint64_t* acc_empty = acc_full + 2;                                // [2]
+  uint64_t* sfull = acc_empty + 2;                                   // [2] int4 scale slot landed
+  uint64_t* sempty = sfull + 2;                                      // [2] int4 scale slot released
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
+  int* s_total = reinterpret_cast<int*>(smem + C::kOffMisc + 16);
+  int* prefix = reinterpret_cast<int*>(smem + C::kOffPrefix);
+  int* s_off = reinterpret_cast<int*>(smem + C::kOffOffsets);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = p.num_groups;
+  const int f_tiles = (p.m_rows + C::kWRows - 1) / C::kWRows;
+  const int nk = p.k / kTcBK;
+  // int4: an item's scales [256 rows x groups] by one bulk copy when the block
+  // lies inside the scale matrix, fits a slot and starts 16-byte aligned
+  // (producer and converters take the same decision per item)
+  const int groups = WFMT == SB_W_INT4 ? static_cast<int>(p.lda / p.group_size) : 0;
+  const __nv_bfloat16* scales = static_cast<const __nv_bfloat16*>(p.a_scale);
+  auto bulk_scales = [&](int64_t arow0) {
+    return WFMT == SB_W_INT4 && arow0 + C::kWRows <= p.a_rows_total && groups <= C::kScaleMaxGroups &&
+           (reinterpret_cast<uintptr_t>(scales + arow0 * groups) & 15) == 0;
+  };
+  if (tid == 0) {
+    for (int r = 0; r < R; ++r) {
+      mbar_init(&rfull[r], 1);
+      mbar_init(&rempty[r], C::kGroupThreads);
+    }
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&conv[s], C::kGroupThreads);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], C::kEpiThreads);
+      mbar_init(&sfull[b], 1);
+      mbar_init(&sempty[b], C::kConvThreads);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 20 && lane == 0) {
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmX);
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (warp == 0) {
+    // per-group items (128-token chunks x 256-row weight tiles) -> exclusive prefix
+    int seen = 0;
+    for (int base = 0; base < G; base += 32) {
+      const int gi = base + lane;
+      int items = 0;
+      if (gi < G) {
+        const int o0 = group_offset(p.offsets, gi, p.max_rows), o1 = group_offset(p.offsets, gi + 1, p.max_rows);
+        s_off[gi] = o0;
+        if (gi == G - 1) s_off[G] = o1;
+        const int lo = min(o0, p.max_rows), hi = min(o1, p.max_rows);
+        items = hi > lo ? (hi - lo + C::kTokM - 1) / C::kTokM * f_tiles : 0;
+      }
+      int incl = items;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += t;
+      }
+      if (gi < G) prefix[gi] = seen + incl - items;
+      seen += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      prefix[G] = seen;
+      *s_total = seen;
+    }
+  }
+  __syncthreads();
+  const int total = *s_total;
+  if (static_cast<int>(blockIdx.x) >= total) return;  // no item for this CTA
+  const int my_items = (total - static_cast<int>(blockIdx.x) + gridDim.x - 1) / gridDim.x;
+
+  if (warp == 21) {
+    tmem_alloc(s_tmem, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 20) {
+    // ---------------------------------------------------------------- packed weight tiles (+ int4 scales)
+    if (lane == 0) {
+      int ri = 0, ub = 0;  // raw tiles and scale blocks issued
+      bool ok = true;
+      for (int j = 0; j < my_items && ok; ++j) {
+        int g, nt, ft;
+        decode_tile(prefix, G, f_tiles, blockIdx.x + j * gridDim.x, g, nt, ft);
+        const int arow = static_cast<int>(static_cast<int64_t>(g) * p.a_group_rows + ft * C::kWRows);
+        if (bulk_scales(arow)) {
+          const int sb = ub & 1;
+          if (!mbar_wait(&sempty[sb], ((ub >> 1) & 1) ^ 1, p.status, SB_DEVERR_CONV_WAIT)) break;
+          const uint32_t bytes = static_cast<uint32_t>(C::kWRows * groups * 2);
+          mbar_expect_tx(&sfull[sb], bytes);
+          bulk_load(smem + C::kOffScale + sb * C::kScaleSlotBytes, scales + static_cast<int64_t>(arow) * groups, bytes,
+                    &sfull[sb]);
+          ++ub;
+        }
+        for (int kk = 0; kk < nk; ++kk, ++ri) {
+          const int r = ri % R;
+          if (!mbar_wait(&rempty[r], ((ri / R) & 1) ^ 1, p.status, SB_DEVERR_CONV_WAIT)) { ok = false; break; }
+          mbar_expect_tx(&rfull[r], C::kRawBytes);
+          const int k0 = kk * kTcBK;
+          tma_load_2d(smem + C::kOffRaw + r * C::kRawBytes, &tmW, &rfull[r], WFMT == SB_W_INT4 ? k0 / 2 : k0, arow);
+        }
+      }
+      for (int i = ri - R > 0 ? ri - R : 0; i < ri; ++i)  // drain
+        if (!mbar_wait(&rfull[i % R], (i / R) & 1, p.status, SB_DEVERR_DRAIN)) break;
+      for (int i = ub - 2 > 0 ? ub - 2 : 0; i < ub; ++i)
+        if (!mbar_wait(&sfull[i & 1], (i >> 1) & 1, p.status, SB_DEVERR_DRAIN)) break;
+    }
+    __syncwarp();
+  } else if (warp == 22) {
+    // ---------------------------------------------------------------- token rows
+    int si = 0;
+    bool ok = true;
+    for (int j = 0; j < my_items && ok; ++j) {
+      int g, nt, ft;
+      decode_tile(prefix, G, f_tiles, blockIdx.x + j * gridDim.x, g, nt, ft);
+      const int n0 = s_off[g] + nt * C::kTokM;
+      const int n_end = min(min(s_off[g + 1], p.max_rows), n0 + C::kTokM);
+      // only the item's rows are fetched: 4-row gathers (one per lane) or 16-row boxes
+      const int nb = kGather ? (n_end - n0 + 3) / 4 : (n_end - n0 + 15) / 16;
+      const uint32_t tx = kGather ? nb * 512u : nb * 2048u;
+      int rix[4] = {0, 0, 0, 0};
+      if (kGather && lane < nb) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) rix[r] = p.x_row_index[min(n0 + 4 * lane + r, n_end - 1)];
+      }
+      for (int kk = 0; kk < nk; ++kk, ++si) {
+        const int s = si % S;
+        bool w = true;
+        if (lane == 0) {
+          w = mbar_wait(&empty[s], ((si / S) & 1) ^ 1, p.status, SB_DEVERR_MMA_WAIT);
+          if (w) mbar_expect_tx(&xfull[s], tx);
+        }
+        w = __shfl_sync(0xffffffffu, w, 0);
+        if (!w) { ok = false; break; }
+        const int k0 = kk * kTcBK;
+        uint8_t* xdst = smem + C::kOffX + s * C::kXBytes;
+        if (kGather) {
+          __syncwarp();
+          if (lane < nb) tma_gather4(xdst + lane * 512, &tmX, &xfull[s], k0, rix[0], rix[1], rix[2], rix[3]);
+        } else if (lane == 0) {
+          for (int q = 0; q < nb; ++q) tma_load_2d(xdst + q * 2048, &tmX, &xfull[s], k0, n0 + 16 * q);
+        }
+      }
+    }
+    if (lane == 0)
+      for (int i = si - S > 0 ? si - S : 0; i < si; ++i)  // drain
+        if (!mbar_wait(&xfull[i % S], (i / S) & 1, p.status, SB_DEVERR_DRAIN)) break;
+    __syncwarp();
+  } else if (warp == 21) {
+    // ---------------------------------------------------------------- MMA issuer: D[token, weight row]
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(C::kTokM, C::kWRows);
+      int si = 0;
+      bool ok = true;
+      for (int j = 0; j < my_items && ok; ++j) {
+        const int buf = j & 1;
+        if (!mbar_wait(&acc_empty[buf], ((j >> 1) & 1) ^ 1, p.status, SB_DEVERR_EPI_WAIT)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + buf * C::kWRows;
+        for (int kk = 0; kk < nk; ++kk, ++si) {
+          const int s = si % S;
+          const uint32_t ph = (si / S) & 1;
+          ok = mbar_wait(&conv[s], ph, p.status, SB_DEVERR_CONV_WAIT) &&
+               mbar_wait(&xfull[s], ph, p.status, SB_DEVERR_TMA_WAIT);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t x_base = smem_u32(smem + C::kOffX + s * C::kXBytes);
+          const uint32_t w_base = smem_u32(smem + C::kOffW + s * C::kWBytes);
+#pragma unroll
+          for (int q = 0; q < kTcBK / 16; ++q)
+            tc_mma_bf16(acc, smem_desc_k_sw128(x_base + q * 32), smem_desc_k_sw128(w_base + q * 32), idesc,
+                        (kk > 0 || q > 0) ? 1u : 0u);
+          tc_commit(&empty[s]);
+        }
+        tc_commit(&acc_full[buf]);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------------- convert (warps 4-19)
+    // Group cg = 0 / 1 converts the stages of even / odd global index.  Thread
+    // gt of a group: int4 rows gt / 2 and 128 + gt / 2, 16-byte chunk gt % 2 of
+    // 32 bytes; fp8 rows gt / 4 + 64 q (q < 4), chunk gt % 4 of 64 bytes.
+    const int cg = (warp - 4) >> 3;
+    const int gt = tid - 128 - cg * C::kGroupThreads;
+    constexpr int kRowStep = WFMT == SB_W_INT4 ? 128 : 64;
+    const int row0 = WFMT == SB_W_INT4 ? gt >> 1 : gt >> 2;
+    const int c16 = WFMT == SB_W_INT4 ? gt & 1 : gt & 3;
+    constexpr int kRowBytes = WFMT == SB_W_INT4 ? kTcBK / 2 : kTcBK;
+    int ub = 0;
+    bool ok = true;
+    for (int j = 0; j < my_items && ok; ++j) {
+      int g, nt, ft;
+      decode_tile(prefix, G, f_tiles, blockIdx.x + j * gridDim.x, g, nt, ft);
+      const int64_t arow0 = static_cast<int64_t>(g) * p.a_group_rows + ft * C::kWRows;
+      // int4 scales of this thread's rows: the item's bulk-copied block, else global memory
+      const bool bulk = bulk_scales(arow0);
+      const __nv_bfloat16* srow[C::kChunks];
+      if (WFMT == SB_W_INT4) {
+        if (bulk && !mbar_wait(&sfull[ub & 1], (ub >> 1) & 1, p.status, SB_DEVERR_TMA_WAIT)) break;
+        const __nv_bfloat16* slot =
+            reinterpret_cast<const __nv_bfloat16*>(smem + C::kOffScale + (ub & 1) * C::kScaleSlotBytes);
+#pragma unroll
+        for (int c = 0; c < C::kChunks; ++c) {
+          const int row = row0 + c * kRowStep;
+          srow[c] = bulk ? slot + row * groups
+                         : (arow0 + row < p.a_rows_total ? scales + (arow0 + row) * groups : nullptr);
+        }
+      }
+      const int ci0 = j * nk;
+      for (int kk = ((ci0 & 1) == cg) ? 0 : 1; kk < nk; kk += 2) {
+        const int ci = ci0 + kk;
+        const int r = ci % R, s = ci % S;
+        const int k0 = kk * kTcBK;
+        __nv_bfloat16 sb[C::kChunks];
+        if (WFMT == SB_W_INT4) {
+#pragma unroll
+          for (int c = 0; c < C::kChunks; ++c) sb[c] = srow[c] ? srow[c][k0 / p.group_size] : __float2bfloat16_rn(0.f);
+        }
+        if (!mbar_wait(&rfull[r], (ci / R) & 1, p.status, SB_DEVERR_TMA_WAIT)) { ok = false; break; }
+        const uint8_t* raw = smem + C::kOffRaw + r * C::kRawBytes;
+        uint4 v[C::kChunks];
+#pragma unroll
+        for (int c = 0; c < C::kChunks; ++c)
+          v[c] = *reinterpret_cast<const uint4*>(raw + (row0 + c * kRowStep) * kRowBytes + c16 * 16);
+        // The packed bytes are in registers: the slot may refill.  The next
+        // write into it is a TMA copy (async proxy), so the generic-proxy reads
+        // above are ordered before it by a proxy fence ahead of the release.
+        fence_proxy_async_smem();
+        mbar_arrive(&rempty[r]);
+        if (!mbar_wait(&empty[s], ((ci / S) & 1) ^ 1, p.status, SB_DEVERR_MMA_WAIT)) { ok = false; break; }
+        uint8_t* dst = smem + C::kOffW + s * C::kWBytes;
+#pragma unroll
+        for (int c = 0; c < C::kChunks; ++c) {
+          if (WFMT == SB_W_INT4)
+            convert_int4_chunk(v[c], sb[c], dst, row0 + c * kRowStep, c16);
+          else
+            convert_fp8_chunk(v[c], dst, row0 + c * kRowStep, c16);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&conv[s]);
+      }
+      if (bulk) {
+        if (ok) {  // the item's scales are no longer read; the slot's next write is a bulk copy
+          fence_proxy_async_smem();
+          mbar_arrive(&sempty[ub & 1]);
+        }
+        ++ub;
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 0-3)
+    // Thread = one token row of the item (TMEM lane); its 256 columns are the
+    // outputs of the item's 256 weight rows.
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    constexpr int kVec = EPI == SB_EPI_LINEAR ? 4 : 8;  // elements per 16-byte store
+    const bool vec_ok = (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && p.ldo % kVec == 0;
+    for (int j = 0; j < my_items; ++j) {
+      int g, nt, ft;
+      decode_tile(prefix, G, f_tiles, blockIdx.x + j * gridDim.x, g, nt, ft);
+      const int buf = j & 1;
+      const int n0 = s_off[g] + nt * C::kTokM;
+      const int tend = min(min(s_off[g + 1], p.max_rows), n0 + C::kTokM);
+      const int tok = n0 + warp * 32 + lane;
+      const bool tvalid = tok < tend;
+      const float rs = (EPI == SB_EPI_LINEAR && p.row_scale && tvalid) ? p.row_scale[tok] : 1.f;
+      const int wr0 = ft * C::kWRows;  // first weight row of the item within its group
+      const int64_t arow0 = static_cast<int64_t>(g) * p.a_group_rows + wr0;
+      const float* bias = p.bias ? p.bias + static_cast<int64_t>(g) * p.bias_group_stride + wr0 : nullptr;
+      const float* fs = WFMT == SB_W_FP8 ? static_cast<const float*>(p.a_scale) + arow0 : nullptr;
+      const int wvalid = min(C::kWRows, p.m_rows - wr0);  // weight rows of this tile inside the group
+      const bool ready =
+          __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (j >> 1) & 1, p.status, SB_DEVERR_EPI_WAIT));
+      tc_fence_after();
+      if (!ready) break;
+      const uint32_t acc_addr = lane_addr + buf * C::kWRows;
+      // weight row wr of the tile -> its fp32 output before the activation
+      auto lin = [&](float a, int wr) {
+        float x = a;
+        if (WFMT == SB_W_FP8 && wr < wvalid && arow0 + wr < p.a_rows_total) x *= fs[wr];
+        if (bias && wr < wvalid) x += bias[wr];
+        return x;
+      };
+      if (__any_sync(0xffffffffu, tvalid)) {  // tcgen05.ld is warp-collective
+        if constexpr (C::kIL) {
+          // columns [gate 64 | up 64] per 128-row block: the features of block b
+          // are (wr0 + 128 b) / 2 + i, i < 64
+#pragma unroll 1
+          for (int b = 0; b < 2; ++b) {
+            if (b * 128 >= wvalid) break;
+            const int64_t feat0 = (wr0 + b * 128) / 2;
+#pragma unroll 1
+            for (int c0 = 0; c0 < 64; c0 += 16) {
+              float gv[16], uv[16], o[16];
+              tmem_ld16(acc_addr + b * 128 + c0, gv);
+              tmem_ld16(acc_addr + b * 128 + 64 + c0, uv);
+#pragma unroll
+              for (int q = 0; q < 16; ++q) {
+                const float gate = silu_bf16out(lin(gv[q], b * 128 + c0 + q));
+                o[q] = lin(uv[q], b * 128 + 64 + c0 + q) * gate;
+              }
+              if (!tvalid) continue;
+              __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(tok) * p.ldo + feat0 + c0;
+              if (vec_ok) {
+                uint32_t w[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                  const __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * q], o[2 * q + 1]);
+                  w[q] = *reinterpret_cast<const uint32_t*>(&h);
+                }
+                reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+              } else {
+#pragma unroll
+                for (int q = 0; q < 16; ++q) dst[q] = __float2bfloat16_rn(o[q]);
+              }
+            }
+          }
+        } else {
+#pragma unroll 1
+          for (int c0 = 0; c0 < C::kWRows; c0 += 16) {
+            if (c0 >= wvalid) break;  // warp-uniform
+            float v[16], o[16];
+            tmem_ld16(acc_addr + c0, v);
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              const float x = lin(v[q], c0 + q);
+              o[q] = EPI == SB_EPI_LINEAR ? x * rs : gelu_bf16out(x);
+            }
+            if (!tvalid) continue;
+            const int nv = min(16, wvalid - c0);
+            const int64_t base = static_cast<int64_t>(tok) * p.ldo + wr0 + c0;
+            if (EPI == SB_EPI_LINEAR) {
+              float* dst = static_cast<float*>(p.out) + base;
+              if (vec_ok && nv == 16) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                  reinterpret_cast<float4*>(dst)[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+              } else {
+#pragma unroll
+                for (int q = 0; q < 16; ++q)
+                  if (q < nv) dst[q] = o[q];
+              }
+            } else {
+              __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + base;
+              if (vec_ok && nv == 16) {
+                uint32_t w[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                  const __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * q], o[2 * q + 1]);
+                  w[q] = *reinterpret_cast<const uint32_t*>(&h);
+                }
+                reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+              } else {
+#pragma unroll
+                for (int q = 0; q < 16; ++q)
+                  if (q < nv) dst[q] = __float2bfloat16_rn(o[q]);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 21) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------ persistent CTA-pair GEMM
 //
 // The persistent schedule of the kernel above on CTA pairs (clusters of two):
@@ -1382,6 +1852,70 @@ static int launch_persistent(const sb_grouped_gemm_args& a, cudaStream_t st) {
   return launch(kern, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, ma, mg, mb, a);
 }
 
+// SPIDER_B200_QDEC=0 keeps quantised decode GEMMs on the tiled kernels (for comparisons).
+static bool use_qdec(const sb_grouped_gemm_args& a) {
+  static const bool enabled = [] {
+    const char* e = std::getenv("SPIDER_B200_QDEC");
+    return !(e && e[0] == '0');
+  }();
+  if (!enabled || (a.wfmt != SB_W_FP8 && a.wfmt != SB_W_INT4)) return false;
+  if (a.splits != 1 || a.num_groups > kPersistentMaxGroups || a.epilogue == SB_EPI_SWIGLU) return false;
+  if (a.x_row_index && a.x_rows <= 0) return false;
+  // decode batches: the expected rows per group are few (the tiled kernels'
+  // column tile would be at most 64)
+  const int hint = a.rows_hint > 0 ? a.rows_hint : a.max_rows;
+  return (hint + a.num_groups - 1) / a.num_groups <= 64;
+}
+
+template <int WFMT, int EPI, bool kGather>
+static int launch_qdec(const sb_grouped_gemm_args& a, cudaStream_t st) {
+  using C = QCfg<WFMT, EPI>;
+  auto kern = tc_gemm_qdec_kernel<WFMT, EPI, kGather>;
+  static int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e);
+    configured_device = dev;
+  }
+  static_assert(C::kMaxG == kPersistentMaxGroups, "prefix table size");
+  if (a.num_groups > C::kMaxG || a.splits != 1) return SB_ERR_UNSUPPORTED;
+  // weights: 256-row boxes of one K step (packed bytes); tokens: 16-row boxes or one-row gathers
+  CUtensorMap mw, mx;
+  const bool ok_w =
+      WFMT == SB_W_FP8
+          ? make_map(&mw, a.a, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.lda, a.a_rows_total, a.lda, kTcBK, C::kWRows,
+                     CU_TENSOR_MAP_SWIZZLE_NONE)
+          : make_map(&mw, a.a, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.lda / 2, a.a_rows_total, a.lda / 2, kTcBK / 2,
+                     C::kWRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  const bool ok_x =
+      kGather ? make_map(&mx, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.k, a.x_rows, a.ldx * 2, kTcBK, 1,
+                         CU_TENSOR_MAP_SWIZZLE_128B)
+              : make_map(&mx, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.k, a.max_rows, a.ldx * 2, kTcBK, 16,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!ok_w || !ok_x) return SB_ERR_UNSUPPORTED;
+  const int f_tiles = (a.m_rows + C::kWRows - 1) / C::kWRows;
+  const int64_t bound = static_cast<int64_t>(f_tiles) * ((a.max_rows + C::kTokM - 1) / C::kTokM + a.num_groups);
+  const int sms = current_sm_count();
+  const int grid = static_cast<int>(bound < sms ? bound : sms);
+  return launch(kern, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, mw, mx, a);
+}
+
+template <int WFMT>
+static int launch_qdec_epi(const sb_grouped_gemm_args& a, cudaStream_t st) {
+  const bool g = a.x_row_index != nullptr;
+  switch (a.epilogue) {
+    case SB_EPI_LINEAR:
+      return g ? launch_qdec<WFMT, SB_EPI_LINEAR, true>(a, st) : launch_qdec<WFMT, SB_EPI_LINEAR, false>(a, st);
+    case SB_EPI_GELU:
+      return g ? launch_qdec<WFMT, SB_EPI_GELU, true>(a, st) : launch_qdec<WFMT, SB_EPI_GELU, false>(a, st);
+    case SB_EPI_SWIGLU_IL:
+      return g ? launch_qdec<WFMT, SB_EPI_SWIGLU_IL, true>(a, st) : launch_qdec<WFMT, SB_EPI_SWIGLU_IL, false>(a, st);
+    default: return SB_ERR_UNSUPPORTED;
+  }
+}
+
 // SPIDER_B200_TMA_STORE=0 makes the large-tile epilogues store element by
 // element instead of through shared memory and bulk tensor stores (for comparisons).
 static bool use_tma_out() {
@@ -1596,6 +2130,10 @@ int dequant_to_bf16(int wfmt, const void* q, const void* scales, int group_size,
 }
 
 int gemm_tcgen05(const sb_grouped_gemm_args& a, cudaStream_t st) {
+  if (use_qdec(a)) {
+    const int rc = a.wfmt == SB_W_FP8 ? launch_qdec_epi<SB_W_FP8>(a, st) : launch_qdec_epi<SB_W_INT4>(a, st);
+    if (rc != SB_ERR_UNSUPPORTED) return rc;
+  }
   const int bn = tc_tile_n(a);
   switch (a.wfmt) {
     case SB_W_BF16: return launch_epi<SB_W_BF16>(a, st, bn);

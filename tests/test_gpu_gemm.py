@@ -171,7 +171,11 @@ SCHEDULES = {
     "fixed16_gather": ([5, 0, 16, 9, 1], 16, 1, True),
     "fixed64": ([40, 64, 3, 0, 57], 64, 1, False),
     "fixed_multi_tile": ([150, 7, 0, 70], 64, 1, False),   # groups beyond the bound loop over row tiles
+    "fixed64_split2": ([40, 64, 3, 0, 57], 64, 2, False),  # fp8 / int4: the fixed kernel's conversion
     "slot64": ([70, 40, 90, 1], 0, 1, False),
+    # fp8 / int4 decode batches with one hot group (2 items of 256 rows) and many
+    # small ones: the quantised decode kernel, token rows gathered
+    "qdec_skewed_gather": ([300, 2, 0, 17, 64, 1, 0, 5, 33, 9, 0, 3, 40, 8, 1, 6], 0, 1, True),
     "slot64_split2": ([70, 40, 90, 1], 0, 2, False),
     "persistent128": ([100, 130, 0, 90, 120], 0, 1, False),
     "persistent256": ([300, 0, 517, 129], 0, 1, False),
@@ -198,8 +202,8 @@ def test_tcgen05_swiglu(sched, wfmt, cuda_device):
     check(got, want, "swiglu")
 
 
-@pytest.mark.parametrize("sched", ["fixed16_gather", "fixed64", "fixed_multi_tile", "slot64", "persistent128",
-                                   "persistent256"])
+@pytest.mark.parametrize("sched", ["fixed16_gather", "fixed64", "fixed_multi_tile", "slot64", "qdec_skewed_gather",
+                                   "persistent128", "persistent256"])
 @pytest.mark.parametrize("wfmt", ["bf16", "fp8", "int4"])
 def test_tcgen05_swiglu_interleaved(sched, wfmt, cuda_device):
     """SB_EPI_SWIGLU_IL, the layout the block's SwiGLU experts use: gate and up
@@ -219,6 +223,23 @@ def test_cta_pair_kernel(epi, rows, cuda_device):
     kernel (tcgen05.mma.cta_group::2); ragged groups end in short tiles whose
     MMA width shrinks to the rows they hold."""
     got, want = run_case(rows, 512, 384, "bf16", epi, "tcgen05", cuda_device, seed=len(rows) + sum(rows) % 7)
+    check(got, want, epi)
+
+
+@pytest.mark.parametrize("wfmt", ["fp8", "int4"])
+@pytest.mark.parametrize("epi", ["linear", "swiglu_il"])
+def test_quantised_decode_many_items(wfmt, epi, cuda_device):
+    """The quantised decode kernel at a cfg5-like shape: 128 groups with
+    Zipf-skewed rows (2048 in all, the largest above 256: two items), a weight
+    matrix whose rows are not a multiple of 128 (LINEAR), and more items than
+    SMs, so every CTA walks several items and both TMEM accumulators turn over."""
+    g = torch.Generator().manual_seed(21)
+    weights = 1.0 / torch.arange(1, 129).float() ** 1.1
+    picks = torch.multinomial(weights, 2048, replacement=True, generator=g)
+    rows = [int(v) for v in torch.bincount(picks, minlength=128)]
+    rows[0] = max(rows[0], 300)
+    m = 192 if epi == "linear" else 256
+    got, want = run_case(rows, m, 512, wfmt, epi, "tcgen05", cuda_device, gather=epi != "linear", seed=13)
     check(got, want, epi)
 
 
