@@ -908,7 +908,10 @@ struct QCfg {
   static constexpr int kScaleMaxGroups = 32;
   static constexpr int kScaleSlotBytes = WFMT == SB_W_INT4 ? kWRows * kScaleMaxGroups * 2 : 0;
   static constexpr int kOffScale = (kOffOffsets + (kMaxG + 1) * 4 + 127) / 128 * 128;  // 16-byte aligned copies
-  static constexpr int kSmemBytes = kOffScale + 2 * kScaleSlotBytes + 1024;
+  // epilogue: per item the 256 weight rows' bias and fp8 scale, two buffers
+  static constexpr int kOffEpi = kOffScale + 2 * kScaleSlotBytes;
+  static constexpr int kEpiBytes = 2 * 2 * kWRows * 4;
+  static constexpr int kSmemBytes = kOffEpi + kEpiBytes + 1024;
   static_assert(WFMT == SB_W_FP8 || WFMT == SB_W_INT4, "packed weight formats only");
   static_assert(EPI == SB_EPI_LINEAR || EPI == SB_EPI_GELU || EPI == SB_EPI_SWIGLU_IL, "one weight operand");
   static_assert(kChunks * 16 * kGroupThreads == kRawBytes, "whole chunks per thread");
@@ -1193,7 +1196,8 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
   } else {
     // ---------------------------------------------------------------- epilogue (warps 0-3)
     // Thread = one token row of the item (TMEM lane); its 256 columns are the
-    // outputs of the item's 256 weight rows.
+    // outputs of the item's 256 weight rows.  The rows' biases (and fp8
+    // scales) are staged in shared memory once per item, two buffers deep.
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     constexpr int kVec = EPI == SB_EPI_LINEAR ? 4 : 8;  // elements per 16-byte store
     const bool vec_ok = (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && p.ldo % kVec == 0;
@@ -1208,21 +1212,25 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
       const float rs = (EPI == SB_EPI_LINEAR && p.row_scale && tvalid) ? p.row_scale[tok] : 1.f;
       const int wr0 = ft * C::kWRows;  // first weight row of the item within its group
       const int64_t arow0 = static_cast<int64_t>(g) * p.a_group_rows + wr0;
-      const float* bias = p.bias ? p.bias + static_cast<int64_t>(g) * p.bias_group_stride + wr0 : nullptr;
-      const float* fs = WFMT == SB_W_FP8 ? static_cast<const float*>(p.a_scale) + arow0 : nullptr;
       const int wvalid = min(C::kWRows, p.m_rows - wr0);  // weight rows of this tile inside the group
-      const bool ready =
-          __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (j >> 1) & 1, p.status, SB_DEVERR_EPI_WAIT));
+      float* s_b = reinterpret_cast<float*>(smem + C::kOffEpi) + buf * 2 * C::kWRows;
+      float* s_s = s_b + C::kWRows;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int wr = tid + h * 128;
+        const bool wv = wr < wvalid;
+        s_b[wr] = (p.bias && wv) ? p.bias[static_cast<int64_t>(g) * p.bias_group_stride + wr0 + wr] : 0.f;
+        s_s[wr] = WFMT == SB_W_FP8 ? ((wv && arow0 + wr < p.a_rows_total)
+                                          ? static_cast<const float*>(p.a_scale)[arow0 + wr] : 0.f)
+                                   : 1.f;
+      }
+      bool ready = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (j >> 1) & 1, p.status, SB_DEVERR_EPI_WAIT));
+      // one barrier of the four epilogue warps: the item's tables are written,
+      // and all four take the same path if a wait gave up
+      ready = named_bar_and(1, C::kEpiThreads, ready);
       tc_fence_after();
       if (!ready) break;
       const uint32_t acc_addr = lane_addr + buf * C::kWRows;
-      // weight row wr of the tile -> its fp32 output before the activation
-      auto lin = [&](float a, int wr) {
-        float x = a;
-        if (WFMT == SB_W_FP8 && wr < wvalid && arow0 + wr < p.a_rows_total) x *= fs[wr];
-        if (bias && wr < wvalid) x += bias[wr];
-        return x;
-      };
       if (__any_sync(0xffffffffu, tvalid)) {  // tcgen05.ld is warp-collective
         if constexpr (C::kIL) {
           // columns [gate 64 | up 64] per 128-row block: the features of block b
@@ -1234,12 +1242,12 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
 #pragma unroll 1
             for (int c0 = 0; c0 < 64; c0 += 16) {
               float gv[16], uv[16], o[16];
-              tmem_ld16(acc_addr + b * 128 + c0, gv);
-              tmem_ld16(acc_addr + b * 128 + 64 + c0, uv);
+              tmem_ld16x2(acc_addr + b * 128 + c0, acc_addr + b * 128 + 64 + c0, gv, uv);
+              const int gr = b * 128 + c0, ur = gr + 64;
 #pragma unroll
               for (int q = 0; q < 16; ++q) {
-                const float gate = silu_bf16out(lin(gv[q], b * 128 + c0 + q));
-                o[q] = lin(uv[q], b * 128 + 64 + c0 + q) * gate;
+                const float gate = silu_bf16out(gv[q] * s_s[gr + q] + s_b[gr + q]);
+                o[q] = (uv[q] * s_s[ur + q] + s_b[ur + q]) * gate;
               }
               if (!tvalid) continue;
               __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(tok) * p.ldo + feat0 + c0;
@@ -1260,44 +1268,50 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
           }
         } else {
 #pragma unroll 1
-          for (int c0 = 0; c0 < C::kWRows; c0 += 16) {
+          for (int c0 = 0; c0 < C::kWRows; c0 += 32) {
             if (c0 >= wvalid) break;  // warp-uniform
-            float v[16], o[16];
-            tmem_ld16(acc_addr + c0, v);
+            float va[16], vb[16];
+            tmem_ld16x2(acc_addr + c0, acc_addr + c0 + 16, va, vb);
 #pragma unroll
-            for (int q = 0; q < 16; ++q) {
-              const float x = lin(v[q], c0 + q);
-              o[q] = EPI == SB_EPI_LINEAR ? x * rs : gelu_bf16out(x);
-            }
-            if (!tvalid) continue;
-            const int nv = min(16, wvalid - c0);
-            const int64_t base = static_cast<int64_t>(tok) * p.ldo + wr0 + c0;
-            if (EPI == SB_EPI_LINEAR) {
-              float* dst = static_cast<float*>(p.out) + base;
-              if (vec_ok && nv == 16) {
+            for (int hh = 0; hh < 2; ++hh) {
+              const float* v = hh ? vb : va;
+              const int cc = c0 + 16 * hh;
+              if (cc >= wvalid || !tvalid) continue;
+              float o[16];
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
-                  reinterpret_cast<float4*>(dst)[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
-              } else {
-#pragma unroll
-                for (int q = 0; q < 16; ++q)
-                  if (q < nv) dst[q] = o[q];
+              for (int q = 0; q < 16; ++q) {
+                const float x = v[q] * s_s[cc + q] + s_b[cc + q];
+                o[q] = EPI == SB_EPI_LINEAR ? x * rs : gelu_bf16out(x);
               }
-            } else {
-              __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + base;
-              if (vec_ok && nv == 16) {
-                uint32_t w[8];
+              const int nv = min(16, wvalid - cc);
+              const int64_t base = static_cast<int64_t>(tok) * p.ldo + wr0 + cc;
+              if (EPI == SB_EPI_LINEAR) {
+                float* dst = static_cast<float*>(p.out) + base;
+                if (vec_ok && nv == 16) {
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                  const __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * q], o[2 * q + 1]);
-                  w[q] = *reinterpret_cast<const uint32_t*>(&h);
+                  for (int q = 0; q < 4; ++q)
+                    reinterpret_cast<float4*>(dst)[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                } else {
+#pragma unroll
+                  for (int q = 0; q < 16; ++q)
+                    if (q < nv) dst[q] = o[q];
                 }
-                reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
               } else {
+                __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + base;
+                if (vec_ok && nv == 16) {
+                  uint32_t w[8];
 #pragma unroll
-                for (int q = 0; q < 16; ++q)
-                  if (q < nv) dst[q] = __float2bfloat16_rn(o[q]);
+                  for (int q = 0; q < 8; ++q) {
+                    const __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * q], o[2 * q + 1]);
+                    w[q] = *reinterpret_cast<const uint32_t*>(&h);
+                  }
+                  reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                  reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                } else {
+#pragma unroll
+                  for (int q = 0; q < 16; ++q)
+                    if (q < nv) dst[q] = __float2bfloat16_rn(o[q]);
+                }
               }
             }
           }

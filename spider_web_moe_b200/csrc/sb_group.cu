@@ -50,19 +50,38 @@ __global__ void __launch_bounds__(kGroupThreads, 1) group_pair_kernel(const Grou
 // of all earlier chunks plus all smaller groups -- straight from the count
 // matrix, and scatters.  Positions equal the single-CTA kernel's.
 constexpr int kChunk = 256;
+// Entries of whole rows a chunk stages in shared memory (the chunk's 256 plus
+// the parts of its first and last rows outside it); wider rows read global memory.
+constexpr int kChunkStageMax = 1024;
 
 // Pass 1 for chunk `chunk` of one grouping (a whole CTA of kChunk threads).
 SB_DEVINL void group_count_chunk(const int32_t* __restrict__ idx, const float* __restrict__ w, int n_rows, int slots,
                                  int G, int flags, int chunk, int32_t* __restrict__ rank_scratch,
                                  float* __restrict__ w_scratch, int32_t* __restrict__ chunk_count) {
   __shared__ int wcnt[kChunk / 32][kGroupMaxG];
+  // the whole rows the chunk's entries belong to, copied once with coalesced
+  // loads: an entry's merge test reads every slot of its row
+  __shared__ int32_t s_idx[kChunkStageMax];
+  __shared__ float s_w[kChunkStageMax];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t total = static_cast<int64_t>(n_rows) * slots;
   for (int i = tid; i < (kChunk / 32) * G; i += kChunk) (&wcnt[0][0])[(i / G) * kGroupMaxG + i % G] = 0;
+  const int64_t c0 = static_cast<int64_t>(chunk) * kChunk;
+  const int64_t c1 = c0 + kChunk < total ? c0 + kChunk : total;
+  const int64_t lo = (c0 / slots) * slots;
+  const int64_t hi = c1 > c0 ? ((c1 - 1) / slots + 1) * slots : lo;
+  const bool staged = hi - lo <= kChunkStageMax;
+  if (staged)
+    for (int64_t i = tid; i < hi - lo; i += kChunk) {
+      s_idx[i] = idx[lo + i];
+      s_w[i] = w ? w[lo + i] : 1.f;
+    }
   __syncthreads();
-  const int64_t e = static_cast<int64_t>(chunk) * kChunk + tid;
+  const int64_t e = c0 + tid;
   float wsum = 0.f;
-  const int g = e < total ? entry_group(idx, w, slots, G, flags, e, wsum) : -1;
+  const int g = e >= total ? -1
+                : staged  ? entry_group_staged(s_idx, s_w, slots, G, flags, static_cast<int>(e - lo), wsum)
+                          : entry_group(idx, w, slots, G, flags, e, wsum);
   const unsigned peers = __match_any_sync(0xffffffffu, g);
   const int rank_w = __popc(peers & ((1u << lane) - 1u));
   if (g >= 0 && rank_w == 0) wcnt[warp][g] = __popc(peers);

@@ -32,6 +32,25 @@ SB_DEVINL int entry_group(const int32_t* __restrict__ idx, const float* __restri
   return g;
 }
 
+// entry_group over a copy of the rows in shared memory: s_idx / s_w hold
+// entries lo .. lo + n of the grouping, lo a multiple of `slots`; `le` = e - lo.
+SB_DEVINL int entry_group_staged(const int32_t* s_idx, const float* s_w, int slots, int G, int flags, int le,
+                                 float& wsum) {
+  const int row0 = (le / slots) * slots;
+  const int s = le - row0;
+  const int g = s_idx[le];
+  wsum = 0.f;
+  if (g < 0 || g >= G) return -1;
+  for (int j = 0; j < s; ++j)
+    if (s_idx[row0 + j] == g) return -1;  // merged into an earlier slot of the same row
+  float acc = 0.f;
+  for (int j = 0; j < slots; ++j)
+    if (s_idx[row0 + j] == g) acc += s_w[row0 + j];
+  wsum = acc;
+  if ((flags & SB_GROUP_POSITIVE_ONLY) && !(acc > 0.f)) return -1;
+  return g;
+}
+
 // The whole grouping in one CTA (any block size that is a multiple of 32).
 SB_DEVINL void group_one_cta(const int32_t* __restrict__ idx, const float* __restrict__ w, int n_rows, int slots,
                              int G, int flags, int32_t* __restrict__ offsets, int32_t* __restrict__ perm_row,
