@@ -79,15 +79,14 @@ struct TcCfg {
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "M=128 MMA needs N in [16, 256], N % 16 == 0");
 };
 
-// Two int4 weights (the nibbles at bit `lo` and bit lo + 4 of x, where x is
-// the packed word with bit 3 of every nibble flipped) as bf16x2 bit patterns
-// of 128 + (nibble ^ 8): exponent 2^7 with the unsigned value in the low
-// mantissa bits, exact for values below 128.
-template <int kLo>
-SB_DEVINL uint32_t int4x2_biased_bf16x2(uint32_t x) {
-  const uint32_t lo = (x >> kLo) & 0xFu;
-  const uint32_t hi = kLo + 4 <= 16 ? (x << (16 - kLo - 4)) & 0xF0000u : (x >> (kLo + 4 - 16)) & 0xF0000u;
-  return lo | hi | 0x43004300u;
+// Two int4 weights -- the low nibbles of byte p of w (element 2p) and of byte
+// p of w >> 4 (element 2p + 1) -- as the bf16x2 bit patterns of 128 + (n ^ 8),
+// n the raw nibble: exponent 2^7 with u = n ^ 8 = q + 8 in the low mantissa
+// bits, exact.  One byte permute and one three-input logic op per pair.
+template <int kP>
+SB_DEVINL uint32_t int4x2_biased_bf16x2(uint32_t w, uint32_t w_shr4) {
+  constexpr uint32_t kSel = kP | (kP << 4) | ((4 + kP) << 8) | ((4 + kP) << 12);
+  return (__byte_perm(w, w_shr4, kSel) & 0x000F000Fu) ^ 0x43084308u;
 }
 
 // One 16-byte chunk of a raw fp8 tile row (16 weights, e4m3) -> two 16-byte
@@ -119,12 +118,13 @@ SB_DEVINL void convert_fp8_chunk(const uint4 v, uint8_t* dst, int row, int c16) 
 SB_DEVINL void convert_int4_chunk(const uint4 v, const __nv_bfloat16 sb, uint8_t* dst, int row, int c16) {
   const __nv_bfloat162 bias = __float2bfloat162_rn(136.f);
   const __nv_bfloat162 s2 = __bfloat162bfloat162(sb);
-  const uint32_t w[4] = {v.x ^ 0x88888888u, v.y ^ 0x88888888u, v.z ^ 0x88888888u, v.w ^ 0x88888888u};
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
   uint32_t out[16];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    uint32_t pr[4] = {int4x2_biased_bf16x2<0>(w[i]), int4x2_biased_bf16x2<8>(w[i]),
-                      int4x2_biased_bf16x2<16>(w[i]), int4x2_biased_bf16x2<24>(w[i])};
+    const uint32_t h = w[i] >> 4;
+    uint32_t pr[4] = {int4x2_biased_bf16x2<0>(w[i], h), int4x2_biased_bf16x2<1>(w[i], h),
+                      int4x2_biased_bf16x2<2>(w[i], h), int4x2_biased_bf16x2<3>(w[i], h)};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const __nv_bfloat162 qv = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&pr[j]), bias);
