@@ -872,6 +872,8 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
 // contiguous block) come with one bulk copy into a double-buffered slot.  Two
 // TMEM accumulators of 256 columns: the epilogue of item i overlaps the MMAs
 // of item i+1; an epilogue thread holds one token row of the item.
+// LINEAR outputs may be K-split (p.splits partial sums, as the other
+// schedules), which multiplies the items of small problems.
 // Warps: 0-3 epilogue, 4-19 convert (two groups of eight), 20 weight TMA,
 // 21 MMA (+TMEM), 22 token-row TMA (16-row boxes, or tile::gather4).
 template <int WFMT, int EPI>
@@ -895,6 +897,9 @@ struct QCfg {
   static constexpr int kChunks = kRawBytes / 16 / kGroupThreads;  // 16-byte chunks per thread and stage
   static constexpr int kEpiThreads = 128;
   static constexpr int kThreads = 736;
+  static constexpr int kWarpW = 20;    // weight TMA
+  static constexpr int kWarpMMA = 21;  // MMA issuer, TMEM owner
+  static constexpr int kWarpX = 22;    // token-row TMA
   static constexpr int kTmemCols = 512;
   static constexpr int kMaxG = 256;
   static constexpr int kOffW = 0;
@@ -944,7 +949,15 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = p.num_groups;
   const int f_tiles = (p.m_rows + C::kWRows - 1) / C::kWRows;
-  const int nk = p.k / kTcBK;
+  const int fs = f_tiles * p.splits;  // items per token chunk: weight tiles x K splits
+  const int nk = p.k / kTcBK / p.splits;
+  // item t -> group g, token chunk nt, weight tile ft, K split ks (weight tile fastest)
+  auto item = [&](int t, int& g, int& nt, int& ft, int& ks) {
+    int fk;
+    decode_tile(prefix, G, fs, t, g, nt, fk);
+    ks = fk / f_tiles;
+    ft = fk - ks * f_tiles;
+  };
   // int4: an item's scales [256 rows x groups] by one bulk copy when the block
   // lies inside the scale matrix, fits a slot and starts 16-byte aligned
   // (producer and converters take the same decision per item)
@@ -972,7 +985,7 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
     }
     fence_barrier_init();
   }
-  if (warp == 20 && lane == 0) {
+  if (warp == C::kWarpW && lane == 0) {
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
   }
@@ -989,7 +1002,7 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
         s_off[gi] = o0;
         if (gi == G - 1) s_off[G] = o1;
         const int lo = min(o0, p.max_rows), hi = min(o1, p.max_rows);
-        items = hi > lo ? (hi - lo + C::kTokM - 1) / C::kTokM * f_tiles : 0;
+        items = hi > lo ? (hi - lo + C::kTokM - 1) / C::kTokM * fs : 0;
       }
       int incl = items;
 #pragma unroll
@@ -1010,7 +1023,7 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
   if (static_cast<int>(blockIdx.x) >= total) return;  // no item for this CTA
   const int my_items = (total - static_cast<int>(blockIdx.x) + gridDim.x - 1) / gridDim.x;
 
-  if (warp == 21) {
+  if (warp == C::kWarpMMA) {
     tmem_alloc(s_tmem, C::kTmemCols);
     tmem_relinquish();
   }
@@ -1019,15 +1032,16 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
 
-  if (warp == 20) {
+  if (warp == C::kWarpW) {
     // ---------------------------------------------------------------- packed weight tiles (+ int4 scales)
     if (lane == 0) {
-      int ri = 0, ub = 0;  // raw tiles and scale blocks issued
+      int ri = 0, ub = 0;  // weight tiles and scale blocks issued
       bool ok = true;
       for (int j = 0; j < my_items && ok; ++j) {
-        int g, nt, ft;
-        decode_tile(prefix, G, f_tiles, blockIdx.x + j * gridDim.x, g, nt, ft);
+        int g, nt, ft, ks;
+        item(blockIdx.x + j * gridDim.x, g, nt, ft, ks);
         const int arow = static_cast<int>(static_cast<int64_t>(g) * p.a_group_rows + ft * C::kWRows);
+        const int kb = ks * nk * kTcBK;
         if (bulk_scales(arow)) {
           const int sb = ub & 1;
           if (!mbar_wait(&sempty[sb], ((ub >> 1) & 1) ^ 1, p.status, SB_DEVERR_CONV_WAIT)) break;
@@ -1038,10 +1052,10 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
           ++ub;
         }
         for (int kk = 0; kk < nk; ++kk, ++ri) {
+          const int k0 = kb + kk * kTcBK;
           const int r = ri % R;
           if (!mbar_wait(&rempty[r], ((ri / R) & 1) ^ 1, p.status, SB_DEVERR_CONV_WAIT)) { ok = false; break; }
           mbar_expect_tx(&rfull[r], C::kRawBytes);
-          const int k0 = kk * kTcBK;
           tma_load_2d(smem + C::kOffRaw + r * C::kRawBytes, &tmW, &rfull[r], WFMT == SB_W_INT4 ? k0 / 2 : k0, arow);
         }
       }
@@ -1051,13 +1065,14 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
         if (!mbar_wait(&sfull[i & 1], (i >> 1) & 1, p.status, SB_DEVERR_DRAIN)) break;
     }
     __syncwarp();
-  } else if (warp == 22) {
+  } else if (warp == C::kWarpX) {
     // ---------------------------------------------------------------- token rows
     int si = 0;
     bool ok = true;
     for (int j = 0; j < my_items && ok; ++j) {
-      int g, nt, ft;
-      decode_tile(prefix, G, f_tiles, blockIdx.x + j * gridDim.x, g, nt, ft);
+      int g, nt, ft, ks;
+      item(blockIdx.x + j * gridDim.x, g, nt, ft, ks);
+      const int kb = ks * nk * kTcBK;
       const int n0 = s_off[g] + nt * C::kTokM;
       const int n_end = min(min(s_off[g + 1], p.max_rows), n0 + C::kTokM);
       // only the item's rows are fetched: 4-row gathers (one per lane) or 16-row boxes
@@ -1077,7 +1092,7 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
         }
         w = __shfl_sync(0xffffffffu, w, 0);
         if (!w) { ok = false; break; }
-        const int k0 = kk * kTcBK;
+        const int k0 = kb + kk * kTcBK;
         uint8_t* xdst = smem + C::kOffX + s * C::kXBytes;
         if (kGather) {
           __syncwarp();
@@ -1091,7 +1106,7 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
       for (int i = si - S > 0 ? si - S : 0; i < si; ++i)  // drain
         if (!mbar_wait(&xfull[i % S], (i / S) & 1, p.status, SB_DEVERR_DRAIN)) break;
     __syncwarp();
-  } else if (warp == 21) {
+  } else if (warp == C::kWarpMMA) {
     // ---------------------------------------------------------------- MMA issuer: D[token, weight row]
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(C::kTokM, C::kWRows);
@@ -1135,8 +1150,9 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
     int ub = 0;
     bool ok = true;
     for (int j = 0; j < my_items && ok; ++j) {
-      int g, nt, ft;
-      decode_tile(prefix, G, f_tiles, blockIdx.x + j * gridDim.x, g, nt, ft);
+      int g, nt, ft, ks;
+      item(blockIdx.x + j * gridDim.x, g, nt, ft, ks);
+      const int kb = ks * nk * kTcBK;
       const int64_t arow0 = static_cast<int64_t>(g) * p.a_group_rows + ft * C::kWRows;
       // int4 scales of this thread's rows: the item's bulk-copied block, else global memory
       const bool bulk = bulk_scales(arow0);
@@ -1156,7 +1172,7 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
       for (int kk = ((ci0 & 1) == cg) ? 0 : 1; kk < nk; kk += 2) {
         const int ci = ci0 + kk;
         const int r = ci % R, s = ci % S;
-        const int k0 = kk * kTcBK;
+        const int k0 = kb + kk * kTcBK;
         __nv_bfloat16 sb[C::kChunks];
         if (WFMT == SB_W_INT4) {
 #pragma unroll
@@ -1200,10 +1216,11 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
     // scales) are staged in shared memory once per item, two buffers deep.
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     constexpr int kVec = EPI == SB_EPI_LINEAR ? 4 : 8;  // elements per 16-byte store
-    const bool vec_ok = (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && p.ldo % kVec == 0;
+    const bool vec_ok = (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 && p.ldo % kVec == 0 &&
+                        (p.splits == 1 || p.split_stride % kVec == 0);
     for (int j = 0; j < my_items; ++j) {
-      int g, nt, ft;
-      decode_tile(prefix, G, f_tiles, blockIdx.x + j * gridDim.x, g, nt, ft);
+      int g, nt, ft, ks;
+      item(blockIdx.x + j * gridDim.x, g, nt, ft, ks);
       const int buf = j & 1;
       const int n0 = s_off[g] + nt * C::kTokM;
       const int tend = min(min(s_off[g + 1], p.max_rows), n0 + C::kTokM);
@@ -1219,7 +1236,8 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
       for (int h = 0; h < 2; ++h) {
         const int wr = tid + h * 128;
         const bool wv = wr < wvalid;
-        s_b[wr] = (p.bias && wv) ? p.bias[static_cast<int64_t>(g) * p.bias_group_stride + wr0 + wr] : 0.f;
+        // K splits: the bias goes with split 0
+        s_b[wr] = (p.bias && wv && ks == 0) ? p.bias[static_cast<int64_t>(g) * p.bias_group_stride + wr0 + wr] : 0.f;
         s_s[wr] = WFMT == SB_W_FP8 ? ((wv && arow0 + wr < p.a_rows_total)
                                           ? static_cast<const float*>(p.a_scale)[arow0 + wr] : 0.f)
                                    : 1.f;
@@ -1284,7 +1302,7 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
                 o[q] = EPI == SB_EPI_LINEAR ? x * rs : gelu_bf16out(x);
               }
               const int nv = min(16, wvalid - cc);
-              const int64_t base = static_cast<int64_t>(tok) * p.ldo + wr0 + cc;
+              const int64_t base = static_cast<int64_t>(ks) * p.split_stride + static_cast<int64_t>(tok) * p.ldo + wr0 + cc;
               if (EPI == SB_EPI_LINEAR) {
                 float* dst = static_cast<float*>(p.out) + base;
                 if (vec_ok && nv == 16) {
@@ -1323,7 +1341,7 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 21) {
+  if (warp == C::kWarpMMA) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
   }
@@ -1872,8 +1890,11 @@ static bool use_qdec(const sb_grouped_gemm_args& a) {
     const char* e = std::getenv("SPIDER_B200_QDEC");
     return !(e && e[0] == '0');
   }();
+  // bf16 decode stays on the fixed-group kernel (measured faster: no
+  // conversion to share, several CTAs per SM stream the weights)
   if (!enabled || (a.wfmt != SB_W_FP8 && a.wfmt != SB_W_INT4)) return false;
-  if (a.splits != 1 || a.num_groups > kPersistentMaxGroups || a.epilogue == SB_EPI_SWIGLU) return false;
+  if (a.num_groups > kPersistentMaxGroups || a.epilogue == SB_EPI_SWIGLU) return false;
+  if (a.splits != 1 && a.epilogue != SB_EPI_LINEAR) return false;
   if (a.x_row_index && a.x_rows <= 0) return false;
   // decode batches: the expected rows per group are few (the tiled kernels'
   // column tile would be at most 64)
@@ -1894,7 +1915,7 @@ static int launch_qdec(const sb_grouped_gemm_args& a, cudaStream_t st) {
     configured_device = dev;
   }
   static_assert(C::kMaxG == kPersistentMaxGroups, "prefix table size");
-  if (a.num_groups > C::kMaxG || a.splits != 1) return SB_ERR_UNSUPPORTED;
+  if (a.num_groups > C::kMaxG || a.splits < 1 || (a.splits != 1 && EPI != SB_EPI_LINEAR)) return SB_ERR_UNSUPPORTED;
   // weights: 256-row boxes of one K step (packed bytes); tokens: 16-row boxes or one-row gathers
   CUtensorMap mw, mx;
   const bool ok_w =
@@ -1910,7 +1931,8 @@ static int launch_qdec(const sb_grouped_gemm_args& a, cudaStream_t st) {
                          CU_TENSOR_MAP_SWIZZLE_128B);
   if (!ok_w || !ok_x) return SB_ERR_UNSUPPORTED;
   const int f_tiles = (a.m_rows + C::kWRows - 1) / C::kWRows;
-  const int64_t bound = static_cast<int64_t>(f_tiles) * ((a.max_rows + C::kTokM - 1) / C::kTokM + a.num_groups);
+  const int64_t bound =
+      static_cast<int64_t>(f_tiles) * a.splits * ((a.max_rows + C::kTokM - 1) / C::kTokM + a.num_groups);
   const int sms = current_sm_count();
   const int grid = static_cast<int>(bound < sms ? bound : sms);
   return launch(kern, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, mw, mx, a);
