@@ -266,6 +266,9 @@ static bool gemm_gathers(const sb_grouped_gemm_args& a, int engine) {
   if (engine == SB_ENGINE_SIMT) return true;
   const bool tc = tcgen05_supported(a);
   if (!tc) return engine == SB_ENGINE_AUTO;  // AUTO falls back to the CUDA-core engine
+  // The quantised decode kernel loads up to 128 rows per item: one tiled box
+  // from a permuted copy beats 32 four-row gathers per K step.
+  if (tc_qdec(a)) return false;
   return tc_tile_n(a) <= 64;
 }
 

@@ -927,7 +927,7 @@ struct QCfg {
 template <int WFMT, int EPI, bool kGather>
 __global__ void __launch_bounds__(QCfg<WFMT, EPI>::kThreads, 1)
 tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-                    const sb_grouped_gemm_args p) {
+                    const __grid_constant__ CUtensorMap tmX128, const sb_grouped_gemm_args p) {
   using C = QCfg<WFMT, EPI>;
   constexpr int S = C::kStages, R = C::kRawStages;
   extern __shared__ uint8_t smem_raw[];
@@ -988,6 +988,7 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
   if (warp == C::kWarpW && lane == 0) {
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
+    if (!kGather) tma_prefetch_desc(&tmX128);
   }
   pdl_wait();
   pdl_trigger();
@@ -1075,9 +1076,12 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
       const int kb = ks * nk * kTcBK;
       const int n0 = s_off[g] + nt * C::kTokM;
       const int n_end = min(min(s_off[g + 1], p.max_rows), n0 + C::kTokM);
-      // only the item's rows are fetched: 4-row gathers (one per lane) or 16-row boxes
-      const int nb = kGather ? (n_end - n0 + 3) / 4 : (n_end - n0 + 15) / 16;
-      const uint32_t tx = kGather ? nb * 512u : nb * 2048u;
+      // only the item's rows are fetched: 4-row gathers (one per lane), 16-row
+      // boxes, or for more than 32 rows one 128-row box (the rows past the
+      // item's end are other groups' or zero fill, and never stored)
+      const bool wide = !kGather && n_end - n0 > 32;
+      const int nb = kGather ? (n_end - n0 + 3) / 4 : (wide ? 1 : (n_end - n0 + 15) / 16);
+      const uint32_t tx = kGather ? nb * 512u : (wide ? static_cast<uint32_t>(C::kXBytes) : nb * 2048u);
       int rix[4] = {0, 0, 0, 0};
       if (kGather && lane < nb) {
 #pragma unroll
@@ -1098,7 +1102,10 @@ tc_gemm_qdec_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
           __syncwarp();
           if (lane < nb) tma_gather4(xdst + lane * 512, &tmX, &xfull[s], k0, rix[0], rix[1], rix[2], rix[3]);
         } else if (lane == 0) {
-          for (int q = 0; q < nb; ++q) tma_load_2d(xdst + q * 2048, &tmX, &xfull[s], k0, n0 + 16 * q);
+          if (wide)
+            tma_load_2d(xdst, &tmX128, &xfull[s], k0, n0);
+          else
+            for (int q = 0; q < nb; ++q) tma_load_2d(xdst + q * 2048, &tmX, &xfull[s], k0, n0 + 16 * q);
         }
       }
     }
@@ -1885,7 +1892,7 @@ static int launch_persistent(const sb_grouped_gemm_args& a, cudaStream_t st) {
 }
 
 // SPIDER_B200_QDEC=0 keeps quantised decode GEMMs on the tiled kernels (for comparisons).
-static bool use_qdec(const sb_grouped_gemm_args& a) {
+bool tc_qdec(const sb_grouped_gemm_args& a) {
   static const bool enabled = [] {
     const char* e = std::getenv("SPIDER_B200_QDEC");
     return !(e && e[0] == '0');
@@ -1924,18 +1931,22 @@ static int launch_qdec(const sb_grouped_gemm_args& a, cudaStream_t st) {
                      CU_TENSOR_MAP_SWIZZLE_NONE)
           : make_map(&mw, a.a, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.lda / 2, a.a_rows_total, a.lda / 2, kTcBK / 2,
                      C::kWRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  CUtensorMap mx128;
   const bool ok_x =
       kGather ? make_map(&mx, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.k, a.x_rows, a.ldx * 2, kTcBK, 1,
                          CU_TENSOR_MAP_SWIZZLE_128B)
               : make_map(&mx, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.k, a.max_rows, a.ldx * 2, kTcBK, 16,
-                         CU_TENSOR_MAP_SWIZZLE_128B);
+                         CU_TENSOR_MAP_SWIZZLE_128B) &&
+                    make_map(&mx128, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.k, a.max_rows, a.ldx * 2, kTcBK,
+                             C::kTokM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!ok_w || !ok_x) return SB_ERR_UNSUPPORTED;
+  if (kGather) mx128 = mx;  // unused
   const int f_tiles = (a.m_rows + C::kWRows - 1) / C::kWRows;
   const int64_t bound =
       static_cast<int64_t>(f_tiles) * a.splits * ((a.max_rows + C::kTokM - 1) / C::kTokM + a.num_groups);
   const int sms = current_sm_count();
   const int grid = static_cast<int>(bound < sms ? bound : sms);
-  return launch(kern, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, mw, mx, a);
+  return launch(kern, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, mw, mx, mx128, a);
 }
 
 template <int WFMT>
@@ -2166,7 +2177,7 @@ int dequant_to_bf16(int wfmt, const void* q, const void* scales, int group_size,
 }
 
 int gemm_tcgen05(const sb_grouped_gemm_args& a, cudaStream_t st) {
-  if (use_qdec(a)) {
+  if (tc_qdec(a)) {
     const int rc = a.wfmt == SB_W_FP8 ? launch_qdec_epi<SB_W_FP8>(a, st) : launch_qdec_epi<SB_W_INT4>(a, st);
     if (rc != SB_ERR_UNSUPPORTED) return rc;
   }

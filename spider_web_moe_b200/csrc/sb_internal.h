@@ -41,6 +41,8 @@ int gemm_tcgen05(const sb_grouped_gemm_args& a, cudaStream_t st);
 bool tcgen05_supported(const sb_grouped_gemm_args& a);
 int tc_tile_n(const sb_grouped_gemm_args& a);  // column tile the tcgen05 engine picks
 bool tc_fixed_groups(const sb_grouped_gemm_args& a);
+// fp8 / int4 decode problems go to the persistent quantised decode kernel
+bool tc_qdec(const sb_grouped_gemm_args& a);
 
 // Kernel launch with programmatic stream serialization (PDL), unless disabled
 // by SPIDER_B200_PDL=0.  Kernels launched this way call pdl_wait() first.
