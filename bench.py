@@ -68,6 +68,9 @@ def parse():
                     help="N > 1: dp = every rank runs the whole block on its own tokens (weights replicated, no "
                          "collective on the data path); ep = token-sharded expert parallelism (experts e % N, "
                          "message rows exchanged with the expert owners every loop)")
+    ap.add_argument("--micro-batches", type=int, default=1, choices=[1, 2],
+                    help="N > 1 expert parallelism: tokens per rank as one batch (1), or as two halves on two "
+                         "streams, one half's exchange overlapping the other's GEMMs (2)")
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="N > 1 expert-parallel exchange: stores into the peers' memory over NVLink (peer) or NCCL "
                          "all-to-all")
@@ -191,9 +194,12 @@ def workload_config(args, cfg, spec, world: int) -> dict:
     elif args.parallel == "dp":
         par = f"dp{world}: tokens sharded by rank, block weights replicated, no collective on the data path"
     else:
+        mb = args.micro_batches
         par = (f"ep{world}: tokens sharded by rank, experts e % {world}, "
                + ("dispatch/combine stored into peer memory over NVLink" if args.transport == "peer"
-                  else "NCCL all-to-all"))
+                  else "NCCL all-to-all")
+               + (", two micro-batches on two streams (exchange overlaps the other half's GEMMs)" if mb == 2
+                  else ""))
     return {"workload": args.config, "tokens_per_step_per_gpu": spec["tokens"], "num_loops": cfg.num_loops,
             "hidden": cfg.hidden_size, "experts": cfg.num_experts, "top_k": cfg.top_k,
             "edges_per_expert": cfg.edges_per_expert, "ffn": cfg.expert_ffn_size,
@@ -414,8 +420,9 @@ def run_b200_ep(args, rank, world, local, device):
     if spec["wfmt"] == "int4":
         cfg.moe_int4_group_size = cfg.moe_int4_group_size or 128
     sd = synth.synthetic_state_dict(cfg, seed=0, device=device, zipf=zipf, round_bf16=True)
+    mb = args.micro_batches
     ep = ExpertParallelBlock(cfg, sd, device, act_dtype=torch.bfloat16, max_tokens=n, weight_format=spec["wfmt"],
-                             engine=args.engine, transport=args.transport)
+                             engine=args.engine, transport=args.transport, micro_batches=mb)
     del sd
     h, _ = synth.block_inputs(n, cfg.hidden_size, seed=1 + rank, device=device, dtype=torch.bfloat16)
     h = h.view(n, -1).contiguous()
@@ -426,7 +433,7 @@ def run_b200_ep(args, rank, world, local, device):
     for _ in range(max(3, args.warmup)):
         ep.graph.replay()
     torch.cuda.synchronize(device)
-    ep.dense.check_status()
+    ep.check_status()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     barrier(world)

@@ -19,6 +19,7 @@ layouts in HBM:
 """
 from __future__ import annotations
 
+import copy
 import ctypes as C
 import os
 
@@ -188,6 +189,18 @@ class BlockEngine:
 
     def weight_bytes(self) -> int:
         return sum(v.numel() * v.element_size() for v in self.t.values())
+
+    def twin(self) -> "BlockEngine":
+        """An engine on the same packed weights with workspaces of its own, so
+        that work for two independent token batches can be in flight on two
+        streams at once (the micro-batches of an expert-parallel step)."""
+        t = copy.copy(self)
+        t.dims = L.BlockDims.from_buffer_copy(self.dims)
+        t.workspace = None
+        for k in ("_epws", "_dws"):  # per-engine scratch, made on first use
+            t.__dict__.pop(k, None)
+        t._ensure_workspace(int(self.dims.max_tokens))
+        return t
 
     def expert_tensors(self, short: str):
         """(weights, scales or None, biases) of one expert projection ("up",

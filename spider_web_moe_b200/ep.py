@@ -180,15 +180,38 @@ def ep_loop_peer(dense: BlockEngine, local: BlockEngine | None, xch: PeerExchang
     return dense.ep_epilogue_peer(xch, ret_pos, h, x0)
 
 
+class _MicroBatch:
+    """One micro-batch of the token-sharded step: engines with workspaces of
+    their own (the weights are shared), its own exchange group, stream and,
+    with the peer transport, its own exchange regions."""
+
+    def __init__(self, dense, local, group, stream, xch, world):
+        self.dense, self.local, self.group, self.stream, self.xch = dense, local, group, stream, xch
+        self.ops = CudaOps(dense, local, world)
+
+
 class ExpertParallelBlock:
-    """The block on one rank of a token-sharded expert-parallel group."""
+    """The block on one rank of a token-sharded expert-parallel group.
+
+    ``micro_batches=2`` splits every rank's tokens into two halves that run
+    all loops on two streams with their own exchange groups (NCCL
+    communicators, or peer regions): one half's dispatch / return exchange
+    overlaps the other half's routing and expert GEMMs.  The block is
+    token-independent, so the halves need no exchange of their own.  Every
+    rank must use the same setting (the groups are created collectively)."""
 
     def __init__(self, cfg, state: dict, device, group=None, act_dtype=torch.bfloat16, max_tokens: int = 64,
-                 weight_format: str | None = None, engine: str = "auto", transport: str = "nccl"):
+                 weight_format: str | None = None, engine: str = "auto", transport: str = "nccl",
+                 micro_batches: int = 1):
         self.cfg = from_any(cfg)
         self.group = group
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if micro_batches not in (1, 2):
+            raise ValueError(f"micro_batches={micro_batches}: 1 or 2")
+        if transport not in ("nccl", "peer"):
+            raise ValueError(f"transport {transport!r}: 'nccl' or 'peer'")
+        self.micro_batches, self.transport, self.max_tokens = int(micro_batches), transport, int(max_tokens)
         E = self.cfg.num_experts
         dense_state = {k: v for k, v in state.items() if not k.startswith(("experts.", "expert_gates."))}
         self.dense = BlockEngine(self.cfg, dense_state, device, act_dtype=act_dtype, max_tokens=max_tokens,
@@ -199,36 +222,74 @@ class ExpertParallelBlock:
             lcfg = dataclasses.replace(self.cfg, num_experts=len(ids))
             self.local = BlockEngine(lcfg, local_expert_state(state, E, self.rank, self.world), device,
                                      act_dtype=act_dtype, max_tokens=1, weight_format=weight_format, engine=engine)
-        self.ops = CudaOps(self.dense, self.local, self.world)
-        self.max_tokens = max_tokens
-        if transport not in ("nccl", "peer"):
-            raise ValueError(f"transport {transport!r}: 'nccl' or 'peer'")
-        self.transport = transport
-        self.xch = None
+        # exchange capacity per micro-batch: its share of max_tokens on every rank
+        self.cap = -(-self.max_tokens // self.micro_batches)
+        pitch = None
         if transport == "peer":
             # every rank's own dense engine workspace exists before the first step
             self.dense._ensure_workspace(max_tokens)
             pitch = self.dense.lib.sb_ep_row_pitch(self.cfg.hidden_size, self.dense.dims.act_dtype, self.cfg.top_k)
-            self.xch = PeerExchange(self.world, self.rank, max_tokens, pitch, self.cfg.hidden_size, device, group)
+        ranks = dist.get_process_group_ranks(group) if (group is not None and dist.is_initialized()) else \
+            list(range(self.world))
+        self.mbs = []
+        for i in range(self.micro_batches):
+            dense = self.dense if i == 0 else self.dense.twin()
+            local = self.local if (i == 0 or self.local is None) else self.local.twin()
+            g = group if i == 0 else (dist.new_group(ranks=ranks) if self.world > 1 else None)
+            stream = None if self.micro_batches == 1 else torch.cuda.Stream(device=device)
+            xch = None
+            if transport == "peer":
+                xch = PeerExchange(self.world, self.rank, self.cap, pitch, self.cfg.hidden_size, device, g)
+            self.mbs.append(_MicroBatch(dense, local, g, stream, xch, self.world))
+        self.ops, self.xch = self.mbs[0].ops, self.mbs[0].xch
+
+    def _loop_mb(self, mb: _MicroBatch, h, x0, loop_idx: int):
+        if self.transport == "peer":
+            return ep_loop_peer(mb.dense, mb.local, mb.xch, h, x0, loop_idx, self.cap * self.cfg.top_k,
+                                stream=mb.stream)
+        return ep_loop(mb.ops, h, x0, loop_idx, self.world, self.cap, mb.group)
 
     def loop(self, h, x0, loop_idx: int):
         """One loop; every rank must call it (the exchange is collective).  The
         exchange capacity is max_tokens on every rank, so ranks may hold
         different token counts up to that."""
-        n = h.numel() // self.cfg.hidden_size
-        if n > self.max_tokens:
-            raise ValueError(f"{n} tokens exceed max_tokens={self.max_tokens} of the expert-parallel block")
-        if self.transport == "peer":
-            return ep_loop_peer(self.dense, self.local, self.xch, h.reshape(n, -1), x0.reshape(n, -1), loop_idx,
-                                self.max_tokens * self.cfg.top_k).view(h.shape)
-        return ep_loop(self.ops, h.reshape(n, -1), x0.reshape(n, -1), loop_idx, self.world, self.max_tokens,
-                       self.group).view(h.shape)
+        return self.forward(h, x0, loop_idx, loop_idx + 1)
 
     def forward(self, h, x0, loop_begin: int = 0, loop_end: int | None = None):
         loop_end = self.cfg.num_loops if loop_end is None else loop_end
+        H = self.cfg.hidden_size
+        n = h.numel() // H
+        if n > self.max_tokens:
+            raise ValueError(f"{n} tokens exceed max_tokens={self.max_tokens} of the expert-parallel block")
+        h2, x2 = h.reshape(n, H), x0.reshape(n, H)
+        if self.micro_batches == 1:
+            for l in range(loop_begin, loop_end):
+                h2 = self._loop_mb(self.mbs[0], h2, x2, l)
+            return h2.view(h.shape)
+        if n < self.micro_batches:
+            raise ValueError(f"{n} tokens: micro_batches={self.micro_batches} needs at least that many per rank")
+        n0 = -(-n // 2)
+        cur = torch.cuda.current_stream(h.device)
+        parts = [(h2[:n0], x2[:n0]), (h2[n0:], x2[n0:])]
+        outs = []
+        for mb, (hp, xp) in zip(self.mbs, parts):
+            mb.stream.wait_stream(cur)
+            hp.record_stream(mb.stream)
+            xp.record_stream(mb.stream)
+            outs.append(hp)
+        # enqueue the halves loop by loop so both streams always hold work
         for l in range(loop_begin, loop_end):
-            h = self.loop(h, x0, l)
-        return h
+            for i, mb in enumerate(self.mbs):
+                with torch.cuda.stream(mb.stream):
+                    outs[i] = self._loop_mb(mb, outs[i], parts[i][1], l)
+        for mb, o in zip(self.mbs, outs):
+            cur.wait_stream(mb.stream)
+            o.record_stream(cur)
+        return torch.cat(outs).view(h.shape)
+
+    def check_status(self):
+        for mb in self.mbs:
+            mb.dense.check_status()
 
     # ------------------------------------------------------------------ CUDA graph
     def capture(self, n_tokens: int):
@@ -267,10 +328,12 @@ class ExpertParallelBlock:
         self.graph = None
 
     def close(self):
-        """Release the peer-memory exchange (all ranks; before the process group
+        """Release the peer-memory exchanges (all ranks; before the process group
         is destroyed)."""
         self.release_graph()
-        if self.xch is not None:
-            self.xch.close(self.group)
-            self.xch = None
+        for mb in self.mbs:
+            if mb.xch is not None:
+                mb.xch.close(mb.group)
+                mb.xch = None
+        self.xch = None
 

@@ -74,6 +74,25 @@ def main():
         same &= torch.equal(got, want)
     peer.dense.check_status()
     peer.close()
+    # two micro-batches per rank on two streams (their own NCCL communicator or
+    # peer regions): the one-batch step's rows, and a graph replays them exactly
+    for tr in ("nccl", "peer"):
+        two = ExpertParallelBlock(cfg, sd, dev, act_dtype=torch.bfloat16, max_tokens=n, weight_format=spec["wfmt"],
+                                  transport=tr, micro_batches=2)
+        got = two.forward(h0, h0)
+        n0 = (n + 1) // 2
+        want_mb = torch.cat([ep.forward(h0[:n0], h0[:n0]), ep.forward(h0[n0:], h0[n0:])])
+        torch.cuda.synchronize()
+        num = (got.float() - want_mb.float()).abs().amax(-1)
+        den = want_mb.float().abs().amax(-1).clamp_min(1e-30)
+        e2 = float((num / den).max())
+        two.capture(n)
+        again = two.replay(h0, h0)
+        torch.cuda.synchronize()
+        two.check_status()
+        ok &= e2 < 2e-2 and torch.equal(again, got)
+        print(f"rank {rank}/{world} {name}: two micro-batches ({tr}) relative error {e2:.3e}", flush=True)
+        two.close()
     ok &= same
     ok &= reference_semantics(cfg, sd, dev, rank, world)
     print(f"rank {rank}/{world} {name}: worst relative error {worst:.3e}, peer transport "

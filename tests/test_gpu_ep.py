@@ -77,6 +77,43 @@ def test_peer_transport_single_gpu_matches_nccl_path(name, n, cuda_device):
         peer.close()
 
 
+@pytest.mark.parametrize("transport", ["nccl", "peer"])
+@pytest.mark.parametrize("name,n", [("cfg2", 41), ("cfg4", 700)])
+def test_micro_batches_match_one_batch(transport, name, n, cuda_device):
+    """micro_batches=2: the rank's tokens as two halves on two streams, each
+    with engines, an exchange group and (peer transport) regions of its own.
+    The block is token-independent, so the result is the one-batch step run on
+    each half (the same routing batch sizes, so no top-k near-tie can flip;
+    the owner's GEMM schedules follow the exchange capacity, hence the GEMM
+    tolerance), and a CUDA graph of the two-stream step replays it bit for bit."""
+    spec = benchmark_configs()[name]
+    cfg = ModelConfig(**spec["model"], expert_activation=spec["activation"]).validate()
+    sd = synth.synthetic_state_dict(cfg, seed=47, device=cuda_device, zipf=1.1 if spec["zipf"] else None,
+                                    round_bf16=True)
+    one = ExpertParallelBlock(cfg, sd, cuda_device, act_dtype=torch.bfloat16, max_tokens=n,
+                              weight_format=spec["wfmt"], transport=transport)
+    two = ExpertParallelBlock(cfg, sd, cuda_device, act_dtype=torch.bfloat16, max_tokens=n,
+                              weight_format=spec["wfmt"], transport=transport, micro_batches=2)
+    h, _ = synth.block_inputs(n, cfg.hidden_size, seed=48, device=cuda_device, dtype=torch.bfloat16)
+    h = h.view(n, -1)
+    try:
+        n0 = (n + 1) // 2
+        want = torch.cat([one.forward(h[:n0], h[:n0]), one.forward(h[n0:], h[n0:])])
+        got = two.forward(h, h)
+        torch.cuda.synchronize()
+        two.check_status()
+        assert rel_err(got, want) < 2e-2
+        two.capture(n)
+        for _ in range(2):
+            out = two.replay(h, h)
+            torch.cuda.synchronize()
+            assert torch.equal(out, got)
+        two.check_status()
+    finally:
+        one.close()
+        two.close()
+
+
 def test_ep_owner_hot_expert_loops_row_tiles(cuda_device):
     """200 tokens with two experts taking every token: the owner plans 64-row tiles
     per expert (32 expected pairs per expert on average), so each hot expert's
