@@ -51,7 +51,8 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # "config:activation"; a workload without a capture reports traffic null.
 #   cfg2:gelu    -- the 18 launches of one cfg2 replay (profiles/gemm_tcgen05_cfg2.txt)
 #   cfg3:swiglu  -- the 18 launches of one cfg3 replay (profiles/cfg3_launch_list.txt)
-NCU_TRAFFIC_PER_STEP = {"cfg2:gelu": 1013465344, "cfg3:swiglu": 3237011456}
+#   cfg5:swiglu  -- the 12 launches of one cfg5 replay (profiles/gemm_qdec_cfg5.txt)
+NCU_TRAFFIC_PER_STEP = {"cfg2:gelu": 1013465344, "cfg3:swiglu": 3237011456, "cfg5:swiglu": 5183200000}
 
 
 def parse():
