@@ -213,7 +213,8 @@ def algorithmic_bytes(cfg, spec, taps, n):
     """Bytes the grouped-GEMM launches of one loop must move (weights of touched
     groups in their stored format + rows in/out), from the loop's routing."""
     H, U, E = cfg.hidden_size, cfg.expert_ffn_size, cfg.num_experts
-    wfmt = spec["wfmt"]
+    # "native" weights take the activation dtype, which the benchmark runs in bf16
+    wfmt = "bf16" if spec["wfmt"] == "native" else spec["wfmt"]
     wb = {"bf16": 2.0, "fp8": 1.0, "int4": 0.5}[wfmt]
     top = taps["top_idx"].long().cpu()
     experts = int(torch.unique(top).numel())
