@@ -71,7 +71,7 @@ class BlockEngine:
 
     def __init__(self, cfg, state: dict, device, act_dtype=torch.bfloat16, max_tokens: int = 64,
                  weight_format: str | None = None, engine: str = "auto",
-                 int4: dict | None = None, fp8: dict | None = None):
+                 int4: dict | None = None, fp8: dict | None = None, resident_bf16: bool = False):
         self.cfg = from_any(cfg)
         self.device = torch.device(device)
         if self.device.type != "cuda":
@@ -138,6 +138,24 @@ class BlockEngine:
                 t["s_" + short] = qt.device_scales().to(dev).contiguous()
             else:
                 raise ValueError(f"unknown weight format {fmt}")
+        if resident_bf16 and fmt in ("fp8", "int4") and names:
+            # The quantised experts held as bf16 with the same values the GEMMs'
+            # conversion makes: e4m3 exactly (the per-row scale stays, applied to
+            # the accumulator), int4 as bf16(q * s).  For callers whose every
+            # call is prefill-sized (an expert-parallel owner), so the tensor-core
+            # schedules of bf16 weights apply without a conversion per call.
+            for short, _ in names:
+                q = t["w_" + short]
+                if fmt == "fp8":
+                    t["w_" + short] = q.view(torch.float8_e4m3fn).to(torch.bfloat16).contiguous()
+                else:
+                    sc = t.pop("s_" + short).float()
+                    lo = (q & 0x0F).to(torch.int8)
+                    hi = (q >> 4).to(torch.int8)
+                    qq = torch.stack([torch.where(lo > 7, lo - 16, lo), torch.where(hi > 7, hi - 16, hi)], dim=-1)
+                    qq = qq.reshape(*q.shape[:-1], q.shape[-1] * 2).float()
+                    t["w_" + short] = (qq * sc.repeat_interleave(self.group_size, dim=-1)).to(torch.bfloat16).contiguous()
+            fmt = "bf16"
         self.swiglu = swiglu and has_experts
         if self.swiglu:
             # SwiGLU: gate and up rows interleaved in blocks of 64 in one tensor

@@ -220,8 +220,12 @@ class ExpertParallelBlock:
         self.local = None
         if ids:
             lcfg = dataclasses.replace(self.cfg, num_experts=len(ids))
+            # an owner receiving prefill-size exchanges (>= 128 expected rows per
+            # local expert) keeps fp8 / int4 experts resident as bf16 copies
+            rows_per_expert = max_tokens * self.world * self.cfg.top_k // max(1, E)
             self.local = BlockEngine(lcfg, local_expert_state(state, E, self.rank, self.world), device,
-                                     act_dtype=act_dtype, max_tokens=1, weight_format=weight_format, engine=engine)
+                                     act_dtype=act_dtype, max_tokens=1, weight_format=weight_format, engine=engine,
+                                     resident_bf16=act_dtype == torch.bfloat16 and rows_per_expert >= 128)
         # exchange capacity per micro-batch: its share of max_tokens on every rank
         self.cap = -(-self.max_tokens // self.micro_batches)
         pitch = None

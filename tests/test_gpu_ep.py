@@ -25,11 +25,14 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 @pytest.mark.parametrize("name,n,activation", [("cfg2", 40, "gelu"), ("cfg5", 40, "gelu"), ("cfg3", 1024, "swiglu"),
-                                               ("cfg4", 700, "swiglu")])
+                                               ("cfg4", 700, "swiglu"), ("cfg4", 2100, "swiglu"),
+                                               ("cfg5", 2048, "swiglu")])
 def test_ep_path_single_gpu_matches_block(name, n, activation, cuda_device):
     """The token-sharded EP loop at a world of one (route, pack, owner-side
     experts on the packed rows, combine, epilogue) against the block; the
-    prefill-size cases take the tensor-core schedules on materialised rows."""
+    prefill-size cases take the tensor-core schedules on materialised rows, and
+    from 128 expected rows per expert (cfg4 at 2100 tokens, cfg5 at 2048) the
+    owner holds its fp8 / int4 experts as resident bf16 copies."""
     spec = benchmark_configs()[name]
     cfg = ModelConfig(**spec["model"], expert_activation=activation).validate()
     sd = synth.synthetic_state_dict(cfg, seed=41, device=cuda_device, zipf=1.1 if spec["zipf"] else None,
