@@ -49,10 +49,12 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum, one ncu capture) of
 # the edge-value, expert-up and expert-down GEMM launches of one step, keyed by
 # "config:activation"; a workload without a capture reports traffic null.
-#   cfg2:gelu    -- the 18 launches of one cfg2 replay (profiles/gemm_tcgen05_cfg2.txt)
+#   cfg2:gelu    -- the 18 launches of one cfg2 replay with GELU experts (profiles/gemm_tcgen05_cfg2.txt)
+#   cfg2:swiglu  -- the 18 launches of one cfg2 replay (profiles/cfg2_launch_list.txt)
 #   cfg3:swiglu  -- the 18 launches of one cfg3 replay (profiles/cfg3_launch_list.txt)
 #   cfg5:swiglu  -- the 12 launches of one cfg5 replay (profiles/gemm_qdec_cfg5.txt)
-NCU_TRAFFIC_PER_STEP = {"cfg2:gelu": 1013465344, "cfg3:swiglu": 3237011456, "cfg5:swiglu": 5183200000}
+NCU_TRAFFIC_PER_STEP = {"cfg2:gelu": 1013465344, "cfg2:swiglu": 1417670144, "cfg3:swiglu": 3237011456,
+                        "cfg5:swiglu": 5183200000}
 
 
 def parse():
