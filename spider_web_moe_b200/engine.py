@@ -27,7 +27,7 @@ import torch
 
 from . import _lib as L
 from .config import ModelConfig, from_any
-from .quant import Int4Tensor, quantize_fp8_per_channel, quantize_int4
+from .quant import Int4Tensor, dequantize_int4, quantize_fp8_per_channel, quantize_int4
 
 
 def _act_code(dtype: torch.dtype) -> int:
@@ -148,13 +148,10 @@ class BlockEngine:
                 q = t["w_" + short]
                 if fmt == "fp8":
                     t["w_" + short] = q.view(torch.float8_e4m3fn).to(torch.bfloat16).contiguous()
-                else:
-                    sc = t.pop("s_" + short).float()
-                    lo = (q & 0x0F).to(torch.int8)
-                    hi = (q >> 4).to(torch.int8)
-                    qq = torch.stack([torch.where(lo > 7, lo - 16, lo), torch.where(hi > 7, hi - 16, hi)], dim=-1)
-                    qq = qq.reshape(*q.shape[:-1], q.shape[-1] * 2).float()
-                    t["w_" + short] = (qq * sc.repeat_interleave(self.group_size, dim=-1)).to(torch.bfloat16).contiguous()
+                else:  # q * (bf16 group scale) in fp32 is exact; one rounding to bf16
+                    sc = t.pop("s_" + short)
+                    shape = (*q.shape[:-1], q.shape[-1] * 2)
+                    t["w_" + short] = dequantize_int4(q, sc, shape, self.group_size, torch.bfloat16).contiguous()
             fmt = "bf16"
         self.swiglu = swiglu and has_experts
         if self.swiglu:
