@@ -875,7 +875,8 @@ tc_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_
 // LINEAR outputs may be K-split (p.splits partial sums, as the other
 // schedules), which multiplies the items of small problems.
 // Warps: 0-3 epilogue, 4-19 convert (two groups of eight), 20 weight TMA,
-// 21 MMA (+TMEM), 22 token-row TMA (16-row boxes, or tile::gather4).
+// 21 MMA (+TMEM), 22 token-row TMA (16-row boxes, one 128-row box for items
+// of more than 32 rows, or tile::gather4).
 template <int WFMT, int EPI>
 struct QCfg {
   static constexpr bool kIL = EPI == SB_EPI_SWIGLU_IL;
