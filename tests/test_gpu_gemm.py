@@ -227,18 +227,19 @@ def test_cta_pair_kernel(epi, rows, cuda_device):
 
 
 @pytest.mark.parametrize("wfmt", ["fp8", "int4"])
-@pytest.mark.parametrize("epi", ["linear", "swiglu_il"])
-def test_quantised_decode_many_items(wfmt, epi, cuda_device):
+@pytest.mark.parametrize("epi,m", [("linear", 192), ("swiglu_il", 256), ("swiglu_il", 192), ("gelu", 320)])
+def test_quantised_decode_many_items(wfmt, epi, m, cuda_device):
     """The quantised decode kernel at a cfg5-like shape: 128 groups with
     Zipf-skewed rows (2048 in all, the largest above 256: two items), a weight
     matrix whose rows are not a multiple of 128 (LINEAR), and more items than
-    SMs, so every CTA walks several items and both TMEM accumulators turn over."""
+    SMs, so every CTA walks several items and both TMEM accumulators turn over.
+    Weight matrices whose rows end inside a 256-row tile: LINEAR 192, GELU 320,
+    SwiGLU 384 interleaved rows (the last tile holds one 128-row block)."""
     g = torch.Generator().manual_seed(21)
     weights = 1.0 / torch.arange(1, 129).float() ** 1.1
     picks = torch.multinomial(weights, 2048, replacement=True, generator=g)
     rows = [int(v) for v in torch.bincount(picks, minlength=128)]
     rows[0] = max(rows[0], 300)
-    m = 192 if epi == "linear" else 256
     got, want = run_case(rows, m, 512, wfmt, epi, "tcgen05", cuda_device, gather=epi != "linear", seed=13)
     check(got, want, epi)
 
