@@ -52,9 +52,10 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 #   cfg2:gelu    -- the 18 launches of one cfg2 replay with GELU experts (profiles/gemm_tcgen05_cfg2.txt)
 #   cfg2:swiglu  -- the 18 launches of one cfg2 replay (profiles/cfg2_launch_list.txt)
 #   cfg3:swiglu  -- the 18 launches of one cfg3 replay (profiles/cfg3_launch_list.txt)
+#   cfg4:swiglu  -- the 18 launches of one cfg4 step (profiles/cfg4_launch_list.txt)
 #   cfg5:swiglu  -- the 12 launches of one cfg5 replay (profiles/gemm_qdec_cfg5.txt)
 NCU_TRAFFIC_PER_STEP = {"cfg2:gelu": 1013465344, "cfg2:swiglu": 1417670144, "cfg3:swiglu": 3237011456,
-                        "cfg5:swiglu": 5183200000}
+                        "cfg4:swiglu": 12730709760, "cfg5:swiglu": 5183200000}
 
 
 def parse():
